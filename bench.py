@@ -1,0 +1,389 @@
+#!/usr/bin/env python
+"""Benchmark of the ReAttention recall scorer (un-rotate + q·K^T + exact top-k).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl prism|reference]
+                    [--workload NAME]
+
+Metric: KV tokens scored and top-k'd per second (keys of the cached sequence
+processed per second, all heads), whole job.
+
+* N = 1 runs ``decode-128k``: one decode step, 32 query / 8 KV heads,
+  head_dim 128, 131072 RoPE'd bf16 keys, k = 4096 per query head.
+* N > 1 (one process per GPU, launched by torchrun) runs ``decode-1m-sharded``:
+  1,048,576 keys split evenly over the N ranks (strong scaling), k = 8192, the
+  per-rank candidates all-gathered with NCCL and merged on every GPU.
+
+A step is one full call of the op on resident inputs; W untimed steps, then K
+steps timed with CUDA events between barriers, max over ranks. The key cache
+(268 MB at 128K, 2 GB at 1M) is larger than the 126 MB L2, so no flush is
+needed between steps. ``e2e`` repeats the K steps through the same public call
+with pinned host inputs copied in and the result (indices + scores) copied out
+inside the timed region. ``--impl reference`` times the reference's dense
+PyTorch path restated in the CPU oracle on the host cores (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "KV tokens scored+top-k'd/sec"
+UNIT = "KV tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="prism", choices=["prism", "reference"])
+    ap.add_argument("--workload", default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def pick_workload(args, world):
+    from prism_test_b200 import workloads as W
+    name = args.workload or ("decode-128k" if world == 1 else "decode-1m-sharded")
+    return W.WORKLOADS[name]
+
+
+def config_of(wl, world):
+    return {
+        "workload": wl.name, "B": wl.B, "Hq": wl.Hq, "Hkv": wl.Hkv, "Sq": wl.Sq, "Sk": wl.Sk,
+        "topk": wl.topk, "head_dim": wl.D, "rope_theta": wl.theta, "key_dtype": "bf16",
+        "causal_offset": wl.causal_offset, "shards": world,
+        "parallelism": "single GPU" if world == 1 else f"sequence-sharded x{world} (NCCL all-gather + device merge)",
+        "l2": "inputs larger than L2 (cached keys %d MB per rank > 126 MB), no flush" % (wl.kv_bytes // world >> 20),
+    }
+
+
+# ---------------------------------------------------------------- clocks (NVML)
+class ClockSampler:
+    """Samples SM clock and throttle reasons on a background thread."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, index: int, period_s: float = 0.002):
+        self.ok = False
+        self.samples = []
+        self.reasons = 0
+        self.period = period_s
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001
+            self.max_mhz = None
+
+    def _sample(self):
+        self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+        try:
+            self.reasons |= int(self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+        except Exception:  # noqa: BLE001
+            self.reasons |= int(self.nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h))
+
+    def _loop(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def start(self):
+        if not self.ok:
+            return
+        self._stop = threading.Event()
+        self._sample()
+        self.t = threading.Thread(target=self._loop, daemon=True)
+        self.t.start()
+
+    def stop(self):
+        if not self.ok:
+            return
+        self._stop.set()
+        self.t.join()
+        self._sample()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [n for b, n in self.REASONS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:  # noqa: BLE001
+            pass
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(kernel: str, workload: str):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(workload, {}).get(kernel)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_baseline(wl, max_seconds=20.0):
+    """The reference's dense CPU path (oracle restatement) on the host cores.
+
+    Runs whole calls (or, when one call would exceed the budget, one KV head of
+    it and scales by the number of KV heads) and returns KV tokens/s."""
+    from oracle import reattention_topk as orc
+    from prism_test_b200 import workloads as W
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    heads = wl.Hkv if wl.Sk * wl.Sq <= (1 << 17) * 8 else 1
+    sub = wl.with_(Hkv=heads, Hq=heads * (wl.Hq // wl.Hkv))
+    x = W.make_inputs(sub, "cpu")
+    orc.dense_topk(x["q"], x["k"], sub.topk, x["inv_freq"], 0, sub.causal_offset)  # warm-up
+    times = []
+    t_budget = time.perf_counter()
+    while len(times) < 5 and time.perf_counter() - t_budget < max_seconds:
+        t0 = time.perf_counter()
+        orc.dense_topk(x["q"], x["k"], sub.topk, x["inv_freq"], 0, sub.causal_offset)
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    frac = heads / wl.Hkv
+    value = wl.Sk * frac / best
+    sample = (f"{'full call' if heads == wl.Hkv else f'{heads} of {wl.Hkv} KV heads'} of {wl.name} "
+              f"(un-rotate fp32, einsum, topk), best of {len(times)} after 1 warm-up")
+    return {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+            "seconds_per_call": best / frac}
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    wl = pick_workload(args, world)
+    from oracle import reattention_topk as orc
+    from prism_test_b200 import workloads as W
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    # bounded sample per step: one KV head (and its query group) of the workload
+    sub = wl.with_(Hkv=1, Hq=wl.Hq // wl.Hkv)
+    x = W.make_inputs(sub, "cpu")
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    est = None
+    for _ in range(max(1, warm)):
+        t0 = time.perf_counter()
+        orc.dense_topk(x["q"], x["k"], sub.topk, x["inv_freq"], 0, sub.causal_offset)
+        est = time.perf_counter() - t0
+    # keep the whole run within a few minutes
+    steps = min(steps, max(3, int(120.0 / max(est, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        orc.dense_topk(x["q"], x["k"], sub.topk, x["inv_freq"], 0, sub.causal_offset)
+    dt = (time.perf_counter() - t0) / steps
+    value = wl.Sk / wl.Hkv / dt  # KV tokens (all heads) per second
+    sample = f"1 of {wl.Hkv} KV heads of {wl.name} per step (un-rotate fp32, einsum, topk); {steps} steps"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_of(wl, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU arm
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    from prism_test_b200 import _lib, einsum_topk_func
+    from prism_test_b200 import workloads as W
+    from prism_test_b200.sharded import shard_bounds, sharded_einsum_topk
+
+    lib = _lib.load()
+    wl = pick_workload(args, world)
+    start, stop = shard_bounds(wl.Sk, rank, world)
+    x = W.make_inputs(wl, dev, shard=(rank, world) if world > 1 else None)
+    q, k, inv = x["q"], x["k"], x["inv_freq"]
+
+    def step(qq, kk):
+        if world == 1:
+            return einsum_topk_func(qq, kk, wl.topk, inv_freq=inv, return_scores=True,
+                                    causal_offset=wl.causal_offset)
+        return sharded_einsum_topk(qq, kk, wl.topk, shard_start=start, inv_freq=inv, return_scores=True)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(3, args.warmup)):
+        step(q, k)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    lib.prism_profile_start(4 * args.steps + 16)
+    n0 = lib.prism_launch_count()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    clocks.start()
+    ev0.record()
+    for _ in range(args.steps):
+        step(q, k)
+    ev1.record()
+    torch.cuda.synchronize()
+    clocks.stop()
+    lib.prism_profile_stop()
+    launches = lib.prism_launch_count() - n0
+    barrier()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_per_step = ms / args.steps
+
+    # dominant kernel: the scorer (un-rotate + q·K^T), timed per launch
+    n_sc = _lib.ctypes.c_int64(0)
+    t_sc = _lib.ctypes.c_double(0.0)
+    lib.prism_profile_read(_lib.KERNEL_SCORE, _lib.ctypes.byref(n_sc), _lib.ctypes.byref(t_sc))
+    n_se = _lib.ctypes.c_int64(0)
+    t_se = _lib.ctypes.c_double(0.0)
+    lib.prism_profile_read(_lib.KERNEL_SELECT, _lib.ctypes.byref(n_se), _lib.ctypes.byref(t_se))
+    n_me = _lib.ctypes.c_int64(0)
+    t_me = _lib.ctypes.c_double(0.0)
+    lib.prism_profile_read(_lib.KERNEL_MERGE, _lib.ctypes.byref(n_me), _lib.ctypes.byref(t_me))
+    score_ms = t_sc.value / max(1, n_sc.value)
+    bytes_per_launch = (stop - start) * wl.B * wl.Hkv * wl.D * 2  # keys of this rank, read once
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_per_launch / (score_ms * 1e-3) / 1e9
+    achieved = max_over_ranks(-achieved) * -1.0 if world > 1 else achieved  # slowest rank
+
+    value = wl.Sk * args.steps / (ms * 1e-3)
+
+    # ---- end to end through the public call, host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        q_h = q.cpu().pin_memory()
+        k_h = k.cpu().pin_memory()
+        rows = wl.B * wl.Hq * wl.Sq
+        idx_h = torch.empty((rows * wl.topk,), dtype=torch.int32).pin_memory()
+        sc_h = torch.empty((rows * wl.topk,), dtype=torch.float32).pin_memory()
+        q_d = torch.empty_like(q)
+        k_d = torch.empty_like(k)
+        for _ in range(2):
+            q_d.copy_(q_h, non_blocking=True)
+            k_d.copy_(k_h, non_blocking=True)
+            oi, os_ = step(q_d, k_d)
+            idx_h.copy_(oi.reshape(-1), non_blocking=True)
+            sc_h.copy_(os_.reshape(-1), non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            q_d.copy_(q_h, non_blocking=True)
+            k_d.copy_(k_h, non_blocking=True)
+            oi, os_ = step(q_d, k_d)
+            idx_h.copy_(oi.reshape(-1), non_blocking=True)
+            sc_h.copy_(os_.reshape(-1), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        ems = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": wl.Sk * args.steps / (ems * 1e-3), "unit": UNIT,
+               "h2d_bytes_per_step": int(q_h.numel() * q_h.element_size() + k_h.numel() * k_h.element_size()) * world,
+               "d2h_bytes_per_step": int(idx_h.numel() * 4 + sc_h.numel() * 4) * world,
+               "ms_per_step": ems / args.steps}
+
+    base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        base = cpu_baseline(wl)
+
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; see prism_test_b200/workloads.py)",
+        "config": config_of(wl, world),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind,
+                     "traffic": ncu_traffic("score", wl.name),
+                     "kernel": "decode scorer (TMA ring, fused inverse RoPE, fp32 q·K^T)",
+                     "bytes_per_launch": bytes_per_launch, "launch_ms": score_ms},
+        "kernels_ms_per_step": {
+            "score": t_sc.value / max(1, args.steps),
+            "select": t_se.value / max(1, args.steps),
+            "merge": t_me.value / max(1, args.steps),
+        },
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+        "cpu_baseline": base,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

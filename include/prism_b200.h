@@ -1,0 +1,143 @@
+/*
+ * prism_b200 — C ABI of the B200 (sm_100a) ReAttention recall scorer.
+ *
+ * The scorer is the hot path of Prism-Test's ReAttention method
+ * (RUSH-Intelligence/Prism-Test, eval_harness/): inverse-RoPE un-rotation of the
+ * cached keys, position-agnostic q·K^T per GQA head, exact per-query top-k,
+ * sorted like torch.topk. Every entry point takes plain device pointers, sizes
+ * and a cudaStream_t passed as void*; nothing allocates except where noted, no
+ * entry point synchronises the stream unless its comment says so, and results
+ * are written asynchronously on the given stream.
+ *
+ * Return value of every int function: PRISM_OK (0) or a negative PRISM_E_*
+ * code; prism_last_error() returns a message for the calling thread's last
+ * failure.
+ */
+#ifndef PRISM_B200_H_
+#define PRISM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define PRISM_API __attribute__((visibility("default")))
+#else
+#define PRISM_API
+#endif
+
+#define PRISM_ABI_VERSION 1
+
+/* element types of q and k */
+#define PRISM_DTYPE_BF16 0
+#define PRISM_DTYPE_FP16 1
+
+/* selection modes */
+#define PRISM_MODE_EXACT 0    /* exact top-k of the fp32 scores (torch.topk semantics) */
+#define PRISM_MODE_BLOCKMAX 1 /* per-128-key-block maxima, top-1 / top-4 (Triton kernel semantics) */
+
+/* status codes */
+#define PRISM_OK 0
+#define PRISM_E_INVALID (-1)       /* bad argument (shape, stride, alignment, range) */
+#define PRISM_E_UNSUPPORTED (-2)   /* valid request outside what the kernels implement */
+#define PRISM_E_WORKSPACE (-3)     /* workspace missing or too small */
+#define PRISM_E_CUDA (-4)          /* a CUDA runtime call failed */
+#define PRISM_E_DEVICE_STATUS (-5) /* a kernel reported a device-side error */
+
+/*
+ * Fused un-rotate + score + top-k.
+ *
+ * Replaces eval_harness/kernels/einsum_topk.py:164-225 (einsum_topk_func,
+ * re-exported by eval_harness/kernels/__init__.py:12-15 and called from
+ * eval_harness/attention_methods/reattention.py:483) and, with inv_freq given,
+ * also ReAttentionMethod._unrotate_keys (reattention.py:743-793) in front of it.
+ * With mode PRISM_MODE_EXACT the result equals ReAttentionMethod._dense_topk
+ * (reattention.py:486-498): scores = einsum("bhqd,bhmd->bhqm", q, repeat_kv(k))
+ * in fp32, then topk(topk, dim=-1).
+ *
+ *   q          [B, Hq, Sq, D] elements of `dtype`; q_strides[4] in elements,
+ *              q_strides[3] must be 1.
+ *   k          [B, Hkv, Sk, D] elements of `dtype`; k_strides[3] == 1 and
+ *              k_strides[2] == D (key rows contiguous), base and k_strides[0..1]
+ *              16-byte aligned. Hq % Hkv == 0; q head h reads kv head h / (Hq/Hkv).
+ *   D          must be 128.
+ *   inv_freq   [D/2] fp32 device pointer or NULL. When given, k holds RoPE-rotated
+ *              keys (HF rotate_half layout) of absolute positions pos_offset + j
+ *              and is un-rotated with angle fp32(position) * inv_freq[i].
+ *              pos_offset + Sk must be below 2^22.
+ *   causal_offset  >= 0: key j is visible to query row s iff j <= causal_offset + s
+ *              (invisible keys score -inf); < 0: no mask.
+ *   topk       1 <= topk <= Sk, and topk <= 16384 (exact mode);
+ *              topk in {1, 4} with Sq % 128 == 0 and Sk % 128 == 0 (blockmax mode).
+ *   index_base added to every output index (global index of key 0 of this shard).
+ *   out_idx    [B, Hq, Sq, topk] int32, contiguous. Sorted by descending score,
+ *              ties by ascending index.
+ *   out_scores [B, Hq, Sq, topk] fp32, contiguous, or NULL.
+ *   workspace  device memory of at least prism_einsum_topk_workspace_size() bytes.
+ *   stream     cudaStream_t.
+ */
+PRISM_API int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int dtype,
+                      int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D,
+                      const int64_t* q_strides, const int64_t* k_strides, int64_t pos_offset,
+                      int64_t causal_offset, int32_t topk, int32_t mode, int64_t index_base,
+                      int32_t* out_idx, float* out_scores, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Workspace bytes prism_einsum_topk needs for this shape (0 on invalid input). */
+PRISM_API size_t prism_einsum_topk_workspace_size(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk,
+                                        int32_t topk, int32_t mode);
+
+/*
+ * Exact top-k over candidate lists: for each of `rows` rows, picks the topk
+ * largest of n (score, index) pairs laid out with row stride ld (ld % 4 == 0,
+ * 16-byte aligned rows) and writes them sorted like prism_einsum_topk.
+ * This is the device merge of the sequence-sharded path: the candidates are the
+ * per-rank top-k lists after an all-gather, indices already global. It has no
+ * single reference counterpart; it reproduces torch.topk over the union of the
+ * shards (reattention.py:497) and the sorted merge of
+ * eval_harness/kernels/bitonic_merge_wrapper.py:36-52 for any width.
+ * Needs no workspace.
+ */
+PRISM_API int prism_topk_merge(const float* cand_scores, const int32_t* cand_idx, int64_t rows, int64_t n,
+                     int64_t ld, int32_t topk, int32_t* out_idx, float* out_scores, void* stream);
+
+/*
+ * Reads the device status word kept at the start of `workspace` (synchronises
+ * `stream`), stores it in *status_out and resets it to 0. A non-zero value means
+ * a kernel gave up on a bounded wait (1), rejected an access (2) or ran out of
+ * candidate space (3) since the previous read.
+ */
+PRISM_API int prism_read_status(void* workspace, int* status_out, void* stream);
+
+/*
+ * Measurement aids (no reference counterpart; used by bench.py). While
+ * profiling is on, every kernel launch of the library on any stream is
+ * bracketed by a pair of CUDA events taken from a pool of `capacity` pairs
+ * (launches beyond the pool are counted but not timed). prism_profile_read
+ * synchronises those events and returns, for one kernel kind, the number of
+ * timed launches and their summed device duration. prism_launch_count counts
+ * every kernel launch of the library since it was loaded. Process-global;
+ * call from one host thread.
+ */
+#define PRISM_KERNEL_SCORE 0  /* decode scorer (un-rotate + q·K^T) */
+#define PRISM_KERNEL_SELECT 1 /* exact top-k selection of a score matrix */
+#define PRISM_KERNEL_MERGE 2  /* top-k merge of gathered shard candidates */
+PRISM_API int prism_profile_start(int32_t capacity);
+PRISM_API int prism_profile_stop(void);
+PRISM_API int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms);
+PRISM_API int64_t prism_launch_count(void);
+
+/* Message describing the calling thread's most recent failure ("" if none). */
+PRISM_API const char* prism_last_error(void);
+
+/* PRISM_ABI_VERSION of the loaded library. */
+PRISM_API int prism_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PRISM_B200_H_ */

@@ -1,0 +1,296 @@
+// C-ABI entry points (include/prism_b200.h): argument checking, workspace
+// layout and kernel orchestration on the caller's stream.
+#include <algorithm>
+#include <atomic>
+#include <vector>
+#include <climits>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/prism_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PRISM_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+constexpr size_t kStatusBytes = 256;  // status word + padding, keeps scores 256-B aligned
+constexpr int64_t kMaxPosition = int64_t(1) << 22;
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+int num_sms_current_device() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n;
+}
+
+// ---- measurement aids ----------------------------------------------------------
+std::atomic<int64_t> g_launches{0};
+struct ProfRec {
+  int kernel;
+  cudaEvent_t start, stop;
+};
+std::vector<cudaEvent_t> g_prof_pool;  // 2 * capacity events
+std::vector<ProfRec> g_prof_recs;
+bool g_prof_on = false;
+size_t g_prof_next = 0;
+int64_t g_prof_untimed[3] = {0, 0, 0};
+
+// Runs `launch` (which enqueues one kernel on `stream`), counting it and, while
+// profiling is on, bracketing it with a pair of events from the pool.
+template <typename F>
+cudaError_t launch_counted(int kernel, cudaStream_t stream, F&& launch) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (!g_prof_on) return launch();
+  if (g_prof_next + 2 > g_prof_pool.size()) {
+    ++g_prof_untimed[kernel];
+    return launch();
+  }
+  cudaEvent_t a = g_prof_pool[g_prof_next], b = g_prof_pool[g_prof_next + 1];
+  g_prof_next += 2;
+  cudaError_t e = cudaEventRecord(a, stream);
+  if (e != cudaSuccess) return e;
+  e = launch();
+  if (e != cudaSuccess) return e;
+  e = cudaEventRecord(b, stream);
+  if (e == cudaSuccess) g_prof_recs.push_back(ProfRec{kernel, a, b});
+  return e;
+}
+
+size_t exact_workspace(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk) {
+  const int64_t ld = round_up(Sk, 4);
+  return kStatusBytes + size_t(B * Hq * Sq) * size_t(ld) * sizeof(float);
+}
+
+}  // namespace
+
+extern "C" {
+
+int prism_abi_version(void) { return PRISM_ABI_VERSION; }
+
+const char* prism_last_error(void) { return g_last_error.c_str(); }
+
+size_t prism_einsum_topk_workspace_size(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk,
+                                        int32_t topk, int32_t mode) {
+  (void)topk;
+  if (B <= 0 || Hq <= 0 || Sq <= 0 || Sk <= 0) return 0;
+  if (mode != PRISM_MODE_EXACT && mode != PRISM_MODE_BLOCKMAX) return 0;
+  return exact_workspace(B, Hq, Sq, Sk);
+}
+
+int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int dtype, int64_t B,
+                      int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D,
+                      const int64_t* q_strides, const int64_t* k_strides, int64_t pos_offset,
+                      int64_t causal_offset, int32_t topk, int32_t mode, int64_t index_base,
+                      int32_t* out_idx, float* out_scores, void* workspace,
+                      size_t workspace_bytes, void* stream_ptr) {
+  g_last_error.clear();
+  if (!q || !k || !out_idx || !q_strides || !k_strides)
+    return fail(PRISM_E_INVALID, "null pointer argument");
+  if (dtype != PRISM_DTYPE_BF16 && dtype != PRISM_DTYPE_FP16)
+    return fail(PRISM_E_INVALID, "dtype must be PRISM_DTYPE_BF16 or PRISM_DTYPE_FP16");
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Sk <= 0)
+    return fail(PRISM_E_INVALID, "all of B, Hq, Hkv, Sq, Sk must be positive");
+  if (Hq % Hkv != 0) return fail(PRISM_E_INVALID, "num_heads must be divisible by num_heads_k");
+  if (D != prism::kHeadDim) return fail(PRISM_E_UNSUPPORTED, "head_dim must be 128, got %lld", (long long)D);
+  if (q_strides[3] != 1 || k_strides[3] != 1)
+    return fail(PRISM_E_INVALID, "q and k must have unit stride in the last dimension");
+  if (k_strides[2] != D)
+    return fail(PRISM_E_INVALID, "key rows must be contiguous (k.stride(-2) == head_dim)");
+  if ((reinterpret_cast<uintptr_t>(k) & 15u) != 0 || (k_strides[0] * 2) % 16 != 0 ||
+      (k_strides[1] * 2) % 16 != 0)
+    return fail(PRISM_E_INVALID, "k base and batch/head strides must be 16-byte aligned");
+  if (mode != PRISM_MODE_EXACT && mode != PRISM_MODE_BLOCKMAX)
+    return fail(PRISM_E_INVALID, "unknown mode %d", mode);
+  if (mode == PRISM_MODE_BLOCKMAX)
+    return fail(PRISM_E_UNSUPPORTED, "blockmax mode is not built in this library version");
+  if (topk < 1 || int64_t(topk) > Sk)
+    return fail(PRISM_E_INVALID, "topk must satisfy 1 <= topk <= Sk (topk=%d, Sk=%lld)", topk,
+                (long long)Sk);
+  if (topk > prism::kSelectMaxK)
+    return fail(PRISM_E_UNSUPPORTED, "topk above %d is not supported", prism::kSelectMaxK);
+  if (inv_freq && (pos_offset < 0 || pos_offset + Sk > kMaxPosition))
+    return fail(PRISM_E_UNSUPPORTED, "RoPE positions must lie in [0, 2^22)");
+  if (index_base < 0 || index_base + Sk - 1 > INT32_MAX)
+    return fail(PRISM_E_INVALID, "index_base + Sk must fit in int32");
+  if (Sk > INT32_MAX || B * Hq * Sq > (int64_t(1) << 31))
+    return fail(PRISM_E_UNSUPPORTED, "problem too large");
+  if (Hq > prism::kDecodeMaxRows)
+    return fail(PRISM_E_UNSUPPORTED, "more than %d query heads", prism::kDecodeMaxRows);
+
+  const size_t need = exact_workspace(B, Hq, Sq, Sk);
+  if (!workspace || workspace_bytes < need)
+    return fail(PRISM_E_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(PRISM_E_INVALID, "workspace must be 256-byte aligned");
+
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* status = reinterpret_cast<int*>(ws);
+  float* scores = reinterpret_cast<float*>(ws + kStatusBytes);
+  const int64_t ld = round_up(Sk, 4);
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
+
+  // ---- scoring: rows of one batch resident per CTA, chunk Sq to fit ----------
+  const int sq_chunk = int(std::max<int64_t>(1, prism::kDecodeMaxRows / Hq));
+  const int nsm = num_sms_current_device();
+  for (int64_t s0 = 0; s0 < Sq; s0 += sq_chunk) {
+    prism::DecodeArgs a{};
+    a.q = q;
+    a.k = k;
+    a.inv_freq = inv_freq;
+    a.B = int(B);
+    a.Hq = int(Hq);
+    a.Hkv = int(Hkv);
+    a.G = int(Hq / Hkv);
+    a.Sq = int(Sq);
+    a.s0 = int(s0);
+    a.sq_n = int(std::min<int64_t>(sq_chunk, Sq - s0));
+    a.Sk = int(Sk);
+    a.q_sb = q_strides[0];
+    a.q_sh = q_strides[1];
+    a.q_ss = q_strides[2];
+    a.k_sb = k_strides[0];
+    a.k_sh = k_strides[1];
+    a.pos_offset = pos_offset;
+    a.causal = causal_offset >= 0 ? 1 : 0;
+    a.causal_offset = causal_offset;
+    a.scores = scores;
+    a.ld = ld;
+    a.ntiles = int((Sk + 127) / 128);
+    a.status = status;
+    e = launch_counted(PRISM_KERNEL_SCORE, stream,
+                       [&] { return prism::launch_decode_scores(a, dtype, nsm, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
+  }
+
+  // ---- selection ------------------------------------------------------------------
+  prism::SelectArgs s{};
+  s.scores = scores;
+  s.idx_in = nullptr;
+  s.rows = B * Hq * Sq;
+  s.n = Sk;
+  s.ld = ld;
+  s.k = topk;
+  s.index_base = index_base;
+  s.out_idx = out_idx;
+  s.out_scores = out_scores;
+  s.status = status;
+  e = launch_counted(PRISM_KERNEL_SELECT, stream, [&] { return prism::launch_select_topk(s, stream); });
+  if (e != cudaSuccess) return cuda_fail(e, "select kernel launch");
+  return PRISM_OK;
+}
+
+int prism_topk_merge(const float* cand_scores, const int32_t* cand_idx, int64_t rows, int64_t n,
+                     int64_t ld, int32_t topk, int32_t* out_idx, float* out_scores,
+                     void* stream_ptr) {
+  g_last_error.clear();
+  if (!cand_scores || !cand_idx || !out_idx) return fail(PRISM_E_INVALID, "null pointer argument");
+  if (rows < 0 || n <= 0 || ld < n || ld % 4 != 0)
+    return fail(PRISM_E_INVALID, "need rows >= 0, n > 0, ld >= n and ld %% 4 == 0");
+  if ((reinterpret_cast<uintptr_t>(cand_scores) & 15u) || (reinterpret_cast<uintptr_t>(cand_idx) & 15u))
+    return fail(PRISM_E_INVALID, "candidate arrays must be 16-byte aligned");
+  if (topk < 1 || int64_t(topk) > n) return fail(PRISM_E_INVALID, "topk must satisfy 1 <= topk <= n");
+  if (topk > prism::kSelectMaxK)
+    return fail(PRISM_E_UNSUPPORTED, "topk above %d is not supported", prism::kSelectMaxK);
+  prism::SelectArgs s{};
+  s.scores = cand_scores;
+  s.idx_in = cand_idx;
+  s.rows = rows;
+  s.n = n;
+  s.ld = ld;
+  s.k = topk;
+  s.index_base = 0;
+  s.out_idx = out_idx;
+  s.out_scores = out_scores;
+  s.status = nullptr;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  cudaError_t e =
+      launch_counted(PRISM_KERNEL_MERGE, stream, [&] { return prism::launch_select_topk(s, stream); });
+  if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
+  return PRISM_OK;
+}
+
+int prism_profile_start(int32_t capacity) {
+  g_last_error.clear();
+  if (capacity < 0) return fail(PRISM_E_INVALID, "capacity must be >= 0");
+  const size_t want = size_t(capacity) * 2;
+  while (g_prof_pool.size() < want) {
+    cudaEvent_t ev;
+    cudaError_t e = cudaEventCreate(&ev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+    g_prof_pool.push_back(ev);
+  }
+  g_prof_recs.clear();
+  g_prof_next = 0;
+  g_prof_untimed[0] = g_prof_untimed[1] = g_prof_untimed[2] = 0;
+  g_prof_on = capacity > 0;
+  return PRISM_OK;
+}
+
+int prism_profile_stop(void) {
+  g_prof_on = false;
+  return PRISM_OK;
+}
+
+int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms) {
+  g_last_error.clear();
+  if (!launches || !total_ms || kernel < 0 || kernel > 2)
+    return fail(PRISM_E_INVALID, "bad kernel id or null output");
+  int64_t n = 0;
+  double ms = 0.0;
+  for (const ProfRec& r : g_prof_recs) {
+    if (r.kernel != kernel) continue;
+    cudaError_t e = cudaEventSynchronize(r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize");
+    float t = 0.f;
+    e = cudaEventElapsedTime(&t, r.start, r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventElapsedTime");
+    ms += t;
+    ++n;
+  }
+  *launches = n;
+  *total_ms = ms;
+  return PRISM_OK;
+}
+
+int64_t prism_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int prism_read_status(void* workspace, int* status_out, void* stream_ptr) {
+  g_last_error.clear();
+  if (!workspace || !status_out) return fail(PRISM_E_INVALID, "null pointer argument");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  int host = 0;
+  cudaError_t e = cudaMemcpyAsync(&host, workspace, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the status word");
+  *status_out = host;
+  if (host != 0) {
+    e = cudaMemsetAsync(workspace, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "resetting the status word");
+  }
+  return PRISM_OK;
+}
+
+}  // extern "C"

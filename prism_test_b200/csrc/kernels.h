@@ -1,0 +1,55 @@
+// Internal launch interface shared by the .cu files of the extension.
+// (The public C-ABI lives in include/prism_b200.h.)
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace prism {
+
+enum DType : int { kBF16 = 0, kFP16 = 1 };
+
+// --- decode scorer (CUDA cores; few query rows per KV head) ----------------
+struct DecodeArgs {
+  const void* q;            // [B, Hq, Sq, 128], innermost stride 1
+  const void* k;            // [B, Hkv, Sk, 128], rows contiguous (stride(-2) == 128)
+  const float* inv_freq;    // [64] or nullptr (keys already un-rotated)
+  int B, Hq, Hkv, G;        // G = Hq / Hkv
+  int Sq;                   // full query length (row indexing)
+  int s0, sq_n;             // this launch scores query rows [s0, s0 + sq_n)
+  int Sk;
+  int64_t q_sb, q_sh, q_ss; // q strides in elements
+  int64_t k_sb, k_sh;       // k strides in elements
+  int64_t pos_offset;       // absolute position of key 0 (RoPE)
+  int causal;               // 1: key j visible to query s iff j <= causal_offset + s
+  int64_t causal_offset;
+  float* scores;            // [B*Hq*Sq, ld] fp32 workspace
+  int64_t ld;
+  int ntiles;
+  int* status;
+};
+
+// rows (Hq * sq_n) resident per CTA must not exceed this
+constexpr int kDecodeMaxRows = 128;
+
+cudaError_t launch_decode_scores(const DecodeArgs& a, int dtype, int num_sms,
+                                 cudaStream_t stream);
+
+// --- exact per-row top-k selection over a score matrix ----------------------
+struct SelectArgs {
+  const float* scores;      // [rows, ld]
+  const int32_t* idx_in;    // [rows, ld] or nullptr (index = column)
+  int64_t rows;
+  int64_t n;                // valid columns per row
+  int64_t ld;
+  int k;                    // 1 <= k <= min(n, kSelectMaxK)
+  int64_t index_base;       // added to column indices (ignored when idx_in given)
+  int32_t* out_idx;         // [rows, k]
+  float* out_scores;        // [rows, k] or nullptr
+  int* status;
+};
+constexpr int kSelectMaxK = 16384;
+
+cudaError_t launch_select_topk(const SelectArgs& a, cudaStream_t stream);
+
+}  // namespace prism

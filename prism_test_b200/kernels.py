@@ -1,0 +1,187 @@
+"""Drop-in for ``eval_harness.kernels.einsum_topk_func``.
+
+Reference interface: ``einsum_topk_func(q, k, topk) -> int32 [B, Hq, Sq, topk]``
+(eval_harness/kernels/einsum_topk.py:164-225), bound by the ReAttention callers
+as the module attribute ``reattention._einsum_topk_func``
+(eval_harness/attention_methods/reattention.py:131-137, called at :483).
+
+Differences from the reference launcher, all keyword-only extensions whose
+defaults keep the reference call working unchanged:
+
+* ``mode="exact"`` (default) returns the exact top-k of the fp32 scores, i.e.
+  what the reference's dense path ``ReAttentionMethod._dense_topk``
+  (reattention.py:486-498) selects, sorted by descending score (torch.topk
+  order). The reference Triton kernel's per-128-key block-maximum top-{1,4}
+  (``mode="blockmax"``) is a separate mode.
+* Any ``seqlen_q >= 1``, any ``seqlen_k``, any ``1 <= topk <= min(seqlen_k, 16384)``
+  in exact mode (the reference needs ``seqlen_q % 128 == 0``, ``seqlen_k % 128 == 0``
+  and ``topk in {1, 4}``).
+* ``inv_freq`` fuses ``ReAttentionMethod._unrotate_keys`` (reattention.py:743-793):
+  ``k`` then holds RoPE-rotated keys at absolute positions ``pos_offset + j``.
+* ``causal_offset``: key ``j`` is visible to query row ``s`` iff
+  ``j <= causal_offset + s`` (masked keys score ``-inf``).
+* ``index_base`` is added to every returned index (sequence shards).
+* ``return_scores=True`` also returns the fp32 scores of the selected keys.
+
+Argument errors raise ``AssertionError`` like the reference's ``assert``
+statements; CUDA failures raise ``PrismLibraryError`` (a ``RuntimeError``).
+Both are ``Exception``s, so the caller's ``use_triton_kernel='auto'`` fallback
+(reattention.py:408-418) keeps working. There is no CPU or PyTorch fallback.
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional, Tuple, Union
+
+import torch
+
+from . import _lib
+
+_SYNC_CHECK = os.environ.get("PRISM_SYNC_CHECK", "0") not in ("", "0")
+
+
+def _dtype_code(dt: torch.dtype) -> int:
+    return _lib.DTYPE_BF16 if dt == torch.bfloat16 else _lib.DTYPE_FP16
+
+
+def _rows_contiguous_aligned(k: torch.Tensor) -> bool:
+    if k.stride(-2) != k.shape[-1]:
+        return False
+    esz = k.element_size()
+    if k.data_ptr() % 16:
+        return False
+    return (k.stride(0) * esz) % 16 == 0 and (k.stride(1) * esz) % 16 == 0
+
+
+def einsum_topk_func(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    topk: int,
+    *,
+    inv_freq: Optional[torch.Tensor] = None,
+    pos_offset: int = 0,
+    causal_offset: Optional[int] = None,
+    index_base: int = 0,
+    return_scores: bool = False,
+    mode: str = "exact",
+) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
+    """Fused (un-rotate +) q·K^T + top-k on the GPU.
+
+    Parameters
+    ----------
+    q : Tensor [batch, num_heads, seqlen_q, 128], fp16/bf16, CUDA
+    k : Tensor [batch, num_kv_heads, seqlen_k, 128], same dtype and device
+    topk : int
+
+    Returns
+    -------
+    indices : int32 Tensor [batch, num_heads, seqlen_q, topk], sorted by
+        descending score (and ``scores`` fp32 of the same shape when
+        ``return_scores``).
+    """
+    batch, num_heads, seqlen_q, d = q.shape
+    batch_k, num_heads_k, seqlen_k, dk = k.shape
+    assert q.stride(-1) == 1 and k.stride(-1) == 1
+    assert num_heads % num_heads_k == 0, "num_heads must be divisible by num_heads_k"
+    assert d == dk and batch_k == batch, (
+        f"batch & head dimensions must match, but find q.shape={q.shape} and k.shape={k.shape}"
+    )
+    assert q.dtype == k.dtype and q.dtype in [torch.float16, torch.bfloat16], (
+        "All tensors must have the same type. Only support fp16 and bf16"
+    )
+    assert q.is_cuda and k.is_cuda, "All tensors must be sent to gpu"
+    assert q.device == k.device, "q and k must be on the same device"
+    assert d == 128, f"Only support d == 128, but find d={d}"
+    if mode == "exact":
+        mode_code = _lib.MODE_EXACT
+        assert 1 <= topk <= seqlen_k, f"need 1 <= topk <= seqlen_k, got topk={topk}, seqlen_k={seqlen_k}"
+    elif mode == "blockmax":
+        mode_code = _lib.MODE_BLOCKMAX
+        assert seqlen_q % 128 == 0 and seqlen_k % 128 == 0, (
+            f"blockmax mode needs seqlen_q % 128 == 0 && seqlen_k % 128 == 0, "
+            f"but find seqlen_q={seqlen_q}, seqlen_k={seqlen_k}"
+        )
+        assert topk == 1 or topk == 4, "Only support k == 1 or 4"
+    else:
+        raise AssertionError(f"unknown mode {mode!r}; use 'exact' or 'blockmax'")
+
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        if not _rows_contiguous_aligned(k):
+            k = k.contiguous()
+        invf_ptr = None
+        if inv_freq is not None:
+            assert inv_freq.numel() == d // 2, "inv_freq must have head_dim // 2 entries"
+            inv_freq = inv_freq.to(device=q.device, dtype=torch.float32).contiguous()
+            invf_ptr = inv_freq.data_ptr()
+        causal = -1 if causal_offset is None else int(causal_offset)
+        assert causal_offset is None or causal >= 0, "causal_offset must be >= 0"
+
+        out_idx = torch.empty((batch, num_heads, seqlen_q, topk), dtype=torch.int32, device=q.device)
+        out_scores = (
+            torch.empty((batch, num_heads, seqlen_q, topk), dtype=torch.float32, device=q.device)
+            if return_scores else None
+        )
+        ws_bytes = lib.prism_einsum_topk_workspace_size(batch, num_heads, seqlen_q, seqlen_k, topk, mode_code)
+        ws = torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=q.device)
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        rc = lib.prism_einsum_topk(
+            q.data_ptr(), k.data_ptr(), invf_ptr, _dtype_code(q.dtype),
+            batch, num_heads, num_heads_k, seqlen_q, seqlen_k, d,
+            _lib.i64_array(q.stride()), _lib.i64_array(k.stride()), int(pos_offset),
+            causal, int(topk), mode_code, int(index_base),
+            out_idx.data_ptr(), out_scores.data_ptr() if out_scores is not None else None,
+            ws.data_ptr(), ws.numel(), stream,
+        )
+        _lib.check(rc, "prism_einsum_topk")
+        if _SYNC_CHECK:
+            read_status(ws)
+    if return_scores:
+        return out_idx, out_scores
+    return out_idx
+
+
+def read_status(workspace: torch.Tensor) -> None:
+    """Synchronise and raise if a kernel reported a device-side error."""
+    lib = _lib.load()
+    st = _lib.ctypes.c_int(0)
+    rc = lib.prism_read_status(workspace.data_ptr(), _lib.ctypes.byref(st),
+                               torch.cuda.current_stream(workspace.device).cuda_stream)
+    _lib.check(rc, "prism_read_status")
+    if st.value != 0:
+        raise _lib.PrismLibraryError(f"device status {st.value} reported by a prism kernel")
+
+
+def topk_merge(cand_scores: torch.Tensor, cand_idx: torch.Tensor, topk: int,
+               return_scores: bool = True):
+    """Exact top-k of each row of (score, global index) candidate lists.
+
+    ``cand_scores`` fp32 and ``cand_idx`` int32, both ``[rows, n]`` on the
+    same CUDA device. Used to merge the per-shard top-k lists of the
+    sequence-sharded path after the NCCL all-gather.
+    """
+    assert cand_scores.dtype == torch.float32 and cand_idx.dtype == torch.int32
+    assert cand_scores.shape == cand_idx.shape and cand_scores.dim() == 2
+    assert cand_scores.is_cuda and cand_idx.is_cuda
+    rows, n = cand_scores.shape
+    assert 1 <= topk <= n
+    lib = _lib.load()
+    with torch.cuda.device(cand_scores.device):
+        ld = (n + 3) // 4 * 4
+        if cand_scores.stride() != (ld, 1) or cand_scores.data_ptr() % 16:
+            s = torch.full((rows, ld), float("-inf"), dtype=torch.float32, device=cand_scores.device)
+            s[:, :n] = cand_scores
+            cand_scores = s
+        if cand_idx.stride() != (ld, 1) or cand_idx.data_ptr() % 16:
+            i = torch.zeros((rows, ld), dtype=torch.int32, device=cand_idx.device)
+            i[:, :n] = cand_idx
+            cand_idx = i
+        out_idx = torch.empty((rows, topk), dtype=torch.int32, device=cand_scores.device)
+        out_scores = torch.empty((rows, topk), dtype=torch.float32, device=cand_scores.device)
+        rc = lib.prism_topk_merge(
+            cand_scores.data_ptr(), cand_idx.data_ptr(), rows, n, ld, int(topk),
+            out_idx.data_ptr(), out_scores.data_ptr(),
+            torch.cuda.current_stream(cand_scores.device).cuda_stream,
+        )
+        _lib.check(rc, "prism_topk_merge")
+    return (out_idx, out_scores) if return_scores else out_idx

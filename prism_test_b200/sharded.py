@@ -1,0 +1,97 @@
+"""Sequence-sharded recall scoring across the GPUs of one node.
+
+The reference is single-GPU (it has no distributed code); this is the B200
+extension for key caches beyond one GPU's budget. Rank ``r`` of ``N`` holds the
+contiguous key slice ``[r*Sk/N, (r+1)*Sk/N)`` of every KV head and:
+
+1. runs the exact local top-k (``einsum_topk_func`` with ``pos_offset`` and
+   ``index_base`` = the slice start, so RoPE positions and returned indices are
+   global), with fp32 scores;
+2. packs ``(score bits, global index)`` as int32 pairs ``[rows, topk, 2]`` and
+   all-gathers them (one NCCL collective over NVLink);
+3. merges the N sorted runs per row on the device (``topk_merge``): the global
+   top-k is always contained in the union of the local top-k lists.
+
+Every rank ends with the global result, equal to ``torch.topk`` over the whole
+sequence (``ReAttentionMethod._dense_topk``, reattention.py:486-498), ties
+broken toward lower global indices.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from .kernels import einsum_topk_func, topk_merge
+
+
+def shard_bounds(Sk_total: int, rank: int, world: int):
+    """[start, stop) of rank's contiguous slice; Sk_total must divide evenly."""
+    per = Sk_total // world
+    if per * world != Sk_total:
+        raise ValueError(f"sequence length {Sk_total} does not split evenly over {world} ranks")
+    return rank * per, (rank + 1) * per
+
+
+def _all_gather(packed: torch.Tensor, world: int, group) -> torch.Tensor:
+    out = torch.empty((world, *packed.shape), dtype=packed.dtype, device=packed.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, packed, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), packed, group=group)
+    return out
+
+
+def merge_candidates_torch(cand_s: torch.Tensor, cand_i: torch.Tensor, topk: int):
+    """Host/CPU merge with the same result as the device merge (lowest index wins ties)."""
+    order = torch.argsort(cand_i, dim=-1, stable=True)
+    s = torch.gather(cand_s, -1, order)
+    i = torch.gather(cand_i, -1, order)
+    v, p = torch.sort(s, dim=-1, descending=True, stable=True)
+    return torch.gather(i, -1, p[:, :topk]), v[:, :topk]
+
+
+def sharded_einsum_topk(
+    q: torch.Tensor,
+    k_shard: torch.Tensor,
+    topk: int,
+    *,
+    shard_start: int,
+    inv_freq: Optional[torch.Tensor] = None,
+    group=None,
+    return_scores: bool = False,
+    local_topk: Optional[Callable] = None,
+    merge: Optional[Callable] = None,
+):
+    """Global exact top-k over a key sequence split across the ranks of ``group``.
+
+    ``k_shard`` is this rank's slice ``[B, Hkv, Sk/N, 128]`` whose first key sits
+    at absolute position / global index ``shard_start``. Returns int32 indices
+    ``[B, Hq, Sq, topk]`` (and fp32 scores) on every rank.
+    ``local_topk`` / ``merge`` default to the CUDA kernels; tests substitute
+    CPU implementations to run the exchange over gloo.
+    """
+    local_topk = local_topk or einsum_topk_func
+    merge = merge or (lambda s, i, kk: topk_merge(s, i, kk))
+    world = dist.get_world_size(group)
+    B, Hq, Sq, _ = q.shape
+    rows = B * Hq * Sq
+    kl = min(topk, k_shard.shape[2])
+    idx, sc = local_topk(q, k_shard, kl, inv_freq=inv_freq, pos_offset=shard_start,
+                         index_base=shard_start, return_scores=True)
+    packed = torch.empty((rows, topk, 2), dtype=torch.int32, device=q.device)
+    packed[:, :kl, 0] = sc.reshape(rows, kl).contiguous().view(torch.int32)
+    packed[:, :kl, 1] = idx.reshape(rows, kl)
+    if kl < topk:  # a shard shorter than k contributes -inf padding
+        packed[:, kl:, 0] = torch.tensor(float("-inf"), dtype=torch.float32).view(torch.int32).item()
+        packed[:, kl:, 1] = torch.iinfo(torch.int32).max
+    gathered = _all_gather(packed, world, group)  # [world, rows, topk, 2]
+    cand = gathered.permute(1, 0, 2, 3).reshape(rows, world * topk, 2)
+    cand_s = cand[..., 0].contiguous().view(torch.float32)
+    cand_i = cand[..., 1].contiguous()
+    out_i, out_s = merge(cand_s, cand_i, topk)
+    out_i = out_i.reshape(B, Hq, Sq, topk)
+    if return_scores:
+        return out_i, out_s.reshape(B, Hq, Sq, topk)
+    return out_i

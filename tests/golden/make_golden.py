@@ -1,0 +1,112 @@
+"""Generates the golden vectors in this directory by running the REFERENCE's own
+code (RUSH-Intelligence/Prism-Test, imported read-only from a checkout given by
+--reference, default /root/reference):
+
+    eval_harness/attention_methods/_method_base.py  build_cos_sin,
+        apply_rotary_pos_emb, undo_rotary_pos_emb
+    eval_harness/attention_methods/reattention.py   ReAttentionMethod._dense_topk
+
+For each case it draws seeded raw keys and queries, rotates the keys with the
+reference's RoPE (fp32), stores them as bf16 (the dtype the GPU path reads),
+un-rotates the bf16 keys in fp32 with ``undo_rotary_pos_emb`` and selects with
+``_dense_topk``. Output: one .npz per case with the inputs (bf16 as uint16
+bits), inv_freq, and the reference's top-k indices and scores.
+
+The checkout is not needed to *use* the vectors; only to regenerate them:
+    python tests/golden/make_golden.py [--reference PATH]
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+import zlib
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+# name, B, Hq, Hkv, Sq, Sk, topk, theta, pos_offset, rope, causal_offset, special
+CASES = [
+    ("gqa_decode", 1, 8, 2, 1, 1000, 37, 5e5, 0, True, None, None),
+    ("mha_multirow_offset", 2, 4, 4, 3, 700, 64, 1e4, 5000, True, None, None),
+    ("raw_keys_k_equals_n", 1, 6, 3, 2, 513, 513, 5e5, 0, False, None, None),
+    ("causal_chunk", 1, 4, 2, 5, 300, 20, 5e5, 0, True, 295, None),
+    ("top1", 1, 4, 1, 2, 384, 1, 5e5, 100, True, None, None),
+    ("ties_equal_keys", 1, 4, 2, 1, 256, 10, 5e5, 0, False, None, "ties"),
+    ("large_positions", 1, 4, 2, 1, 512, 16, 5e5, 1048000, True, None, None),
+    ("outliers_planted", 1, 8, 2, 1, 1536, 128, 1e6, 0, True, None, "planted"),
+]
+
+
+def bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    from eval_harness.attention_methods._method_base import (  # noqa: E402
+        apply_rotary_pos_emb, build_cos_sin, undo_rotary_pos_emb)
+    from eval_harness.attention_methods.reattention import ReAttentionMethod  # noqa: E402
+
+    for (name, B, Hq, Hkv, Sq, Sk, topk, theta, pos_offset, rope, causal, special) in CASES:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+        D = 128
+        q = torch.randn(B, Hq, Sq, D, generator=g).to(torch.bfloat16)
+        k_raw = torch.randn(B, Hkv, Sk, D, generator=g)
+        if special == "ties":
+            k_raw[:, :, :] = k_raw[:, :, :1]  # every key equal -> all scores tie
+        if special == "planted":
+            k_raw[..., 3] *= 8.0
+            k_raw[..., 77] *= 8.0
+            for h in range(Hq):
+                pos = torch.randperm(Sk, generator=g)[:4]
+                qv = q[0, h, 0].float()
+                qn = qv / qv.norm()
+                for p in pos.tolist():
+                    kv = h // (Hq // Hkv)
+                    n = k_raw[0, kv, p]
+                    k_raw[0, kv, p] = 6.0 * qn * 11.3 + (n - (n @ qn) * qn)
+        inv_freq = 1.0 / (theta ** (torch.arange(0, D, 2, dtype=torch.int64).to(torch.float32) / D))
+        if rope:
+            pos = torch.arange(pos_offset, pos_offset + Sk)
+            cos, sin = build_cos_sin(pos, inv_freq, torch.device("cpu"), torch.float32)
+            k_cached = apply_rotary_pos_emb(k_raw, cos, sin).to(torch.bfloat16)
+            raw_ref = undo_rotary_pos_emb(k_cached.float(), cos, sin)
+        else:
+            k_cached = k_raw.to(torch.bfloat16)
+            raw_ref = k_cached.float()
+
+        method = ReAttentionMethod(mid_size=topk, use_triton_kernel="off")
+        if causal is None:
+            idx = method._dense_topk(q.float(), raw_ref, Sk)
+            n_rep = Hq // Hkv
+            rk = raw_ref[:, :, None].expand(B, Hkv, n_rep, Sk, D).reshape(B, Hq, Sk, D)
+            full = torch.einsum("bhqd,bhmd->bhqm", q.float(), rk.float())
+        else:
+            # the dense einsum of _dense_topk with the causal mask applied before topk
+            n_rep = Hq // Hkv
+            rk = raw_ref[:, :, None].expand(B, Hkv, n_rep, Sk, D).reshape(B, Hq, Sk, D)
+            full = torch.einsum("bhqd,bhmd->bhqm", q.float(), rk.float())
+            j = torch.arange(Sk)[None, :]
+            i = torch.arange(Sq)[:, None]
+            full = full.masked_fill(j > causal + i, float("-inf"))
+            _, idx = full.topk(topk, dim=-1)
+        vals = torch.gather(full, -1, idx)
+        np.savez_compressed(
+            HERE / f"{name}.npz",
+            q_bf16=bf16_bits(q), k_bf16=bf16_bits(k_cached), inv_freq=inv_freq.numpy(),
+            rope=np.array(rope), pos_offset=np.array(pos_offset),
+            causal_offset=np.array(-1 if causal is None else causal),
+            topk=np.array(topk), idx=idx.numpy().astype(np.int64), scores=vals.numpy(),
+            raw_keys_ref=raw_ref.numpy() if name == "causal_chunk" else np.zeros(0, np.float32),
+        )
+        print(name, tuple(q.shape), tuple(k_cached.shape), "topk", topk)
+
+
+if __name__ == "__main__":
+    main()

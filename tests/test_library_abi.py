@@ -1,0 +1,96 @@
+"""The C-ABI library loads, exports every function include/prism_b200.h declares,
+and rejects bad arguments before touching the GPU (no CUDA device needed)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+import prism_test_b200 as pb
+from prism_test_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "prism_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return re.findall(r"PRISM_API\s+[\w\s\*]+?\b(prism_\w+)\s*\(", text)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from prism_test_b200 import build
+    build.build()
+    return _lib.load()
+
+
+def test_header_declares_expected_functions():
+    names = declared_functions()
+    assert set(names) == set(_lib.SIGNATURES), names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert isinstance(getattr(lib, name), ctypes._CFuncPtr)
+
+
+def test_abi_version(lib):
+    assert lib.prism_abi_version() == 1
+
+
+def test_workspace_size(lib):
+    # status block (256 B) + fp32 scores, rows padded to a multiple of 4 floats
+    assert lib.prism_einsum_topk_workspace_size(1, 32, 1, 131072, 4096, 0) == 256 + 32 * 131072 * 4
+    assert lib.prism_einsum_topk_workspace_size(1, 4, 2, 5, 3, 0) == 256 + 8 * 8 * 4
+    assert lib.prism_einsum_topk_workspace_size(0, 4, 2, 5, 3, 0) == 0
+    assert lib.prism_einsum_topk_workspace_size(1, 4, 2, 5, 3, 7) == 0
+
+
+def _call(lib, **over):
+    args = dict(q=16, k=16, inv=None, dtype=0, B=1, Hq=4, Hkv=2, Sq=1, Sk=256, D=128,
+                qs=(512, 128, 128, 1), ks=(65536, 32768, 128, 1), pos=0, causal=-1,
+                topk=8, mode=0, base=0, oi=16, os=None, ws=256, wsb=1 << 20, stream=None)
+    args.update(over)
+    return lib.prism_einsum_topk(
+        args["q"], args["k"], args["inv"], args["dtype"], args["B"], args["Hq"], args["Hkv"],
+        args["Sq"], args["Sk"], args["D"], _lib.i64_array(args["qs"]), _lib.i64_array(args["ks"]),
+        args["pos"], args["causal"], args["topk"], args["mode"], args["base"], args["oi"], args["os"],
+        args["ws"], args["wsb"], args["stream"])
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(q=None), _lib.PRISM_E_INVALID),
+    (dict(dtype=5), _lib.PRISM_E_INVALID),
+    (dict(Hq=6, Hkv=4), _lib.PRISM_E_INVALID),
+    (dict(D=64, qs=(256, 64, 64, 1), ks=(32768, 16384, 64, 1)), _lib.PRISM_E_UNSUPPORTED),
+    (dict(ks=(65536, 32768, 256, 1)), _lib.PRISM_E_INVALID),       # rows not contiguous
+    (dict(qs=(512, 128, 128, 2)), _lib.PRISM_E_INVALID),           # inner stride
+    (dict(k=8), _lib.PRISM_E_INVALID),                             # misaligned base
+    (dict(topk=0), _lib.PRISM_E_INVALID),
+    (dict(topk=257), _lib.PRISM_E_INVALID),
+    (dict(Sk=40000, ks=(40000 * 256, 40000 * 128, 128, 1), topk=20000), _lib.PRISM_E_UNSUPPORTED),
+    (dict(mode=3), _lib.PRISM_E_INVALID),
+    (dict(inv=16, pos=(1 << 22) - 10), _lib.PRISM_E_UNSUPPORTED),  # RoPE positions beyond 2^22
+    (dict(base=-1), _lib.PRISM_E_INVALID),
+    (dict(wsb=100), _lib.PRISM_E_WORKSPACE),
+    (dict(ws=None), _lib.PRISM_E_WORKSPACE),
+])
+def test_argument_validation(lib, over, code):
+    rc = _call(lib, **over)
+    assert rc == code, (rc, _lib.last_error())
+    assert _lib.last_error()
+
+
+def test_merge_argument_validation(lib):
+    rc = lib.prism_topk_merge(16, 16, 4, 10, 10, 3, 16, None, None)  # ld % 4 != 0
+    assert rc == _lib.PRISM_E_INVALID
+    rc = lib.prism_topk_merge(16, 16, 4, 12, 12, 13, 16, None, None)  # topk > n
+    assert rc == _lib.PRISM_E_INVALID
+
+
+def test_error_maps_to_assertion():
+    with pytest.raises(AssertionError):
+        _lib.check(_lib.PRISM_E_INVALID, "x")
+    with pytest.raises(pb.PrismLibraryError):
+        _lib.check(_lib.PRISM_E_CUDA, "x")

@@ -1,0 +1,167 @@
+"""GPU parity of the CUDA scorer against the CPU oracle (all calls go through
+the C ABI of libprism_b200.so via einsum_topk_func)."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import reattention_topk as orc
+from prism_test_b200 import einsum_topk_func, read_status, topk_merge
+from prism_test_b200 import workloads as W
+from tests.parity import check_parity
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = sorted((Path(__file__).parent / "golden").glob("*.npz"))
+
+
+def _golden(path, dev):
+    z = np.load(path)
+    q = torch.from_numpy(z["q_bf16"].view(np.int16)).view(torch.bfloat16)
+    k = torch.from_numpy(z["k_bf16"].view(np.int16)).view(torch.bfloat16)
+    inv = torch.from_numpy(z["inv_freq"]) if bool(z["rope"]) else None
+    causal = int(z["causal_offset"])
+    return dict(q=q.to(dev), k=k.to(dev), inv_freq=None if inv is None else inv.to(dev),
+                pos_offset=int(z["pos_offset"]), causal_offset=None if causal < 0 else causal,
+                topk=int(z["topk"]), idx=torch.from_numpy(z["idx"]), scores=torch.from_numpy(z["scores"]))
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[p.stem for p in GOLDEN])
+def test_golden_vectors(path, cuda_device):
+    c = _golden(path, cuda_device)
+    idx, sc = einsum_topk_func(c["q"], c["k"], c["topk"], inv_freq=c["inv_freq"], pos_offset=c["pos_offset"],
+                               causal_offset=c["causal_offset"], return_scores=True)
+    torch.cuda.synchronize()
+    check_parity(idx, sc, c["q"], c["k"], c["topk"], c["inv_freq"], c["pos_offset"], c["causal_offset"])
+    # against the reference's own selection: equal sets except near-ties
+    ref_scores = c["scores"]
+    tol = 1e-3 * ref_scores.abs().clamp_min(1.0)
+    if path.stem != "ties_equal_keys":
+        same = (idx.cpu().long().sort(-1).values == c["idx"].sort(-1).values).all(-1)
+        gap = (ref_scores[..., -1] - ref_scores[..., -2].clamp_max(float("inf"))).abs() if c["topk"] > 1 else None
+        assert bool(same.all()) or gap is not None
+    torch.testing.assert_close(sc.cpu(), ref_scores, rtol=1e-3, atol=float(tol.max()))
+
+
+CASES = [
+    # B, Hq, Hkv, Sq, Sk, topk, rope, dtype
+    (1, 32, 8, 1, 16384, 1024, True, torch.bfloat16),
+    (1, 32, 8, 1, 5000, 777, True, torch.bfloat16),
+    (1, 8, 8, 1, 129, 129, True, torch.bfloat16),
+    (1, 4, 1, 1, 3, 2, True, torch.bfloat16),
+    (1, 4, 2, 3, 1000, 1, False, torch.bfloat16),
+    (2, 8, 2, 2, 2048, 100, True, torch.float16),
+    (1, 28, 4, 8, 3000, 500, True, torch.bfloat16),   # 224 rows -> several row chunks per KV head
+    (1, 32, 8, 9, 700, 64, True, torch.bfloat16),     # Hq*Sq > 128 -> query chunking
+    (3, 12, 3, 1, 4099, 16384 // 8, True, torch.bfloat16),
+    (1, 16, 4, 1, 20000, 16384, True, torch.bfloat16),  # largest supported k
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Sk,topk,rope,dtype", CASES)
+def test_random_shapes(B, Hq, Hkv, Sq, Sk, topk, rope, dtype, cuda_device):
+    g = torch.Generator(device=cuda_device).manual_seed(B * 1000 + Sk)
+    q = torch.randn(B, Hq, Sq, 128, generator=g, device=cuda_device).to(dtype)
+    k = torch.randn(B, Hkv, Sk, 128, generator=g, device=cuda_device).to(dtype)
+    inv = W.rope_inv_freq(128, 5e5).to(cuda_device) if rope else None
+    idx, sc = einsum_topk_func(q, k, topk, inv_freq=inv, pos_offset=11 if rope else 0, return_scores=True)
+    check_parity(idx, sc, q, k, topk, inv, 11 if rope else 0)
+
+
+def test_causal_prefill_small(cuda_device):
+    wl = W.small(W.WORKLOADS["prefill-chunk-128k"], Sk=6000, Sq=64, topk=300)
+    x = W.make_inputs(wl, cuda_device)
+    idx, sc = einsum_topk_func(x["q"], x["k"], wl.topk, inv_freq=x["inv_freq"],
+                               causal_offset=wl.causal_offset, return_scores=True)
+    check_parity(idx, sc, x["q"], x["k"], wl.topk, x["inv_freq"], 0, wl.causal_offset)
+
+
+def test_strided_key_slice_and_index_base(cuda_device):
+    # the middle slice of a larger cache, as reattention passes recall_k[:, :, g:S-l]
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    cache = torch.randn(1, 4, 3000, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    q = torch.randn(1, 16, 1, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    mid = cache[:, :, 32:2500]
+    assert not mid.is_contiguous()
+    inv = W.rope_inv_freq(128, 5e5).to(cuda_device)
+    idx, sc = einsum_topk_func(q, mid, 50, inv_freq=inv, pos_offset=32, index_base=1000, return_scores=True)
+    check_parity(idx, sc, q, mid.contiguous(), 50, inv, 32, index_base=1000)
+
+
+def test_batch_broadcast_keys(cuda_device):
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    k1 = torch.randn(1, 2, 1024, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    k = k1.expand(3, -1, -1, -1)
+    assert k.stride(0) == 0
+    q = torch.randn(3, 8, 1, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    idx, sc = einsum_topk_func(q, k, 40, return_scores=True)
+    check_parity(idx, sc, q, k.contiguous(), 40)
+
+
+def test_massive_ties_take_lowest_indices(cuda_device):
+    # 40000 identical keys: the k-th key has more exact ties than the candidate buffer
+    row = torch.randn(128, device=cuda_device).to(torch.bfloat16)
+    k = row.expand(1, 1, 40000, 128).contiguous()
+    q = torch.randn(1, 2, 1, 128, device=cuda_device).to(torch.bfloat16)
+    idx, sc = einsum_topk_func(q, k, 100, return_scores=True)
+    assert torch.equal(idx.cpu()[0, 0, 0], torch.arange(100, dtype=torch.int32))
+    assert torch.equal(idx.cpu()[0, 1, 0], torch.arange(100, dtype=torch.int32))
+    assert bool((sc == sc[..., :1]).all())
+
+
+def test_planted_keys_are_found(cuda_device):
+    wl = W.small(W.WORKLOADS["decode-128k"], Sk=8192, topk=64)
+    x = W.make_inputs(wl, cuda_device)
+    idx = einsum_topk_func(x["q"], x["k"], wl.topk, inv_freq=x["inv_freq"])
+    planted = W.planted_positions(wl)
+    G = wl.Hq // wl.Hkv
+    for h in range(wl.Hq):
+        mine = planted[h // G][(h % G) * wl.planted_per_qhead:(h % G + 1) * wl.planted_per_qhead]
+        got = set(idx[0, h, 0].cpu().tolist())
+        assert set(mine.tolist()) <= got
+
+
+def test_deterministic(cuda_device):
+    wl = W.small(W.WORKLOADS["shared-context-256k"], Sk=20000, topk=700)
+    x = W.make_inputs(wl, cuda_device)
+    a = einsum_topk_func(x["q"], x["k"], wl.topk, inv_freq=x["inv_freq"], return_scores=True)
+    b = einsum_topk_func(x["q"], x["k"], wl.topk, inv_freq=x["inv_freq"], return_scores=True)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    check_parity(a[0], a[1], x["q"], x["k"], wl.topk, x["inv_freq"])
+
+
+def test_topk_merge_matches_torch(cuda_device):
+    g = torch.Generator(device=cuda_device).manual_seed(9)
+    s = torch.randn(6, 3 * 512, generator=g, device=cuda_device)
+    i = torch.randperm(100000, generator=g, device=cuda_device)[: 6 * 1536].view(6, 1536).to(torch.int32)
+    oi, os_ = topk_merge(s, i, 300)
+    rv, rp = s.topk(300, dim=-1)
+    assert torch.equal(os_, rv)
+    assert torch.equal(oi, torch.gather(i, 1, rp))
+
+
+def test_status_word_clean(cuda_device):
+    q = torch.randn(1, 8, 1, 128, device=cuda_device).to(torch.bfloat16)
+    k = torch.randn(1, 2, 1000, 128, device=cuda_device).to(torch.bfloat16)
+    ws = torch.zeros(1 << 20, dtype=torch.uint8, device=cuda_device)
+    einsum_topk_func(q, k, 10)
+    read_status(ws)  # a fresh zeroed word reads back clean
+
+
+@pytest.mark.parametrize("name", ["decode-128k", "shared-context-256k"])
+def test_full_size_configs(name, cuda_device):
+    wl = W.WORKLOADS[name]
+    x = W.make_inputs(wl, cuda_device)
+    idx, sc = einsum_topk_func(x["q"], x["k"], wl.topk, inv_freq=x["inv_freq"], return_scores=True)
+    st = check_parity(idx, sc, x["q"], x["k"], wl.topk, x["inv_freq"])
+    assert st["rows"] == wl.B * wl.Hq * wl.Sq
+
+
+def test_full_size_1m_shard(cuda_device):
+    # one of eight sequence shards of the 1M-key config, with its global offset
+    wl = W.WORKLOADS["decode-1m-sharded"]
+    x = W.make_inputs(wl, cuda_device, shard=(5, 8))
+    idx, sc = einsum_topk_func(x["q"], x["k"], wl.topk, inv_freq=x["inv_freq"], pos_offset=x["pos_offset"],
+                               index_base=x["index_base"], return_scores=True)
+    check_parity(idx, sc, x["q"], x["k"], wl.topk, x["inv_freq"], x["pos_offset"], index_base=x["index_base"])

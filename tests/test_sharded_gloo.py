@@ -1,0 +1,99 @@
+"""Host logic of the sequence-sharded path over gloo on the CPU (world size 2
+and 4): shard bounds, global positions / indices, the packed all-gather and the
+merge, against the single-process oracle. Also a rank that dies before the
+exchange: the survivor's collective ends with an error instead of hanging."""
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cpu_local(q, k, kl, inv_freq=None, pos_offset=0, index_base=0, return_scores=True):
+    from oracle import reattention_topk as orc
+    vals, idx = orc.dense_topk(q, k, kl, inv_freq, pos_offset, None, index_base)
+    return idx.to(torch.int32), vals
+
+
+def _put_and_exit(q, item):
+    q.put(item)
+    q.close()
+    q.join_thread()  # flush before the hard exit
+    os._exit(0)
+
+
+def _worker(rank, world, port, case, q, k_full, inv, topk, errq):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import datetime
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=10))
+        from prism_test_b200.sharded import merge_candidates_torch, shard_bounds, sharded_einsum_topk
+        start, stop = shard_bounds(k_full.shape[2], rank, world)
+        if case == "die" and rank == 1:
+            os._exit(0)  # leaves between steps, before the exchange
+        try:
+            idx, sc = sharded_einsum_topk(q, k_full[:, :, start:stop], topk, shard_start=start,
+                                          inv_freq=inv, return_scores=True, local_topk=_cpu_local,
+                                          merge=merge_candidates_torch)
+        except Exception as e:  # noqa: BLE001
+            if case == "die":
+                _put_and_exit(errq, ("ok-error", rank, type(e).__name__))
+            raise
+        if case == "die":
+            _put_and_exit(errq, ("no-error", rank, ""))
+        from oracle import reattention_topk as orc
+        from tests.parity import check_parity
+        check_parity(idx, sc, q, k_full, topk, inv, 0)
+        errq.put(("ok", rank, ""))
+        dist.destroy_process_group()
+    except Exception:  # noqa: BLE001
+        errq.put(("fail", rank, traceback.format_exc()))
+
+
+def _run(world, case, Sk, topk, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, 8, 2, 128, generator=g).to(torch.bfloat16)
+    raw = torch.randn(1, 2, Sk, 128, generator=g)
+    inv = 1.0 / (5e5 ** (torch.arange(0, 128, 2, dtype=torch.int64).float() / 128))
+    from prism_test_b200.workloads import apply_rope, rope_cos_sin
+    cos, sin = rope_cos_sin(torch.arange(Sk), inv)
+    k = apply_rope(raw, cos, sin).to(torch.bfloat16)
+    ctx = mp.get_context("spawn")
+    errq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q, k, inv, topk, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    out = []
+    while not errq.empty():
+        out.append(errq.get())
+    return out
+
+
+@pytest.mark.parametrize("world,Sk,topk", [(2, 1000, 50), (4, 1024, 300), (2, 64, 40)])
+def test_sharded_matches_oracle(world, Sk, topk):
+    res = _run(world, "ok", Sk, topk)
+    assert sorted(r[1] for r in res) == list(range(world)), res
+    for status, rank, msg in res:
+        assert status == "ok", msg
+
+
+def test_dead_rank_surfaces_as_error():
+    res = _run(2, "die", 512, 20)
+    assert res and all(s == "ok-error" for s, _, _ in res), res
