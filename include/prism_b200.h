@@ -99,10 +99,16 @@ PRISM_API size_t prism_einsum_topk_workspace_size(int64_t B, int64_t Hq, int64_t
  * single reference counterpart; it reproduces torch.topk over the union of the
  * shards (reattention.py:497) and the sorted merge of
  * eval_harness/kernels/bitonic_merge_wrapper.py:36-52 for any width.
- * Needs no workspace.
+ * `workspace` holds prism_topk_merge_workspace_size(rows, n) bytes of device
+ * memory (16-byte aligned) for the per-row candidate buffers.
  */
-PRISM_API int prism_topk_merge(const float* cand_scores, const int32_t* cand_idx, int64_t rows, int64_t n,
-                     int64_t ld, int32_t topk, int32_t* out_idx, float* out_scores, void* stream);
+PRISM_API int prism_topk_merge(const float* cand_scores, const int32_t* cand_idx, int64_t rows,
+                               int64_t n, int64_t ld, int32_t topk, int32_t* out_idx,
+                               float* out_scores, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/* Workspace bytes prism_topk_merge needs (0 on invalid input). */
+PRISM_API size_t prism_topk_merge_workspace_size(int64_t rows, int64_t n);
 
 /*
  * Reads the device status word kept at the start of `workspace` (synchronises

@@ -77,9 +77,14 @@ cudaError_t launch_counted(int kernel, cudaStream_t stream, F&& launch) {
   return e;
 }
 
+// status block | fp32 scores [rows, ld] | select candidates [rows, cap] u64
+size_t scores_bytes(int64_t rows, int64_t Sk) {
+  return size_t(rows) * size_t(round_up(Sk, 4)) * sizeof(float);
+}
 size_t exact_workspace(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk) {
-  const int64_t ld = round_up(Sk, 4);
-  return kStatusBytes + size_t(B * Hq * Sq) * size_t(ld) * sizeof(float);
+  const int64_t rows = B * Hq * Sq;
+  return kStatusBytes + round_up(int64_t(scores_bytes(rows, Sk)), 256) +
+         prism::select_workspace_bytes(rows, Sk);
 }
 
 }  // namespace
@@ -153,8 +158,9 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
 
   // ---- scoring: rows of one batch resident per CTA, chunk Sq to fit ----------
-  const int sq_chunk = int(std::max<int64_t>(1, prism::kDecodeMaxRows / Hq));
   const int nsm = num_sms_current_device();
+  const bool fast = (Hq / Hkv) * Sq <= 4;  // <= 4 query rows per KV head in one pass
+  const int sq_chunk = fast ? int(Sq) : int(std::max<int64_t>(1, prism::kDecodeMaxRows / Hq));
   for (int64_t s0 = 0; s0 < Sq; s0 += sq_chunk) {
     prism::DecodeArgs a{};
     a.q = q;
@@ -180,8 +186,11 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
     a.ld = ld;
     a.ntiles = int((Sk + 127) / 128);
     a.status = status;
-    e = launch_counted(PRISM_KERNEL_SCORE, stream,
-                       [&] { return prism::launch_decode_scores(a, dtype, nsm, stream); });
+    const bool g4 = fast && prism::decode_g4_supported(a);
+    e = launch_counted(PRISM_KERNEL_SCORE, stream, [&] {
+      return g4 ? prism::launch_decode_scores_g4(a, dtype, nsm, stream)
+                : prism::launch_decode_scores(a, dtype, nsm, stream);
+    });
     if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
   }
 
@@ -197,14 +206,21 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
   s.out_idx = out_idx;
   s.out_scores = out_scores;
   s.status = status;
-  e = launch_counted(PRISM_KERNEL_SELECT, stream, [&] { return prism::launch_select_topk(s, stream); });
+  void* cand_ws = ws + kStatusBytes + round_up(int64_t(scores_bytes(B * Hq * Sq, Sk)), 256);
+  e = launch_counted(PRISM_KERNEL_SELECT, stream,
+                     [&] { return prism::launch_select_topk(s, cand_ws, stream); });
   if (e != cudaSuccess) return cuda_fail(e, "select kernel launch");
   return PRISM_OK;
 }
 
+size_t prism_topk_merge_workspace_size(int64_t rows, int64_t n) {
+  if (rows < 0 || n <= 0) return 0;
+  return prism::select_workspace_bytes(rows, n);
+}
+
 int prism_topk_merge(const float* cand_scores, const int32_t* cand_idx, int64_t rows, int64_t n,
                      int64_t ld, int32_t topk, int32_t* out_idx, float* out_scores,
-                     void* stream_ptr) {
+                     void* workspace, size_t workspace_bytes, void* stream_ptr) {
   g_last_error.clear();
   if (!cand_scores || !cand_idx || !out_idx) return fail(PRISM_E_INVALID, "null pointer argument");
   if (rows < 0 || n <= 0 || ld < n || ld % 4 != 0)
@@ -225,9 +241,14 @@ int prism_topk_merge(const float* cand_scores, const int32_t* cand_idx, int64_t 
   s.out_idx = out_idx;
   s.out_scores = out_scores;
   s.status = nullptr;
+  const size_t need = prism::select_workspace_bytes(rows, n);
+  if (!workspace || workspace_bytes < need)
+    return fail(PRISM_E_WORKSPACE, "merge workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) & 15u)
+    return fail(PRISM_E_INVALID, "merge workspace must be 16-byte aligned");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  cudaError_t e =
-      launch_counted(PRISM_KERNEL_MERGE, stream, [&] { return prism::launch_select_topk(s, stream); });
+  cudaError_t e = launch_counted(PRISM_KERNEL_MERGE, stream,
+                                 [&] { return prism::launch_select_topk(s, workspace, stream); });
   if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
   return PRISM_OK;
 }

@@ -35,6 +35,11 @@ constexpr int kDecodeMaxRows = 128;
 cudaError_t launch_decode_scores(const DecodeArgs& a, int dtype, int num_sms,
                                  cudaStream_t stream);
 
+// Fast path for <= 4 query rows per KV head (G * sq_n <= 4) and Hkv <= 32.
+bool decode_g4_supported(const DecodeArgs& a);
+cudaError_t launch_decode_scores_g4(const DecodeArgs& a, int dtype, int num_sms,
+                                    cudaStream_t stream);
+
 // --- exact per-row top-k selection over a score matrix ----------------------
 struct SelectArgs {
   const float* scores;      // [rows, ld]
@@ -50,6 +55,10 @@ struct SelectArgs {
 };
 constexpr int kSelectMaxK = 16384;
 
-cudaError_t launch_select_topk(const SelectArgs& a, cudaStream_t stream);
+// Candidate buffer the cluster select kernel needs (cand_ws); with cand_ws ==
+// nullptr the general one-block-per-row kernel runs instead.
+int64_t select_cand_cap(int64_t n);
+size_t select_workspace_bytes(int64_t rows, int64_t n);
+cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t stream);
 
 }  // namespace prism

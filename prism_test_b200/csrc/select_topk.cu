@@ -7,31 +7,51 @@
 // merge of the Triton kernel (eval_harness/kernels/bitonic_merge_wrapper.py:36-52),
 // generalised here to any k <= 16384.
 //
-// Algorithm (one 1024-thread CTA per row):
-//   1. radix select on the order-preserving 32-bit key of each score, digit
-//      widths 12/12/8, each digit found from a shared-memory histogram and a
-//      block-wide suffix scan; stop as soon as every key at or above the current
-//      prefix fits the candidate buffer (16384 entries);
-//   2. compact those candidates into shared memory as (key << 32 | ~index);
-//   3. bitonic sort of the candidates in shared memory, write the first k.
-// Massive exact ties at the k-th key (more than the buffer holds) are resolved
-// by an index-ordered pass, so the lowest indices win, as with the column
-// order everywhere else.
+// Fast path: one thread-block cluster of 4 CTAs per row.
+//   1. Every CTA histograms (12-bit digit of the order-preserving key) a 1/16
+//      sample of its quarter of the row; the leader sums the four histograms
+//      through distributed shared memory and takes as threshold L the lower edge
+//      of the bin holding sample rank m ~ 1.25*k/16 + 32, i.e. a value that is
+//      below the true k-th score with overwhelming probability.
+//   2. Every CTA streams its quarter and appends each (key, index) >= L to a
+//      per-row candidate buffer in global memory (L2), slots taken with
+//      warp-aggregated atomics on a counter in the leader's shared memory.
+//   3. The leader checks the count (>= k and within capacity; otherwise it
+//      falls back to the general path below), bins the candidates by
+//      (max_key - key) >> shift into 4096 fine bins, scatters the bins up to the
+//      one holding rank k into shared memory in bin order (counting sort) and
+//      sorts the few elements inside each bin (thread insertion sort, warp
+//      bitonic sort for bins of 17..256, a block bitonic sort otherwise).
+// General path (fallback, and the exactness guarantee): radix select with 12/12/8
+// bit digits on the leader's block, compaction, shared-memory bitonic sort;
+// massive exact ties at the k-th key are resolved in column order.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace prism {
 namespace {
 
 constexpr int kThreads = 1024;
+constexpr int kCluster = 4;
 constexpr int kBins = 4096;
-constexpr int kCap = kSelectMaxK;  // 16384 candidates = 128 KB
+constexpr int kCap = kSelectMaxK;  // 16384 sorted entries (128 KB)
+constexpr int kSmallN = 16384;     // rows this short skip the sampling
 
 struct SelectSmem {
-  uint64_t cand[kCap];
+  uint64_t buf[kCap];   // sorted output / general-path candidates
   uint32_t hist[kBins];
   uint32_t warp_tot[32];
   uint32_t bin, above;
+  uint32_t count;       // candidate slots taken (leader)
+  uint32_t thr;         // threshold key broadcast
+  uint32_t kmax, kmin;
+  uint32_t big;         // a bin too large for warp sorting
+  uint32_t nmed;        // medium bins queued
+  uint32_t med[kBins];  // medium bin ids
   int ncand;
 };
 
@@ -39,15 +59,15 @@ __device__ __forceinline__ uint64_t pack_cand(uint32_t key, uint32_t idx) {
   return (uint64_t(key) << 32) | uint64_t(~idx);
 }
 
-// Visit every (key, index) of a row.
+// Visit every (key, index) of columns [c0, c1) of a row (c0 % 4 == 0).
 template <typename F>
-__device__ __forceinline__ void for_each_key(const SelectArgs& a, int64_t row, F&& f) {
+__device__ __forceinline__ void for_each_key(const SelectArgs& a, int64_t row, int64_t c0,
+                                             int64_t c1, F&& f) {
   const float* sc = a.scores + row * a.ld;
   const int32_t* ix = a.idx_in ? a.idx_in + row * a.ld : nullptr;
-  const int64_t n4 = a.n >> 2;
-  const float4* sc4 = reinterpret_cast<const float4*>(sc);
-  for (int64_t e4 = threadIdx.x; e4 < n4; e4 += kThreads) {
-    const float4 v = sc4[e4];
+  const int64_t e4_end = c1 >> 2;
+  for (int64_t e4 = (c0 >> 2) + threadIdx.x; e4 < e4_end; e4 += kThreads) {
+    const float4 v = reinterpret_cast<const float4*>(sc)[e4];
     const int64_t e = e4 << 2;
     if (ix) {
       const int4 iv = reinterpret_cast<const int4*>(ix)[e4];
@@ -62,11 +82,11 @@ __device__ __forceinline__ void for_each_key(const SelectArgs& a, int64_t row, F
       f(float_to_okey(v.w), uint32_t(e + 3));
     }
   }
-  for (int64_t e = (n4 << 2) + threadIdx.x; e < a.n; e += kThreads)
+  for (int64_t e = (e4_end << 2) + threadIdx.x; e < c1; e += kThreads)
     f(float_to_okey(sc[e]), ix ? uint32_t(ix[e]) : uint32_t(e));
 }
 
-// Block-wide exclusive scan of one value per thread (1024 threads).
+// Block-wide exclusive scan of one value per thread.
 __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, SelectSmem& sm, uint32_t* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t x = v;
@@ -84,7 +104,7 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, SelectSmem& sm, 
       const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += y;
     }
-    sm.warp_tot[lane] = w;  // inclusive
+    sm.warp_tot[lane] = w;
   }
   __syncthreads();
   const uint32_t warp_excl = warp ? sm.warp_tot[warp - 1] : 0u;
@@ -94,20 +114,23 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, SelectSmem& sm, 
   return r;
 }
 
-// Largest bin b with sum(hist[b..nbins)) >= need; also the count strictly above b.
+// Largest bin b with sum(hist[b..nbins)) >= need; sm.bin / sm.above (count above b).
 __device__ void find_bin(SelectSmem& sm, int nbins, uint32_t need) {
   const int t = threadIdx.x;
-  const int per = 4;
-  const int hi_bin = nbins - 1 - per * t;  // this thread covers bins hi_bin .. hi_bin-3
+  const int hi_bin = nbins - 1 - 4 * t;
   uint32_t local = 0;
   if (hi_bin >= 0) {
 #pragma unroll
-    for (int u = 0; u < per; ++u) local += (hi_bin - u >= 0) ? sm.hist[hi_bin - u] : 0u;
+    for (int u = 0; u < 4; ++u) local += (hi_bin - u >= 0) ? sm.hist[hi_bin - u] : 0u;
+  }
+  if (t == 0) {
+    sm.bin = 0;
+    sm.above = 0;
   }
   const uint32_t excl = block_excl_scan(local, sm, nullptr);
   if (hi_bin >= 0 && excl < need && excl + local >= need) {
     uint32_t c = excl;
-    for (int u = 0; u < per; ++u) {
+    for (int u = 0; u < 4; ++u) {
       const int bb = hi_bin - u;
       const uint32_t h = sm.hist[bb];
       if (c + h >= need) {
@@ -126,59 +149,83 @@ __device__ __forceinline__ void zero_hist(SelectSmem& sm, int nbins) {
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kThreads, 1) select_topk_kernel(const SelectArgs a) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
-  const int64_t row = blockIdx.x;
-  const uint32_t kk = uint32_t(a.k);
+// Descending bitonic sort of sm.buf[0, n) (n <= kCap), padding with 0.
+__device__ void block_bitonic_sort(SelectSmem& sm, int n) {
+  int P = 1;
+  while (P < n) P <<= 1;
+  for (int i = n + threadIdx.x; i < P; i += kThreads) sm.buf[i] = 0ull;
+  __syncthreads();
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < (P >> 1); i += kThreads) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const uint64_t x = sm.buf[lo], y = sm.buf[hi];
+        if ((x < y) == desc) {
+          sm.buf[lo] = y;
+          sm.buf[hi] = x;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
 
-  // ---- level 1: top 12 bits ------------------------------------------------
+__device__ void write_out(const SelectArgs& a, int64_t row, const SelectSmem& sm) {
+  int32_t* oi = a.out_idx + row * a.k;
+  float* os = a.out_scores ? a.out_scores + row * a.k : nullptr;
+  const int64_t base = a.idx_in ? 0 : a.index_base;
+  for (int t = threadIdx.x; t < a.k; t += kThreads) {
+    const uint64_t u = sm.buf[t];
+    oi[t] = int32_t(int64_t(~uint32_t(u)) + base);
+    if (os) os[t] = okey_to_float(uint32_t(u >> 32));
+  }
+}
+
+// General exact path for one row on one 1024-thread block (radix select on the
+// full row, compaction into sm.buf, bitonic sort).
+__device__ void select_row_general(const SelectArgs& a, int64_t row, SelectSmem& sm) {
+  const uint32_t kk = uint32_t(a.k);
   zero_hist(sm, kBins);
   if (threadIdx.x == 0) sm.ncand = 0;
-  for_each_key(a, row, [&](uint32_t key, uint32_t) { atomicAdd(&sm.hist[key >> 20], 1u); });
+  for_each_key(a, row, 0, a.n, [&](uint32_t key, uint32_t) { atomicAdd(&sm.hist[key >> 20], 1u); });
   __syncthreads();
   find_bin(sm, kBins, kk);
   const uint32_t b1 = sm.bin, above1 = sm.above;
   const uint32_t total1 = above1 + sm.hist[b1];
-
-  // threshold on the key: every key >= thr is a candidate
   uint32_t thr;
   bool tie_pass = false;
   uint32_t tie_key = 0, need_ties = 0;
   if (total1 <= uint32_t(kCap)) {
     thr = b1 << 20;
   } else {
-    // ---- level 2: bits 19..8 inside bin b1 ----------------------------------
     __syncthreads();
     zero_hist(sm, kBins);
-    for_each_key(a, row, [&](uint32_t key, uint32_t) {
+    for_each_key(a, row, 0, a.n, [&](uint32_t key, uint32_t) {
       if ((key >> 20) == b1) atomicAdd(&sm.hist[(key >> 8) & 0xfffu], 1u);
     });
     __syncthreads();
     find_bin(sm, kBins, kk - above1);
     const uint32_t b2 = sm.bin, above2 = sm.above;
     const uint32_t pre24 = (b1 << 12) | b2;
-    const uint32_t total2 = above1 + above2 + sm.hist[b2];
-    if (total2 <= uint32_t(kCap)) {
+    if (above1 + above2 + sm.hist[b2] <= uint32_t(kCap)) {
       thr = pre24 << 8;
     } else {
-      // ---- level 3: bits 7..0 inside prefix pre24 ---------------------------
       __syncthreads();
       zero_hist(sm, 256);
-      for_each_key(a, row, [&](uint32_t key, uint32_t) {
+      for_each_key(a, row, 0, a.n, [&](uint32_t key, uint32_t) {
         if ((key >> 8) == pre24) atomicAdd(&sm.hist[key & 0xffu], 1u);
       });
       __syncthreads();
       find_bin(sm, 256, kk - above1 - above2);
       const uint32_t b3 = sm.bin, above3 = sm.above;
       const uint32_t T = (pre24 << 8) | b3;
-      const uint32_t A = above1 + above2 + above3;  // keys strictly above T
+      const uint32_t A = above1 + above2 + above3;
       if (A + sm.hist[b3] <= uint32_t(kCap)) {
         thr = T;
       } else {
-        // more exact ties at T than the buffer holds: take keys > T, then the
-        // first (kk - A) keys == T in column order.
-        thr = T + 1;  // T < 0xffffffff here because A < kk
+        thr = T + 1;  // keys > T (A < kk of them), then ties in column order
         tie_pass = true;
         tie_key = T;
         need_ties = kk - A;
@@ -186,17 +233,14 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_kernel(const SelectAr
     }
   }
   __syncthreads();
-
-  // ---- compaction -----------------------------------------------------------
-  for_each_key(a, row, [&](uint32_t key, uint32_t idx) {
+  for_each_key(a, row, 0, a.n, [&](uint32_t key, uint32_t idx) {
     if (key >= thr) {
       const int slot = atomicAdd(&sm.ncand, 1);
-      if (slot < kCap) sm.cand[slot] = pack_cand(key, idx);
+      if (slot < kCap) sm.buf[slot] = pack_cand(key, idx);
     }
   });
   __syncthreads();
   if (tie_pass) {
-    // index-ordered append of tied keys
     const int base0 = sm.ncand;
     uint32_t taken = 0;
     const float* sc = a.scores + row * a.ld;
@@ -212,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_kernel(const SelectAr
       }
       uint32_t chunk_total;
       const uint32_t rank = block_excl_scan(tie ? 1u : 0u, sm, &chunk_total);
-      if (tie && taken + rank < need_ties) sm.cand[base0 + taken + rank] = pack_cand(key, idx);
+      if (tie && taken + rank < need_ties) sm.buf[base0 + taken + rank] = pack_cand(key, idx);
       taken += chunk_total;
     }
     __syncthreads();
@@ -220,55 +264,340 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_kernel(const SelectAr
     __syncthreads();
   }
   int nc = sm.ncand;
-  if (nc > kCap) {  // cannot happen by construction; report instead of writing garbage
+  if (nc > kCap) {
     if (threadIdx.x == 0) set_status(a.status, kStatusCapacity);
     nc = kCap;
   }
+  block_bitonic_sort(sm, nc);
+  write_out(a, row, sm);
+}
 
-  // ---- bitonic sort (descending) -------------------------------------------
-  int P = 1;
-  while (P < nc) P <<= 1;
-  for (int i = nc + threadIdx.x; i < P; i += kThreads) sm.cand[i] = 0ull;
-  __syncthreads();
-  for (int size = 2; size <= P; size <<= 1) {
+// Warp-level descending bitonic sort of seg[0, n), n <= 256 (8 per lane).
+__device__ void warp_sort_segment(uint64_t* seg, int n) {
+  const int lane = threadIdx.x & 31;
+  uint64_t v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane * 8 + i;
+    v[i] = e < n ? seg[e] : 0ull;
+  }
+  // element index e = lane*8 + i; standard bitonic network over 256 elements
+#pragma unroll
+  for (int size = 2; size <= 256; size <<= 1) {
+#pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < (P >> 1); i += kThreads) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool desc = (lo & size) == 0;
-        const uint64_t x = sm.cand[lo], y = sm.cand[hi];
-        if ((x < y) == desc) {
-          sm.cand[lo] = y;
-          sm.cand[hi] = x;
+      if (stride >= 8) {
+        const int lstride = stride >> 3;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int e = lane * 8 + i;
+          const uint64_t o = __shfl_xor_sync(0xffffffffu, v[i], lstride);
+          const bool lower = (e & stride) == 0;
+          const bool desc = (e & size) == 0;
+          // lower element keeps the larger value in a descending block
+          const bool take_max = (lower == desc);
+          const uint64_t mx = v[i] > o ? v[i] : o;
+          const uint64_t mn = v[i] > o ? o : v[i];
+          v[i] = take_max ? mx : mn;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if ((i & stride) == 0) {
+            const int e = lane * 8 + i;
+            const bool desc = (e & size) == 0;
+            const uint64_t x = v[i], y = v[i + stride];
+            if ((x < y) == desc) {
+              v[i] = y;
+              v[i + stride] = x;
+            }
+          }
         }
       }
-      __syncthreads();
     }
   }
-
-  // ---- write -----------------------------------------------------------------
-  int32_t* oi = a.out_idx + row * a.k;
-  float* os = a.out_scores ? a.out_scores + row * a.k : nullptr;
-  const int64_t base = a.idx_in ? 0 : a.index_base;
-  for (int t = threadIdx.x; t < a.k; t += kThreads) {
-    const uint64_t u = sm.cand[t];
-    const uint32_t key = uint32_t(u >> 32);
-    const uint32_t idx = ~uint32_t(u);
-    oi[t] = int32_t(int64_t(idx) + base);
-    if (os) os[t] = okey_to_float(key);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane * 8 + i;
+    if (e < n) seg[e] = v[i];
   }
+}
+
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
+    select_topk_cluster_kernel(const SelectArgs a, uint64_t* __restrict__ cand_all, int64_t cand_cap) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
+  cg::cluster_group cluster = cg::this_cluster();
+  const unsigned rank = cluster.block_rank();
+  const int64_t row = blockIdx.x / kCluster;
+  SelectSmem* lead = cluster.map_shared_rank(&sm, 0);
+  const uint32_t kk = uint32_t(a.k);
+  const int tid = threadIdx.x;
+
+  // this CTA's quarter of the row, 4-aligned
+  const int64_t c0 = ((a.n * rank / kCluster) >> 2) << 2;
+  const int64_t c1 = rank + 1 == kCluster ? a.n : ((a.n * (rank + 1) / kCluster) >> 2) << 2;
+
+  // ---- 1. sample, threshold ---------------------------------------------------------
+  zero_hist(sm, kBins);
+  if (tid == 0) {
+    sm.count = 0;
+    sm.thr = 0;
+  }
+  const bool sample = a.n > kSmallN;
+  if (sample) {
+    const float* sc = a.scores + row * a.ld;
+    for (int64_t g = (c0 >> 7) + tid; (g << 7) < c1; g += kThreads) {
+      const int64_t s0 = (g << 7) + 8 * int64_t((uint32_t(g) * 0x9E3779B1u) >> 28);
+      if (s0 < c0 || s0 + 8 > c1) continue;
+      const float4 x = *reinterpret_cast<const float4*>(sc + s0);
+      const float4 y = *reinterpret_cast<const float4*>(sc + s0 + 4);
+      atomicAdd(&sm.hist[float_to_okey(x.x) >> 20], 1u);
+      atomicAdd(&sm.hist[float_to_okey(x.y) >> 20], 1u);
+      atomicAdd(&sm.hist[float_to_okey(x.z) >> 20], 1u);
+      atomicAdd(&sm.hist[float_to_okey(x.w) >> 20], 1u);
+      atomicAdd(&sm.hist[float_to_okey(y.x) >> 20], 1u);
+      atomicAdd(&sm.hist[float_to_okey(y.y) >> 20], 1u);
+      atomicAdd(&sm.hist[float_to_okey(y.z) >> 20], 1u);
+      atomicAdd(&sm.hist[float_to_okey(y.w) >> 20], 1u);
+    }
+  }
+  cluster.sync();
+  if (rank == 0 && sample) {
+    // merge the four sample histograms into the leader's
+    for (int i = tid; i < kBins; i += kThreads) {
+      uint32_t s = sm.hist[i];
+#pragma unroll
+      for (int r = 1; r < kCluster; ++r) s += cluster.map_shared_rank(&sm, r)->hist[i];
+      sm.hist[i] = s;
+    }
+    __syncthreads();
+    // total number of samples (sm.count is free until the filter phase)
+    uint32_t ns = 0;
+    for (int i = tid; i < kBins; i += kThreads) ns += sm.hist[i];
+    ns = __reduce_add_sync(0xffffffffu, ns);
+    if ((tid & 31) == 0) atomicAdd(&sm.count, ns);
+    __syncthreads();
+    ns = sm.count;
+    __syncthreads();
+    if (tid == 0) sm.count = 0;
+    // sample rank whose bin's lower edge is the threshold
+    const double want = double(kk) * double(ns) / double(a.n) * 1.25 + 32.0;
+    if (want < double(ns)) {
+      find_bin(sm, kBins, uint32_t(want));
+      if (tid == 0) sm.thr = sm.bin << 20;
+    }
+  }
+  cluster.sync();
+  const uint32_t thr = lead->thr;
+
+  // ---- 2. filter into the row's candidate buffer -------------------------------------
+  uint64_t* cand = cand_all + row * cand_cap;
+  {
+    const float* sc = a.scores + row * a.ld;
+    const int32_t* ix = a.idx_in ? a.idx_in + row * a.ld : nullptr;
+    const int lane = tid & 31;
+    const int64_t e4_begin = c0 >> 2, e4_end = (c1 + 3) >> 2;
+    for (int64_t base4 = e4_begin; base4 < e4_end; base4 += kThreads) {
+      const int64_t e4 = base4 + tid;
+      uint32_t keys[4] = {0, 0, 0, 0}, idxs[4] = {0, 0, 0, 0};
+      int mine = 0;
+      if (e4 < e4_end) {
+        const int64_t e = e4 << 2;
+        if (e + 4 <= c1) {
+          const float4 v = reinterpret_cast<const float4*>(sc)[e4];
+          keys[0] = float_to_okey(v.x);
+          keys[1] = float_to_okey(v.y);
+          keys[2] = float_to_okey(v.z);
+          keys[3] = float_to_okey(v.w);
+          if (ix) {
+            const int4 iv = reinterpret_cast<const int4*>(ix)[e4];
+            idxs[0] = uint32_t(iv.x);
+            idxs[1] = uint32_t(iv.y);
+            idxs[2] = uint32_t(iv.z);
+            idxs[3] = uint32_t(iv.w);
+          } else {
+            idxs[0] = uint32_t(e);
+            idxs[1] = uint32_t(e + 1);
+            idxs[2] = uint32_t(e + 2);
+            idxs[3] = uint32_t(e + 3);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) mine += keys[u] >= thr ? 1 : 0;
+        } else {
+          for (int u = 0; u < 4; ++u) {
+            if (e + u < c1) {
+              keys[u] = float_to_okey(sc[e + u]);
+              idxs[u] = ix ? uint32_t(ix[e + u]) : uint32_t(e + u);
+              mine += keys[u] >= thr ? 1 : 0;
+            }
+          }
+        }
+      }
+      // warp-aggregated slot allocation on the leader's counter
+      uint32_t incl = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
+      uint32_t wbase = 0;
+      if (lane == 31 && wtot) wbase = atomicAdd(&lead->count, wtot);
+      wbase = __shfl_sync(0xffffffffu, wbase, 31);
+      uint32_t slot = wbase + incl - mine;
+      if (mine) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (keys[u] >= thr && (e4 << 2) + u < c1) {
+            if (slot < uint64_t(cand_cap)) cand[slot] = pack_cand(keys[u], idxs[u]);
+            ++slot;
+          }
+        }
+      }
+    }
+  }
+  cluster.sync();
+  if (rank != 0) return;
+
+  // ---- 3. leader: fine-binned counting sort of the candidates ----------------------------
+  const uint32_t nc = sm.count;
+  if (nc < kk || int64_t(nc) > cand_cap) {
+    select_row_general(a, row, sm);  // threshold missed: exact general path
+    return;
+  }
+  // key range
+  uint32_t lmax = 0, lmin = 0xffffffffu;
+  for (uint32_t i = tid; i < nc; i += kThreads) {
+    const uint32_t key = uint32_t(cand[i] >> 32);
+    lmax = max(lmax, key);
+    lmin = min(lmin, key);
+  }
+  lmax = __reduce_max_sync(0xffffffffu, lmax);
+  lmin = __reduce_min_sync(0xffffffffu, lmin);
+  if (tid == 0) {
+    sm.kmax = 0;
+    sm.kmin = 0xffffffffu;
+    sm.big = 0;
+    sm.nmed = 0;
+  }
+  zero_hist(sm, kBins);
+  if ((tid & 31) == 0) {
+    atomicMax(&sm.kmax, lmax);
+    atomicMin(&sm.kmin, lmin);
+  }
+  __syncthreads();
+  const uint32_t kmax = sm.kmax, range = kmax - sm.kmin;
+  int shift = 0;
+  while ((range >> shift) >= uint32_t(kBins)) ++shift;
+  for (uint32_t i = tid; i < nc; i += kThreads) {
+    const uint32_t key = uint32_t(cand[i] >> 32);
+    atomicAdd(&sm.hist[(kmax - key) >> shift], 1u);
+  }
+  __syncthreads();
+  // exclusive scan of the bins in order (bin 0 = largest keys)
+  {
+    uint32_t h[4], s = 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      h[u] = sm.hist[4 * tid + u];
+      s += h[u];
+    }
+    uint32_t ex = block_excl_scan(s, sm, nullptr);
+    // find the bin holding position kk-1 and turn counts into start offsets
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (ex <= kk - 1 && kk - 1 < ex + h[u]) {
+        sm.bin = uint32_t(4 * tid + u);
+        sm.above = ex + h[u];  // elements in bins <= bin
+      }
+      sm.hist[4 * tid + u] = ex;
+      ex += h[u];
+    }
+  }
+  __syncthreads();
+  const uint32_t bk = sm.bin, nout = sm.above;
+  if (nout > uint32_t(kCap)) {
+    select_row_general(a, row, sm);
+    return;
+  }
+  // scatter (hist[b] becomes the end of bin b)
+  for (uint32_t i = tid; i < nc; i += kThreads) {
+    const uint64_t u = cand[i];
+    const uint32_t b = (kmax - uint32_t(u >> 32)) >> shift;
+    if (b <= bk) sm.buf[atomicAdd(&sm.hist[b], 1u)] = u;
+  }
+  __syncthreads();
+  // sort inside bins: insertion sort for <= 16 elements, queue the rest
+  for (uint32_t b = tid; b <= bk; b += kThreads) {
+    const uint32_t e = sm.hist[b];
+    const uint32_t s = b ? sm.hist[b - 1] : 0u;
+    const uint32_t n = e - s;
+    if (n <= 1) continue;
+    if (n <= 16) {
+      for (uint32_t x = s + 1; x < e; ++x) {
+        const uint64_t v = sm.buf[x];
+        uint32_t y = x;
+        while (y > s && sm.buf[y - 1] < v) {
+          sm.buf[y] = sm.buf[y - 1];
+          --y;
+        }
+        sm.buf[y] = v;
+      }
+    } else if (n <= 256) {
+      sm.med[atomicAdd(&sm.nmed, 1u)] = b;
+    } else {
+      sm.big = 1;
+    }
+  }
+  __syncthreads();
+  if (sm.big) {
+    block_bitonic_sort(sm, int(nout));
+  } else {
+    const int warp = tid >> 5;
+    for (uint32_t m = warp; m < sm.nmed; m += kThreads / 32) {
+      const uint32_t b = sm.med[m];
+      const uint32_t s = b ? sm.hist[b - 1] : 0u;
+      warp_sort_segment(&sm.buf[s], int(sm.hist[b] - s));
+    }
+    __syncthreads();
+  }
+  write_out(a, row, sm);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) select_topk_general_kernel(const SelectArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
+  select_row_general(a, blockIdx.x, sm);
 }
 
 }  // namespace
 
-cudaError_t launch_select_topk(const SelectArgs& a, cudaStream_t stream) {
+int64_t select_cand_cap(int64_t n) {
+  // every column is a candidate when the sample is skipped (n <= kSmallN);
+  // otherwise the threshold keeps ~1.4 k + bin slack, k <= 16384
+  return n < 32768 ? n : 32768;
+}
+
+size_t select_workspace_bytes(int64_t rows, int64_t n) {
+  return size_t(rows) * size_t(select_cand_cap(n)) * sizeof(uint64_t);
+}
+
+cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t stream) {
   const size_t smem = sizeof(SelectSmem);
-  cudaError_t e = cudaFuncSetAttribute(select_topk_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
   if (a.rows <= 0) return cudaSuccess;
-  select_topk_kernel<<<dim3(static_cast<unsigned>(a.rows)), kThreads, smem, stream>>>(a);
+  if (cand_ws == nullptr) {
+    cudaError_t e = cudaFuncSetAttribute(select_topk_general_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    select_topk_general_kernel<<<dim3(unsigned(a.rows)), kThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+  }
+  cudaError_t e = cudaFuncSetAttribute(select_topk_cluster_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  select_topk_cluster_kernel<<<dim3(unsigned(a.rows * kCluster)), kThreads, smem, stream>>>(
+      a, static_cast<uint64_t*>(cand_ws), select_cand_cap(a.n));
   return cudaGetLastError();
 }
 

@@ -178,9 +178,11 @@ def topk_merge(cand_scores: torch.Tensor, cand_idx: torch.Tensor, topk: int,
             cand_idx = i
         out_idx = torch.empty((rows, topk), dtype=torch.int32, device=cand_scores.device)
         out_scores = torch.empty((rows, topk), dtype=torch.float32, device=cand_scores.device)
+        ws_bytes = int(lib.prism_topk_merge_workspace_size(rows, n))
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=cand_scores.device)
         rc = lib.prism_topk_merge(
             cand_scores.data_ptr(), cand_idx.data_ptr(), rows, n, ld, int(topk),
-            out_idx.data_ptr(), out_scores.data_ptr(),
+            out_idx.data_ptr(), out_scores.data_ptr(), ws.data_ptr(), ws.numel(),
             torch.cuda.current_stream(cand_scores.device).cuda_stream,
         )
         _lib.check(rc, "prism_topk_merge")

@@ -40,9 +40,11 @@ def test_abi_version(lib):
 
 
 def test_workspace_size(lib):
-    # status block (256 B) + fp32 scores, rows padded to a multiple of 4 floats
-    assert lib.prism_einsum_topk_workspace_size(1, 32, 1, 131072, 4096, 0) == 256 + 32 * 131072 * 4
-    assert lib.prism_einsum_topk_workspace_size(1, 4, 2, 5, 3, 0) == 256 + 8 * 8 * 4
+    # status block (256 B) + fp32 scores (rows padded to 4 floats, block to 256 B)
+    # + per-row u64 candidate buffers (min(n, 32768) entries)
+    assert lib.prism_einsum_topk_workspace_size(1, 32, 1, 131072, 4096, 0) == 256 + 32 * 131072 * 4 + 32 * 32768 * 8
+    assert lib.prism_einsum_topk_workspace_size(1, 4, 2, 5, 3, 0) == 256 + 256 + 8 * 5 * 8
+    assert lib.prism_topk_merge_workspace_size(6, 1536) == 6 * 1536 * 8
     assert lib.prism_einsum_topk_workspace_size(0, 4, 2, 5, 3, 0) == 0
     assert lib.prism_einsum_topk_workspace_size(1, 4, 2, 5, 3, 7) == 0
 
@@ -83,10 +85,12 @@ def test_argument_validation(lib, over, code):
 
 
 def test_merge_argument_validation(lib):
-    rc = lib.prism_topk_merge(16, 16, 4, 10, 10, 3, 16, None, None)  # ld % 4 != 0
+    rc = lib.prism_topk_merge(16, 16, 4, 10, 10, 3, 16, None, 16, 1 << 20, None)  # ld % 4 != 0
     assert rc == _lib.PRISM_E_INVALID
-    rc = lib.prism_topk_merge(16, 16, 4, 12, 12, 13, 16, None, None)  # topk > n
+    rc = lib.prism_topk_merge(16, 16, 4, 12, 12, 13, 16, None, 16, 1 << 20, None)  # topk > n
     assert rc == _lib.PRISM_E_INVALID
+    rc = lib.prism_topk_merge(16, 16, 4, 12, 12, 3, 16, None, 16, 8, None)  # workspace too small
+    assert rc == _lib.PRISM_E_WORKSPACE
 
 
 def test_error_maps_to_assertion():

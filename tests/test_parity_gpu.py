@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from oracle import reattention_topk as orc
-from prism_test_b200 import einsum_topk_func, read_status, topk_merge
+from prism_test_b200 import einsum_topk_func, topk_merge
 from prism_test_b200 import workloads as W
 from tests.parity import check_parity
 
@@ -34,14 +34,11 @@ def test_golden_vectors(path, cuda_device):
                                causal_offset=c["causal_offset"], return_scores=True)
     torch.cuda.synchronize()
     check_parity(idx, sc, c["q"], c["k"], c["topk"], c["inv_freq"], c["pos_offset"], c["causal_offset"])
-    # against the reference's own selection: equal sets except near-ties
+    # against the reference's own sorted top-k scores (rank by rank)
     ref_scores = c["scores"]
-    tol = 1e-3 * ref_scores.abs().clamp_min(1.0)
-    if path.stem != "ties_equal_keys":
-        same = (idx.cpu().long().sort(-1).values == c["idx"].sort(-1).values).all(-1)
-        gap = (ref_scores[..., -1] - ref_scores[..., -2].clamp_max(float("inf"))).abs() if c["topk"] > 1 else None
-        assert bool(same.all()) or gap is not None
-    torch.testing.assert_close(sc.cpu(), ref_scores, rtol=1e-3, atol=float(tol.max()))
+    finite = torch.isfinite(ref_scores)
+    assert torch.equal(torch.isfinite(sc.cpu()), finite)
+    torch.testing.assert_close(sc.cpu()[finite], ref_scores[finite], rtol=1e-3, atol=1e-3)
 
 
 CASES = [
@@ -141,12 +138,14 @@ def test_topk_merge_matches_torch(cuda_device):
     assert torch.equal(oi, torch.gather(i, 1, rp))
 
 
-def test_status_word_clean(cuda_device):
+def test_status_word_clean(cuda_device, monkeypatch):
+    # with the synchronous check on, every call reads its own device status word
+    from prism_test_b200 import kernels
+    monkeypatch.setattr(kernels, "_SYNC_CHECK", True)
     q = torch.randn(1, 8, 1, 128, device=cuda_device).to(torch.bfloat16)
-    k = torch.randn(1, 2, 1000, 128, device=cuda_device).to(torch.bfloat16)
-    ws = torch.zeros(1 << 20, dtype=torch.uint8, device=cuda_device)
-    einsum_topk_func(q, k, 10)
-    read_status(ws)  # a fresh zeroed word reads back clean
+    k = torch.randn(1, 2, 50000, 128, device=cuda_device).to(torch.bfloat16)
+    einsum_topk_func(q, k, 10, inv_freq=W.rope_inv_freq(128, 5e5).to(cuda_device))
+    einsum_topk_func(q, k, 3000)
 
 
 @pytest.mark.parametrize("name", ["decode-128k", "shared-context-256k"])
@@ -165,3 +164,49 @@ def test_full_size_1m_shard(cuda_device):
     idx, sc = einsum_topk_func(x["q"], x["k"], wl.topk, inv_freq=x["inv_freq"], pos_offset=x["pos_offset"],
                                index_base=x["index_base"], return_scores=True)
     check_parity(idx, sc, x["q"], x["k"], wl.topk, x["inv_freq"], x["pos_offset"], index_base=x["index_base"])
+
+
+def _sampled_mask(n):
+    """Columns the select kernel's 1/16 threshold sample reads (white-box)."""
+    import numpy as np
+    g = np.arange((n + 127) // 128, dtype=np.uint64)
+    off = ((g * np.uint64(0x9E3779B1)) & np.uint64(0xFFFFFFFF)) >> np.uint64(28)
+    m = np.zeros(n, dtype=bool)
+    for gi, o in zip(g.tolist(), off.tolist()):
+        s = 128 * gi + 8 * o
+        if s + 8 <= n:
+            m[s:s + 8] = True
+    return torch.from_numpy(m)
+
+
+@pytest.mark.parametrize("sampled_high", [True, False])
+def test_select_threshold_miss_falls_back_exactly(sampled_high, cuda_device):
+    # keys along q with magnitudes chosen so the sample misleads the threshold:
+    # sampled columns high -> too few candidates; sampled columns low -> too many
+    n, topk = 40000, 3000
+    q = torch.zeros(1, 1, 1, 128)
+    q[..., 0] = 1.0
+    m = _sampled_mask(n)
+    g = torch.Generator().manual_seed(5)
+    mag = torch.rand(n, generator=g)
+    mag = torch.where(m, mag + (2.0 if sampled_high else -2.0), mag)
+    k = torch.zeros(1, 1, n, 128)
+    k[0, 0, :, 0] = mag
+    k[0, 0, :, 1:] = 0.01 * torch.randn(n, 127, generator=g)
+    q = q.to(torch.bfloat16).to(cuda_device)
+    k = k.to(torch.bfloat16).to(cuda_device)
+    idx, sc = einsum_topk_func(q, k, topk, return_scores=True)
+    check_parity(idx, sc, q, k, topk)
+
+
+def test_topk_merge_large_rows(cuda_device):
+    # 8 sorted runs of 8192 (the 8-shard merge of the 1M config) -> sampled path
+    g = torch.Generator(device=cuda_device).manual_seed(11)
+    runs = [torch.randn(32, 8192, generator=g, device=cuda_device).sort(dim=-1, descending=True).values
+            for _ in range(8)]
+    s = torch.cat(runs, dim=1)
+    i = (torch.arange(8 * 8192, device=cuda_device, dtype=torch.int32)[None, :] * 3).expand(32, -1).contiguous()
+    oi, os_ = topk_merge(s, i, 8192)
+    rv, rp = s.topk(8192, dim=-1)
+    assert torch.equal(os_, rv)
+    assert torch.equal(oi, torch.gather(i, 1, rp))
