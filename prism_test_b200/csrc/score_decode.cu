@@ -57,6 +57,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_scores_kernel(const Decode
   const int t_begin = static_cast<int>(int64_t(blockIdx.x) * a.ntiles / gridDim.x);
   const int t_end = static_cast<int>(int64_t(blockIdx.x + 1) * a.ntiles / gridDim.x);
 
+  asm volatile("griddepcontrol.launch_dependents;");
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&tail->full[s], 1);

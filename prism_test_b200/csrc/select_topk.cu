@@ -37,13 +37,16 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kCluster = 4;
-constexpr int kBins = 4096;
+constexpr int kBins = 4096;        // radix digit histogram of the general path
+constexpr int kSampleBins = 4096;  // 12-bit digit histogram of the threshold sample
+constexpr int kFineBins = 8192;    // counting-sort bins of the fast path
+constexpr int kRegCand = 8;        // candidates per thread held in registers (8192 per row)
 constexpr int kCap = kSelectMaxK;  // 16384 sorted entries (128 KB)
 constexpr int kSmallN = 16384;     // rows this short skip the sampling
 
 struct SelectSmem {
   uint64_t buf[kCap];   // sorted output / general-path candidates
-  uint32_t hist[kBins];
+  uint32_t hist[kFineBins];
   uint32_t warp_tot[32];
   uint32_t bin, above;
   uint32_t count;       // candidate slots taken (leader)
@@ -51,7 +54,7 @@ struct SelectSmem {
   uint32_t kmax, kmin;
   uint32_t big;         // a bin too large for warp sorting
   uint32_t nmed;        // medium bins queued
-  uint32_t med[kBins];  // medium bin ids
+  uint32_t med[kFineBins];  // medium bin ids
   int ncand;
 };
 
@@ -323,6 +326,12 @@ __device__ void warp_sort_segment(uint64_t* seg, int n) {
   }
 }
 
+__device__ __forceinline__ void grid_dependency_wait() {
+  // programmatic dependent launch: wait until the producing kernel (the scorer)
+  // has completed and its writes are visible; a no-op for a normal launch
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     select_topk_cluster_kernel(const SelectArgs a, uint64_t* __restrict__ cand_all, int64_t cand_cap) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -333,20 +342,23 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   SelectSmem* lead = cluster.map_shared_rank(&sm, 0);
   const uint32_t kk = uint32_t(a.k);
   const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
 
   // this CTA's quarter of the row, 4-aligned
   const int64_t c0 = ((a.n * rank / kCluster) >> 2) << 2;
   const int64_t c1 = rank + 1 == kCluster ? a.n : ((a.n * (rank + 1) / kCluster) >> 2) << 2;
 
-  // ---- 1. sample, threshold ---------------------------------------------------------
-  zero_hist(sm, kBins);
+  zero_hist(sm, kSampleBins);
   if (tid == 0) {
     sm.count = 0;
     sm.thr = 0;
   }
+  grid_dependency_wait();
+
+  // ---- 1. sample, threshold ---------------------------------------------------------
   const bool sample = a.n > kSmallN;
+  const float* sc = a.scores + row * a.ld;
   if (sample) {
-    const float* sc = a.scores + row * a.ld;
     for (int64_t g = (c0 >> 7) + tid; (g << 7) < c1; g += kThreads) {
       const int64_t s0 = (g << 7) + 8 * int64_t((uint32_t(g) * 0x9E3779B1u) >> 28);
       if (s0 < c0 || s0 + 8 > c1) continue;
@@ -365,26 +377,25 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   cluster.sync();
   if (rank == 0 && sample) {
     // merge the four sample histograms into the leader's
-    for (int i = tid; i < kBins; i += kThreads) {
+    uint32_t ns = 0;
+    for (int i = tid; i < kSampleBins; i += kThreads) {
       uint32_t s = sm.hist[i];
 #pragma unroll
       for (int r = 1; r < kCluster; ++r) s += cluster.map_shared_rank(&sm, r)->hist[i];
       sm.hist[i] = s;
+      ns += s;
     }
-    __syncthreads();
     // total number of samples (sm.count is free until the filter phase)
-    uint32_t ns = 0;
-    for (int i = tid; i < kBins; i += kThreads) ns += sm.hist[i];
     ns = __reduce_add_sync(0xffffffffu, ns);
-    if ((tid & 31) == 0) atomicAdd(&sm.count, ns);
+    if (lane == 0) atomicAdd(&sm.count, ns);
     __syncthreads();
     ns = sm.count;
     __syncthreads();
     if (tid == 0) sm.count = 0;
-    // sample rank whose bin's lower edge is the threshold
+    // the threshold is the lower edge of the bin holding this sample rank
     const double want = double(kk) * double(ns) / double(a.n) * 1.25 + 32.0;
     if (want < double(ns)) {
-      find_bin(sm, kBins, uint32_t(want));
+      find_bin(sm, kSampleBins, uint32_t(want));
       if (tid == 0) sm.thr = sm.bin << 20;
     }
   }
@@ -392,49 +403,34 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t thr = lead->thr;
 
   // ---- 2. filter into the row's candidate buffer -------------------------------------
+  // a warp takes 512 consecutive columns per round (4 float4 per lane, all
+  // loads in flight together) and one slot range from the leader's counter
   uint64_t* cand = cand_all + row * cand_cap;
   {
-    const float* sc = a.scores + row * a.ld;
     const int32_t* ix = a.idx_in ? a.idx_in + row * a.ld : nullptr;
-    const int lane = tid & 31;
-    const int64_t e4_begin = c0 >> 2, e4_end = (c1 + 3) >> 2;
-    for (int64_t base4 = e4_begin; base4 < e4_end; base4 += kThreads) {
-      const int64_t e4 = base4 + tid;
-      uint32_t keys[4] = {0, 0, 0, 0}, idxs[4] = {0, 0, 0, 0};
-      int mine = 0;
-      if (e4 < e4_end) {
-        const int64_t e = e4 << 2;
-        if (e + 4 <= c1) {
-          const float4 v = reinterpret_cast<const float4*>(sc)[e4];
-          keys[0] = float_to_okey(v.x);
-          keys[1] = float_to_okey(v.y);
-          keys[2] = float_to_okey(v.z);
-          keys[3] = float_to_okey(v.w);
-          if (ix) {
-            const int4 iv = reinterpret_cast<const int4*>(ix)[e4];
-            idxs[0] = uint32_t(iv.x);
-            idxs[1] = uint32_t(iv.y);
-            idxs[2] = uint32_t(iv.z);
-            idxs[3] = uint32_t(iv.w);
-          } else {
-            idxs[0] = uint32_t(e);
-            idxs[1] = uint32_t(e + 1);
-            idxs[2] = uint32_t(e + 2);
-            idxs[3] = uint32_t(e + 3);
-          }
+    for (int64_t wb = c0 + int64_t(warp) * 512; wb < c1; wb += int64_t(kThreads / 32) * 512) {
+      uint32_t keys[16];
+      uint32_t hit = 0;  // bit u*4+e: element (lane + 32u)*4 + e passes
 #pragma unroll
-          for (int u = 0; u < 4; ++u) mine += keys[u] >= thr ? 1 : 0;
+      for (int u = 0; u < 4; ++u) {
+        const int64_t e = wb + int64_t(lane + 32 * u) * 4;
+        if (e + 4 <= c1) {
+          const float4 v = *reinterpret_cast<const float4*>(sc + e);
+          keys[4 * u + 0] = float_to_okey(v.x);
+          keys[4 * u + 1] = float_to_okey(v.y);
+          keys[4 * u + 2] = float_to_okey(v.z);
+          keys[4 * u + 3] = float_to_okey(v.w);
         } else {
-          for (int u = 0; u < 4; ++u) {
-            if (e + u < c1) {
-              keys[u] = float_to_okey(sc[e + u]);
-              idxs[u] = ix ? uint32_t(ix[e + u]) : uint32_t(e + u);
-              mine += keys[u] >= thr ? 1 : 0;
-            }
-          }
+#pragma unroll
+          for (int x = 0; x < 4; ++x) keys[4 * u + x] = e + x < c1 ? float_to_okey(sc[e + x]) : 0u;
         }
       }
-      // warp-aggregated slot allocation on the leader's counter
+#pragma unroll
+      for (int x = 0; x < 16; ++x) {
+        const int64_t e = wb + int64_t(lane + 32 * (x >> 2)) * 4 + (x & 3);
+        if (keys[x] >= thr && e < c1) hit |= 1u << x;
+      }
+      const uint32_t mine = __popc(hit);
       uint32_t incl = mine;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -446,13 +442,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
       if (lane == 31 && wtot) wbase = atomicAdd(&lead->count, wtot);
       wbase = __shfl_sync(0xffffffffu, wbase, 31);
       uint32_t slot = wbase + incl - mine;
-      if (mine) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (keys[u] >= thr && (e4 << 2) + u < c1) {
-            if (slot < uint64_t(cand_cap)) cand[slot] = pack_cand(keys[u], idxs[u]);
-            ++slot;
-          }
+      for (int x = 0; x < 16; ++x) {  // static indices keep keys[] in registers
+        if (hit & (1u << x)) {
+          const int64_t e = wb + int64_t(lane + 32 * (x >> 2)) * 4 + (x & 3);
+          const uint32_t idx = ix ? uint32_t(ix[e]) : uint32_t(e);
+          if (slot < uint64_t(cand_cap)) cand[slot] = pack_cand(keys[x], idx);
+          ++slot;
         }
       }
     }
@@ -462,16 +458,21 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
 
   // ---- 3. leader: fine-binned counting sort of the candidates ----------------------------
   const uint32_t nc = sm.count;
-  if (nc < kk || int64_t(nc) > cand_cap) {
-    select_row_general(a, row, sm);  // threshold missed: exact general path
+  if (nc < kk || int64_t(nc) > cand_cap || nc > uint32_t(kThreads * kRegCand)) {
+    select_row_general(a, row, sm);  // threshold missed (or too many): exact general path
     return;
   }
-  // key range
+  uint64_t rc[kRegCand];  // this thread's candidates i = tid + kThreads*u
   uint32_t lmax = 0, lmin = 0xffffffffu;
-  for (uint32_t i = tid; i < nc; i += kThreads) {
-    const uint32_t key = uint32_t(cand[i] >> 32);
-    lmax = max(lmax, key);
-    lmin = min(lmin, key);
+#pragma unroll
+  for (int u = 0; u < kRegCand; ++u) {
+    const uint32_t i = tid + kThreads * u;
+    rc[u] = i < nc ? cand[i] : 0ull;
+    if (i < nc) {
+      const uint32_t key = uint32_t(rc[u] >> 32);
+      lmax = max(lmax, key);
+      lmin = min(lmin, key);
+    }
   }
   lmax = __reduce_max_sync(0xffffffffu, lmax);
   lmin = __reduce_min_sync(0xffffffffu, lmin);
@@ -481,37 +482,38 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     sm.big = 0;
     sm.nmed = 0;
   }
-  zero_hist(sm, kBins);
-  if ((tid & 31) == 0) {
+  zero_hist(sm, kFineBins);
+  if (lane == 0) {
     atomicMax(&sm.kmax, lmax);
     atomicMin(&sm.kmin, lmin);
   }
   __syncthreads();
   const uint32_t kmax = sm.kmax, range = kmax - sm.kmin;
   int shift = 0;
-  while ((range >> shift) >= uint32_t(kBins)) ++shift;
-  for (uint32_t i = tid; i < nc; i += kThreads) {
-    const uint32_t key = uint32_t(cand[i] >> 32);
-    atomicAdd(&sm.hist[(kmax - key) >> shift], 1u);
+  while ((range >> shift) >= uint32_t(kFineBins)) ++shift;
+#pragma unroll
+  for (int u = 0; u < kRegCand; ++u) {
+    if (tid + kThreads * u < nc) atomicAdd(&sm.hist[(kmax - uint32_t(rc[u] >> 32)) >> shift], 1u);
   }
   __syncthreads();
   // exclusive scan of the bins in order (bin 0 = largest keys)
   {
-    uint32_t h[4], s = 0;
+    constexpr int kPer = kFineBins / kThreads;
+    uint32_t h[kPer], s = 0;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      h[u] = sm.hist[4 * tid + u];
+    for (int u = 0; u < kPer; ++u) {
+      h[u] = sm.hist[kPer * tid + u];
       s += h[u];
     }
     uint32_t ex = block_excl_scan(s, sm, nullptr);
     // find the bin holding position kk-1 and turn counts into start offsets
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < kPer; ++u) {
       if (ex <= kk - 1 && kk - 1 < ex + h[u]) {
-        sm.bin = uint32_t(4 * tid + u);
+        sm.bin = uint32_t(kPer * tid + u);
         sm.above = ex + h[u];  // elements in bins <= bin
       }
-      sm.hist[4 * tid + u] = ex;
+      sm.hist[kPer * tid + u] = ex;
       ex += h[u];
     }
   }
@@ -522,10 +524,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     return;
   }
   // scatter (hist[b] becomes the end of bin b)
-  for (uint32_t i = tid; i < nc; i += kThreads) {
-    const uint64_t u = cand[i];
-    const uint32_t b = (kmax - uint32_t(u >> 32)) >> shift;
-    if (b <= bk) sm.buf[atomicAdd(&sm.hist[b], 1u)] = u;
+#pragma unroll
+  for (int u = 0; u < kRegCand; ++u) {
+    if (tid + kThreads * u < nc) {
+      const uint32_t b = (kmax - uint32_t(rc[u] >> 32)) >> shift;
+      if (b <= bk) sm.buf[atomicAdd(&sm.hist[b], 1u)] = rc[u];
+    }
   }
   __syncthreads();
   // sort inside bins: insertion sort for <= 16 elements, queue the rest
@@ -554,7 +558,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   if (sm.big) {
     block_bitonic_sort(sm, int(nout));
   } else {
-    const int warp = tid >> 5;
     for (uint32_t m = warp; m < sm.nmed; m += kThreads / 32) {
       const uint32_t b = sm.med[m];
       const uint32_t s = b ? sm.hist[b - 1] : 0u;

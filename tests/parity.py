@@ -51,9 +51,13 @@ def check_parity(idx: torch.Tensor, scores: Optional[torch.Tensor], q: torch.Ten
             err = (sc - ref_at_mine).abs()
             lim = torch.maximum(rel * ref_at_mine.abs(), tol_at_mine)
             ok = torch.where(finite, err <= lim, sc == ref_at_mine)
-            assert bool(ok.all()), (
-                f"score mismatch kv head {hk}: worst err {float(err[finite].max()):.4g} vs lim "
-                f"{float(lim[finite].min()):.4g}")
+            if not bool(ok.all()):
+                bad = torch.nonzero(~ok)[:12].tolist()
+                detail = [(b_, hk * G + g_, s_, c_, int(mine[b_, g_, s_, c_]),
+                           float(sc[b_, g_, s_, c_]), float(ref_at_mine[b_, g_, s_, c_])) for b_, g_, s_, c_ in bad]
+                raise AssertionError(
+                    f"score mismatch kv head {hk}: {int((~ok).sum())} bad; worst err "
+                    f"{float(err[finite].max()):.4g}; (b, head, row, rank, idx, got, ref): {detail}")
             if bool(finite.any()):
                 stats["max_rel_err"] = max(stats["max_rel_err"],
                                            float((err[finite] / lim[finite].clamp_min(1e-30)).max()) * rel)
