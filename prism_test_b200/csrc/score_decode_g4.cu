@@ -1,27 +1,35 @@
 // Decode scorer, fast path for at most 4 query rows per KV head (GQA decode:
 // Hq/Hkv <= 4 query heads per KV head at one query position) — the decode
-// shape of the reference's recall (reattention.py:486-498 with q_len = 1).
+// shape of the reference's recall (reattention.py:486-498 with q_len = 1) —
+// and Hkv in {1, 2, 4, 8, 16}.
 //
 // Same math as score_decode.cu (inverse RoPE fused into the key load, fp32
-// dot products), organised for issue rate and shared-memory bandwidth:
+// dot products), organised for instruction issue and shared-memory bandwidth:
 //
-//  * a stage holds Tp key positions of EVERY KV head of one batch row (one TMA
-//    bulk copy per head, one mbarrier, <= 32 KB); four stages, three tiles in
-//    flight while one is consumed. Thread 0 issues the copies of tile t+3 right
-//    after the per-tile barrier, which proves every warp is done with tile t-1;
-//  * 16 warps; a work item is (kv head, 4 positions), 8 lanes per key, each
-//    lane 8 rotation pairs (dims [8j, 8j+8) and [64+8j, 64+8j+8)). Items are
-//    dealt head-major in contiguous ranges so a warp keeps its head's query
-//    rows in registers (4 rows x 16 values per lane);
-//  * the RoPE cos/sin of a tile (Tp positions x 64 frequencies) is computed
-//    once by all threads into a double-buffered shared table, stored with a
-//    rotation swizzle so each 8-lane phase of a 128-bit load hits 8 distinct
-//    bank groups (key rows are read conflict-free as laid out);
-//  * rotation and dot products in packed fp32x2 FMA (__ffma2_rn / __fmul2_rn),
-//    two accumulator chains per row.
+//  * a stage holds Tp key positions of EVERY KV head of one batch row, brought
+//    in by ONE tiled TMA copy (a 4-D tensor map over [B, Hkv, Sk, 128], box
+//    {128, Tp, Hkv, 1}; rows past Sk are zero-filled), 32 KB per stage; four
+//    stages, three tiles in flight while one is consumed;
+//  * per tile, all threads compute the RoPE cos/sin of Tp positions x 64
+//    frequencies into a double-buffered shared table; thread 0 then issues the
+//    copies of tile t+3 and alone waits for tile t's bytes, and the block
+//    barrier that follows publishes both (no thread spins on the mbarrier; the
+//    barrier also proves tile t-1's stage and table are no longer read);
+//  * 16 warps, 32 work items (kv head, 4 positions) per tile, 2 per warp, both
+//    of the same head: each warp keeps its head's query rows in registers
+//    (4 rows x 16 values per lane) for the whole kernel, and every address of
+//    an item is precomputed once;
+//  * 8 lanes per key, each owning rotation pairs [8j, 8j+8) of the two halves.
+//    Key rows are read conflict-free as laid out; the cos/sin table gives lane
+//    j a contiguous 64-byte block at 80*j bytes (rows padded to 640 B), so the
+//    8 lanes of a key hit 8 distinct bank groups with immediate offsets;
+//  * rotation and dot products in packed fp32x2 FMA (__ffma2_rn / __fmul2_rn).
 #include "common.cuh"
 #include "kernels.h"
 #include "rope_sincos.cuh"
+#include "tensor_map.h"
+
+#include <type_traits>
 
 namespace prism {
 namespace {
@@ -30,16 +38,18 @@ constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 4;
 constexpr int kMaxR = 4;
-constexpr int kMaxStageBytes = 32 * 1024;
+constexpr int kItemsPerWarp = 2;
+constexpr int kCsRow = 640;  // bytes per position in the cos/sin table (512 + padding)
 
 struct __align__(16) G4Tail {
   uint64_t full[kStages];
   float inv_freq[64];
+  int abort;
 };
 
-// physical 16-byte chunk of logical chunk q (0..31) in a position's cos/sin row:
-// each group of 8 chunks is rotated by q/8
-__device__ __forceinline__ int cs_phys(int q) { return (q & ~7) | (((q & 7) + (q >> 3)) & 7); }
+// physical 16-byte chunk of logical chunk qc (pairs 2qc, 2qc+1): lane j = qc/4
+// owns chunks 5j .. 5j+3
+__device__ __forceinline__ int cs_phys(int qc) { return 5 * (qc >> 2) + (qc & 3); }
 
 template <typename T>
 __device__ __forceinline__ void unpack4(const uint4& v, float2 out[4]) {
@@ -50,16 +60,15 @@ __device__ __forceinline__ void unpack4(const uint4& v, float2 out[4]) {
 }
 
 template <typename T, bool kRope>
-__global__ void __launch_bounds__(kThreads, 1) decode_g4_kernel(const DecodeArgs a, int Tp) {
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_g4_kernel(const __grid_constant__ CUtensorMap kmap, const DecodeArgs a, int Tp) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int Hkv = a.Hkv;
   const int R = a.G * a.sq_n;  // <= 4
-  const int rows = Hkv * R;
-  const size_t stage_bytes = size_t(Hkv) * Tp * kRowBytes;
+  const uint32_t stage_bytes = uint32_t(Hkv) * Tp * kRowBytes;
   uint8_t* stages = smem;
-  uint8_t* cs_tab = smem + kStages * stage_bytes;                // [2][Tp][512 B]
-  float* q_s = reinterpret_cast<float*>(cs_tab + 2 * Tp * 512);  // [Hkv][R][128]
-  G4Tail* tail = reinterpret_cast<G4Tail*>(q_s + size_t(rows) * kHeadDim);
+  uint8_t* cs_tab = smem + kStages * stage_bytes;  // [2][Tp][kCsRow]
+  G4Tail* tail = reinterpret_cast<G4Tail*>(cs_tab + 2 * Tp * kCsRow);
 
   const int tid = threadIdx.x;
   const int b = blockIdx.y;
@@ -70,69 +79,71 @@ __global__ void __launch_bounds__(kThreads, 1) decode_g4_kernel(const DecodeArgs
   // be scheduled while this grid drains; it waits for our completion itself
   asm volatile("griddepcontrol.launch_dependents;");
   if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&kmap) : "memory");
     for (int s = 0; s < kStages; ++s) mbar_init(&tail->full[s], 1);
+    tail->abort = 0;
     fence_mbar_init();
-  }
-  const T* qg = static_cast<const T*>(a.q);
-  for (int e = tid; e < rows * kHeadDim; e += kThreads) {
-    const int row = e / kHeadDim, d = e % kHeadDim;
-    const int hk = row / R, r = row % R;
-    const int gi = r / a.sq_n, sl = r % a.sq_n;
-    q_s[e] = to_f32(qg[int64_t(b) * a.q_sb + int64_t(hk * a.G + gi) * a.q_sh +
-                       int64_t(a.s0 + sl) * a.q_ss + d]);
   }
   if (kRope) {
     for (int i = tid; i < kHeadDim / 2; i += kThreads) tail->inv_freq[i] = a.inv_freq[i];
   }
+
+  // ---- per-lane constants ------------------------------------------------------------
+  const int warp = tid >> 5, lane = tid & 31;
+  const int j = lane & 7;    // rotation pairs [8j, 8j+8)
+  const int pl = lane >> 3;  // key within an item (0..3)
+  const int npass = Tp / 4;
+  const int nitems = Hkv * npass;   // 16 or 32
+  const int ipw = nitems / kWarps;  // 1 or 2 items per warp
+  const int item0 = warp * ipw;
+  const int h = item0 / npass;  // kv head of this warp's items
+  int k_off[kItemsPerWarp], cs_off[kItemsPerWarp], p_of[kItemsPerWarp];
+#pragma unroll
+  for (int i = 0; i < kItemsPerWarp; ++i) {
+    const int p = 4 * ((item0 % npass) + i) + pl;  // key position within the tile
+    p_of[i] = p;
+    k_off[i] = (h * Tp + p) * kRowBytes + 16 * j;
+    cs_off[i] = p * kCsRow + 80 * j;
+  }
+  // query rows of head h: row r -> (q head h*G + r / sq_n, query s0 + r % sq_n)
+  float2 q_lo[kMaxR][4], q_hi[kMaxR][4];  // dims 8j+2m, 8j+2m+1 (and +64)
+  {
+    const T* qg = static_cast<const T*>(a.q);
+#pragma unroll
+    for (int r = 0; r < kMaxR; ++r) {
+      const int rr = min(r, R - 1);
+      const T* qr = qg + int64_t(b) * a.q_sb + int64_t(h * a.G + rr / a.sq_n) * a.q_sh +
+                    int64_t(a.s0 + rr % a.sq_n) * a.q_ss;
+      const uint4 lo = *reinterpret_cast<const uint4*>(qr + 8 * j);
+      const uint4 hi = *reinterpret_cast<const uint4*>(qr + 64 + 8 * j);
+      unpack4<T>(lo, q_lo[r]);
+      unpack4<T>(hi, q_hi[r]);
+    }
+  }
+  // output row of this lane: row r = j/2 of the head's group
+  const int r_lane = j >> 1;
+  const bool writer = (j & 1) == 0 && r_lane < R;
+  const int s_abs = a.s0 + r_lane % a.sq_n;
+  float* const out =
+      a.scores + ((int64_t(b) * a.Hq + h * a.G + r_lane / a.sq_n) * a.Sq + s_abs) * a.ld;
+  const int64_t vis_limit = a.causal ? a.causal_offset + s_abs : INT64_MAX;
   __syncthreads();
 
-  const uint8_t* kb = static_cast<const uint8_t*>(a.k) + int64_t(b) * a.k_sb * int64_t(sizeof(T));
-  // bulk copies of tile t into stage s (thread 0 only)
+  const int kb_coord = (a.B > 1 && a.k_sb != 0) ? b : 0;
+  // one tensor copy brings tile t (all KV heads) into stage s (thread 0 only)
   auto issue = [&](int t, int s) {
     const uint64_t pol = l2_policy_evict_first();
-    const int p0 = t * Tp;
-    const int nvalid = min(Tp, a.Sk - p0);
-    const uint32_t bytes = uint32_t(nvalid) * kRowBytes;
-    mbar_arrive_expect_tx(&tail->full[s], bytes * uint32_t(Hkv));
-    uint8_t* dst = stages + s * stage_bytes;
-    for (int h = 0; h < Hkv; ++h)
-      bulk_g2s(dst + size_t(h) * Tp * kRowBytes,
-               kb + (int64_t(h) * a.k_sh + int64_t(p0) * kHeadDim) * int64_t(sizeof(T)), bytes,
-               &tail->full[s], pol);
+    mbar_arrive_expect_tx(&tail->full[s], stage_bytes);
+    tma_load_4d(stages + s * stage_bytes, &kmap, 0, t * Tp, 0, kb_coord, &tail->full[s], pol);
   };
   if (tid == 0) {
     for (int k = 0; k < kStages - 1 && t_begin + k < t_end; ++k) issue(t_begin + k, k);
   }
 
-  const int warp = tid >> 5, lane = tid & 31;
-  const int j = lane & 7;    // rotation pairs [8j, 8j+8)
-  const int pl = lane >> 3;  // position within an item (0..3)
-  const int npass = Tp / 4;
-  const int nitems = Hkv * npass;  // item i -> head i / npass, positions 4*(i % npass) ..
-  const int i_begin = warp * nitems / kWarps;
-  const int i_end = (warp + 1) * nitems / kWarps;
-  // byte offsets of this lane's 4 cos/sin chunks inside a position row
-  int cs_off[4];
-#pragma unroll
-  for (int m = 0; m < 4; ++m) cs_off[m] = cs_phys(4 * j + m) * 16;
-
-  float2 q_lo[kMaxR][4], q_hi[kMaxR][4];  // dims 8j+2m, 8j+2m+1 (and +64)
-  int q_head = -1;
-  // first item's (head, pass); later items advance incrementally (no divisions
-  // in the loop)
-  const int h_begin = i_begin / npass, pass_begin = i_begin % npass;
-  // output row of this lane (row r = j/2 of the head's group), minus the head term
-  const int r_lane = j >> 1;
-  const int gi_lane = r_lane / a.sq_n, s_abs_lane = a.s0 + r_lane % a.sq_n;
-  const bool writer = (j & 1) == 0 && r_lane < R;
-  const int64_t row_lane = int64_t(b) * a.Hq * a.Sq + int64_t(gi_lane) * a.Sq + s_abs_lane;
-  const int64_t vis_limit = a.causal ? a.causal_offset + s_abs_lane : INT64_MAX;
-  float* out_row = nullptr;
-
   int it = 0;
   for (int t = t_begin; t < t_end; ++t, ++it) {
     const int p0 = t * Tp;
-    uint8_t* cs_buf = cs_tab + (it & 1) * Tp * 512;
+    uint8_t* cs_buf = cs_tab + (it & 1) * Tp * kCsRow;
     if (kRope) {
       for (int idx = tid; idx < Tp * 32; idx += kThreads) {
         const int p = idx >> 5, qc = idx & 31;
@@ -140,51 +151,36 @@ __global__ void __launch_bounds__(kThreads, 1) decode_g4_kernel(const DecodeArgs
         float4 v;  // (cos f0, cos f1, sin f0, sin f1) of freqs 2qc, 2qc+1
         rope_sincos_fast(__fmul_rn(pf, tail->inv_freq[2 * qc]), v.z, v.x);
         rope_sincos_fast(__fmul_rn(pf, tail->inv_freq[2 * qc + 1]), v.w, v.y);
-        *reinterpret_cast<float4*>(cs_buf + p * 512 + cs_phys(qc) * 16) = v;
+        *reinterpret_cast<float4*>(cs_buf + p * kCsRow + cs_phys(qc) * 16) = v;
       }
     }
-    __syncthreads();  // cos/sin of tile t ready; every warp is done with tile t-1
-    if (tid == 0 && t + kStages - 1 < t_end) issue(t + kStages - 1, (it + kStages - 1) % kStages);
-
     const int s = it % kStages;
-    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&tail->full[s], (it / kStages) & 1))) {
-      set_status(a.status, kStatusTimeout);
-      return;
+    if (tid == 0) {
+      if (t + kStages - 1 < t_end) issue(t + kStages - 1, (it + kStages - 1) % kStages);
+      if (!mbar_wait_bounded(&tail->full[s], (it / kStages) & 1)) {
+        set_status(a.status, kStatusTimeout);
+        tail->abort = 1;
+      }
     }
+    __syncthreads();  // tile t's keys and cos/sin are ready; tile t-1 is retired
+    if (tail->abort) return;
+
     const uint8_t* st = stages + s * stage_bytes;
-    int h = h_begin, pass = pass_begin;
-    for (int item = i_begin; item < i_end; ++item) {
-      if (h != q_head) {
-        q_head = h;
-        out_row = a.scores + (row_lane + int64_t(h) * a.G * a.Sq) * a.ld;
-        const float* qh = q_s + size_t(h) * R * kHeadDim;
 #pragma unroll
-        for (int r = 0; r < kMaxR; ++r) {
-          const float* qr = qh + min(r, R - 1) * kHeadDim + 8 * j;
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            q_lo[r][m] = *reinterpret_cast<const float2*>(qr + 2 * m);
-            q_hi[r][m] = *reinterpret_cast<const float2*>(qr + 64 + 2 * m);
-          }
-        }
-      }
-      const int p = 4 * pass + pl;  // position within the tile
-      const uint8_t* krow = st + (size_t(h) * Tp + p) * kRowBytes;
-      if (++pass == npass) {  // advance to the next item's (head, pass)
-        pass = 0;
-        ++h;
-      }
-      const uint4 wl = lds128(krow + 16 * j);
-      const uint4 wh = lds128(krow + 128 + 16 * j);
+    for (int i = 0; i < kItemsPerWarp; ++i) {
+      if (i >= ipw) break;
+      const uint8_t* krow = st + k_off[i];
+      const uint4 wl = lds128(krow);
+      const uint4 wh = lds128(krow + 128);
       float2 lo[4], hi[4];
       unpack4<T>(wl, lo);
       unpack4<T>(wh, hi);
       float2 kr_lo[4], kr_hi[4];
       if (kRope) {
-        const uint8_t* csrow = cs_buf + p * 512;
+        const uint8_t* csl = cs_buf + cs_off[i];
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
-          const float4 c = *reinterpret_cast<const float4*>(csrow + cs_off[m]);
+          const float4 c = *reinterpret_cast<const float4*>(csl + 16 * m);
           const float2 cc = make_float2(c.x, c.y), ss = make_float2(c.z, c.w);
           const float2 ns = make_float2(-c.z, -c.w);
           kr_lo[m] = __ffma2_rn(hi[m], ss, __fmul2_rn(lo[m], cc));
@@ -200,15 +196,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_g4_kernel(const DecodeArgs
       float v[kMaxR];
 #pragma unroll
       for (int r = 0; r < kMaxR; ++r) {
-        float2 a0 = __fmul2_rn(q_lo[r][0], kr_lo[0]);
-        float2 a1 = __fmul2_rn(q_hi[r][0], kr_hi[0]);
+        float2 acc = __fmul2_rn(q_lo[r][0], kr_lo[0]);
 #pragma unroll
-        for (int m = 1; m < 4; ++m) {
-          a0 = __ffma2_rn(q_lo[r][m], kr_lo[m], a0);
-          a1 = __ffma2_rn(q_hi[r][m], kr_hi[m], a1);
-        }
-        const float2 a2 = __fadd2_rn(a0, a1);
-        v[r] = a2.x + a2.y;
+        for (int m = 1; m < 4; ++m) acc = __ffma2_rn(q_lo[r][m], kr_lo[m], acc);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) acc = __ffma2_rn(q_hi[r][m], kr_hi[m], acc);
+        v[r] = acc.x + acc.y;
       }
       // transposed reduction over the 8 lanes of a key: lanes 2r, 2r+1 end with row r
       const bool b2 = (j & 4) != 0, b1 = (j & 2) != 0;
@@ -216,39 +209,36 @@ __global__ void __launch_bounds__(kThreads, 1) decode_g4_kernel(const DecodeArgs
       const float u1 = (b2 ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, b2 ? v[1] : v[3], 4);
       float w = (b1 ? u1 : u0) + __shfl_xor_sync(0xffffffffu, b1 ? u0 : u1, 2);
       w += __shfl_xor_sync(0xffffffffu, w, 1);
-      const int pos = p0 + p;
-      if (writer && pos < a.Sk) out_row[pos] = int64_t(pos) > vis_limit ? -INFINITY : w;
+      const int pos = p0 + p_of[i];
+      if (writer && pos < a.Sk) out[pos] = int64_t(pos) > vis_limit ? -INFINITY : w;
     }
   }
 }
 
-int positions_per_stage(int Hkv) {
-  // stage = Hkv * Tp * 256 B <= 32 KB, Tp a multiple of 4 (one item), at most 64
-  int tp = kMaxStageBytes / (Hkv * kRowBytes);
-  tp = tp > 64 ? 64 : tp;
-  return tp & ~3;
-}
+int positions_per_stage(int Hkv) { return min(64, 128 / Hkv); }
 
-size_t g4_smem_bytes(int Hkv, int rows, int Tp) {
-  return size_t(kStages) * Hkv * Tp * kRowBytes + size_t(2) * Tp * 512 +
-         size_t(rows) * kHeadDim * sizeof(float) + sizeof(G4Tail);
+size_t g4_smem_bytes(int Hkv, int Tp) {
+  return size_t(kStages) * Hkv * Tp * kRowBytes + size_t(2) * Tp * kCsRow + sizeof(G4Tail);
 }
 
 template <typename T, bool kRope>
 cudaError_t launch_g4(const DecodeArgs& a, int num_sms, cudaStream_t stream) {
   const int Tp = positions_per_stage(a.Hkv);
-  const int rows = a.Hkv * a.G * a.sq_n;
-  const size_t smem = g4_smem_bytes(a.Hkv, rows, Tp);
+  const size_t smem = g4_smem_bytes(a.Hkv, Tp);
   auto kern = decode_g4_kernel<T, kRope>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  CUtensorMap kmap;
+  e = make_key_tensor_map(&kmap, a.k, std::is_same<T, __nv_bfloat16>::value ? kBF16 : kFP16, a.B,
+                          a.Hkv, a.Sk, a.k_sb, a.k_sh, Tp);
   if (e != cudaSuccess) return e;
   DecodeArgs b = a;
   b.ntiles = (a.Sk + Tp - 1) / Tp;
   int ctas = num_sms;
   if (a.B > 1) ctas = (num_sms + a.B - 1) / a.B;
   ctas = max(1, min(ctas, b.ntiles));
-  kern<<<dim3(ctas, a.B), kThreads, smem, stream>>>(b, Tp);
+  kern<<<dim3(ctas, a.B), kThreads, smem, stream>>>(kmap, b, Tp);
   return cudaGetLastError();
 }
 
@@ -256,9 +246,12 @@ cudaError_t launch_g4(const DecodeArgs& a, int num_sms, cudaStream_t stream) {
 
 bool decode_g4_supported(const DecodeArgs& a) {
   const int R = a.G * a.sq_n;
-  if (R > kMaxR || a.Hkv > 32) return false;
-  const int Tp = positions_per_stage(a.Hkv);
-  return Tp >= 4 && g4_smem_bytes(a.Hkv, a.Hkv * R, Tp) <= 227 * 1024;
+  const int H = a.Hkv;
+  const bool pow2 = H == 1 || H == 2 || H == 4 || H == 8 || H == 16;
+  // 16-byte aligned query rows for the direct vector loads of q
+  const bool q_aligned = (reinterpret_cast<uintptr_t>(a.q) & 15u) == 0 && a.q_sb % 8 == 0 &&
+                         a.q_sh % 8 == 0 && a.q_ss % 8 == 0;
+  return R <= kMaxR && pow2 && q_aligned && g4_smem_bytes(H, positions_per_stage(H)) <= 227 * 1024;
 }
 
 cudaError_t launch_decode_scores_g4(const DecodeArgs& a, int dtype, int num_sms,

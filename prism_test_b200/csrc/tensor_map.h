@@ -1,0 +1,20 @@
+// Host-side construction of TMA tensor maps (cuTensorMapEncodeTiled, obtained
+// from the driver through the runtime so the library needs no -lcuda).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+
+namespace prism {
+
+// 4-D map over a key cache [B, Hkv, Sk, 128] of 2-byte elements with element
+// strides (k_sb, k_sh, 128, 1); box {128, box_rows, Hkv, 1}. Rows beyond Sk are
+// zero-filled. A batch stride of 0 (broadcast keys) maps every batch to b = 0.
+// Returns cudaErrorInvalidValue when the driver rejects the description.
+cudaError_t make_key_tensor_map(CUtensorMap* map, const void* k, int dtype, int64_t B, int64_t Hkv,
+                                int64_t Sk, int64_t k_sb, int64_t k_sh, int box_rows);
+
+}  // namespace prism
