@@ -157,41 +157,58 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
   cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
 
-  // ---- scoring: rows of one batch resident per CTA, chunk Sq to fit ----------
+  // ---- scoring ----------------------------------------------------------------------
   const int nsm = num_sms_current_device();
-  const bool fast = (Hq / Hkv) * Sq <= 4;  // <= 4 query rows per KV head in one pass
-  const int sq_chunk = fast ? int(Sq) : int(std::max<int64_t>(1, prism::kDecodeMaxRows / Hq));
-  for (int64_t s0 = 0; s0 < Sq; s0 += sq_chunk) {
-    prism::DecodeArgs a{};
-    a.q = q;
-    a.k = k;
-    a.inv_freq = inv_freq;
-    a.B = int(B);
-    a.Hq = int(Hq);
-    a.Hkv = int(Hkv);
-    a.G = int(Hq / Hkv);
-    a.Sq = int(Sq);
-    a.s0 = int(s0);
-    a.sq_n = int(std::min<int64_t>(sq_chunk, Sq - s0));
-    a.Sk = int(Sk);
-    a.q_sb = q_strides[0];
-    a.q_sh = q_strides[1];
-    a.q_ss = q_strides[2];
-    a.k_sb = k_strides[0];
-    a.k_sh = k_strides[1];
-    a.pos_offset = pos_offset;
-    a.causal = causal_offset >= 0 ? 1 : 0;
-    a.causal_offset = causal_offset;
-    a.scores = scores;
-    a.ld = ld;
-    a.ntiles = int((Sk + 127) / 128);
-    a.status = status;
-    const bool g4 = fast && prism::decode_g4_supported(a);
-    e = launch_counted(PRISM_KERNEL_SCORE, stream, [&] {
-      return g4 ? prism::launch_decode_scores_g4(a, dtype, nsm, stream)
-                : prism::launch_decode_scores(a, dtype, nsm, stream);
-    });
+  prism::DecodeArgs a{};
+  a.q = q;
+  a.k = k;
+  a.inv_freq = inv_freq;
+  a.B = int(B);
+  a.Hq = int(Hq);
+  a.Hkv = int(Hkv);
+  a.G = int(Hq / Hkv);
+  a.Sq = int(Sq);
+  a.s0 = 0;
+  a.sq_n = int(Sq);
+  a.Sk = int(Sk);
+  a.q_sb = q_strides[0];
+  a.q_sh = q_strides[1];
+  a.q_ss = q_strides[2];
+  a.k_sb = k_strides[0];
+  a.k_sh = k_strides[1];
+  a.pos_offset = pos_offset;
+  a.causal = causal_offset >= 0 ? 1 : 0;
+  a.causal_offset = causal_offset;
+  a.scores = scores;
+  a.ld = ld;
+  a.ntiles = int((Sk + 127) / 128);
+  a.status = status;
+  // specialised kernels take every query row of a KV head in one launch:
+  // tensor-core tiles for <= 16 rows per KV head, CUDA cores for <= 4
+  if (prism::decode_hp_supported(a, dtype)) {
+    e = launch_counted(PRISM_KERNEL_SCORE, stream,
+                       [&] { return prism::launch_decode_scores_hp(a, nsm, stream); });
     if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
+  } else if (prism::decode_mma_supported(a)) {
+    e = launch_counted(PRISM_KERNEL_SCORE, stream,
+                       [&] { return prism::launch_decode_scores_mma(a, dtype, nsm, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
+  } else if (prism::decode_g4_supported(a)) {
+    e = launch_counted(PRISM_KERNEL_SCORE, stream,
+                       [&] { return prism::launch_decode_scores_g4(a, dtype, nsm, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
+  } else {
+    // general kernel: the query rows of one batch row resident per CTA, so the
+    // query positions are taken in chunks of at most 128 / Hq
+    const int sq_chunk = int(std::max<int64_t>(1, prism::kDecodeMaxRows / Hq));
+    for (int64_t s0 = 0; s0 < Sq; s0 += sq_chunk) {
+      prism::DecodeArgs ac = a;
+      ac.s0 = int(s0);
+      ac.sq_n = int(std::min<int64_t>(sq_chunk, Sq - s0));
+      e = launch_counted(PRISM_KERNEL_SCORE, stream,
+                         [&] { return prism::launch_decode_scores(ac, dtype, nsm, stream); });
+      if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
+    }
   }
 
   // ---- selection ------------------------------------------------------------------

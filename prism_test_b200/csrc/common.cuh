@@ -133,6 +133,22 @@ __device__ __forceinline__ uint4 lds128(const void* p) {
   return v;
 }
 
+// 128-bit shared loads from a 32-bit shared-window address
+__device__ __forceinline__ uint4 lds128_u32(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float4 lds128f_u32(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+
 // ---------------------------------------------------------------------------
 // Packed 16-bit -> fp32 unpacking. A 32-bit word holds elements (lo, hi).
 // ---------------------------------------------------------------------------

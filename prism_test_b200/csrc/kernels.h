@@ -35,7 +35,17 @@ constexpr int kDecodeMaxRows = 128;
 cudaError_t launch_decode_scores(const DecodeArgs& a, int dtype, int num_sms,
                                  cudaStream_t stream);
 
-// Fast path for <= 4 query rows per KV head (G * sq_n <= 4) and Hkv <= 32.
+// Head-pair tensor-core path: bf16, <= 4 query rows per KV head, Hkv in {2, 4, 8}.
+bool decode_hp_supported(const DecodeArgs& a, int dtype);
+cudaError_t launch_decode_scores_hp(const DecodeArgs& a, int num_sms, cudaStream_t stream);
+
+// Register tensor-core (mma.sync TF32) path: <= 16 query rows per KV head,
+// Hkv in {2, 4, 8}.
+bool decode_mma_supported(const DecodeArgs& a);
+cudaError_t launch_decode_scores_mma(const DecodeArgs& a, int dtype, int num_sms,
+                                     cudaStream_t stream);
+
+// CUDA-core path for <= 4 query rows per KV head, Hkv in {1, 2, 4, 8, 16}.
 bool decode_g4_supported(const DecodeArgs& a);
 cudaError_t launch_decode_scores_g4(const DecodeArgs& a, int dtype, int num_sms,
                                     cudaStream_t stream);

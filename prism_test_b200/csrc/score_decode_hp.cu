@@ -1,0 +1,266 @@
+// Decode scorer on register tensor-core tiles shared by head pairs (bf16 keys,
+// Hkv in {2, 4, 8}, at most 4 query rows per KV head) — the 128K / 1M decode
+// shapes of the reference's recall (reattention.py:486-498 with q_len = 1,
+// keys un-rotated as in _unrotate_keys, reattention.py:743-793).
+//
+// One mma.sync m16n8k8 TF32 tile covers 8 key positions x 2 KV heads:
+//   A rows 0..7  = positions p..p+7 of head h0, rows 8..15 = the same positions
+//   of head h1 (rotated keys, 8 dims per k-step);
+//   B columns 0..3 = the (<= 4) query rows of h0, columns 4..7 those of h1.
+// Lane (g, c) owns A rows g and g+8 — the SAME position in two heads — and
+// rotation pairs [16c, 16c+16) of both halves, so the RoPE cos/sin of its 16
+// pairs (computed once per 8-position sub-tile, 16 angles per lane) stay in
+// registers for every head pair: no shared cos/sin table, no block barrier.
+// Of the tile's outputs, lanes c < 2 keep rows (h0 key, h0 queries) and lanes
+// c >= 2 keep (h1 key, h1 queries); the off-diagonal quarters are discarded.
+//
+// Precision: rotated keys enter the MMA rounded to TF32 (round-to-nearest,
+// 10-bit mantissa), bf16 queries are exact in TF32, accumulation is fp32; the
+// score error is at most 2^-11 * sum_i |q_i k_i| <= 0.49 of the 1e-3 * ||q|| ||k||
+// tolerance.
+//
+// Memory: each of the 4 warps streams its own sub-tiles (8 positions x Hkv heads,
+// one tiled TMA copy, 16 KB at Hkv = 8) through a private 3-stage ring: two
+// sub-tiles in flight per warp, 128 KB per SM.
+#include <type_traits>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "rope_sincos.cuh"
+#include "tensor_map.h"
+
+namespace prism {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kStages = 3;
+constexpr int kP = 8;         // positions per sub-tile
+constexpr int kMaxPairs = 4;  // Hkv <= 8
+
+struct __align__(16) HpTail {
+  uint64_t full[kWarps][kStages];
+};
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t tf32_rn(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void unpack_bf16x8(const uint4& v, float2 out[4]) {
+  Unpack<__nv_bfloat16>::run(v.x, out[0].x, out[0].y);
+  Unpack<__nv_bfloat16>::run(v.y, out[1].x, out[1].y);
+  Unpack<__nv_bfloat16>::run(v.z, out[2].x, out[2].y);
+  Unpack<__nv_bfloat16>::run(v.w, out[3].x, out[3].y);
+}
+
+template <bool kRope>
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_hp_kernel(const __grid_constant__ CUtensorMap kmap, const DecodeArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int Hkv = a.Hkv;
+  const int npairs = Hkv / 2;
+  const int R = a.G * a.sq_n;  // <= 4
+  const uint32_t sub_bytes = uint32_t(Hkv) * kP * kRowBytes;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2;  // position g of the sub-tile; B column g
+  const int c = lane & 3;   // rotation pairs [16c, 16c+16)
+  const int b = blockIdx.y;
+  HpTail* tail = reinterpret_cast<HpTail*>(smem + kWarps * kStages * sub_bytes);
+  uint8_t* ring = smem + warp * kStages * sub_bytes;
+  uint64_t* full = tail->full[warp];
+
+  // sub-tiles of this warp: a contiguous range of the row's kP-position slices
+  const int nsub = (a.Sk + kP - 1) / kP;
+  const int64_t gw = int64_t(blockIdx.x) * kWarps + warp, nw = int64_t(gridDim.x) * kWarps;
+  const int i_begin = int(gw * nsub / nw), i_end = int((gw + 1) * nsub / nw);
+
+  asm volatile("griddepcontrol.launch_dependents;");
+  if (lane == 0) {
+    if (warp == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&kmap) : "memory");
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  const int kb_coord = (a.B > 1 && a.k_sb != 0) ? b : 0;
+  auto issue = [&](int i, int s) {
+    const uint64_t pol = l2_policy_evict_first();
+    mbar_arrive_expect_tx(&full[s], sub_bytes);
+    tma_load_4d(ring + s * sub_bytes, &kmap, 0, i * kP, 0, kb_coord, &full[s], pol);
+  };
+  if (lane == 0) {
+    for (int k = 0; k < kStages && i_begin + k < i_end; ++k) issue(i_begin + k, k);
+  }
+
+  // ---- per-lane constants ------------------------------------------------------------
+  // this lane's 16 frequencies (pairs 16c + 2i, 16c + 2i + 1)
+  float2 inv[8];
+  if (kRope) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      inv[i] = make_float2(a.inv_freq[16 * c + 2 * i], a.inv_freq[16 * c + 2 * i + 1]);
+  }
+  // B fragments, bf16 pairs: bq[hp][ks] = q[row][d], q[row][d+1] with
+  // row = B column g (h0 row g for g < 4, h1 row g-4 otherwise),
+  // d = 16c + 2ks (ks < 8) or 64 + 16c + 2(ks - 8)
+  uint32_t bq[kMaxPairs][16];
+  {
+    const int qrow = g & 3;
+    const __nv_bfloat16* qg = static_cast<const __nv_bfloat16*>(a.q);
+#pragma unroll
+    for (int hp = 0; hp < kMaxPairs; ++hp) {
+      const int h = 2 * hp + (g >> 2);
+      const bool live = hp < npairs && qrow < R;
+      const __nv_bfloat16* qr =
+          qg + int64_t(b) * a.q_sb + int64_t(h * a.G + qrow / a.sq_n) * a.q_sh +
+          int64_t(a.s0 + qrow % a.sq_n) * a.q_ss;
+#pragma unroll
+      for (int ks = 0; ks < 16; ++ks) {
+        const int d = ks < 8 ? 16 * c + 2 * ks : 64 + 16 * c + 2 * (ks - 8);
+        bq[hp][ks] = live ? *reinterpret_cast<const uint32_t*>(qr + d) : 0u;
+      }
+    }
+  }
+  // outputs of this lane: head h0 (c < 2) or h1 (c >= 2) of each pair, query
+  // rows r0 = (2c) & 3 and r0 + 1
+  const int r0 = (2 * c) & 3;
+  const bool wr0 = r0 < R, wr1 = r0 + 1 < R;
+  const int s_abs0 = a.s0 + r0 % a.sq_n, s_abs1 = a.s0 + (r0 + 1) % a.sq_n;
+  const int64_t vis0 = a.causal ? a.causal_offset + s_abs0 : INT64_MAX;
+  const int64_t vis1 = a.causal ? a.causal_offset + s_abs1 : INT64_MAX;
+  const int hsel = c >> 1;
+  // score row of (head 2hp + hsel, query row r0) = row_base + hp * pair_stride;
+  // query row r0 + 1 adds row1_delta
+  const int64_t row_base =
+      ((int64_t(b) * a.Hq + hsel * a.G + r0 / a.sq_n) * a.Sq + s_abs0) * a.ld;
+  const int64_t row1_delta =
+      ((int64_t((r0 + 1) / a.sq_n) - r0 / a.sq_n) * a.Sq + (s_abs1 - s_abs0)) * a.ld;
+  const int64_t pair_stride = int64_t(2) * a.G * a.Sq * a.ld;
+  const uint32_t ring_u32 = smem_u32(ring);
+  const uint32_t lane_off = uint32_t(g) * kRowBytes + 32 * c;
+
+  int it = 0;
+  for (int i = i_begin; i < i_end; ++i, ++it) {
+    const int s = it % kStages;
+    const int pos = i * kP + g;
+    // cos/sin of this lane's 16 pairs at its position (overlaps the copy)
+    float2 cc[8], ss[8];
+    if (kRope) {
+      const float pf = static_cast<float>(a.pos_offset + pos);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        rope_sincos_fast(__fmul_rn(pf, inv[q].x), ss[q].x, cc[q].x);
+        rope_sincos_fast(__fmul_rn(pf, inv[q].y), ss[q].y, cc[q].y);
+      }
+    }
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (it / kStages) & 1))) {
+      set_status(a.status, kStatusTimeout);
+      return;
+    }
+    const uint32_t st = ring_u32 + s * sub_bytes + lane_off;
+#pragma unroll
+    for (int hp = 0; hp < kMaxPairs; ++hp) {
+      if (hp >= npairs) break;
+      // A rows: g -> head 2hp, g+8 -> head 2hp+1 (same position); packed bf16
+      // words: [row][0..7] dims 16c..16c+15, [row][8..15] dims 64+16c..
+      uint32_t kw[2][16];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const uint32_t row = st + uint32_t(2 * hp + rr) * kP * kRowBytes;
+        const uint4 w0 = lds128_u32(row), w1 = lds128_u32(row + 16);
+        const uint4 w2 = lds128_u32(row + 128), w3 = lds128_u32(row + 144);
+        kw[rr][0] = w0.x; kw[rr][1] = w0.y; kw[rr][2] = w0.z; kw[rr][3] = w0.w;
+        kw[rr][4] = w1.x; kw[rr][5] = w1.y; kw[rr][6] = w1.z; kw[rr][7] = w1.w;
+        kw[rr][8] = w2.x; kw[rr][9] = w2.y; kw[rr][10] = w2.z; kw[rr][11] = w2.w;
+        kw[rr][12] = w3.x; kw[rr][13] = w3.y; kw[rr][14] = w3.z; kw[rr][15] = w3.w;
+      }
+      // pair q (dims 16c+2q, +1 and +64) feeds k-step q (lo half, acc0) and
+      // k-step 8+q (hi half, acc1)
+      float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float2 klo[2], khi[2];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          float2 lo, hi;
+          Unpack<__nv_bfloat16>::run(kw[rr][q], lo.x, lo.y);
+          Unpack<__nv_bfloat16>::run(kw[rr][8 + q], hi.x, hi.y);
+          if (kRope) {
+            const float2 ns = make_float2(-ss[q].x, -ss[q].y);
+            klo[rr] = __ffma2_rn(hi, ss[q], __fmul2_rn(lo, cc[q]));
+            khi[rr] = __ffma2_rn(lo, ns, __fmul2_rn(hi, cc[q]));
+          } else {
+            klo[rr] = lo;
+            khi[rr] = hi;
+          }
+        }
+        const uint32_t wl = bq[hp][q], wh = bq[hp][8 + q];
+        mma_tf32(acc0, tf32_rn(klo[0].x), tf32_rn(klo[1].x), tf32_rn(klo[0].y), tf32_rn(klo[1].y),
+                 wl << 16, wl & 0xffff0000u);
+        mma_tf32(acc1, tf32_rn(khi[0].x), tf32_rn(khi[1].x), tf32_rn(khi[0].y), tf32_rn(khi[1].y),
+                 wh << 16, wh & 0xffff0000u);
+      }
+      // d0,d1: (h0 key, columns 2c, 2c+1); d2,d3: (h1 key, same columns)
+      const float v0 = hsel ? acc0[2] + acc1[2] : acc0[0] + acc1[0];
+      const float v1 = hsel ? acc0[3] + acc1[3] : acc0[1] + acc1[1];
+      if (pos < a.Sk) {
+        const int64_t ro = row_base + int64_t(hp) * pair_stride;
+        if (wr0) a.scores[ro + pos] = int64_t(pos) > vis0 ? -INFINITY : v0;
+        if (wr1) a.scores[ro + row1_delta + pos] = int64_t(pos) > vis1 ? -INFINITY : v1;
+      }
+    }
+    __syncwarp();  // every lane is done with stage s
+    if (lane == 0 && i + kStages < i_end) issue(i + kStages, s);
+  }
+}
+
+size_t hp_smem_bytes(int Hkv) {
+  return size_t(kWarps) * kStages * Hkv * kP * kRowBytes + sizeof(HpTail);
+}
+
+template <bool kRope>
+cudaError_t launch_hp(const DecodeArgs& a, int num_sms, cudaStream_t stream) {
+  const size_t smem = hp_smem_bytes(a.Hkv);
+  auto kern = decode_hp_kernel<kRope>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  CUtensorMap kmap;
+  e = make_key_tensor_map(&kmap, a.k, kBF16, a.B, a.Hkv, a.Sk, a.k_sb, a.k_sh, kP);
+  if (e != cudaSuccess) return e;
+  const int nsub = (a.Sk + kP - 1) / kP;
+  int ctas = num_sms;
+  if (a.B > 1) ctas = (num_sms + a.B - 1) / a.B;
+  ctas = max(1, min(ctas, (nsub + kWarps - 1) / kWarps));
+  kern<<<dim3(ctas, a.B), kThreads, smem, stream>>>(kmap, a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool decode_hp_supported(const DecodeArgs& a, int dtype) {
+  const int R = a.G * a.sq_n;
+  const int H = a.Hkv;
+  const bool q_ok = (reinterpret_cast<uintptr_t>(a.q) & 3u) == 0 && a.q_sb % 2 == 0 &&
+                    a.q_sh % 2 == 0 && a.q_ss % 2 == 0;
+  return dtype == kBF16 && R <= 4 && (H == 2 || H == 4 || H == 8) && q_ok;
+}
+
+cudaError_t launch_decode_scores_hp(const DecodeArgs& a, int num_sms, cudaStream_t stream) {
+  return a.inv_freq != nullptr ? launch_hp<true>(a, num_sms, stream)
+                               : launch_hp<false>(a, num_sms, stream);
+}
+
+}  // namespace prism

@@ -34,11 +34,17 @@ def test_golden_vectors(path, cuda_device):
                                causal_offset=c["causal_offset"], return_scores=True)
     torch.cuda.synchronize()
     check_parity(idx, sc, c["q"], c["k"], c["topk"], c["inv_freq"], c["pos_offset"], c["causal_offset"])
-    # against the reference's own sorted top-k scores (rank by rank)
+    # against the reference's own sorted top-k scores, rank by rank: a near-tie
+    # swap moves a value by less than its neighbour's gap, so each rank agrees
+    # within three times the parity tolerance
     ref_scores = c["scores"]
     finite = torch.isfinite(ref_scores)
     assert torch.equal(torch.isfinite(sc.cpu()), finite)
-    torch.testing.assert_close(sc.cpu()[finite], ref_scores[finite], rtol=1e-3, atol=1e-3)
+    qn = c["q"].float().norm(dim=-1).cpu()[..., None]  # [B,Hq,Sq,1]
+    kmax = orc.unrotate_keys(c["k"].cpu(), None if c["inv_freq"] is None else c["inv_freq"].cpu(),
+                             c["pos_offset"]).norm(dim=-1).max()
+    lim = 3e-3 * torch.maximum(ref_scores.abs(), qn * kmax)
+    assert bool(((sc.cpu() - ref_scores).abs() <= lim)[finite].all())
 
 
 CASES = [
