@@ -111,6 +111,28 @@ PRISM_API int prism_topk_merge(const float* cand_scores, const int32_t* cand_idx
 PRISM_API size_t prism_topk_merge_workspace_size(int64_t rows, int64_t n);
 
 /*
+ * prism_topk_merge without a workspace, for callers that cannot allocate device
+ * memory (no cudaMalloc / cudaFree / allocating library call anywhere in the
+ * call). It has no counterpart in the reference. Same arguments, kernel and
+ * results as prism_topk_merge; the per-row candidate buffers live in one static
+ * device array of PRISM_NOALLOC_SCRATCH_BYTES per device, so the request must
+ * satisfy rows * min(n, 32768) * 8 <= PRISM_NOALLOC_SCRATCH_BYTES (e.g. 32 rows
+ * of up to 65536 candidates); larger requests return PRISM_E_WORKSPACE.
+ *   - The first call on a device, made with that device current, looks the
+ *     scratch address up (cudaGetSymbolAddress) and caches it; make that first
+ *     call before any stream capture starts on the device.
+ *   - Nothing in the scratch needs to start at zero.
+ *   - All calls on one device share the scratch: calls whose executions overlap
+ *     (different streams, concurrent host threads) race and give wrong results.
+ *     Calls on one stream are serialised and safe.
+ *   - Not counted by the measurement aids below.
+ */
+#define PRISM_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20) /* 8 MiB */
+PRISM_API int prism_topk_merge_noalloc(const float* cand_scores, const int32_t* cand_idx,
+                                       int64_t rows, int64_t n, int64_t ld, int32_t topk,
+                                       int32_t* out_idx, float* out_scores, void* stream);
+
+/*
  * Reads the device status word kept at the start of `workspace` (synchronises
  * `stream`), stores it in *status_out and resets it to 0. A non-zero value means
  * a kernel gave up on a bounded wait (1), rejected an access (2) or ran out of

@@ -89,6 +89,10 @@ size_t exact_workspace(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk) {
 
 }  // namespace
 
+namespace prism {
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace prism
+
 extern "C" {
 
 int prism_abi_version(void) { return PRISM_ABI_VERSION; }

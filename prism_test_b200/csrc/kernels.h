@@ -71,4 +71,7 @@ int64_t select_cand_cap(int64_t n);
 size_t select_workspace_bytes(int64_t rows, int64_t n);
 cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t stream);
 
+// Sets the message prism_last_error() returns for the calling thread.
+void set_last_error(const char* msg);
+
 }  // namespace prism
