@@ -14,14 +14,19 @@
 // Of the tile's outputs, lanes c < 2 keep rows (h0 key, h0 queries) and lanes
 // c >= 2 keep (h1 key, h1 queries); the off-diagonal quarters are discarded.
 //
-// Precision: rotated keys enter the MMA rounded to TF32 (round-to-nearest,
-// 10-bit mantissa), bf16 queries are exact in TF32, accumulation is fp32; the
-// score error is at most 2^-11 * sum_i |q_i k_i| <= 0.49 of the 1e-3 * ||q|| ||k||
-// tolerance.
+// Precision: the tensor core reads a TF32 operand's top 19 bits and ignores the
+// rest, i.e. it truncates. The cos/sin factors are therefore scaled by
+// (1 + 2^-11), so that the rotated key enters the MMA as trunc(k_raw * (1 + 2^-11)):
+// for k_raw = m * 2^e (1 <= m < 2) the scale adds m/2 TF32 ulps before the
+// truncation, and the result lies within (-(1 - m/2), m/2] ulps of k_raw, a
+// relative error below 2^-11 — the bound of round-to-nearest, at no per-element
+// cost. bf16 queries (and un-rotated bf16 keys) are exact in TF32; accumulation
+// is fp32. The score error is at most 2^-11 * sum_i |q_i k_i| <= 0.49 of the
+// 1e-3 * ||q|| ||k|| tolerance.
 //
-// Memory: each of the 4 warps streams its own sub-tiles (8 positions x Hkv heads,
-// one tiled TMA copy, 16 KB at Hkv = 8) through a private 3-stage ring: two
-// sub-tiles in flight per warp, 128 KB per SM.
+// Memory: each warp streams its own copies (8 positions x up to 4 heads, one
+// tiled TMA copy, 8 KB) through a private 3-stage ring, two copies in flight per
+// warp; 8 warps (two per scheduler) hide each other's latencies.
 #include <type_traits>
 
 #include "common.cuh"
@@ -32,11 +37,13 @@
 namespace prism {
 namespace {
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 3;
-constexpr int kP = 8;         // positions per sub-tile
-constexpr int kMaxPairs = 4;  // Hkv <= 8
+constexpr int kP = 8;              // positions per sub-tile
+constexpr int kMaxPairs = 4;       // Hkv <= 8
+constexpr int kPairsPerCopy = 2;   // one TMA copy holds <= 2 head pairs (4 heads)
+constexpr float kTruncScale = 1.0f + 0x1.0p-11f;  // see the precision note
 
 struct __align__(16) HpTail {
   uint64_t full[kWarps][kStages];
@@ -51,40 +58,30 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t tf32_rn(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
-
-__device__ __forceinline__ void unpack_bf16x8(const uint4& v, float2 out[4]) {
-  Unpack<__nv_bfloat16>::run(v.x, out[0].x, out[0].y);
-  Unpack<__nv_bfloat16>::run(v.y, out[1].x, out[1].y);
-  Unpack<__nv_bfloat16>::run(v.z, out[2].x, out[2].y);
-  Unpack<__nv_bfloat16>::run(v.w, out[3].x, out[3].y);
-}
-
 template <bool kRope>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_hp_kernel(const __grid_constant__ CUtensorMap kmap, const DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int Hkv = a.Hkv;
   const int npairs = Hkv / 2;
+  const int ppc = npairs < kPairsPerCopy ? npairs : kPairsPerCopy;  // pairs per copy
+  const int copies = npairs / ppc;                                  // copies per sub-tile: 1 or 2
   const int R = a.G * a.sq_n;  // <= 4
-  const uint32_t sub_bytes = uint32_t(Hkv) * kP * kRowBytes;
+  const uint32_t copy_bytes = uint32_t(ppc) * 2 * kP * kRowBytes;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2;  // position g of the sub-tile; B column g
   const int c = lane & 3;   // rotation pairs [16c, 16c+16)
   const int b = blockIdx.y;
-  HpTail* tail = reinterpret_cast<HpTail*>(smem + kWarps * kStages * sub_bytes);
-  uint8_t* ring = smem + warp * kStages * sub_bytes;
+  HpTail* tail = reinterpret_cast<HpTail*>(smem + kWarps * kStages * copy_bytes);
+  uint8_t* ring = smem + warp * kStages * copy_bytes;
   uint64_t* full = tail->full[warp];
 
   // sub-tiles of this warp: a contiguous range of the row's kP-position slices
   const int nsub = (a.Sk + kP - 1) / kP;
   const int64_t gw = int64_t(blockIdx.x) * kWarps + warp, nw = int64_t(gridDim.x) * kWarps;
   const int i_begin = int(gw * nsub / nw), i_end = int((gw + 1) * nsub / nw);
+  const int ncopies = (i_end - i_begin) * copies;
 
   asm volatile("griddepcontrol.launch_dependents;");
   if (lane == 0) {
@@ -95,13 +92,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
 
   const int kb_coord = (a.B > 1 && a.k_sb != 0) ? b : 0;
-  auto issue = [&](int i, int s) {
+  // copy t of this warp: sub-tile i_begin + t / copies, heads [part * 2ppc, +2ppc)
+  auto issue = [&](int t, int s) {
     const uint64_t pol = l2_policy_evict_first();
-    mbar_arrive_expect_tx(&full[s], sub_bytes);
-    tma_load_4d(ring + s * sub_bytes, &kmap, 0, i * kP, 0, kb_coord, &full[s], pol);
+    const int i = i_begin + (copies == 2 ? (t >> 1) : t);
+    const int part = t & (copies - 1);
+    mbar_arrive_expect_tx(&full[s], copy_bytes);
+    tma_load_4d(ring + s * copy_bytes, &kmap, 0, i * kP, part * 2 * ppc, kb_coord, &full[s], pol);
   };
   if (lane == 0) {
-    for (int k = 0; k < kStages && i_begin + k < i_end; ++k) issue(i_begin + k, k);
+    for (int t = 0; t < kStages && t < ncopies; ++t) issue(t, t);
   }
 
   // ---- per-lane constants ------------------------------------------------------------
@@ -151,34 +151,47 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t ring_u32 = smem_u32(ring);
   const uint32_t lane_off = uint32_t(g) * kRowBytes + 32 * c;
 
-  int it = 0;
-  for (int i = i_begin; i < i_end; ++i, ++it) {
-    const int s = it % kStages;
+  int t = 0;  // copies consumed
+  for (int i = i_begin; i < i_end; ++i) {
     const int pos = i * kP + g;
-    // cos/sin of this lane's 16 pairs at its position (overlaps the copy)
+    // cos/sin of this lane's 16 pairs at its position (overlaps the copy),
+    // pre-scaled for the truncating TF32 operand
     float2 cc[8], ss[8];
     if (kRope) {
       const float pf = static_cast<float>(a.pos_offset + pos);
+      const float2 scale = make_float2(kTruncScale, kTruncScale);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         rope_sincos_fast(__fmul_rn(pf, inv[q].x), ss[q].x, cc[q].x);
         rope_sincos_fast(__fmul_rn(pf, inv[q].y), ss[q].y, cc[q].y);
+        ss[q] = __fmul2_rn(ss[q], scale);
+        cc[q] = __fmul2_rn(cc[q], scale);
       }
     }
-    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (it / kStages) & 1))) {
-      set_status(a.status, kStatusTimeout);
-      return;
-    }
-    const uint32_t st = ring_u32 + s * sub_bytes + lane_off;
+    uint32_t st = 0;
 #pragma unroll
     for (int hp = 0; hp < kMaxPairs; ++hp) {
       if (hp >= npairs) break;
+      const int slot = hp & (ppc - 1);  // pair within the current copy
+      if (slot == 0) {
+        if (hp > 0) {  // release the previous copy of this sub-tile
+          __syncwarp();
+          if (lane == 0 && t - 1 + kStages < ncopies) issue(t - 1 + kStages, (t - 1) % kStages);
+        }
+        const int s = t % kStages;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (t / kStages) & 1))) {
+          set_status(a.status, kStatusTimeout);
+          return;
+        }
+        st = ring_u32 + s * copy_bytes + lane_off;
+        ++t;
+      }
       // A rows: g -> head 2hp, g+8 -> head 2hp+1 (same position); packed bf16
       // words: [row][0..7] dims 16c..16c+15, [row][8..15] dims 64+16c..
       uint32_t kw[2][16];
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
-        const uint32_t row = st + uint32_t(2 * hp + rr) * kP * kRowBytes;
+        const uint32_t row = st + uint32_t(2 * slot + rr) * kP * kRowBytes;
         const uint4 w0 = lds128_u32(row), w1 = lds128_u32(row + 16);
         const uint4 w2 = lds128_u32(row + 128), w3 = lds128_u32(row + 144);
         kw[rr][0] = w0.x; kw[rr][1] = w0.y; kw[rr][2] = w0.z; kw[rr][3] = w0.w;
@@ -207,10 +220,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const uint32_t wl = bq[hp][q], wh = bq[hp][8 + q];
-        mma_tf32(acc0, tf32_rn(klo[0].x), tf32_rn(klo[1].x), tf32_rn(klo[0].y), tf32_rn(klo[1].y),
-                 wl << 16, wl & 0xffff0000u);
-        mma_tf32(acc1, tf32_rn(khi[0].x), tf32_rn(khi[1].x), tf32_rn(khi[0].y), tf32_rn(khi[1].y),
-                 wh << 16, wh & 0xffff0000u);
+        mma_tf32(acc0, __float_as_uint(klo[0].x), __float_as_uint(klo[1].x),
+                 __float_as_uint(klo[0].y), __float_as_uint(klo[1].y), wl << 16, wl & 0xffff0000u);
+        mma_tf32(acc1, __float_as_uint(khi[0].x), __float_as_uint(khi[1].x),
+                 __float_as_uint(khi[0].y), __float_as_uint(khi[1].y), wh << 16, wh & 0xffff0000u);
       }
       // d0,d1: (h0 key, columns 2c, 2c+1); d2,d3: (h1 key, same columns)
       const float v0 = hsel ? acc0[2] + acc1[2] : acc0[0] + acc1[0];
@@ -221,13 +234,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (wr1) a.scores[ro + row1_delta + pos] = int64_t(pos) > vis1 ? -INFINITY : v1;
       }
     }
-    __syncwarp();  // every lane is done with stage s
-    if (lane == 0 && i + kStages < i_end) issue(i + kStages, s);
+    __syncwarp();  // every lane is done with the last copy of this sub-tile
+    if (lane == 0 && t - 1 + kStages < ncopies) issue(t - 1 + kStages, (t - 1) % kStages);
   }
 }
 
 size_t hp_smem_bytes(int Hkv) {
-  return size_t(kWarps) * kStages * Hkv * kP * kRowBytes + sizeof(HpTail);
+  const int heads_per_copy = Hkv < 2 * kPairsPerCopy ? Hkv : 2 * kPairsPerCopy;
+  return size_t(kWarps) * kStages * heads_per_copy * kP * kRowBytes + sizeof(HpTail);
 }
 
 template <bool kRope>
@@ -238,7 +252,8 @@ cudaError_t launch_hp(const DecodeArgs& a, int num_sms, cudaStream_t stream) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   CUtensorMap kmap;
-  e = make_key_tensor_map(&kmap, a.k, kBF16, a.B, a.Hkv, a.Sk, a.k_sb, a.k_sh, kP);
+  const int heads_per_copy = a.Hkv < 2 * kPairsPerCopy ? a.Hkv : 2 * kPairsPerCopy;
+  e = make_key_tensor_map(&kmap, a.k, kBF16, a.B, a.Hkv, a.Sk, a.k_sb, a.k_sh, kP, heads_per_copy);
   if (e != cudaSuccess) return e;
   const int nsub = (a.Sk + kP - 1) / kP;
   int ctas = num_sms;

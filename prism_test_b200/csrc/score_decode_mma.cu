@@ -9,10 +9,13 @@
 // Reference path: ReAttentionMethod._unrotate_keys + _dense_topk's einsum
 // (eval_harness/attention_methods/reattention.py:743-793, 486-498).
 //
-// Precision: the rotated key enters the MMA as TF32 (10-bit mantissa; the low
-// 13 bits of the fp32 value are dropped), the bf16/fp16 query is exact in TF32,
-// products and sums are fp32. For N(0,1) data the score error has a standard
-// deviation of ~2.5e-5 * ||q|| * ||k||, 40x inside the 1e-3 tolerance.
+// Precision: the tensor core truncates a TF32 operand to its top 19 bits. The
+// cos/sin table is scaled by (1 + 2^-11), so a rotated key k_raw = m * 2^e
+// (1 <= m < 2) gains m/2 TF32 ulps before the truncation and enters the MMA
+// within a relative 2^-11 of k_raw (the round-to-nearest bound, without a
+// per-element rounding instruction). bf16/fp16 queries and un-rotated keys are
+// exact in TF32; products and sums are fp32. The score error is at most
+// 2^-11 * sum_i |q_i k_i| <= 0.49 of the 1e-3 * ||q|| ||k|| tolerance.
 //
 // Layout and scheduling:
 //  * a stage = Tp key positions of every KV head of a batch row, one tiled TMA
@@ -173,6 +176,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         float4 v;  // (cos f0, cos f1, sin f0, sin f1)
         rope_sincos_fast(__fmul_rn(pf, tail->inv_freq[2 * qc]), v.z, v.x);
         rope_sincos_fast(__fmul_rn(pf, tail->inv_freq[2 * qc + 1]), v.w, v.y);
+        constexpr float kTruncScale = 1.0f + 0x1.0p-11f;  // see the precision note
+        v.x *= kTruncScale;
+        v.y *= kTruncScale;
+        v.z *= kTruncScale;
+        v.w *= kTruncScale;
         const uint32_t addr = cs_buf + p * kCsRow + kCsLane * (qc >> 3) + 16 * (qc & 7);
         asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y),
                      "f"(v.z), "f"(v.w)

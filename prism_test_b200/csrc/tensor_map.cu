@@ -23,14 +23,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }  // namespace
 
 cudaError_t make_key_tensor_map(CUtensorMap* map, const void* k, int dtype, int64_t B, int64_t Hkv,
-                                int64_t Sk, int64_t k_sb, int64_t k_sh, int box_rows) {
+                                int64_t Sk, int64_t k_sb, int64_t k_sh, int box_rows,
+                                int box_heads) {
   PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
   if (fn == nullptr) return cudaErrorNotSupported;
   const bool batched = B > 1 && k_sb != 0;
   cuuint64_t dims[4] = {128, cuuint64_t(Sk), cuuint64_t(Hkv), cuuint64_t(batched ? B : 1)};
   cuuint64_t strides[3] = {256, cuuint64_t(k_sh) * 2,
                            cuuint64_t(batched ? k_sb : k_sh * Hkv) * 2};
-  cuuint32_t box[4] = {128, cuuint32_t(box_rows), cuuint32_t(Hkv), 1};
+  cuuint32_t box[4] = {128, cuuint32_t(box_rows), cuuint32_t(box_heads > 0 ? box_heads : Hkv), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUtensorMapDataType dt =
       dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

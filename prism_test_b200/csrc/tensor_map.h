@@ -11,10 +11,12 @@
 namespace prism {
 
 // 4-D map over a key cache [B, Hkv, Sk, 128] of 2-byte elements with element
-// strides (k_sb, k_sh, 128, 1); box {128, box_rows, Hkv, 1}. Rows beyond Sk are
-// zero-filled. A batch stride of 0 (broadcast keys) maps every batch to b = 0.
-// Returns cudaErrorInvalidValue when the driver rejects the description.
+// strides (k_sb, k_sh, 128, 1); box {128, box_rows, box_heads, 1} (box_heads <= 0
+// means all Hkv heads). Rows beyond Sk are zero-filled. A batch stride of 0
+// (broadcast keys) maps every batch to b = 0. Returns cudaErrorInvalidValue when
+// the driver rejects the description.
 cudaError_t make_key_tensor_map(CUtensorMap* map, const void* k, int dtype, int64_t B, int64_t Hkv,
-                                int64_t Sk, int64_t k_sb, int64_t k_sh, int box_rows);
+                                int64_t Sk, int64_t k_sb, int64_t k_sh, int box_rows,
+                                int box_heads = 0);
 
 }  // namespace prism
