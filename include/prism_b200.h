@@ -116,8 +116,8 @@ PRISM_API size_t prism_topk_merge_workspace_size(int64_t rows, int64_t n);
  * call). It has no counterpart in the reference. Same arguments, kernel and
  * results as prism_topk_merge; the per-row candidate buffers live in one static
  * device array of PRISM_NOALLOC_SCRATCH_BYTES per device, so the request must
- * satisfy rows * min(n, 32768) * 8 <= PRISM_NOALLOC_SCRATCH_BYTES (e.g. 32 rows
- * of up to 65536 candidates); larger requests return PRISM_E_WORKSPACE.
+ * satisfy rows * min(n, 16384) * 8 <= PRISM_NOALLOC_SCRATCH_BYTES (e.g. 64 rows
+ * of any length); larger requests return PRISM_E_WORKSPACE.
  *   - The first call on a device, made with that device current, looks the
  *     scratch address up (cudaGetSymbolAddress) and caches it; make that first
  *     call before any stream capture starts on the device.

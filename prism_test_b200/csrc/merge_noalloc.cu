@@ -86,7 +86,7 @@ int prism_topk_merge_noalloc(const float* cand_scores, const int32_t* cand_idx, 
   const size_t need = prism::select_workspace_bytes(rows, n);
   if (need > kScratchBytes) {
     char detail[128];
-    snprintf(detail, sizeof(detail), "rows * min(n, 32768) * 8 = %zu bytes, limit %zu bytes", need,
+    snprintf(detail, sizeof(detail), "rows * min(n, 16384) * 8 = %zu bytes, limit %zu bytes", need,
              kScratchBytes);
     return noalloc_fail(PRISM_E_WORKSPACE, "request exceeds the static merge scratch", detail);
   }

@@ -7,24 +7,17 @@
 // merge of the Triton kernel (eval_harness/kernels/bitonic_merge_wrapper.py:36-52),
 // generalised here to any k <= 16384.
 //
-// Fast path: one thread-block cluster of 4 CTAs per row.
-//   1. Every CTA histograms (12-bit digit of the order-preserving key) a 1/16
-//      sample of its quarter of the row; the leader sums the four histograms
-//      through distributed shared memory and takes as threshold L the lower edge
-//      of the bin holding sample rank m ~ 1.25*k/16 + 32, i.e. a value that is
-//      below the true k-th score with overwhelming probability.
-//   2. Every CTA streams its quarter and appends each (key, index) >= L to a
-//      per-row candidate buffer in global memory (L2), slots taken with
-//      warp-aggregated atomics on a counter in the leader's shared memory.
-//   3. The leader checks the count (>= k and within capacity; otherwise it
-//      falls back to the general path below), bins the candidates by
-//      (max_key - key) >> shift into 4096 fine bins, scatters the bins up to the
-//      one holding rank k into shared memory in bin order (counting sort) and
-//      sorts the few elements inside each bin (thread insertion sort, warp
-//      bitonic sort for bins of 17..256, a block bitonic sort otherwise).
-// General path (fallback, and the exactness guarantee): radix select with 12/12/8
-// bit digits on the leader's block, compaction, shared-memory bitonic sort;
-// massive exact ties at the k-th key are resolved in column order.
+// Scores are compared through an order-preserving 32-bit key (NaN largest, as in
+// torch.topk); a candidate is (key << 32) | ~index, so one unsigned 64-bit
+// comparison orders by score and then by ascending index.
+//
+// Fast path: one thread-block cluster of 4 CTAs per row (select_topk_cluster_kernel
+// below): an exact radix threshold from cluster-summed histograms, an append of
+// the keys above it to a per-row candidate buffer, and a counting sort on the
+// leader. General path (no candidate buffer, and the fallback when exact key ties
+// alone exceed 16384 candidates): radix select with 12/12/8-bit digits on one
+// block, compaction, shared-memory bitonic sort; massive ties at the k-th key are
+// resolved in column order.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -37,24 +30,23 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kCluster = 4;
-constexpr int kBins = 4096;        // radix digit histogram of the general path
-constexpr int kSampleBins = 4096;  // 12-bit digit histogram of the threshold sample
+constexpr int kBins = 4096;        // 12-bit radix digit histogram
 constexpr int kFineBins = 8192;    // counting-sort bins of the fast path
-constexpr int kRegCand = 8;        // candidates per thread held in registers (8192 per row)
 constexpr int kCap = kSelectMaxK;  // 16384 sorted entries (128 KB)
-constexpr int kSmallN = 16384;     // rows this short skip the sampling
 
 struct SelectSmem {
-  uint64_t buf[kCap];   // sorted output / general-path candidates
+  uint64_t buf[kCap];     // candidates (leader) / private level histograms / general path
   uint32_t hist[kFineBins];
+  uint16_t perm[kCap];    // candidate numbers in fine-bin order (leader)
   uint32_t warp_tot[32];
-  uint32_t bin, above;
-  uint32_t count;       // candidate slots taken (leader)
-  uint32_t thr;         // threshold key broadcast
-  uint32_t kmax, kmin;
-  uint32_t big;         // a bin too large for warp sorting
-  uint32_t nmed;        // medium bins queued
-  uint32_t med[kFineBins];  // medium bin ids
+  uint32_t bin, above, bcount;  // threshold digit (the leader's answer)
+  uint32_t gt[4], acc[4];       // per cluster CTA: keys above the digit; above earlier digits
+  uint32_t base[4], total;      // first candidate slot of each CTA; candidates of the row
+  uint32_t kmax;          // largest key of the row
+  uint32_t woff;          // candidate slots taken inside this CTA's range
+  uint32_t thr, cbase;    // sampled threshold; this CTA's first slot (fast path)
+  uint32_t count;         // candidates of the row (the leader's slot counter, fast path)
+  uint32_t big;           // largest fine bin
   int ncand;
 };
 
@@ -275,297 +267,545 @@ __device__ void select_row_general(const SelectArgs& a, int64_t row, SelectSmem&
   write_out(a, row, sm);
 }
 
-// Warp-level descending bitonic sort of seg[0, n), n <= 256 (8 per lane).
-__device__ void warp_sort_segment(uint64_t* seg, int n) {
-  const int lane = threadIdx.x & 31;
-  uint64_t v[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int e = lane * 8 + i;
-    v[i] = e < n ? seg[e] : 0ull;
-  }
-  // element index e = lane*8 + i; standard bitonic network over 256 elements
-#pragma unroll
-  for (int size = 2; size <= 256; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      if (stride >= 8) {
-        const int lstride = stride >> 3;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int e = lane * 8 + i;
-          const uint64_t o = __shfl_xor_sync(0xffffffffu, v[i], lstride);
-          const bool lower = (e & stride) == 0;
-          const bool desc = (e & size) == 0;
-          // lower element keeps the larger value in a descending block
-          const bool take_max = (lower == desc);
-          const uint64_t mx = v[i] > o ? v[i] : o;
-          const uint64_t mn = v[i] > o ? o : v[i];
-          v[i] = take_max ? mx : mn;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if ((i & stride) == 0) {
-            const int e = lane * 8 + i;
-            const bool desc = (e & size) == 0;
-            const uint64_t x = v[i], y = v[i + stride];
-            if ((x < y) == desc) {
-              v[i] = y;
-              v[i + stride] = x;
-            }
-          }
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int e = lane * 8 + i;
-    if (e < n) seg[e] = v[i];
-  }
-}
-
 __device__ __forceinline__ void grid_dependency_wait() {
   // programmatic dependent launch: wait until the producing kernel (the scorer)
   // has completed and its writes are visible; a no-op for a normal launch
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// ---- cluster select ------------------------------------------------------------------
+// Thread t of CTA r holds, for pass p, the kKeys keys of columns
+//   p * kPass + r * kThreads * kKeys + ((j >> 2) * kThreads + t) * 4 + (j & 3),  j < kKeys
+// (coalesced float4 loads). Key 0 marks a column beyond n: no fp32 value maps to 0.
+constexpr int kKeys = 32;
+constexpr int kPass = kCluster * kThreads * kKeys;  // 131072 columns per pass
+constexpr int kLevelBins = 2048;                    // 11-bit digits (10 at the last level)
+constexpr int kPriv = 8;                            // private histograms, one per lane & 7
+constexpr int kPrivStride = kLevelBins + 4;         // copies start in different banks
+constexpr int kRankMax = 256;                       // larger fine bins: bitonic sort instead
+
+__device__ __forceinline__ void load_keys(const float* sc, int64_t base, int64_t n,
+                                          uint32_t (&kv)[kKeys]) {
+#pragma unroll
+  for (int u = 0; u < kKeys / 4; ++u) {
+    const int64_t e = base + (int64_t(u * kThreads + int(threadIdx.x)) << 2);
+    if (e + 4 <= n) {
+      const float4 v = *reinterpret_cast<const float4*>(sc + e);
+      kv[4 * u + 0] = float_to_okey(v.x);
+      kv[4 * u + 1] = float_to_okey(v.y);
+      kv[4 * u + 2] = float_to_okey(v.z);
+      kv[4 * u + 3] = float_to_okey(v.w);
+    } else {
+#pragma unroll
+      for (int x = 0; x < 4; ++x) kv[4 * u + x] = e + x < n ? float_to_okey(sc[e + x]) : 0u;
+    }
+  }
+}
+
+__device__ __forceinline__ int64_t key_column(int64_t base, int j) {
+  return base + (int64_t((j >> 2) * kThreads + int(threadIdx.x)) << 2) + (j & 3);
+}
+
+// Split cluster barrier (arrive publishes this CTA's prior writes; wait acquires
+// everyone's). Every thread of every CTA alternates arrive and wait.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Leader, over the per-CTA histograms hist[r * kLevelBins + digit]: the largest
+// digit b with (keys in digits >= b) >= need, the keys above it (sm.above) and in
+// it (sm.bcount), and each CTA's count of keys in digits above b (sm.gt[r]).
+__device__ void leader_find(SelectSmem& sm, int nb, uint32_t need) {
+  const int t = threadIdx.x, lane = t & 31;
+  uint32_t v[2] = {0u, 0u};
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int bb = nb - 1 - 2 * t - u;
+    if (bb >= 0)
+#pragma unroll
+      for (int r = 0; r < kCluster; ++r) v[u] += sm.hist[r * kLevelBins + bb];
+  }
+  if (t == 0) {
+    sm.bin = 0;
+    sm.above = 0;
+    sm.bcount = 0;
+  }
+  if (t < kCluster) sm.gt[t] = 0;
+  const uint32_t excl = block_excl_scan(v[0] + v[1], sm, nullptr);
+  if (excl < need && excl + v[0] + v[1] >= need) {
+    const int bb = nb - 1 - 2 * t;
+    const bool first = excl + v[0] >= need;
+    sm.bin = uint32_t(first ? bb : bb - 1);
+    sm.above = first ? excl : excl + v[0];
+    sm.bcount = first ? v[0] : v[1];
+  }
+  __syncthreads();
+  const int b = int(sm.bin);
+#pragma unroll
+  for (int r = 0; r < kCluster; ++r) {
+    uint32_t c = 0;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int bb = nb - 1 - 2 * t - u;
+      if (bb > b) c += sm.hist[r * kLevelBins + bb];
+    }
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (lane == 0 && c) atomicAdd(&sm.gt[r], c);
+  }
+  __syncthreads();
+}
+
+// Smallest fine bin f whose end (sm.hist after the scatter) exceeds position p.
+__device__ __forceinline__ uint32_t bin_of_position(const SelectSmem& sm, uint32_t p) {
+  uint32_t lo = 0, hi = kFineBins - 1;
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (sm.hist[mid] > p) hi = mid;
+    else lo = mid + 1;
+  }
+  return lo;
+}
+
+// ---- fast path: sampled threshold, candidates replicated in every CTA -------------------
+constexpr int kSampleBins = 4096;                // 12-bit digits (key >> 20)
+constexpr int kSampleCopies = 4;                 // private copies, one per lane & 3
+constexpr int kSampleStride = kSampleBins + 4;
+// Keys j = 0, 9, 18, 27 of a thread are sampled: column offsets (u*1024 + t)*4 + e
+// for (u, e) = (0, 0), (2, 1), (4, 2), (6, 3) — one column in eight.
+__device__ __forceinline__ bool sampled_key(int j) { return j == 0 || j == 9 || j == 18 || j == 27; }
+
+// Number of sampled columns below n (the same for every CTA of the row).
+__device__ __forceinline__ uint32_t sampled_columns(int64_t n) {
+  uint32_t ns = 0;
+  for (int r = 0; r < kCluster; ++r)
+    for (int u = 0; u < 4; ++u) {
+      const int64_t first = int64_t(r) * kThreads * kKeys + int64_t(2 * u) * kThreads * 4 + u;
+      const int64_t cnt = first < n ? (n - first + 3) / 4 : 0;
+      ns += uint32_t(cnt < kThreads ? cnt : kThreads);
+    }
+  return ns;
+}
+
+// Every CTA of the cluster holds all nc candidates in sm.buf (identical slots).
+// Fine-bin counting sort as on the general leader path; CTA r then ranks and
+// stores the whole bins that cover output positions [r*P, (r+1)*P), P = ceil(k/4).
+// A straddling bin is ranked by both neighbours, which store identical values.
+__device__ void replicated_sort_store(const SelectArgs& a, int64_t row, SelectSmem& sm,
+                                      uint32_t nc, uint32_t thr, uint32_t kmax, unsigned rank) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const uint32_t range = kmax - thr;
+  int shift = 0;
+  while ((range >> shift) >= uint32_t(kFineBins)) ++shift;
+  for (uint32_t i = tid; i < nc; i += kThreads)
+    atomicAdd(&sm.hist[(kmax - uint32_t(sm.buf[i] >> 32)) >> shift], 1u);
+  __syncthreads();
+  {
+    constexpr int kPer = kFineBins / kThreads;
+    uint32_t h[kPer], tot = 0, hmax = 0;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      h[u] = sm.hist[kPer * tid + u];
+      tot += h[u];
+      hmax = max(hmax, h[u]);
+    }
+    hmax = __reduce_max_sync(0xffffffffu, hmax);
+    if (lane == 0) atomicMax(&sm.big, hmax);
+    uint32_t ex = block_excl_scan(tot, sm, nullptr);
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      sm.hist[kPer * tid + u] = ex;  // start of bin
+      ex += h[u];
+    }
+  }
+  __syncthreads();
+  if (sm.big > uint32_t(kRankMax)) {
+    if (rank == 0) {
+      block_bitonic_sort(sm, int(nc));
+      write_out(a, row, sm);
+    }
+    return;
+  }
+  for (uint32_t i = tid; i < nc; i += kThreads) {
+    const uint32_t f = (kmax - uint32_t(sm.buf[i] >> 32)) >> shift;
+    sm.perm[atomicAdd(&sm.hist[f], 1u)] = uint16_t(i);
+  }
+  __syncthreads();  // hist[f] is now the end of bin f
+  const uint32_t kk = uint32_t(a.k);
+  const uint32_t P = (kk + kCluster - 1) / kCluster;
+  const uint32_t p0 = rank * P, p1 = min(kk, p0 + P);
+  if (p0 >= p1) return;
+  const uint32_t f0 = bin_of_position(sm, p0), f1 = bin_of_position(sm, p1 - 1);
+  const uint32_t q0 = f0 ? sm.hist[f0 - 1] : 0u, q1 = sm.hist[f1];
+  int32_t* oi = a.out_idx + row * a.k;
+  float* os = a.out_scores ? a.out_scores + row * a.k : nullptr;
+  const int64_t ibase = a.idx_in ? 0 : a.index_base;
+  for (uint32_t q = q0 + tid; q < q1; q += kThreads) {
+    const uint32_t i = sm.perm[q];
+    const uint64_t x = sm.buf[i];
+    const uint32_t f = (kmax - uint32_t(x >> 32)) >> shift;
+    const uint32_t s = f ? sm.hist[f - 1] : 0u;
+    const uint32_t e = sm.hist[f];
+    uint32_t p = s;
+    for (uint32_t j = s; j < e; ++j) {
+      const uint32_t pj = sm.perm[j];
+      const uint64_t y = sm.buf[pj];
+      p += (y > x) || (y == x && pj < i);
+    }
+    if (p < kk) {
+      oi[p] = int32_t(int64_t(~uint32_t(x)) + ibase);
+      if (os) os[p] = okey_to_float(uint32_t(x >> 32));
+    }
+  }
+}
+
+// One row per cluster of kCluster CTAs.
+//  1. Radix threshold: every CTA histograms the top 11 key bits of its columns
+//     (8 private copies, one per lane & 7, against same-address atomics) and
+//     stores the histogram into its slice of the leader's shared memory; the
+//     leader finds the digit holding the k-th largest key and each CTA's count
+//     of keys at or above it. While that digit would bring more than kCap
+//     candidates, the next 11 (then 10) bits of the keys inside it are
+//     histogrammed the same way. The threshold T is the lower edge of the chosen
+//     digit, so exactly the keys >= T — at least k, at most kCap — are candidates.
+//  2. Every CTA writes its keys >= T, packed with their indices, into its own
+//     slot range of the row's candidate buffer.
+//  3. The leader counting-sorts the candidates into 8192 fine bins of
+//     (max_key - key); a candidate's output position is its bin's start plus the
+//     number of bin members ahead of it, and the threads walk the candidates in
+//     bin order so that a warp's member loads and output stores stay together.
+//     A fine bin above kRankMax members switches to a bitonic sort of all
+//     candidates.
+// Keys are loaded once and kept in registers when the row fits one pass
+// (kResident); longer rows are re-read for each histogram level and the append.
+// If even whole-key ties exceed kCap, the leader runs the general path.
+template <bool kResident>
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
-    select_topk_cluster_kernel(const SelectArgs a, uint64_t* __restrict__ cand_all, int64_t cand_cap) {
+    select_topk_cluster_kernel(const SelectArgs a, uint64_t* __restrict__ cand_all,
+                               int64_t cand_cap) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
   const unsigned rank = cluster.block_rank();
   const int64_t row = blockIdx.x / kCluster;
-  SelectSmem* lead = cluster.map_shared_rank(&sm, 0);
-  const uint32_t kk = uint32_t(a.k);
   const int tid = threadIdx.x;
-  const int lane = tid & 31, warp = tid >> 5;
-
-  // this CTA's quarter of the row, 4-aligned
-  const int64_t c0 = ((a.n * rank / kCluster) >> 2) << 2;
-  const int64_t c1 = rank + 1 == kCluster ? a.n : ((a.n * (rank + 1) / kCluster) >> 2) << 2;
-
-  zero_hist(sm, kSampleBins);
-  if (tid == 0) {
-    sm.count = 0;
-    sm.thr = 0;
-  }
-  grid_dependency_wait();
-
-  // ---- 1. sample, threshold ---------------------------------------------------------
-  const bool sample = a.n > kSmallN;
+  const int lane = tid & 31;
   const float* sc = a.scores + row * a.ld;
-  if (sample) {
-    for (int64_t g = (c0 >> 7) + tid; (g << 7) < c1; g += kThreads) {
-      const int64_t s0 = (g << 7) + 8 * int64_t((uint32_t(g) * 0x9E3779B1u) >> 28);
-      if (s0 < c0 || s0 + 8 > c1) continue;
-      const float4 x = *reinterpret_cast<const float4*>(sc + s0);
-      const float4 y = *reinterpret_cast<const float4*>(sc + s0 + 4);
-      atomicAdd(&sm.hist[float_to_okey(x.x) >> 20], 1u);
-      atomicAdd(&sm.hist[float_to_okey(x.y) >> 20], 1u);
-      atomicAdd(&sm.hist[float_to_okey(x.z) >> 20], 1u);
-      atomicAdd(&sm.hist[float_to_okey(x.w) >> 20], 1u);
-      atomicAdd(&sm.hist[float_to_okey(y.x) >> 20], 1u);
-      atomicAdd(&sm.hist[float_to_okey(y.y) >> 20], 1u);
-      atomicAdd(&sm.hist[float_to_okey(y.z) >> 20], 1u);
-      atomicAdd(&sm.hist[float_to_okey(y.w) >> 20], 1u);
-    }
-  }
-  cluster.sync();
-  if (rank == 0 && sample) {
-    // merge the four sample histograms into the leader's
-    uint32_t ns = 0;
-    for (int i = tid; i < kSampleBins; i += kThreads) {
-      uint32_t s = sm.hist[i];
-#pragma unroll
-      for (int r = 1; r < kCluster; ++r) s += cluster.map_shared_rank(&sm, r)->hist[i];
-      sm.hist[i] = s;
-      ns += s;
-    }
-    // total number of samples (sm.count is free until the filter phase)
-    ns = __reduce_add_sync(0xffffffffu, ns);
-    if (lane == 0) atomicAdd(&sm.count, ns);
-    __syncthreads();
-    ns = sm.count;
-    __syncthreads();
-    if (tid == 0) sm.count = 0;
-    // the threshold is the lower edge of the bin holding this sample rank
-    const double want = double(kk) * double(ns) / double(a.n) * 1.25 + 32.0;
-    if (want < double(ns)) {
-      find_bin(sm, kSampleBins, uint32_t(want));
-      if (tid == 0) sm.thr = sm.bin << 20;
-    }
-  }
-  cluster.sync();
-  const uint32_t thr = lead->thr;
+  const int32_t* ix = a.idx_in ? a.idx_in + row * a.ld : nullptr;
+  const int64_t npass = kResident ? 1 : (a.n + kPass - 1) / kPass;
+  const int64_t my_base = int64_t(rank) * kThreads * kKeys;
+  uint32_t* priv = reinterpret_cast<uint32_t*>(sm.buf);  // [kPriv][kPrivStride]
+  uint32_t* my_priv = priv + (lane & (kPriv - 1)) * kPrivStride;
+  SelectSmem* lead = cluster.map_shared_rank(&sm, 0);
+  uint32_t* lead_slice = cluster.map_shared_rank(sm.hist, 0) + rank * kLevelBins;
 
-  // ---- 2. filter into the row's candidate buffer -------------------------------------
-  // a warp takes 512 consecutive columns per round (4 float4 per lane, all
-  // loads in flight together) and one slot range from the leader's counter
-  uint64_t* cand = cand_all + row * cand_cap;
-  {
-    const int32_t* ix = a.idx_in ? a.idx_in + row * a.ld : nullptr;
-    for (int64_t wb = c0 + int64_t(warp) * 512; wb < c1; wb += int64_t(kThreads / 32) * 512) {
-      uint32_t keys[16];
-      uint32_t hit = 0;  // bit u*4+e: element (lane + 32u)*4 + e passes
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t e = wb + int64_t(lane + 32 * u) * 4;
-        if (e + 4 <= c1) {
-          const float4 v = *reinterpret_cast<const float4*>(sc + e);
-          keys[4 * u + 0] = float_to_okey(v.x);
-          keys[4 * u + 1] = float_to_okey(v.y);
-          keys[4 * u + 2] = float_to_okey(v.z);
-          keys[4 * u + 3] = float_to_okey(v.w);
-        } else {
-#pragma unroll
-          for (int x = 0; x < 4; ++x) keys[4 * u + x] = e + x < c1 ? float_to_okey(sc[e + x]) : 0u;
-        }
-      }
-#pragma unroll
-      for (int x = 0; x < 16; ++x) {
-        const int64_t e = wb + int64_t(lane + 32 * (x >> 2)) * 4 + (x & 3);
-        if (keys[x] >= thr && e < c1) hit |= 1u << x;
-      }
-      const uint32_t mine = __popc(hit);
-      uint32_t incl = mine;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
-      uint32_t wbase = 0;
-      if (lane == 31 && wtot) wbase = atomicAdd(&lead->count, wtot);
-      wbase = __shfl_sync(0xffffffffu, wbase, 31);
-      uint32_t slot = wbase + incl - mine;
-#pragma unroll
-      for (int x = 0; x < 16; ++x) {  // static indices keep keys[] in registers
-        if (hit & (1u << x)) {
-          const int64_t e = wb + int64_t(lane + 32 * (x >> 2)) * 4 + (x & 3);
-          const uint32_t idx = ix ? uint32_t(ix[e]) : uint32_t(e);
-          if (slot < uint64_t(cand_cap)) cand[slot] = pack_cand(keys[x], idx);
-          ++slot;
-        }
-      }
-    }
-  }
-  cluster.sync();
-  if (rank != 0) return;
-
-  // ---- 3. leader: fine-binned counting sort of the candidates ----------------------------
-  const uint32_t nc = sm.count;
-  if (nc < kk || int64_t(nc) > cand_cap || nc > uint32_t(kThreads * kRegCand)) {
-    select_row_general(a, row, sm);  // threshold missed (or too many): exact general path
-    return;
-  }
-  uint64_t rc[kRegCand];  // this thread's candidates i = tid + kThreads*u
-  uint32_t lmax = 0, lmin = 0xffffffffu;
-#pragma unroll
-  for (int u = 0; u < kRegCand; ++u) {
-    const uint32_t i = tid + kThreads * u;
-    rc[u] = i < nc ? cand[i] : 0ull;
-    if (i < nc) {
-      const uint32_t key = uint32_t(rc[u] >> 32);
-      lmax = max(lmax, key);
-      lmin = min(lmin, key);
-    }
-  }
-  lmax = __reduce_max_sync(0xffffffffu, lmax);
-  lmin = __reduce_min_sync(0xffffffffu, lmin);
+  for (int i = tid; i < kPriv * kPrivStride; i += kThreads) priv[i] = 0u;
+  for (int i = tid; i < kSampleBins; i += kThreads) sm.hist[i] = 0u;
   if (tid == 0) {
     sm.kmax = 0;
-    sm.kmin = 0xffffffffu;
+    sm.woff = 0;
     sm.big = 0;
-    sm.nmed = 0;
   }
-  zero_hist(sm, kFineBins);
-  if (lane == 0) {
-    atomicMax(&sm.kmax, lmax);
-    atomicMin(&sm.kmin, lmin);
-  }
+  if (tid < kCluster) sm.acc[tid] = 0;
   __syncthreads();
-  const uint32_t kmax = sm.kmax, range = kmax - sm.kmin;
+  cluster_arrive();  // every CTA has started and initialised its shared memory
+  grid_dependency_wait();
+  uint32_t kv[kKeys];
+  if (kResident) load_keys(sc, my_base, a.n, kv);
+
+  if (kResident) {
+    // ---- fast path: threshold from a 1/8 sample, candidates in every CTA -------------
+    uint32_t* my_samp = priv + (lane & (kSampleCopies - 1)) * kSampleStride;
+    uint32_t kmx = 0;
+#pragma unroll
+    for (int j = 0; j < kKeys; ++j) {
+      kmx = max(kmx, kv[j]);
+      if (sampled_key(j) && kv[j] != 0u) atomicAdd(&my_samp[kv[j] >> 20], 1u);
+    }
+    kmx = __reduce_max_sync(0xffffffffu, kmx);
+    if (lane == 0) atomicMax(&sm.kmax, kmx);
+    __syncthreads();
+    cluster_wait();  // the leader's histogram is zeroed
+    uint32_t* lead_hist = cluster.map_shared_rank(sm.hist, 0);
+    for (int i = tid; i < kSampleBins; i += kThreads) {
+      uint32_t c = 0;
+#pragma unroll
+      for (int q = 0; q < kSampleCopies; ++q) c += priv[q * kSampleStride + i];
+      if (c) atomicAdd(&lead_hist[i], c);
+    }
+    if (tid == 0) atomicMax(&lead->kmax, sm.kmax);
+    cluster.sync();  // the sample histogram is complete
+    if (rank == 0) {
+      // threshold: lower edge of the digit holding sample rank m, a margin of 10%
+      // plus four binomial deviations below the expected rank of the k-th key
+      const double ns = double(sampled_columns(a.n));
+      const double expect = double(a.k) * ns / double(a.n);
+      const double m = expect * 1.1 + 4.0 * sqrt(expect) + 8.0;
+      if (m < ns) {
+        find_bin(sm, kSampleBins, uint32_t(m));
+        if (tid == 0) sm.thr = sm.bin << 20;
+      } else if (tid == 0) {
+        sm.thr = 1u;  // every key
+      }
+      if (tid == 0) sm.count = 0;
+    }
+    for (int i = tid; i < kFineBins; i += kThreads) sm.hist[i] = 0u;  // the leader's after find
+    cluster.sync();  // threshold ready
+    if (tid == 0) {
+      sm.thr = lead->thr;
+      sm.kmax = lead->kmax;
+    }
+    __syncthreads();
+    const uint32_t fthr = sm.thr;
+    uint32_t hit = 0;
+#pragma unroll
+    for (int j = 0; j < kKeys; ++j)
+      if (kv[j] >= fthr) hit |= 1u << j;
+    const uint32_t mine = __popc(hit);
+    uint32_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
+    uint32_t wbase = 0;
+    if (lane == 31 && wtot) wbase = atomicAdd(&sm.woff, wtot);
+    wbase = __shfl_sync(0xffffffffu, wbase, 31);
+    __syncthreads();
+    if (tid == 0) sm.cbase = sm.woff ? atomicAdd(&lead->count, sm.woff) : 0u;
+    __syncthreads();
+    uint32_t slot = sm.cbase + wbase + incl - mine;
+    uint64_t* rbuf[kCluster];
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) rbuf[r] = cluster.map_shared_rank(sm.buf, r);
+#pragma unroll
+    for (int j = 0; j < kKeys; ++j) {
+      if (hit & (1u << j)) {
+        if (slot < uint32_t(kCap)) {
+          const int64_t col = key_column(my_base, j);
+          const uint64_t v = pack_cand(kv[j], ix ? uint32_t(ix[col]) : uint32_t(col));
+#pragma unroll
+          for (int r = 0; r < kCluster; ++r) rbuf[r][slot] = v;
+        }
+        ++slot;
+      }
+    }
+    cluster.sync();  // every CTA holds all candidates
+    if (tid == 0) sm.count = lead->count;
+    __syncthreads();
+    const uint32_t total = sm.count;
+    if (total >= uint32_t(a.k) && total <= uint32_t(kCap)) {
+      replicated_sort_store(a, row, sm, total, fthr, sm.kmax, rank);
+      return;
+    }
+    // the sample missed (fewer than k keys above the threshold, or more than kCap):
+    // take the exact path below from a clean state
+    for (int i = tid; i < kPriv * kPrivStride; i += kThreads) priv[i] = 0u;
+    if (tid == 0) sm.woff = 0;
+    cluster.sync();  // nobody reads the leader's counter any more
+    if (tid == 0) sm.count = 0;
+    __syncthreads();
+    cluster_arrive();
+  }
+
+  // ---- 1. threshold ------------------------------------------------------------------
+  uint32_t need = uint32_t(a.k), above_total = 0, pfx = 0, thr = 0, kmax_local = 0;
+  bool found = false;
+#pragma unroll 1
+  for (int level = 0; level < 3; ++level) {
+    const int dshift = level == 0 ? 21 : (level == 1 ? 10 : 0);
+    const int nbits = level == 2 ? 10 : 11;
+    const int pshift = level == 1 ? 21 : 10;  // prefix bits above the digit (levels 1, 2)
+    const int nb = 1 << nbits;
+    const uint32_t dmask = uint32_t(nb) - 1u;
+    if (level > 0) {
+      for (int i = tid; i < kPriv * kPrivStride; i += kThreads) priv[i] = 0u;
+      __syncthreads();
+    }
+    auto accumulate = [&](const uint32_t (&keys)[kKeys]) {
+#pragma unroll
+      for (int j = 0; j < kKeys; ++j) {
+        const uint32_t key = keys[j];
+        const bool match = level == 0 ? key != 0u : (key >> pshift) == pfx;
+        if (match) atomicAdd(&my_priv[(key >> dshift) & dmask], 1u);
+        if (level == 0) kmax_local = max(kmax_local, key);
+      }
+    };
+    if (kResident) {
+      accumulate(kv);
+    } else {
+      for (int64_t p = 0; p < npass; ++p) {
+        uint32_t kp[kKeys];
+        load_keys(sc, p * kPass + my_base, a.n, kp);
+        accumulate(kp);
+      }
+    }
+    if (level == 0) {
+      kmax_local = __reduce_max_sync(0xffffffffu, kmax_local);
+      if (lane == 0) atomicMax(&sm.kmax, kmax_local);
+    }
+    __syncthreads();
+    if (level == 0) cluster_wait();
+    for (int i = tid; i < nb; i += kThreads) {
+      uint32_t c = 0;
+#pragma unroll
+      for (int q = 0; q < kPriv; ++q) c += priv[q * kPrivStride + i];
+      lead_slice[i] = c;
+    }
+    if (level == 0 && tid == 0) atomicMax(&lead->kmax, sm.kmax);
+    cluster.sync();  // every CTA's histogram is in the leader's shared memory
+    if (rank == 0) {
+      leader_find(sm, nb, need);
+      if (tid == 0) {
+        // final level: CTA r's candidates are its keys above earlier digits, above
+        // this digit and in it; otherwise carry the keys above this digit forward
+        const bool fits = above_total + sm.above + sm.bcount <= uint32_t(kCap);
+        uint32_t slot = 0;
+        for (int r = 0; r < kCluster; ++r) {
+          const uint32_t eq = sm.hist[r * kLevelBins + sm.bin];
+          if (fits) {
+            sm.base[r] = slot;
+            slot += sm.acc[r] + sm.gt[r] + eq;
+          } else {
+            sm.acc[r] += sm.gt[r];
+          }
+        }
+        sm.total = slot;
+      }
+    }
+    cluster.sync();  // the leader's answer is ready
+    if (tid == 0 && rank != 0) {
+      sm.bin = lead->bin;
+      sm.above = lead->above;
+      sm.bcount = lead->bcount;
+      sm.base[rank] = lead->base[rank];
+    }
+    __syncthreads();
+    const uint32_t b = sm.bin, above = sm.above, bcount = sm.bcount;
+    const uint32_t digits = (pfx << nbits) | b;
+    if (above_total + above + bcount <= uint32_t(kCap)) {
+      thr = digits << dshift;
+      found = true;
+      break;
+    }
+    above_total += above;
+    need -= above;
+    pfx = digits;
+    cluster.sync();  // everyone has read the answer before the next level reuses it
+  }
+  if (!found) {
+    if (rank == 0) select_row_general(a, row, sm);
+    return;
+  }
+
+  // ---- 2. write keys >= thr into this CTA's slot range -------------------------------------
+  uint64_t* cand = cand_all + row * cand_cap;
+  const uint32_t cta_base = sm.base[rank];
+  auto append = [&](const uint32_t (&keys)[kKeys], int64_t base) {
+    uint32_t hit = 0;
+#pragma unroll
+    for (int j = 0; j < kKeys; ++j)
+      if (keys[j] >= thr) hit |= 1u << j;
+    const uint32_t mine = __popc(hit);
+    uint32_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
+    uint32_t wbase = 0;
+    if (lane == 31 && wtot) wbase = atomicAdd(&sm.woff, wtot);
+    wbase = __shfl_sync(0xffffffffu, wbase, 31);
+    uint32_t slot = cta_base + wbase + incl - mine;
+#pragma unroll
+    for (int j = 0; j < kKeys; ++j) {
+      if (hit & (1u << j)) {
+        const int64_t col = key_column(base, j);
+        const uint32_t idx = ix ? uint32_t(ix[col]) : uint32_t(col);
+        if (slot < uint64_t(cand_cap)) cand[slot] = pack_cand(keys[j], idx);
+        ++slot;
+      }
+    }
+  };
+  if (kResident) {
+    append(kv, my_base);
+  } else {
+    for (int64_t p = 0; p < npass; ++p) {
+      uint32_t kp[kKeys];
+      load_keys(sc, p * kPass + my_base, a.n, kp);
+      append(kp, p * kPass + my_base);
+    }
+  }
+  cluster.sync();  // candidates written
+  if (rank != 0) return;
+
+  // ---- 3. leader: fine-bin counting sort, rank inside bins, permute, store ------------------
+  const uint32_t nc = min(sm.total, uint32_t(cand_cap));
+  for (uint32_t i = tid; i < nc; i += kThreads) sm.buf[i] = cand[i];
+  for (int i = tid; i < kFineBins; i += kThreads) sm.hist[i] = 0u;
+  __syncthreads();
+  const uint32_t kmax = sm.kmax, range = kmax - thr;
   int shift = 0;
   while ((range >> shift) >= uint32_t(kFineBins)) ++shift;
-#pragma unroll
-  for (int u = 0; u < kRegCand; ++u) {
-    if (tid + kThreads * u < nc) atomicAdd(&sm.hist[(kmax - uint32_t(rc[u] >> 32)) >> shift], 1u);
-  }
+  for (uint32_t i = tid; i < nc; i += kThreads)
+    atomicAdd(&sm.hist[(kmax - uint32_t(sm.buf[i] >> 32)) >> shift], 1u);
   __syncthreads();
-  // exclusive scan of the bins in order (bin 0 = largest keys)
   {
     constexpr int kPer = kFineBins / kThreads;
-    uint32_t h[kPer], s = 0;
+    uint32_t h[kPer], tot = 0, hmax = 0;
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
       h[u] = sm.hist[kPer * tid + u];
-      s += h[u];
+      tot += h[u];
+      hmax = max(hmax, h[u]);
     }
-    uint32_t ex = block_excl_scan(s, sm, nullptr);
-    // find the bin holding position kk-1 and turn counts into start offsets
+    hmax = __reduce_max_sync(0xffffffffu, hmax);
+    if (lane == 0) atomicMax(&sm.big, hmax);
+    uint32_t ex = block_excl_scan(tot, sm, nullptr);
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
-      if (ex <= kk - 1 && kk - 1 < ex + h[u]) {
-        sm.bin = uint32_t(kPer * tid + u);
-        sm.above = ex + h[u];  // elements in bins <= bin
-      }
-      sm.hist[kPer * tid + u] = ex;
+      sm.hist[kPer * tid + u] = ex;  // start of bin
       ex += h[u];
     }
   }
   __syncthreads();
-  const uint32_t bk = sm.bin, nout = sm.above;
-  if (nout > uint32_t(kCap)) {
-    select_row_general(a, row, sm);
+  if (sm.big > uint32_t(kRankMax)) {
+    block_bitonic_sort(sm, int(nc));
+    write_out(a, row, sm);
     return;
   }
-  // scatter (hist[b] becomes the end of bin b)
-#pragma unroll
-  for (int u = 0; u < kRegCand; ++u) {
-    if (tid + kThreads * u < nc) {
-      const uint32_t b = (kmax - uint32_t(rc[u] >> 32)) >> shift;
-      if (b <= bk) sm.buf[atomicAdd(&sm.hist[b], 1u)] = rc[u];
+  for (uint32_t i = tid; i < nc; i += kThreads) {
+    const uint32_t f = (kmax - uint32_t(sm.buf[i] >> 32)) >> shift;
+    sm.perm[atomicAdd(&sm.hist[f], 1u)] = uint16_t(i);
+  }
+  __syncthreads();  // hist[f] is now the end of bin f
+  // walk the candidates in bin order: the lanes of a warp share bins, so the
+  // member loads broadcast and the stores of a bin land together
+  int32_t* oi = a.out_idx + row * a.k;
+  float* os = a.out_scores ? a.out_scores + row * a.k : nullptr;
+  const int64_t ibase = a.idx_in ? 0 : a.index_base;
+  for (uint32_t q = tid; q < nc; q += kThreads) {
+    const uint32_t i = sm.perm[q];
+    const uint64_t x = sm.buf[i];
+    const uint32_t f = (kmax - uint32_t(x >> 32)) >> shift;
+    const uint32_t s = f ? sm.hist[f - 1] : 0u;
+    if (s >= uint32_t(a.k)) continue;
+    const uint32_t e = sm.hist[f];
+    uint32_t p = s;
+    for (uint32_t j = s; j < e; ++j) {
+      const uint32_t pj = sm.perm[j];
+      const uint64_t y = sm.buf[pj];
+      p += (y > x) || (y == x && pj < i);
+    }
+    if (p < uint32_t(a.k)) {
+      oi[p] = int32_t(int64_t(~uint32_t(x)) + ibase);
+      if (os) os[p] = okey_to_float(uint32_t(x >> 32));
     }
   }
-  __syncthreads();
-  // sort inside bins: insertion sort for <= 16 elements, queue the rest
-  for (uint32_t b = tid; b <= bk; b += kThreads) {
-    const uint32_t e = sm.hist[b];
-    const uint32_t s = b ? sm.hist[b - 1] : 0u;
-    const uint32_t n = e - s;
-    if (n <= 1) continue;
-    if (n <= 16) {
-      for (uint32_t x = s + 1; x < e; ++x) {
-        const uint64_t v = sm.buf[x];
-        uint32_t y = x;
-        while (y > s && sm.buf[y - 1] < v) {
-          sm.buf[y] = sm.buf[y - 1];
-          --y;
-        }
-        sm.buf[y] = v;
-      }
-    } else if (n <= 256) {
-      sm.med[atomicAdd(&sm.nmed, 1u)] = b;
-    } else {
-      sm.big = 1;
-    }
-  }
-  __syncthreads();
-  if (sm.big) {
-    block_bitonic_sort(sm, int(nout));
-  } else {
-    for (uint32_t m = warp; m < sm.nmed; m += kThreads / 32) {
-      const uint32_t b = sm.med[m];
-      const uint32_t s = b ? sm.hist[b - 1] : 0u;
-      warp_sort_segment(&sm.buf[s], int(sm.hist[b] - s));
-    }
-    __syncthreads();
-  }
-  write_out(a, row, sm);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) select_topk_general_kernel(const SelectArgs a) {
@@ -577,9 +817,8 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_general_kernel(const 
 }  // namespace
 
 int64_t select_cand_cap(int64_t n) {
-  // every column is a candidate when the sample is skipped (n <= kSmallN);
-  // otherwise the threshold keeps ~1.4 k + bin slack, k <= 16384
-  return n < 32768 ? n : 32768;
+  // the threshold admits at most kCap candidates (and never more than n)
+  return n < kCap ? n : kCap;
 }
 
 size_t select_workspace_bytes(int64_t rows, int64_t n) {
@@ -596,10 +835,11 @@ cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t 
     select_topk_general_kernel<<<dim3(unsigned(a.rows)), kThreads, smem, stream>>>(a);
     return cudaGetLastError();
   }
-  cudaError_t e = cudaFuncSetAttribute(select_topk_cluster_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  const bool resident = a.n <= kPass;
+  auto kern = resident ? select_topk_cluster_kernel<true> : select_topk_cluster_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  select_topk_cluster_kernel<<<dim3(unsigned(a.rows * kCluster)), kThreads, smem, stream>>>(
+  kern<<<dim3(unsigned(a.rows * kCluster)), kThreads, smem, stream>>>(
       a, static_cast<uint64_t*>(cand_ws), select_cand_cap(a.n));
   return cudaGetLastError();
 }

@@ -41,8 +41,8 @@ def test_abi_version(lib):
 
 def test_workspace_size(lib):
     # status block (256 B) + fp32 scores (rows padded to 4 floats, block to 256 B)
-    # + per-row u64 candidate buffers (min(n, 32768) entries)
-    assert lib.prism_einsum_topk_workspace_size(1, 32, 1, 131072, 4096, 0) == 256 + 32 * 131072 * 4 + 32 * 32768 * 8
+    # + per-row u64 candidate buffers (min(n, 16384) entries)
+    assert lib.prism_einsum_topk_workspace_size(1, 32, 1, 131072, 4096, 0) == 256 + 32 * 131072 * 4 + 32 * 16384 * 8
     assert lib.prism_einsum_topk_workspace_size(1, 4, 2, 5, 3, 0) == 256 + 256 + 8 * 5 * 8
     assert lib.prism_topk_merge_workspace_size(6, 1536) == 6 * 1536 * 8
     assert lib.prism_einsum_topk_workspace_size(0, 4, 2, 5, 3, 0) == 0

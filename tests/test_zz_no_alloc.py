@@ -45,7 +45,7 @@ def _shard_candidates(rows, shards, per_shard, seed, device):
 def test_noalloc_rejects_requests_beyond_the_scratch(lib):
     # rejected before any CUDA call, so no device is needed; the pointers are
     # never dereferenced
-    rows, n = 33, 65536  # 33 * 32768 * 8 > 8 MiB
+    rows, n = 65, 65536  # 65 * 16384 * 8 > 8 MiB
     rc = lib.prism_topk_merge_noalloc(16, 16, rows, n, n, 10, 16, None, None)
     assert rc == _lib.PRISM_E_WORKSPACE
     msg = _lib.last_error()
@@ -57,9 +57,9 @@ def test_noalloc_rejects_requests_beyond_the_scratch(lib):
 
 @pytest.mark.gpu
 def test_noalloc_matches_workspace_merge_twice_in_a_row(cuda_device, lib):
-    # 8 shards x 8192 sorted candidates for 32 query heads: the 1M-key sharded
-    # decode merge, exactly the 8 MiB scratch limit; then a small case
-    big = _shard_candidates(32, 8, 8192, seed=11, device=cuda_device)
+    # 8 shards x 8192 sorted candidates for 64 rows (the 1M-key sharded decode
+    # merge has 32), exactly the 8 MiB scratch limit; then a small case
+    big = _shard_candidates(64, 8, 8192, seed=11, device=cuda_device)
     small_s = torch.randn(5, 1000, generator=torch.Generator().manual_seed(12)).to(cuda_device)
     small_i = torch.arange(small_s.shape[1], dtype=torch.int32, device=cuda_device).expand(5, -1).contiguous()
     cases = [(big[0], big[1], 8192), (small_s, small_i, 37)]
