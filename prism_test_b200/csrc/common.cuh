@@ -141,6 +141,11 @@ __device__ __forceinline__ uint4 lds128_u32(uint32_t addr) {
                : "r"(addr));
   return v;
 }
+__device__ __forceinline__ uint2 lds64_u32(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ float4 lds128f_u32(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"

@@ -24,9 +24,11 @@
 // is fp32. The score error is at most 2^-11 * sum_i |q_i k_i| <= 0.49 of the
 // 1e-3 * ||q|| ||k|| tolerance.
 //
-// Memory: each warp streams its own copies (8 positions x up to 4 heads, one
-// tiled TMA copy, 8 KB) through a private 3-stage ring, two copies in flight per
-// warp; 8 warps (two per scheduler) hide each other's latencies.
+// Memory: each warp streams its own copies (16 positions x one head pair, one
+// tiled TMA copy of 8 KB with 4 KB contiguous per head) through a private 3-stage
+// ring, two copies in flight per warp; 8 warps (two per scheduler) hide each
+// other's latencies. The query fragments live in a shared table, so registers
+// hold only keys, angles and accumulators.
 #include <type_traits>
 
 #include "common.cuh"
@@ -40,12 +42,17 @@ namespace {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 3;
-constexpr int kP = 8;              // positions per sub-tile
+constexpr int kP = 8;              // positions per sub-tile (MMA rows per head)
+constexpr int kSubs = 2;           // sub-tiles per copy
+constexpr int kPc = kP * kSubs;    // positions per copy: 4 KB contiguous per head
 constexpr int kMaxPairs = 4;       // Hkv <= 8
-constexpr int kPairsPerCopy = 2;   // one TMA copy holds <= 2 head pairs (4 heads)
+constexpr int kPairsPerCopy = 1;   // one TMA copy holds one head pair (2 heads)
 constexpr float kTruncScale = 1.0f + 0x1.0p-11f;  // see the precision note
 
 struct __align__(16) HpTail {
+  // B fragments in fragment order: bfrag[hp][ks][lane] = (b0, b1) of the k-step ks
+  // MMA of head pair hp, as fp32 (bf16 queries are exact in TF32)
+  float2 bfrag[kMaxPairs][16][32];
   uint64_t full[kWarps][kStages];
 };
 
@@ -65,9 +72,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int Hkv = a.Hkv;
   const int npairs = Hkv / 2;
   const int ppc = npairs < kPairsPerCopy ? npairs : kPairsPerCopy;  // pairs per copy
-  const int copies = npairs / ppc;                                  // copies per sub-tile: 1 or 2
+  const int copies = npairs / ppc;                                  // copies per sub-tile: 1, 2, 4
+  const int cshift = copies == 4 ? 2 : (copies == 2 ? 1 : 0);
   const int R = a.G * a.sq_n;  // <= 4
-  const uint32_t copy_bytes = uint32_t(ppc) * 2 * kP * kRowBytes;
+  const uint32_t copy_bytes = uint32_t(ppc) * 2 * kPc * kRowBytes;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2;  // position g of the sub-tile; B column g
@@ -77,8 +85,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* ring = smem + warp * kStages * copy_bytes;
   uint64_t* full = tail->full[warp];
 
-  // sub-tiles of this warp: a contiguous range of the row's kP-position slices
-  const int nsub = (a.Sk + kP - 1) / kP;
+  // blocks of this warp: a contiguous range of the row's kPc-position slices
+  const int nsub = (a.Sk + kPc - 1) / kPc;
   const int64_t gw = int64_t(blockIdx.x) * kWarps + warp, nw = int64_t(gridDim.x) * kWarps;
   const int i_begin = int(gw * nsub / nw), i_end = int((gw + 1) * nsub / nw);
   const int ncopies = (i_end - i_begin) * copies;
@@ -95,10 +103,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // copy t of this warp: sub-tile i_begin + t / copies, heads [part * 2ppc, +2ppc)
   auto issue = [&](int t, int s) {
     const uint64_t pol = l2_policy_evict_first();
-    const int i = i_begin + (copies == 2 ? (t >> 1) : t);
+    const int i = i_begin + (t >> cshift);
     const int part = t & (copies - 1);
     mbar_arrive_expect_tx(&full[s], copy_bytes);
-    tma_load_4d(ring + s * copy_bytes, &kmap, 0, i * kP, part * 2 * ppc, kb_coord, &full[s], pol);
+    tma_load_4d(ring + s * copy_bytes, &kmap, 0, i * kPc, part * 2 * ppc, kb_coord, &full[s], pol);
   };
   if (lane == 0) {
     for (int t = 0; t < kStages && t < ncopies; ++t) issue(t, t);
@@ -112,27 +120,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 8; ++i)
       inv[i] = make_float2(a.inv_freq[16 * c + 2 * i], a.inv_freq[16 * c + 2 * i + 1]);
   }
-  // B fragments, bf16 pairs: bq[hp][ks] = q[row][d], q[row][d+1] with
-  // row = B column g (h0 row g for g < 4, h1 row g-4 otherwise),
-  // d = 16c + 2ks (ks < 8) or 64 + 16c + 2(ks - 8)
-  uint32_t bq[kMaxPairs][16];
+  // B fragments: lane (g, c) of k-step ks holds rows k = c and c + 4 of column g,
+  // i.e. q[row][d] and q[row][d + 1] with row = B column g (h0 row g for g < 4, h1
+  // row g - 4 otherwise) and d = 16c + 2ks (ks < 8) or 64 + 16c + 2(ks - 8)
   {
-    const int qrow = g & 3;
     const __nv_bfloat16* qg = static_cast<const __nv_bfloat16*>(a.q);
-#pragma unroll
-    for (int hp = 0; hp < kMaxPairs; ++hp) {
-      const int h = 2 * hp + (g >> 2);
-      const bool live = hp < npairs && qrow < R;
-      const __nv_bfloat16* qr =
-          qg + int64_t(b) * a.q_sb + int64_t(h * a.G + qrow / a.sq_n) * a.q_sh +
-          int64_t(a.s0 + qrow % a.sq_n) * a.q_ss;
-#pragma unroll
-      for (int ks = 0; ks < 16; ++ks) {
-        const int d = ks < 8 ? 16 * c + 2 * ks : 64 + 16 * c + 2 * (ks - 8);
-        bq[hp][ks] = live ? *reinterpret_cast<const uint32_t*>(qr + d) : 0u;
+    for (int e = tid; e < kMaxPairs * 16 * 32; e += kThreads) {
+      const int ln = e & 31, ks = (e >> 5) & 15, hp = e >> 9;
+      const int gg = ln >> 2, cc4 = ln & 3;
+      const int qrow = gg & 3, h = 2 * hp + (gg >> 2);
+      float2 v = make_float2(0.f, 0.f);
+      if (hp < npairs && qrow < R) {
+        const __nv_bfloat16* qr = qg + int64_t(b) * a.q_sb + int64_t(h * a.G + qrow / a.sq_n) * a.q_sh +
+                                  int64_t(a.s0 + qrow % a.sq_n) * a.q_ss;
+        const int d = ks < 8 ? 16 * cc4 + 2 * ks : 64 + 16 * cc4 + 2 * (ks - 8);
+        v = make_float2(__bfloat162float(qr[d]), __bfloat162float(qr[d + 1]));
       }
+      tail->bfrag[hp][ks][ln] = v;
     }
   }
+  __syncthreads();
+  const uint32_t bfrag_lane = smem_u32(&tail->bfrag[0][0][lane]);
   // outputs of this lane: head h0 (c < 2) or h1 (c >= 2) of each pair, query
   // rows r0 = (2c) & 3 and r0 + 1
   const int r0 = (2 * c) & 3;
@@ -153,19 +161,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   int t = 0;  // copies consumed
   for (int i = i_begin; i < i_end; ++i) {
-    const int pos = i * kP + g;
-    // cos/sin of this lane's 16 pairs at its position (overlaps the copy),
-    // pre-scaled for the truncating TF32 operand
-    float2 cc[8], ss[8];
+    // cos/sin of this lane's 16 pairs at its position in each sub-tile (overlaps
+    // the copy), pre-scaled for the truncating TF32 operand
+    // (each value twice: the packed FMAs below pair the two heads of a head
+    // pair, which share the angle)
+    float2 cc[kSubs][16], ss[kSubs][16];
     if (kRope) {
-      const float pf = static_cast<float>(a.pos_offset + pos);
-      const float2 scale = make_float2(kTruncScale, kTruncScale);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        rope_sincos_fast(__fmul_rn(pf, inv[q].x), ss[q].x, cc[q].x);
-        rope_sincos_fast(__fmul_rn(pf, inv[q].y), ss[q].y, cc[q].y);
-        ss[q] = __fmul2_rn(ss[q], scale);
-        cc[q] = __fmul2_rn(cc[q], scale);
+      for (int sb = 0; sb < kSubs; ++sb) {
+        const float pf = static_cast<float>(a.pos_offset + i * kPc + sb * kP + g);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float sv, cv;
+            rope_sincos_fast(__fmul_rn(pf, e ? inv[q].y : inv[q].x), sv, cv);
+            sv *= kTruncScale;
+            cv *= kTruncScale;
+            ss[sb][2 * q + e] = make_float2(sv, sv);
+            cc[sb][2 * q + e] = make_float2(cv, cv);
+          }
+        }
       }
     }
     uint32_t st = 0;
@@ -174,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (hp >= npairs) break;
       const int slot = hp & (ppc - 1);  // pair within the current copy
       if (slot == 0) {
-        if (hp > 0) {  // release the previous copy of this sub-tile
+        if (hp > 0) {  // release the previous copy of this block
           __syncwarp();
           if (lane == 0 && t - 1 + kStages < ncopies) issue(t - 1 + kStages, (t - 1) % kStages);
         }
@@ -186,62 +202,74 @@ __global__ void __launch_bounds__(kThreads, 1)
         st = ring_u32 + s * copy_bytes + lane_off;
         ++t;
       }
-      // A rows: g -> head 2hp, g+8 -> head 2hp+1 (same position); packed bf16
-      // words: [row][0..7] dims 16c..16c+15, [row][8..15] dims 64+16c..
-      uint32_t kw[2][16];
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const uint32_t row = st + uint32_t(2 * slot + rr) * kP * kRowBytes;
-        const uint4 w0 = lds128_u32(row), w1 = lds128_u32(row + 16);
-        const uint4 w2 = lds128_u32(row + 128), w3 = lds128_u32(row + 144);
-        kw[rr][0] = w0.x; kw[rr][1] = w0.y; kw[rr][2] = w0.z; kw[rr][3] = w0.w;
-        kw[rr][4] = w1.x; kw[rr][5] = w1.y; kw[rr][6] = w1.z; kw[rr][7] = w1.w;
-        kw[rr][8] = w2.x; kw[rr][9] = w2.y; kw[rr][10] = w2.z; kw[rr][11] = w2.w;
-        kw[rr][12] = w3.x; kw[rr][13] = w3.y; kw[rr][14] = w3.z; kw[rr][15] = w3.w;
-      }
-      // pair q (dims 16c+2q, +1 and +64) feeds k-step q (lo half, acc0) and
-      // k-step 8+q (hi half, acc1)
-      float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float2 klo[2], khi[2];
+      for (int sb = 0; sb < kSubs; ++sb) {
+        const int pos = i * kPc + sb * kP + g;
+        // A rows: g -> head 2hp, g+8 -> head 2hp+1 (same position); packed bf16
+        // words: [row][0..7] dims 16c..16c+15, [row][8..15] dims 64+16c..
+        uint32_t kw[2][16];
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
-          float2 lo, hi;
-          Unpack<__nv_bfloat16>::run(kw[rr][q], lo.x, lo.y);
-          Unpack<__nv_bfloat16>::run(kw[rr][8 + q], hi.x, hi.y);
-          if (kRope) {
-            const float2 ns = make_float2(-ss[q].x, -ss[q].y);
-            klo[rr] = __ffma2_rn(hi, ss[q], __fmul2_rn(lo, cc[q]));
-            khi[rr] = __ffma2_rn(lo, ns, __fmul2_rn(hi, cc[q]));
-          } else {
-            klo[rr] = lo;
-            khi[rr] = hi;
-          }
+          const uint32_t row = st + uint32_t((2 * slot + rr) * kPc + sb * kP) * kRowBytes;
+          const uint4 w0 = lds128_u32(row), w1 = lds128_u32(row + 16);
+          const uint4 w2 = lds128_u32(row + 128), w3 = lds128_u32(row + 144);
+          kw[rr][0] = w0.x; kw[rr][1] = w0.y; kw[rr][2] = w0.z; kw[rr][3] = w0.w;
+          kw[rr][4] = w1.x; kw[rr][5] = w1.y; kw[rr][6] = w1.z; kw[rr][7] = w1.w;
+          kw[rr][8] = w2.x; kw[rr][9] = w2.y; kw[rr][10] = w2.z; kw[rr][11] = w2.w;
+          kw[rr][12] = w3.x; kw[rr][13] = w3.y; kw[rr][14] = w3.z; kw[rr][15] = w3.w;
         }
-        const uint32_t wl = bq[hp][q], wh = bq[hp][8 + q];
-        mma_tf32(acc0, __float_as_uint(klo[0].x), __float_as_uint(klo[1].x),
-                 __float_as_uint(klo[0].y), __float_as_uint(klo[1].y), wl << 16, wl & 0xffff0000u);
-        mma_tf32(acc1, __float_as_uint(khi[0].x), __float_as_uint(khi[1].x),
-                 __float_as_uint(khi[0].y), __float_as_uint(khi[1].y), wh << 16, wh & 0xffff0000u);
-      }
-      // d0,d1: (h0 key, columns 2c, 2c+1); d2,d3: (h1 key, same columns)
-      const float v0 = hsel ? acc0[2] + acc1[2] : acc0[0] + acc1[0];
-      const float v1 = hsel ? acc0[3] + acc1[3] : acc0[1] + acc1[1];
-      if (pos < a.Sk) {
-        const int64_t ro = row_base + int64_t(hp) * pair_stride;
-        if (wr0) a.scores[ro + pos] = int64_t(pos) > vis0 ? -INFINITY : v0;
-        if (wr1) a.scores[ro + row1_delta + pos] = int64_t(pos) > vis1 ? -INFINITY : v1;
+        // pair q (dims 16c+2q, +1 and +64) feeds k-step q (lo half, acc0) and
+        // k-step 8+q (hi half, acc1). Packed operands pair the two heads:
+        // x = head 2hp (A row g), y = head 2hp+1 (A row g+8), so that the
+        // rotated values land in the MMA's A registers in order
+        // (row g, row g+8) for dims 16c+2q and 16c+2q+1.
+        float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t w0 = kw[0][q], w1 = kw[1][q], u0 = kw[0][8 + q], u1 = kw[1][8 + q];
+          const float2 L0 = make_float2(__uint_as_float(w0 << 16), __uint_as_float(w1 << 16));
+          const float2 L1 = make_float2(__uint_as_float(w0 & 0xffff0000u), __uint_as_float(w1 & 0xffff0000u));
+          const float2 H0 = make_float2(__uint_as_float(u0 << 16), __uint_as_float(u1 << 16));
+          const float2 H1 = make_float2(__uint_as_float(u0 & 0xffff0000u), __uint_as_float(u1 & 0xffff0000u));
+          float2 klo0, klo1, khi0, khi1;
+          if (kRope) {
+            const float2 s0 = ss[sb][2 * q], s1 = ss[sb][2 * q + 1];
+            const float2 c0 = cc[sb][2 * q], c1 = cc[sb][2 * q + 1];
+            klo0 = __ffma2_rn(H0, s0, __fmul2_rn(L0, c0));
+            klo1 = __ffma2_rn(H1, s1, __fmul2_rn(L1, c1));
+            khi0 = __ffma2_rn(L0, make_float2(-s0.x, -s0.y), __fmul2_rn(H0, c0));
+            khi1 = __ffma2_rn(L1, make_float2(-s1.x, -s1.y), __fmul2_rn(H1, c1));
+          } else {
+            klo0 = L0;
+            klo1 = L1;
+            khi0 = H0;
+            khi1 = H1;
+          }
+          const uint2 bl = lds64_u32(bfrag_lane + uint32_t((hp * 16 + q) * 32 * 8));
+          const uint2 bh = lds64_u32(bfrag_lane + uint32_t((hp * 16 + 8 + q) * 32 * 8));
+          mma_tf32(acc0, __float_as_uint(klo0.x), __float_as_uint(klo0.y), __float_as_uint(klo1.x),
+                   __float_as_uint(klo1.y), bl.x, bl.y);
+          mma_tf32(acc1, __float_as_uint(khi0.x), __float_as_uint(khi0.y), __float_as_uint(khi1.x),
+                   __float_as_uint(khi1.y), bh.x, bh.y);
+        }
+        // d0,d1: (h0 key, columns 2c, 2c+1); d2,d3: (h1 key, same columns)
+        const float v0 = hsel ? acc0[2] + acc1[2] : acc0[0] + acc1[0];
+        const float v1 = hsel ? acc0[3] + acc1[3] : acc0[1] + acc1[1];
+        if (pos < a.Sk) {
+          const int64_t ro = row_base + int64_t(hp) * pair_stride;
+          if (wr0) a.scores[ro + pos] = int64_t(pos) > vis0 ? -INFINITY : v0;
+          if (wr1) a.scores[ro + row1_delta + pos] = int64_t(pos) > vis1 ? -INFINITY : v1;
+        }
       }
     }
-    __syncwarp();  // every lane is done with the last copy of this sub-tile
+    __syncwarp();  // every lane is done with the last copy of this block
     if (lane == 0 && t - 1 + kStages < ncopies) issue(t - 1 + kStages, (t - 1) % kStages);
   }
 }
 
 size_t hp_smem_bytes(int Hkv) {
   const int heads_per_copy = Hkv < 2 * kPairsPerCopy ? Hkv : 2 * kPairsPerCopy;
-  return size_t(kWarps) * kStages * heads_per_copy * kP * kRowBytes + sizeof(HpTail);
+  return size_t(kWarps) * kStages * heads_per_copy * kPc * kRowBytes + sizeof(HpTail);
 }
 
 template <bool kRope>
@@ -253,9 +281,9 @@ cudaError_t launch_hp(const DecodeArgs& a, int num_sms, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   CUtensorMap kmap;
   const int heads_per_copy = a.Hkv < 2 * kPairsPerCopy ? a.Hkv : 2 * kPairsPerCopy;
-  e = make_key_tensor_map(&kmap, a.k, kBF16, a.B, a.Hkv, a.Sk, a.k_sb, a.k_sh, kP, heads_per_copy);
+  e = make_key_tensor_map(&kmap, a.k, kBF16, a.B, a.Hkv, a.Sk, a.k_sb, a.k_sh, kPc, heads_per_copy);
   if (e != cudaSuccess) return e;
-  const int nsub = (a.Sk + kP - 1) / kP;
+  const int nsub = (a.Sk + kPc - 1) / kPc;
   int ctas = num_sms;
   if (a.B > 1) ctas = (num_sms + a.B - 1) / a.B;
   ctas = max(1, min(ctas, (nsub + kWarps - 1) / kWarps));
