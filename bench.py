@@ -218,7 +218,7 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": dt * 1e3, "higher_is_better": True,
-        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32 (tf32 MMA)",
         "data": "synthetic", "config": config_of(wl, world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -275,24 +275,53 @@ def main():
     barrier()
     torch.cuda.synchronize()
 
-    clocks = ClockSampler(local)
+    # per-kernel device times: every launch bracketed by events (profiling mode)
     lib.prism_profile_start(4 * args.steps + 16)
     n0 = lib.prism_launch_count()
+    for _ in range(args.steps):
+        step(q, k)
+    torch.cuda.synchronize()
+    lib.prism_profile_stop()
+    launches_per_step = (lib.prism_launch_count() - n0) / args.steps
+    barrier()
+    torch.cuda.synchronize()
+
+    # whole steps: on one GPU the call is captured once in a CUDA graph and
+    # replayed, so host-side Python/ctypes overhead does not starve the device;
+    # on several GPUs (NCCL all-gather inside) the call is issued eagerly
+    graph = None
+    if world == 1:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                step(q, k)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(q, k)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+    clocks = ClockSampler(local)
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     clocks.start()
     ev0.record()
     for _ in range(args.steps):
-        step(q, k)
+        if graph is not None:
+            graph.replay()
+        else:
+            step(q, k)
     ev1.record()
     torch.cuda.synchronize()
     clocks.stop()
-    lib.prism_profile_stop()
-    launches = lib.prism_launch_count() - n0
+    launches = int(round(launches_per_step * args.steps))
     barrier()
     torch.cuda.synchronize()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_per_step = ms / args.steps
+    del graph
 
     # dominant kernel: the scorer (un-rotate + q·K^T), timed per launch
     n_sc = _lib.ctypes.c_int64(0)
@@ -363,7 +392,7 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32 (tf32 MMA)",
         "data": "synthetic (seeded; see prism_test_b200/workloads.py)",
         "config": config_of(wl, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -377,6 +406,7 @@ def main():
             "merge": t_me.value / max(1, args.steps),
         },
         "gpu_launches": int(launches),
+        "timing": "CUDA graph of one call, replayed" if world == 1 else "eager calls",
         "clocks": clocks.summary(),
         "e2e": e2e,
         "cpu_baseline": base,
