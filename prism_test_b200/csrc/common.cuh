@@ -115,7 +115,8 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
 }
 
 // Tiled 4-D tensor copy global -> shared (TMA), completing on an mbarrier. The
-// tensor map lives in kernel parameter space (__grid_constant__). No multicast.
+// tensor map lives in kernel parameter space (__grid_constant__); the copy lands
+// only in this CTA's shared memory.
 __device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, int c0, int c1, int c2,
                                             int c3, uint64_t* bar, uint64_t policy) {
   asm volatile(
