@@ -131,8 +131,10 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
     return fail(PRISM_E_INVALID, "k base and batch/head strides must be 16-byte aligned");
   if (mode != PRISM_MODE_EXACT && mode != PRISM_MODE_BLOCKMAX)
     return fail(PRISM_E_INVALID, "unknown mode %d", mode);
-  if (mode == PRISM_MODE_BLOCKMAX)
-    return fail(PRISM_E_UNSUPPORTED, "blockmax mode is not built in this library version");
+  if (mode == PRISM_MODE_BLOCKMAX && topk != 1 && topk != 4)
+    return fail(PRISM_E_INVALID, "blockmax mode supports topk 1 or 4, got %d", topk);
+  if (mode == PRISM_MODE_BLOCKMAX && Sk % 128 != 0)
+    return fail(PRISM_E_INVALID, "blockmax mode needs Sk %% 128 == 0, got %lld", (long long)Sk);
   if (topk < 1 || int64_t(topk) > Sk)
     return fail(PRISM_E_INVALID, "topk must satisfy 1 <= topk <= Sk (topk=%d, Sk=%lld)", topk,
                 (long long)Sk);
@@ -228,6 +230,12 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
   s.out_scores = out_scores;
   s.status = status;
   void* cand_ws = ws + kStatusBytes + round_up(int64_t(scores_bytes(B * Hq * Sq, Sk)), 256);
+  if (mode == PRISM_MODE_BLOCKMAX) {
+    e = launch_counted(PRISM_KERNEL_SELECT, stream,
+                       [&] { return prism::launch_select_blockmax(s, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "blockmax select kernel launch");
+    return PRISM_OK;
+  }
   e = launch_counted(PRISM_KERNEL_SELECT, stream,
                      [&] { return prism::launch_select_topk(s, cand_ws, stream); });
   if (e != cudaSuccess) return cuda_fail(e, "select kernel launch");

@@ -71,6 +71,10 @@ int64_t select_cand_cap(int64_t n);
 size_t select_workspace_bytes(int64_t rows, int64_t n);
 cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t stream);
 
+// Block-maximum top-1 / top-4 (the reference Triton kernels' selection); a.k in
+// {1, 4}, a.n % 128 == 0.
+cudaError_t launch_select_blockmax(const SelectArgs& a, cudaStream_t stream);
+
 // Sets the message prism_last_error() returns for the calling thread.
 void set_last_error(const char* msg);
 

@@ -73,6 +73,8 @@ def _call(lib, **over):
     (dict(topk=257), _lib.PRISM_E_INVALID),
     (dict(Sk=40000, ks=(40000 * 256, 40000 * 128, 128, 1), topk=20000), _lib.PRISM_E_UNSUPPORTED),
     (dict(mode=3), _lib.PRISM_E_INVALID),
+    (dict(mode=1, topk=8), _lib.PRISM_E_INVALID),                 # blockmax: topk 1 or 4
+    (dict(mode=1, topk=4, Sk=200, ks=(200 * 256, 200 * 128, 128, 1)), _lib.PRISM_E_INVALID),  # Sk % 128
     (dict(inv=16, pos=(1 << 22) - 10), _lib.PRISM_E_UNSUPPORTED),  # RoPE positions beyond 2^22
     (dict(base=-1), _lib.PRISM_E_INVALID),
     (dict(wsb=100), _lib.PRISM_E_WORKSPACE),
