@@ -286,11 +286,11 @@ def main():
     barrier()
     torch.cuda.synchronize()
 
-    # whole steps: on one GPU the call is captured once in a CUDA graph and
-    # replayed, so host-side Python/ctypes overhead does not starve the device;
-    # on several GPUs (NCCL all-gather inside) the call is issued eagerly
+    # whole steps: the call (with its NCCL all-gather on several GPUs) is captured
+    # once in a CUDA graph and replayed, so host-side Python/ctypes overhead does
+    # not starve the device
     graph = None
-    if world == 1:
+    if True:
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
@@ -321,7 +321,8 @@ def main():
     torch.cuda.synchronize()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_per_step = ms / args.steps
-    del graph
+    del graph  # a graph holding NCCL work must go before the process group
+    torch.cuda.synchronize()
 
     # dominant kernel: the scorer (un-rotate + q·K^T), timed per launch
     n_sc = _lib.ctypes.c_int64(0)
@@ -406,7 +407,7 @@ def main():
             "merge": t_me.value / max(1, args.steps),
         },
         "gpu_launches": int(launches),
-        "timing": "CUDA graph of one call, replayed" if world == 1 else "eager calls",
+        "timing": "CUDA graph of one call, replayed",
         "clocks": clocks.summary(),
         "e2e": e2e,
         "cpu_baseline": base,

@@ -111,6 +111,23 @@ PRISM_API int prism_topk_merge(const float* cand_scores, const int32_t* cand_idx
 PRISM_API size_t prism_topk_merge_workspace_size(int64_t rows, int64_t n);
 
 /*
+ * Top-k of the union of `nruns` sorted runs, the merge of the sequence-sharded
+ * path when every rank contributes its own prism_einsum_topk result.
+ *   runs     int32 [nruns, rows, run_len, 2]: (fp32 score bits, int32 global index)
+ *            pairs, each run sorted by descending score then ascending index, as
+ *            prism_einsum_topk returns them (and as an all-gather of the ranks'
+ *            packed results lays them out). Indices must be distinct across runs.
+ *   1 <= nruns <= 16, 1 <= topk <= run_len, topk <= 16384.
+ *   out_idx / out_scores [rows, topk] as prism_topk_merge.
+ * No workspace. Replaces the same reference merge as prism_topk_merge
+ * (bitonic_merge_wrapper.py:36-52, torch.topk over the union, reattention.py:497)
+ * for inputs that are already sorted runs.
+ */
+PRISM_API int prism_topk_merge_runs(const int32_t* runs, int32_t nruns, int64_t rows,
+                                    int64_t run_len, int32_t topk, int32_t* out_idx,
+                                    float* out_scores, void* stream);
+
+/*
  * prism_topk_merge without a workspace, for callers that cannot allocate device
  * memory (no cudaMalloc / cudaFree / allocating library call anywhere in the
  * call). It has no counterpart in the reference. Same arguments, kernel and

@@ -45,6 +45,9 @@ SIGNATURES = {
         _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i32, _vp, _vp, _vp, ctypes.c_size_t, _vp,
     ]),
     "prism_topk_merge_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64]),
+    "prism_topk_merge_runs": (ctypes.c_int, [
+        _vp, _c_i32, _c_i64, _c_i64, _c_i32, _vp, _vp, _vp,
+    ]),
     "prism_topk_merge_noalloc": (ctypes.c_int, [
         _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i32, _vp, _vp, _vp,
     ]),

@@ -282,6 +282,25 @@ int prism_topk_merge(const float* cand_scores, const int32_t* cand_idx, int64_t 
   return PRISM_OK;
 }
 
+int prism_topk_merge_runs(const int32_t* runs, int32_t nruns, int64_t rows, int64_t run_len,
+                          int32_t topk, int32_t* out_idx, float* out_scores, void* stream_ptr) {
+  g_last_error.clear();
+  if (!runs || !out_idx) return fail(PRISM_E_INVALID, "null pointer argument");
+  if (nruns < 1 || nruns > 16) return fail(PRISM_E_UNSUPPORTED, "1 to 16 runs are supported, got %d", nruns);
+  if (rows < 0 || run_len < 1) return fail(PRISM_E_INVALID, "need rows >= 0 and run_len >= 1");
+  if (topk < 1 || int64_t(topk) > run_len)
+    return fail(PRISM_E_INVALID, "topk must satisfy 1 <= topk <= run_len");
+  if (topk > prism::kSelectMaxK)
+    return fail(PRISM_E_UNSUPPORTED, "topk above %d is not supported", prism::kSelectMaxK);
+  if (reinterpret_cast<uintptr_t>(runs) & 7u) return fail(PRISM_E_INVALID, "runs must be 8-byte aligned");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  cudaError_t e = launch_counted(PRISM_KERNEL_MERGE, stream, [&] {
+    return prism::launch_merge_runs(runs, nruns, rows, run_len, topk, out_idx, out_scores, stream);
+  });
+  if (e != cudaSuccess) return cuda_fail(e, "run merge kernel launch");
+  return PRISM_OK;
+}
+
 int prism_profile_start(int32_t capacity) {
   g_last_error.clear();
   if (capacity < 0) return fail(PRISM_E_INVALID, "capacity must be >= 0");

@@ -71,6 +71,11 @@ int64_t select_cand_cap(int64_t n);
 size_t select_workspace_bytes(int64_t rows, int64_t n);
 cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t stream);
 
+// Top-k of the union of nruns sorted runs [nruns, rows, run_len, 2] of (fp32
+// score bits, int32 index) pairs, run_len >= k, k <= 16384.
+cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int64_t run_len, int k,
+                              int32_t* out_idx, float* out_scores, cudaStream_t stream);
+
 // Block-maximum top-1 / top-4 (the reference Triton kernels' selection); a.k in
 // {1, 4}, a.n % 128 == 0.
 cudaError_t launch_select_blockmax(const SelectArgs& a, cudaStream_t stream);

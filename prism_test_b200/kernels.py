@@ -187,3 +187,28 @@ def topk_merge(cand_scores: torch.Tensor, cand_idx: torch.Tensor, topk: int,
         )
         _lib.check(rc, "prism_topk_merge")
     return (out_idx, out_scores) if return_scores else out_idx
+
+
+def topk_merge_runs(runs: torch.Tensor, topk: int, return_scores: bool = True):
+    """Top-k of the union of sorted runs.
+
+    ``runs`` int32 ``[nruns, rows, run_len, 2]`` of (fp32 score bits, global index)
+    pairs, each run sorted like ``einsum_topk_func`` output (descending score, then
+    ascending index) — the layout of an all-gather of the ranks' packed results.
+    Returns int32 indices ``[rows, topk]`` (and fp32 scores).
+    """
+    assert runs.dtype == torch.int32 and runs.dim() == 4 and runs.shape[-1] == 2
+    assert runs.is_cuda
+    nruns, rows, run_len, _ = runs.shape
+    assert 1 <= topk <= run_len
+    runs = runs.contiguous()
+    lib = _lib.load()
+    with torch.cuda.device(runs.device):
+        out_idx = torch.empty((rows, topk), dtype=torch.int32, device=runs.device)
+        out_scores = torch.empty((rows, topk), dtype=torch.float32, device=runs.device)
+        rc = lib.prism_topk_merge_runs(
+            runs.data_ptr(), nruns, rows, run_len, int(topk), out_idx.data_ptr(),
+            out_scores.data_ptr(), torch.cuda.current_stream(runs.device).cuda_stream,
+        )
+        _lib.check(rc, "prism_topk_merge_runs")
+    return (out_idx, out_scores) if return_scores else out_idx

@@ -9,8 +9,9 @@ contiguous key slice ``[r*Sk/N, (r+1)*Sk/N)`` of every KV head and:
    global), with fp32 scores;
 2. packs ``(score bits, global index)`` as int32 pairs ``[rows, topk, 2]`` and
    all-gathers them (one NCCL collective over NVLink);
-3. merges the N sorted runs per row on the device (``topk_merge``): the global
-   top-k is always contained in the union of the local top-k lists.
+3. merges the N sorted runs per row on the device (``topk_merge_runs``, reading
+   the gathered buffer in place): the global top-k is always contained in the
+   union of the local top-k lists.
 
 Every rank ends with the global result, equal to ``torch.topk`` over the whole
 sequence (``ReAttentionMethod._dense_topk``, reattention.py:486-498), ties
@@ -23,7 +24,7 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-from .kernels import einsum_topk_func, topk_merge
+from .kernels import einsum_topk_func, topk_merge_runs
 
 
 def shard_bounds(Sk_total: int, rank: int, world: int):
@@ -73,7 +74,6 @@ def sharded_einsum_topk(
     CPU implementations to run the exchange over gloo.
     """
     local_topk = local_topk or einsum_topk_func
-    merge = merge or (lambda s, i, kk: topk_merge(s, i, kk))
     world = dist.get_world_size(group)
     B, Hq, Sq, _ = q.shape
     rows = B * Hq * Sq
@@ -86,11 +86,14 @@ def sharded_einsum_topk(
     if kl < topk:  # a shard shorter than k contributes -inf padding
         packed[:, kl:, 0] = torch.tensor(float("-inf"), dtype=torch.float32).view(torch.int32).item()
         packed[:, kl:, 1] = torch.iinfo(torch.int32).max
-    gathered = _all_gather(packed, world, group)  # [world, rows, topk, 2]
-    cand = gathered.permute(1, 0, 2, 3).reshape(rows, world * topk, 2)
-    cand_s = cand[..., 0].contiguous().view(torch.float32)
-    cand_i = cand[..., 1].contiguous()
-    out_i, out_s = merge(cand_s, cand_i, topk)
+    gathered = _all_gather(packed, world, group)  # [world, rows, topk, 2]: sorted runs
+    if merge is None:
+        out_i, out_s = topk_merge_runs(gathered, topk)
+    else:
+        cand = gathered.permute(1, 0, 2, 3).reshape(rows, world * topk, 2)
+        cand_s = cand[..., 0].contiguous().view(torch.float32)
+        cand_i = cand[..., 1].contiguous()
+        out_i, out_s = merge(cand_s, cand_i, topk)
     out_i = out_i.reshape(B, Hq, Sq, topk)
     if return_scores:
         return out_i, out_s.reshape(B, Hq, Sq, topk)

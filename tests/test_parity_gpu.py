@@ -216,3 +216,33 @@ def test_topk_merge_large_rows(cuda_device):
     rv, rp = s.topk(8192, dim=-1)
     assert torch.equal(os_, rv)
     assert torch.equal(oi, torch.gather(i, 1, rp))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("nruns,run_len,topk", [(2, 8192, 8192), (8, 8192, 8192), (4, 1000, 300), (3, 5000, 5000)])
+def test_topk_merge_runs_matches_torch(cuda_device, nruns, run_len, topk):
+    # sorted runs with distinct global indices, as the sharded path gathers them;
+    # one run holds a block of much larger scores (a skewed shard)
+    from prism_test_b200 import topk_merge_runs
+    rows = 6
+    g = torch.Generator().manual_seed(nruns * 131 + run_len)
+    s = torch.randn(nruns, rows, run_len, generator=g)
+    s[0, :, : run_len // 3] += 4.0
+    perm = torch.randperm(nruns * run_len * 4, generator=g)[: nruns * run_len].view(nruns, 1, run_len)
+    idx = perm.expand(nruns, rows, run_len).to(torch.int32)
+    # sort each run by (score desc, index asc)
+    order = torch.argsort(idx.long(), dim=-1, stable=True)
+    s = torch.gather(s, -1, order)
+    idx = torch.gather(idx, -1, order)
+    v, p = torch.sort(s, dim=-1, descending=True, stable=True)
+    idx = torch.gather(idx, -1, p)
+    runs = torch.stack([v.view(torch.int32), idx], dim=-1).to(cuda_device)
+    oi, os_ = topk_merge_runs(runs, topk)
+    flat_s = v.permute(1, 0, 2).reshape(rows, -1)
+    flat_i = idx.permute(1, 0, 2).reshape(rows, -1)
+    o2 = torch.argsort(flat_i.long(), dim=-1, stable=True)
+    fs, fi = torch.gather(flat_s, -1, o2), torch.gather(flat_i, -1, o2)
+    ws, wp = torch.sort(fs, dim=-1, descending=True, stable=True)
+    wi = torch.gather(fi, -1, wp)
+    assert torch.equal(os_.cpu(), ws[:, :topk])
+    assert torch.equal(oi.cpu(), wi[:, :topk])
