@@ -190,7 +190,8 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
   a.ntiles = int((Sk + 127) / 128);
   a.status = status;
   // specialised kernels take every query row of a KV head in one launch:
-  // tensor-core tiles for <= 16 rows per KV head, CUDA cores for <= 4
+  // tensor-core tiles (keys as M for <= 16 rows per KV head, queries as M up
+  // to 256 / Hkv rows), CUDA cores for <= 4
   if (prism::decode_hp_supported(a, dtype)) {
     e = launch_counted(PRISM_KERNEL_SCORE, stream,
                        [&] { return prism::launch_decode_scores_hp(a, nsm, stream); });
@@ -198,6 +199,10 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
   } else if (prism::decode_mma_supported(a)) {
     e = launch_counted(PRISM_KERNEL_SCORE, stream,
                        [&] { return prism::launch_decode_scores_mma(a, dtype, nsm, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
+  } else if (prism::decode_wide_supported(a)) {
+    e = launch_counted(PRISM_KERNEL_SCORE, stream,
+                       [&] { return prism::launch_decode_scores_wide(a, dtype, nsm, stream); });
     if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
   } else if (prism::decode_g4_supported(a)) {
     e = launch_counted(PRISM_KERNEL_SCORE, stream,

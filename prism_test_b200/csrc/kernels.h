@@ -45,6 +45,12 @@ bool decode_mma_supported(const DecodeArgs& a);
 cudaError_t launch_decode_scores_mma(const DecodeArgs& a, int dtype, int num_sms,
                                      cudaStream_t stream);
 
+// Tensor-core path with the query rows as the MMA's M dimension: up to
+// 256 / Hkv rows per KV head, Hkv in {2, 4, 8}.
+bool decode_wide_supported(const DecodeArgs& a);
+cudaError_t launch_decode_scores_wide(const DecodeArgs& a, int dtype, int num_sms,
+                                      cudaStream_t stream);
+
 // CUDA-core path for <= 4 query rows per KV head, Hkv in {1, 2, 4, 8, 16}.
 bool decode_g4_supported(const DecodeArgs& a);
 cudaError_t launch_decode_scores_g4(const DecodeArgs& a, int dtype, int num_sms,

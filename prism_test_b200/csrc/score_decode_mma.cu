@@ -188,15 +188,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     const int s = it % kStages;
-    if (tid == 0) {
-      if (t + kStages - 1 < t_end) issue(t + kStages - 1, (it + kStages - 1) % kStages);
-      if (!mbar_wait_bounded(&tail->full[s], (it / kStages) & 1)) {
-        set_status(a.status, kStatusTimeout);
-        tail->abort = 1;
-      }
+    if (tid == 0 && !mbar_wait_bounded(&tail->full[s], (it / kStages) & 1)) {
+      set_status(a.status, kStatusTimeout);
+      tail->abort = 1;
     }
     __syncthreads();  // tile t's keys and cos/sin are ready; tile t-1 is retired
     if (tail->abort) return;
+    // refill the stage every warp finished with in the previous iteration
+    if (tid == 0 && t + kStages - 1 < t_end) issue(t + kStages - 1, (it + kStages - 1) % kStages);
 
     // rotated keys: kr[key][k-step] as (slot c, slot c+4) pairs
     float2 kr[2][16];

@@ -59,6 +59,11 @@ CASES = [
     (1, 32, 8, 9, 700, 64, True, torch.bfloat16),     # Hq*Sq > 128 -> query chunking
     (3, 12, 3, 1, 4099, 16384 // 8, True, torch.bfloat16),
     (1, 16, 4, 1, 20000, 16384, True, torch.bfloat16),  # largest supported k
+    # many query rows per KV head: the queries-as-M tensor-core scorer
+    (1, 16, 2, 8, 3001, 300, True, torch.bfloat16),    # 64 rows per KV head, Hkv 2
+    (1, 32, 8, 5, 2500, 200, True, torch.float16),     # 20 rows per KV head, fp16
+    (1, 32, 8, 8, 2500, 200, False, torch.bfloat16),   # 32 rows per KV head, Hkv 8, raw keys
+    (2, 28, 4, 6, 1777, 50, True, torch.float16),      # 42 rows, ragged n-tiles, B = 2
 ]
 
 
@@ -246,3 +251,14 @@ def test_topk_merge_runs_matches_torch(cuda_device, nruns, run_len, topk):
     wi = torch.gather(fi, -1, wp)
     assert torch.equal(os_.cpu(), ws[:, :topk])
     assert torch.equal(oi.cpu(), wi[:, :topk])
+
+
+@pytest.mark.gpu
+def test_wide_rows_causal(cuda_device):
+    # 56 rows per KV head (8 queries x 7 heads) with a causal mask
+    g = torch.Generator(device=cuda_device).manual_seed(77)
+    q = torch.randn(1, 28, 8, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    k = torch.randn(1, 4, 4000, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    inv = W.rope_inv_freq(128, 1e6).to(cuda_device)
+    idx, sc = einsum_topk_func(q, k, 400, inv_freq=inv, causal_offset=3990, return_scores=True)
+    check_parity(idx, sc, q, k, 400, inv, 0, 3990)
