@@ -33,6 +33,9 @@ constexpr int kCluster = 4;
 constexpr int kBins = 4096;        // 12-bit radix digit histogram
 constexpr int kFineBins = 8192;    // counting-sort bins of the fast path
 constexpr int kCap = kSelectMaxK;  // 16384 sorted entries (128 KB)
+// From this many rows on, one CTA per row (enough rows to fill the SMs) beats a
+// 4-CTA cluster per row, whose grid would take several waves.
+constexpr int64_t kRowKernelMinRows = 64;
 
 struct SelectSmem {
   uint64_t buf[kCap];     // candidates (leader) / private level histograms / general path
@@ -394,7 +397,8 @@ __device__ __forceinline__ uint32_t sampled_columns(int64_t n) {
 // stores the whole bins that cover output positions [r*P, (r+1)*P), P = ceil(k/4).
 // A straddling bin is ranked by both neighbours, which store identical values.
 __device__ void replicated_sort_store(const SelectArgs& a, int64_t row, SelectSmem& sm,
-                                      uint32_t nc, uint32_t thr, uint32_t kmax, unsigned rank) {
+                                      uint32_t nc, uint32_t thr, uint32_t kmax, unsigned rank,
+                                      unsigned nparts = kCluster) {
   const int tid = threadIdx.x, lane = tid & 31;
   const uint32_t range = kmax - thr;
   int shift = 0;
@@ -434,7 +438,7 @@ __device__ void replicated_sort_store(const SelectArgs& a, int64_t row, SelectSm
   }
   __syncthreads();  // hist[f] is now the end of bin f
   const uint32_t kk = uint32_t(a.k);
-  const uint32_t P = (kk + kCluster - 1) / kCluster;
+  const uint32_t P = (kk + nparts - 1) / nparts;
   const uint32_t p0 = rank * P, p1 = min(kk, p0 + P);
   if (p0 >= p1) return;
   const uint32_t f0 = bin_of_position(sm, p0), f1 = bin_of_position(sm, p1 - 1);
@@ -808,6 +812,130 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   }
 }
 
+// One CTA per row, no cluster, for many rows: the threshold comes from a 1/16
+// sample (8 consecutive columns of every 128, at a hashed offset; same rank rule
+// as the cluster fast path),
+// one streaming pass appends the keys >= T to shared memory, and the CTA
+// counting-sorts and stores them. Rows where the sample misses (fewer than k or
+// more than kCap candidates) take the general one-block path.
+__global__ void __launch_bounds__(kThreads, 1) select_topk_row_kernel(const SelectArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const float* sc = a.scores + row * a.ld;
+  const int32_t* ix = a.idx_in ? a.idx_in + row * a.ld : nullptr;
+  uint32_t* priv = reinterpret_cast<uint32_t*>(sm.buf);
+  uint32_t* my_samp = priv + (lane & (kSampleCopies - 1)) * kSampleStride;
+
+  for (int i = tid; i < kSampleCopies * kSampleStride; i += kThreads) priv[i] = 0u;
+  if (tid == 0) {
+    sm.kmax = 0;
+    sm.woff = 0;
+    sm.big = 0;
+  }
+  __syncthreads();
+  grid_dependency_wait();
+
+  // ---- sample: 8 consecutive columns of every 128, at a hashed offset ----------------
+  const int64_t ngroups = (a.n + 127) / 128;
+  uint32_t ns = 0;
+  for (int64_t g0 = 0; g0 < ngroups; g0 += int64_t(kThreads) * 4) {
+    float4 v[4][2];
+    int64_t e[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t g = g0 + int64_t(u) * kThreads + tid;
+      e[u] = g * 128 + 8 * int64_t((uint32_t(g) * 0x9E3779B1u) >> 28);
+      const bool full = g < ngroups && e[u] + 8 <= a.n;
+      v[u][0] = full ? *reinterpret_cast<const float4*>(sc + e[u]) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[u][1] = full ? *reinterpret_cast<const float4*>(sc + e[u] + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!full) e[u] = g < ngroups ? -e[u] - 1 : INT64_MIN;  // partial or absent group
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (e[u] == INT64_MIN) continue;
+      const bool full = e[u] >= 0;
+      const int64_t eb = full ? e[u] : -e[u] - 1;
+      const float f[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w,
+                          v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+#pragma unroll
+      for (int x = 0; x < 8; ++x) {
+        if (eb + x >= a.n) continue;
+        const uint32_t key = float_to_okey(full ? f[x] : sc[eb + x]);
+        atomicAdd(&my_samp[key >> 20], 1u);
+        ++ns;
+      }
+    }
+  }
+  ns = __reduce_add_sync(0xffffffffu, ns);
+  if (lane == 0) atomicAdd(&sm.woff, ns);  // sample count (woff is reset below)
+  __syncthreads();
+  for (int i = tid; i < kSampleBins; i += kThreads) {
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int q = 0; q < kSampleCopies; ++q) cnt += priv[q * kSampleStride + i];
+    sm.hist[i] = cnt;
+  }
+  __syncthreads();
+  const double nsd = double(sm.woff);
+  const double expect = double(a.k) * nsd / double(a.n);
+  const double m = expect * 1.1 + 4.0 * sqrt(expect) + 8.0;
+  uint32_t thr = 1u;  // every key
+  if (m < nsd) {
+    find_bin(sm, kSampleBins, uint32_t(m));
+    thr = sm.bin << 20;
+  }
+  __syncthreads();
+  if (tid == 0) sm.woff = 0;
+  __syncthreads();
+
+  // ---- one pass: append keys >= thr ------------------------------------------------------
+  uint32_t kmx = 0;
+  for (int64_t base = 0; base < a.n; base += int64_t(kThreads) * kKeys) {
+    uint32_t kv[kKeys];
+    load_keys(sc, base, a.n, kv);
+    uint32_t hit = 0;
+#pragma unroll
+    for (int j = 0; j < kKeys; ++j) {
+      kmx = max(kmx, kv[j]);
+      if (kv[j] >= thr) hit |= 1u << j;
+    }
+    const uint32_t mine = __popc(hit);
+    uint32_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
+    uint32_t wbase = 0;
+    if (lane == 31 && wtot) wbase = atomicAdd(&sm.woff, wtot);
+    uint32_t slot = __shfl_sync(0xffffffffu, wbase, 31) + incl - mine;
+#pragma unroll
+    for (int j = 0; j < kKeys; ++j) {
+      if (hit & (1u << j)) {
+        if (slot < uint32_t(kCap)) {
+          const int64_t col = key_column(base, j);
+          sm.buf[slot] = pack_cand(kv[j], ix ? uint32_t(ix[col]) : uint32_t(col));
+        }
+        ++slot;
+      }
+    }
+  }
+  kmx = __reduce_max_sync(0xffffffffu, kmx);
+  if (lane == 0) atomicMax(&sm.kmax, kmx);
+  __syncthreads();
+  const uint32_t total = sm.woff;
+  if (total < uint32_t(a.k) || total > uint32_t(kCap)) {
+    select_row_general(a, row, sm);
+    return;
+  }
+  for (int i = tid; i < kFineBins; i += kThreads) sm.hist[i] = 0u;
+  __syncthreads();
+  replicated_sort_store(a, row, sm, total, thr, sm.kmax, 0, 1);
+}
+
 __global__ void __launch_bounds__(kThreads, 1) select_topk_general_kernel(const SelectArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
@@ -833,6 +961,13 @@ cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t 
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
     select_topk_general_kernel<<<dim3(unsigned(a.rows)), kThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+  }
+  if (a.rows >= kRowKernelMinRows) {
+    cudaError_t e = cudaFuncSetAttribute(select_topk_row_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    select_topk_row_kernel<<<dim3(unsigned(a.rows)), kThreads, smem, stream>>>(a);
     return cudaGetLastError();
   }
   const bool resident = a.n <= kPass;
