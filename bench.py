@@ -307,6 +307,10 @@ def main():
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     clocks.start()
+    # every rank enters the timed region together (the sampler start is host work)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
     ev0.record()
     for _ in range(args.steps):
         if graph is not None:

@@ -113,10 +113,11 @@ PRISM_API size_t prism_topk_merge_workspace_size(int64_t rows, int64_t n);
 /*
  * Top-k of the union of `nruns` sorted runs, the merge of the sequence-sharded
  * path when every rank contributes its own prism_einsum_topk result.
- *   runs     int32 [nruns, rows, run_len, 2]: (fp32 score bits, int32 global index)
- *            pairs, each run sorted by descending score then ascending index, as
- *            prism_einsum_topk returns them (and as an all-gather of the ranks'
- *            packed results lays them out). Indices must be distinct across runs.
+ *   runs     int32 [nruns, 2, rows, run_len]: per run a plane of fp32 score bits
+ *            and a plane of int32 global indices, each row sorted by descending
+ *            score then ascending index, as prism_einsum_topk returns them (an
+ *            all-gather of the ranks' [out_scores; out_idx] buffers lays them
+ *            out so). Indices must be distinct across runs.
  *   1 <= nruns <= 16, 1 <= topk <= run_len, topk <= 16384.
  *   out_idx / out_scores [rows, topk] as prism_topk_merge.
  * No workspace. Replaces the same reference merge as prism_topk_merge

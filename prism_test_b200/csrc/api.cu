@@ -297,7 +297,7 @@ int prism_topk_merge_runs(const int32_t* runs, int32_t nruns, int64_t rows, int6
     return fail(PRISM_E_INVALID, "topk must satisfy 1 <= topk <= run_len");
   if (topk > prism::kSelectMaxK)
     return fail(PRISM_E_UNSUPPORTED, "topk above %d is not supported", prism::kSelectMaxK);
-  if (reinterpret_cast<uintptr_t>(runs) & 7u) return fail(PRISM_E_INVALID, "runs must be 8-byte aligned");
+  if (reinterpret_cast<uintptr_t>(runs) & 3u) return fail(PRISM_E_INVALID, "runs must be 4-byte aligned");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   cudaError_t e = launch_counted(PRISM_KERNEL_MERGE, stream, [&] {
     return prism::launch_merge_runs(runs, nruns, rows, run_len, topk, out_idx, out_scores, stream);

@@ -49,6 +49,8 @@ struct SelectSmem {
   uint32_t woff;          // candidate slots taken inside this CTA's range
   uint32_t thr, cbase;    // sampled threshold; this CTA's first slot (fast path)
   uint32_t count;         // candidates of the row (the leader's slot counter, fast path)
+  uint32_t rlen[17], roff[17];  // run merge: prefix length and staging offset of each run
+  unsigned long long rthr;      // run merge: threshold candidate
   uint32_t big;           // largest fine bin
   int ncand;
 };
@@ -936,6 +938,158 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_row_kernel(const Sele
   replicated_sort_store(a, row, sm, total, thr, sm.kmax, 0, 1);
 }
 
+// ---- top-k of the union of sorted runs (the sharded path's merge) --------------------
+// Runs are int32 [nruns, 2, rows, run_len]: per run a plane of fp32 score bits and a
+// plane of global indices, each row sorted by descending score then ascending
+// index (what every rank's prism_einsum_topk returns). Candidates are compared as
+// (key << 32) | ~index. A summary of every run — its entries at positions s-1,
+// 2s-1, ... with s = max(1, k / 128) — bounds from below how many of its entries
+// are at or above a value (s per summary entry at or above it). The threshold T is
+// the largest summary entry whose bound, summed over the runs, reaches k: the
+// global k-th candidate is at or above T, and fewer than k + (N + 1) s candidates
+// are, however the top keys are split over the runs. Those prefixes are staged in
+// shared memory and counting-sorted exactly like the selection's candidates. If
+// ties at T make the prefixes exceed 16384 entries, each candidate is ranked by
+// binary searches in the other runs in global memory instead (slow, same result).
+constexpr int kMergeMaxRuns = 16;
+constexpr int kMergeSumm = 128;
+
+__device__ __forceinline__ uint64_t run_cand(const int32_t* runs, int r, int64_t rows, int64_t row,
+                                             int64_t run_len, int64_t j) {
+  const int32_t* s = runs + ((int64_t(r) * 2) * rows + row) * run_len + j;
+  return (uint64_t(float_to_okey(__int_as_float(s[0]))) << 32) | uint64_t(~uint32_t(s[rows * run_len]));
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    merge_runs_kernel(const int32_t* __restrict__ runs, int nruns, int64_t rows, int64_t run_len,
+                      int k, int32_t* __restrict__ out_idx, float* __restrict__ out_scores) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  auto cand_at = [&](int r, int64_t j) { return run_cand(runs, r, rows, row, run_len, j); };
+  uint64_t* summ = reinterpret_cast<uint64_t*>(sm.hist);  // [nruns][kMergeSumm]
+
+  // ---- threshold from the run summaries ----------------------------------------------------
+  const int64_t sstep = k / kMergeSumm > 1 ? k / kMergeSumm : 1;
+  const int nsum = int(run_len / sstep < kMergeSumm ? run_len / sstep : kMergeSumm);
+  if (tid == 0) {
+    sm.rthr = 0;
+    sm.kmax = 0;
+  }
+  for (int e = tid; e < nruns * nsum; e += kThreads) {
+    const int r = e / nsum, i = e - r * nsum;
+    summ[r * kMergeSumm + i] = cand_at(r, (int64_t(i) + 1) * sstep - 1);
+  }
+  __syncthreads();
+  for (int e = tid; e < nruns * nsum; e += kThreads) {
+    const uint64_t v = summ[(e / nsum) * kMergeSumm + e % nsum];
+    int64_t c = 0;
+    for (int q = 0; q < nruns; ++q) {
+      const uint64_t* sq = summ + q * kMergeSumm;
+      int lo = 0, hi = nsum;  // summary entries of run q at or above v
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (sq[mid] >= v) lo = mid + 1;
+        else hi = mid;
+      }
+      c += lo;
+    }
+    if (c * sstep >= int64_t(k)) atomicMax(&sm.rthr, (unsigned long long)v);
+  }
+  __syncthreads();
+  if (sm.rthr == 0 && warp == 0) {  // no summary reaches k: the largest last candidate
+    uint64_t t = 0;
+    if (lane < nruns) t = cand_at(lane, run_len - 1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t u = __shfl_xor_sync(0xffffffffu, t, o);
+      t = u > t ? u : t;
+    }
+    if (lane == 0) sm.rthr = t;
+  }
+  __syncthreads();
+  const uint64_t thr = sm.rthr;
+  // prefix of each run at or above T: warp r narrows the boundary 32-fold per step
+  if (warp < nruns) {
+    int64_t lo = 0, hi = run_len;  // entries [0, lo) are >= T, entries [hi, run_len) are < T
+    while (lo < hi) {
+      const int64_t step = (hi - lo + 31) / 32;
+      const int64_t p = lo + int64_t(lane) * step;
+      const bool ge = p < hi && cand_at(warp, p) >= thr;
+      const int c = __popc(__ballot_sync(0xffffffffu, ge));  // passing probes: lanes 0 .. c-1
+      if (c == 0) break;
+      const int64_t nhi = lo + int64_t(c) * step;
+      lo = lo + int64_t(c - 1) * step + 1;
+      hi = nhi < hi ? nhi : hi;
+    }
+    if (lane == 0) sm.rlen[warp] = uint32_t(lo);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t acc = 0;
+    for (int r = 0; r < nruns; ++r) {
+      sm.roff[r] = acc;
+      acc += sm.rlen[r];
+    }
+    sm.roff[nruns] = acc;
+  }
+  __syncthreads();
+  const uint32_t total = sm.roff[nruns];
+
+  if (total > uint32_t(kCap)) {
+    // rank every prefix candidate against the other runs in global memory
+    int32_t* oi = out_idx + row * k;
+    float* os = out_scores ? out_scores + row * k : nullptr;
+    for (uint32_t e = tid; e < total; e += kThreads) {
+      int r = 0;
+      while (e >= sm.roff[r + 1]) ++r;
+      const uint32_t j = e - sm.roff[r];
+      const uint64_t x = cand_at(r, j);
+      uint32_t p = j;
+      for (int q = 0; q < nruns; ++q) {
+        if (q == r) continue;
+        uint32_t lo = 0, hi = sm.rlen[q];  // entries of run q ahead of x (ties: lower run first)
+        while (lo < hi) {
+          const uint32_t mid = (lo + hi) >> 1;
+          const uint64_t v = cand_at(q, mid);
+          if (v > x || (q < r && v == x)) lo = mid + 1;
+          else hi = mid;
+        }
+        p += lo;
+      }
+      if (p < uint32_t(k)) {
+        oi[p] = int32_t(~uint32_t(x));
+        if (os) os[p] = okey_to_float(uint32_t(x >> 32));
+      }
+    }
+    return;
+  }
+  uint32_t kmx = 0;
+  for (int r = 0; r < nruns; ++r) {
+    const uint32_t o = sm.roff[r], n = sm.rlen[r];
+    for (uint32_t j = tid; j < n; j += kThreads) {
+      const uint64_t v = cand_at(r, j);
+      sm.buf[o + j] = v;
+      kmx = max(kmx, uint32_t(v >> 32));
+    }
+  }
+  kmx = __reduce_max_sync(0xffffffffu, kmx);
+  if (lane == 0) atomicMax(&sm.kmax, kmx);
+  __syncthreads();  // the summaries in hist are no longer needed
+  for (int i = tid; i < kFineBins; i += kThreads) sm.hist[i] = 0u;
+  if (tid == 0) sm.big = 0;
+  __syncthreads();
+  SelectArgs a{};
+  a.idx_in = runs;  // indices are the runs' own (no index_base)
+  a.rows = rows;
+  a.n = run_len;
+  a.k = k;
+  a.out_idx = out_idx;
+  a.out_scores = out_scores;
+  replicated_sort_store(a, row, sm, total, uint32_t(thr >> 32), sm.kmax, 0, 1);
+}
+
 __global__ void __launch_bounds__(kThreads, 1) select_topk_general_kernel(const SelectArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
@@ -951,6 +1105,19 @@ int64_t select_cand_cap(int64_t n) {
 
 size_t select_workspace_bytes(int64_t rows, int64_t n) {
   return size_t(rows) * size_t(select_cand_cap(n)) * sizeof(uint64_t);
+}
+
+cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int64_t run_len, int k,
+                              int32_t* out_idx, float* out_scores, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  if (nruns < 1 || nruns > kMergeMaxRuns) return cudaErrorInvalidValue;
+  const size_t smem = sizeof(SelectSmem);
+  cudaError_t e = cudaFuncSetAttribute(merge_runs_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  merge_runs_kernel<<<dim3(unsigned(rows)), kThreads, smem, stream>>>(runs, nruns, rows, run_len, k,
+                                                                      out_idx, out_scores);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t stream) {

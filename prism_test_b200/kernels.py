@@ -64,6 +64,7 @@ def einsum_topk_func(
     index_base: int = 0,
     return_scores: bool = False,
     mode: str = "exact",
+    out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
 ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """Fused (un-rotate +) q·K^T + top-k on the GPU.
 
@@ -78,6 +79,10 @@ def einsum_topk_func(
     indices : int32 Tensor [batch, num_heads, seqlen_q, topk], sorted by
         descending score (and ``scores`` fp32 of the same shape when
         ``return_scores``).
+
+    ``out=(indices, scores)`` writes into caller tensors instead (contiguous,
+    int32 and fp32, ``batch * num_heads * seqlen_q * topk`` elements each) and
+    returns them.
     """
     batch, num_heads, seqlen_q, d = q.shape
     batch_k, num_heads_k, seqlen_k, dk = k.shape
@@ -117,11 +122,19 @@ def einsum_topk_func(
         causal = -1 if causal_offset is None else int(causal_offset)
         assert causal_offset is None or causal >= 0, "causal_offset must be >= 0"
 
-        out_idx = torch.empty((batch, num_heads, seqlen_q, topk), dtype=torch.int32, device=q.device)
-        out_scores = (
-            torch.empty((batch, num_heads, seqlen_q, topk), dtype=torch.float32, device=q.device)
-            if return_scores else None
-        )
+        if out is not None:
+            out_idx, out_scores = out
+            n_out = batch * num_heads * seqlen_q * topk
+            assert out_idx.dtype == torch.int32 and out_idx.is_contiguous() and out_idx.numel() == n_out
+            assert out_scores.dtype == torch.float32 and out_scores.is_contiguous() and out_scores.numel() == n_out
+            assert out_idx.device == q.device and out_scores.device == q.device
+            return_scores = True
+        else:
+            out_idx = torch.empty((batch, num_heads, seqlen_q, topk), dtype=torch.int32, device=q.device)
+            out_scores = (
+                torch.empty((batch, num_heads, seqlen_q, topk), dtype=torch.float32, device=q.device)
+                if return_scores else None
+            )
         ws_bytes = lib.prism_einsum_topk_workspace_size(batch, num_heads, seqlen_q, seqlen_k, topk, mode_code)
         ws = torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=q.device)
         stream = torch.cuda.current_stream(q.device).cuda_stream
@@ -192,14 +205,15 @@ def topk_merge(cand_scores: torch.Tensor, cand_idx: torch.Tensor, topk: int,
 def topk_merge_runs(runs: torch.Tensor, topk: int, return_scores: bool = True):
     """Top-k of the union of sorted runs.
 
-    ``runs`` int32 ``[nruns, rows, run_len, 2]`` of (fp32 score bits, global index)
-    pairs, each run sorted like ``einsum_topk_func`` output (descending score, then
-    ascending index) — the layout of an all-gather of the ranks' packed results.
-    Returns int32 indices ``[rows, topk]`` (and fp32 scores).
+    ``runs`` int32 ``[nruns, 2, rows, run_len]``: plane 0 the fp32 score bits, plane
+    1 the global indices, each run's rows sorted like ``einsum_topk_func`` output
+    (descending score, then ascending index) — the layout of an all-gather of the
+    ranks' results written with ``out=``. Returns int32 indices ``[rows, topk]``
+    (and fp32 scores).
     """
-    assert runs.dtype == torch.int32 and runs.dim() == 4 and runs.shape[-1] == 2
+    assert runs.dtype == torch.int32 and runs.dim() == 4 and runs.shape[1] == 2
     assert runs.is_cuda
-    nruns, rows, run_len, _ = runs.shape
+    nruns, _, rows, run_len = runs.shape
     assert 1 <= topk <= run_len
     runs = runs.contiguous()
     lib = _lib.load()

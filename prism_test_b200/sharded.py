@@ -7,8 +7,8 @@ contiguous key slice ``[r*Sk/N, (r+1)*Sk/N)`` of every KV head and:
 1. runs the exact local top-k (``einsum_topk_func`` with ``pos_offset`` and
    ``index_base`` = the slice start, so RoPE positions and returned indices are
    global), with fp32 scores;
-2. packs ``(score bits, global index)`` as int32 pairs ``[rows, topk, 2]`` and
-   all-gathers them (one NCCL collective over NVLink);
+2. writes its result straight into an int32 ``[2, rows, topk]`` buffer (score
+   bits, global indices) and all-gathers it (one NCCL collective over NVLink);
 3. merges the N sorted runs per row on the device (``topk_merge_runs``, reading
    the gathered buffer in place): the global top-k is always contained in the
    union of the local top-k lists.
@@ -78,21 +78,24 @@ def sharded_einsum_topk(
     B, Hq, Sq, _ = q.shape
     rows = B * Hq * Sq
     kl = min(topk, k_shard.shape[2])
-    idx, sc = local_topk(q, k_shard, kl, inv_freq=inv_freq, pos_offset=shard_start,
-                         index_base=shard_start, return_scores=True)
-    packed = torch.empty((rows, topk, 2), dtype=torch.int32, device=q.device)
-    packed[:, :kl, 0] = sc.reshape(rows, kl).contiguous().view(torch.int32)
-    packed[:, :kl, 1] = idx.reshape(rows, kl)
-    if kl < topk:  # a shard shorter than k contributes -inf padding
-        packed[:, kl:, 0] = torch.tensor(float("-inf"), dtype=torch.float32).view(torch.int32).item()
-        packed[:, kl:, 1] = torch.iinfo(torch.int32).max
-    gathered = _all_gather(packed, world, group)  # [world, rows, topk, 2]: sorted runs
+    packed = torch.empty((2, rows, topk), dtype=torch.int32, device=q.device)
+    if kl == topk and local_topk is einsum_topk_func:
+        local_topk(q, k_shard, kl, inv_freq=inv_freq, pos_offset=shard_start, index_base=shard_start,
+                   out=(packed[1], packed[0].view(torch.float32)))
+    else:
+        idx, sc = local_topk(q, k_shard, kl, inv_freq=inv_freq, pos_offset=shard_start,
+                             index_base=shard_start, return_scores=True)
+        packed[0, :, :kl] = sc.reshape(rows, kl).contiguous().view(torch.int32)
+        packed[1, :, :kl] = idx.reshape(rows, kl)
+        if kl < topk:  # a shard shorter than k contributes -inf padding
+            packed[0, :, kl:] = torch.tensor(float("-inf"), dtype=torch.float32).view(torch.int32).item()
+            packed[1, :, kl:] = torch.iinfo(torch.int32).max
+    gathered = _all_gather(packed, world, group)  # [world, 2, rows, topk]: sorted runs
     if merge is None:
         out_i, out_s = topk_merge_runs(gathered, topk)
     else:
-        cand = gathered.permute(1, 0, 2, 3).reshape(rows, world * topk, 2)
-        cand_s = cand[..., 0].contiguous().view(torch.float32)
-        cand_i = cand[..., 1].contiguous()
+        cand_s = gathered[:, 0].permute(1, 0, 2).reshape(rows, world * topk).contiguous().view(torch.float32)
+        cand_i = gathered[:, 1].permute(1, 0, 2).reshape(rows, world * topk).contiguous()
         out_i, out_s = merge(cand_s, cand_i, topk)
     out_i = out_i.reshape(B, Hq, Sq, topk)
     if return_scores:

@@ -241,7 +241,7 @@ def test_topk_merge_runs_matches_torch(cuda_device, nruns, run_len, topk):
     idx = torch.gather(idx, -1, order)
     v, p = torch.sort(s, dim=-1, descending=True, stable=True)
     idx = torch.gather(idx, -1, p)
-    runs = torch.stack([v.view(torch.int32), idx], dim=-1).to(cuda_device)
+    runs = torch.stack([v.view(torch.int32), idx], dim=1).to(cuda_device)  # [nruns, 2, rows, len]
     oi, os_ = topk_merge_runs(runs, topk)
     flat_s = v.permute(1, 0, 2).reshape(rows, -1)
     flat_i = idx.permute(1, 0, 2).reshape(rows, -1)
