@@ -557,7 +557,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
       }
       if (tid == 0) sm.count = 0;
     }
-    for (int i = tid; i < kFineBins; i += kThreads) sm.hist[i] = 0u;  // the leader's after find
     cluster.sync();  // threshold ready
     if (tid == 0) {
       sm.thr = lead->thr;
@@ -583,20 +582,37 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (tid == 0) sm.cbase = sm.woff ? atomicAdd(&lead->count, sm.woff) : 0u;
     __syncthreads();
-    uint32_t slot = sm.cbase + wbase + incl - mine;
     uint64_t* rbuf[kCluster];
 #pragma unroll
     for (int r = 0; r < kCluster; ++r) rbuf[r] = cluster.map_shared_rank(sm.buf, r);
+    // this CTA's candidates are compacted in its fine-bin histogram space first
+    // (free until the sort), then copied to every CTA with coalesced stores
+    uint64_t* stage = reinterpret_cast<uint64_t*>(sm.hist);
+    const uint32_t ncta = sm.woff, cbase = sm.cbase;
+    const bool staged = ncta <= uint32_t(kFineBins / 2);
+    uint32_t slot = (staged ? 0u : cbase) + wbase + incl - mine;
 #pragma unroll
     for (int j = 0; j < kKeys; ++j) {
       if (hit & (1u << j)) {
-        if (slot < uint32_t(kCap)) {
-          const int64_t col = key_column(my_base, j);
-          const uint64_t v = pack_cand(kv[j], ix ? uint32_t(ix[col]) : uint32_t(col));
+        const int64_t col = key_column(my_base, j);
+        const uint64_t v = pack_cand(kv[j], ix ? uint32_t(ix[col]) : uint32_t(col));
+        if (staged) {
+          stage[slot] = v;
+        } else if (slot < uint32_t(kCap)) {
 #pragma unroll
           for (int r = 0; r < kCluster; ++r) rbuf[r][slot] = v;
         }
         ++slot;
+      }
+    }
+    if (staged) {
+      __syncthreads();
+      for (uint32_t i = tid; i < ncta; i += kThreads) {
+        const uint64_t v = stage[i];
+        if (cbase + i < uint32_t(kCap)) {
+#pragma unroll
+          for (int r = 0; r < kCluster; ++r) rbuf[r][cbase + i] = v;
+        }
       }
     }
     cluster.sync();  // every CTA holds all candidates
@@ -604,6 +620,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     __syncthreads();
     const uint32_t total = sm.count;
     if (total >= uint32_t(a.k) && total <= uint32_t(kCap)) {
+      for (int i = tid; i < kFineBins; i += kThreads) sm.hist[i] = 0u;  // was the staging area
+      __syncthreads();
       replicated_sort_store(a, row, sm, total, fthr, sm.kmax, rank);
       return;
     }
