@@ -151,6 +151,35 @@ PRISM_API int prism_topk_merge_noalloc(const float* cand_scores, const int32_t* 
                                        int32_t* out_idx, float* out_scores, void* stream);
 
 /*
+ * Post-selection of the recall path, on the device: the sorted, deduplicated
+ * union of the selected middle positions, each widened into a span. Replaces
+ * ReAttentionMethod._global_unique + _expand_spans
+ * (eval_harness/attention_methods/reattention.py:844-874; span_mode
+ * PRISM_SPAN_CENTERED) and the span expansion of
+ * eval_harness/attention_methods/reattention_exact.py:571-585 (PRISM_SPAN_FLOOR).
+ *   topk_idx     int32 [n_idx] middle-relative indices (e.g. the flattened
+ *                prism_einsum_topk output); entries outside [0, n_mid) are ignored.
+ *   recall_clip  < 0: keep every selected position; otherwise keep the recall_clip
+ *                most frequently selected (ties toward lower positions; torch.topk
+ *                leaves them unspecified); at most 16384.
+ *   span_size    >= 0. CENTERED: offsets [-(s/2), (s+1)/2), s = 0 keeps the position.
+ *                FLOOR: offsets [floor(-s/2), (s+1)/2) (one more before the position
+ *                for odd s), s = 0 keeps nothing.
+ *   out_pos      int32 [n_mid]: the result in ascending order, clamped to [0, n_mid).
+ *   out_count    int32 device scalar: number of positions written.
+ *   workspace    prism_post_select_workspace_size(n_mid, recall_clip) bytes, 256-byte aligned.
+ */
+#define PRISM_SPAN_CENTERED 0
+#define PRISM_SPAN_FLOOR 1
+PRISM_API int prism_post_select(const int32_t* topk_idx, int64_t n_idx, int64_t n_mid,
+                                int32_t recall_clip, int32_t span_size, int32_t span_mode,
+                                int32_t* out_pos, int32_t* out_count, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/* Workspace bytes prism_post_select needs (0 on invalid input). */
+PRISM_API size_t prism_post_select_workspace_size(int64_t n_mid, int32_t recall_clip);
+
+/*
  * Reads the device status word kept at the start of `workspace` (synchronises
  * `stream`), stores it in *status_out and resets it to 0. A non-zero value means
  * a kernel gave up on a bounded wait (1), rejected an access (2) or ran out of

@@ -163,3 +163,37 @@ def score_tolerance(q: torch.Tensor, k_raw: torch.Tensor, rel: float = 1e-3) -> 
     qn = q.to(torch.float32).norm(dim=-1)  # [B,Hq,Sq]
     kn = repeat_kv(k_raw, n_rep).norm(dim=-1)  # [B,Hq,Sk]
     return rel * qn[..., :, None] * kn[..., None, :]
+
+
+def global_unique(topk_idx: torch.Tensor, recall_clip: int) -> torch.Tensor:
+    """ReAttentionMethod._global_unique (eval_harness/attention_methods/reattention.py:844-859):
+    the sorted unique selected indices, or — when recall_clip >= 0 and more than
+    recall_clip survive — the recall_clip most frequently selected (torch.topk over
+    the counts; its order among equal counts is unspecified)."""
+    flat = topk_idx.reshape(-1).to(torch.int64)
+    if recall_clip is None or recall_clip < 0:
+        return torch.unique(flat)
+    uniq, counts = torch.unique(flat, return_counts=True)
+    if uniq.numel() > recall_clip:
+        _, keep = torch.topk(counts, k=recall_clip)
+        uniq = uniq[keep]
+    return uniq
+
+
+def expand_spans(sel: torch.Tensor, n_middle: int, span_size: int, mode: str = "centered") -> torch.Tensor:
+    """Span expansion, clamp to [0, n_middle), unique (sorted).
+
+    centered: ReAttentionMethod._expand_spans (reattention.py:861-874), offsets
+    [-(span // 2), (span + 1) // 2), span 0 keeps the positions.
+    floor: reattention_exact.py:578-581, offsets [floor(-span / 2), (span + 1) // 2),
+    span 0 keeps nothing."""
+    if mode == "centered":
+        if span_size > 0:
+            offsets = torch.arange(-(span_size // 2), (span_size + 1) // 2)
+            ids = (sel[:, None] + offsets[None, :]).reshape(-1)
+        else:
+            ids = sel
+    else:
+        offsets = torch.arange(-span_size // 2, (span_size + 1) // 2)
+        ids = (sel[:, None] + offsets[None, :]).reshape(-1)
+    return torch.unique(ids.clamp(0, n_middle - 1))

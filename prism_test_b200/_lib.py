@@ -25,6 +25,8 @@ KERNEL_SELECT = 1
 KERNEL_MERGE = 2
 MODE_EXACT = 0
 MODE_BLOCKMAX = 1
+SPAN_CENTERED = 0
+SPAN_FLOOR = 1
 
 # Every function the header declares: name -> (restype, argtypes)
 _c_i64 = ctypes.c_int64
@@ -51,6 +53,10 @@ SIGNATURES = {
     "prism_topk_merge_noalloc": (ctypes.c_int, [
         _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i32, _vp, _vp, _vp,
     ]),
+    "prism_post_select": (ctypes.c_int, [
+        _vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _vp, _vp, _vp, ctypes.c_size_t, _vp,
+    ]),
+    "prism_post_select_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i32]),
     "prism_read_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), _vp]),
     "prism_profile_start": (ctypes.c_int, [_c_i32]),
     "prism_profile_stop": (ctypes.c_int, []),

@@ -306,6 +306,55 @@ int prism_topk_merge_runs(const int32_t* runs, int32_t nruns, int64_t rows, int6
   return PRISM_OK;
 }
 
+size_t prism_post_select_workspace_size(int64_t n_mid, int32_t recall_clip) {
+  if (n_mid <= 0) return 0;
+  return prism::post_select_workspace_bytes(n_mid, recall_clip);
+}
+
+int prism_post_select(const int32_t* topk_idx, int64_t n_idx, int64_t n_mid, int32_t recall_clip,
+                      int32_t span_size, int32_t span_mode, int32_t* out_pos, int32_t* out_count,
+                      void* workspace, size_t workspace_bytes, void* stream_ptr) {
+  g_last_error.clear();
+  if ((!topk_idx && n_idx > 0) || !out_pos || !out_count)
+    return fail(PRISM_E_INVALID, "null pointer argument");
+  if (n_idx < 0 || n_mid <= 0 || n_mid > INT32_MAX)
+    return fail(PRISM_E_INVALID, "need n_idx >= 0 and 0 < n_mid <= INT32_MAX");
+  if (span_size < 0) return fail(PRISM_E_INVALID, "span_size must be >= 0");
+  if (span_mode != PRISM_SPAN_CENTERED && span_mode != PRISM_SPAN_FLOOR)
+    return fail(PRISM_E_INVALID, "unknown span_mode %d", span_mode);
+  const int32_t clip = recall_clip < 0 || int64_t(recall_clip) >= n_mid ? -1 : recall_clip;
+  if (clip > prism::kSelectMaxK)
+    return fail(PRISM_E_UNSUPPORTED, "recall_clip above %d is not supported", prism::kSelectMaxK);
+  const size_t need = prism::post_select_workspace_bytes(n_mid, clip);
+  if (!workspace || workspace_bytes < need)
+    return fail(PRISM_E_WORKSPACE, "post-select workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(PRISM_E_INVALID, "workspace must be 256-byte aligned");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  // offsets [lo, hi): centered = [-(s/2), (s+1)/2) and s = 0 keeps the position;
+  // floor = [floor(-s/2), (s+1)/2), empty for s = 0
+  int lo, hi;
+  if (span_mode == PRISM_SPAN_CENTERED) {
+    lo = span_size > 0 ? -(span_size / 2) : 0;
+    hi = span_size > 0 ? (span_size + 1) / 2 : 1;
+  } else {
+    lo = -((span_size + 1) / 2);
+    hi = (span_size + 1) / 2;
+  }
+  if (clip == 0 || lo >= hi) {
+    cudaError_t e = cudaMemsetAsync(out_count, 0, sizeof(int32_t), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(out_count)");
+    return PRISM_OK;
+  }
+  const int nsm = num_sms_current_device();
+  cudaError_t e = launch_counted(PRISM_KERNEL_SELECT, stream, [&] {
+    return prism::launch_post_select(topk_idx, n_idx, n_mid, clip, lo, hi, out_pos, out_count,
+                                     workspace, nsm, stream);
+  });
+  if (e != cudaSuccess) return cuda_fail(e, "post-select kernel launch");
+  return PRISM_OK;
+}
+
 int prism_profile_start(int32_t capacity) {
   g_last_error.clear();
   if (capacity < 0) return fail(PRISM_E_INVALID, "capacity must be >= 0");

@@ -82,6 +82,14 @@ cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t 
 cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int64_t run_len, int k,
                               int32_t* out_idx, float* out_scores, cudaStream_t stream);
 
+// Post-selection: sorted union of the selected middle positions (optionally the
+// recall_clip most frequent), each widened to [p + lo, p + hi) and clamped to
+// [0, n_mid). out_pos holds up to n_mid positions, out_count the number written.
+size_t post_select_workspace_bytes(int64_t n_mid, int32_t recall_clip);
+cudaError_t launch_post_select(const int32_t* idx, int64_t n_idx, int64_t n_mid, int32_t recall_clip,
+                               int lo, int hi, int32_t* out_pos, int32_t* out_count, void* workspace,
+                               int num_sms, cudaStream_t stream);
+
 // Block-maximum top-1 / top-4 (the reference Triton kernels' selection); a.k in
 // {1, 4}, a.n % 128 == 0.
 cudaError_t launch_select_blockmax(const SelectArgs& a, cudaStream_t stream);

@@ -226,3 +226,38 @@ def topk_merge_runs(runs: torch.Tensor, topk: int, return_scores: bool = True):
         )
         _lib.check(rc, "prism_topk_merge_runs")
     return (out_idx, out_scores) if return_scores else out_idx
+
+
+def post_select(topk_idx: torch.Tensor, n_middle: int, recall_clip: int = -1, span_size: int = 0,
+                span_mode: str = "centered") -> torch.Tensor:
+    """Sorted, deduplicated middle positions to keep, computed on the device.
+
+    ``topk_idx``: middle-relative indices of any shape (e.g. the ``[B, Hq, Sq, k]``
+    output of ``einsum_topk_func``). Equals
+    ``ReAttentionMethod._expand_spans(ReAttentionMethod._global_unique(topk_idx,
+    recall_clip), n_middle)`` (eval_harness/attention_methods/reattention.py:844-874)
+    for ``span_mode="centered"``, and the span arithmetic of
+    eval_harness/attention_methods/reattention_exact.py:578-581 for
+    ``span_mode="floor"``. Returns an int64 tensor on the same device; reading its
+    length synchronises the stream, as ``torch.unique`` does.
+    """
+    assert topk_idx.is_cuda, "topk_idx must be on the GPU"
+    assert n_middle > 0 and span_size >= 0
+    modes = {"centered": _lib.SPAN_CENTERED, "floor": _lib.SPAN_FLOOR}
+    assert span_mode in modes, f"span_mode must be one of {sorted(modes)}"
+    idx = topk_idx.reshape(-1).to(torch.int32).contiguous()
+    lib = _lib.load()
+    with torch.cuda.device(idx.device):
+        out_pos = torch.empty(n_middle, dtype=torch.int32, device=idx.device)
+        out_count = torch.zeros(1, dtype=torch.int32, device=idx.device)
+        clip = -1 if recall_clip is None else int(recall_clip)
+        ws_bytes = int(lib.prism_post_select_workspace_size(n_middle, clip))
+        ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=idx.device)
+        rc = lib.prism_post_select(
+            idx.data_ptr(), idx.numel(), int(n_middle), clip, int(span_size), modes[span_mode],
+            out_pos.data_ptr(), out_count.data_ptr(), ws.data_ptr(), ws.numel(),
+            torch.cuda.current_stream(idx.device).cuda_stream,
+        )
+        _lib.check(rc, "prism_post_select")
+        n = int(out_count.item())
+    return out_pos[:n].to(torch.int64)

@@ -4,7 +4,8 @@ code (RUSH-Intelligence/Prism-Test, imported read-only from a checkout given by
 
     eval_harness/attention_methods/_method_base.py  build_cos_sin,
         apply_rotary_pos_emb, undo_rotary_pos_emb
-    eval_harness/attention_methods/reattention.py   ReAttentionMethod._dense_topk
+    eval_harness/attention_methods/reattention.py   ReAttentionMethod._dense_topk,
+        ReAttentionMethod._global_unique, ReAttentionMethod._expand_spans
 
 For each case it draws seeded raw keys and queries, rotates the keys with the
 reference's RoPE (fp32), stores them as bf16 (the dtype the GPU path reads),
@@ -106,6 +107,50 @@ def main() -> None:
             raw_keys_ref=raw_ref.numpy() if name == "causal_chunk" else np.zeros(0, np.float32),
         )
         print(name, tuple(q.shape), tuple(k_cached.shape), "topk", topk)
+    post_select_cases(ReAttentionMethod)
+
+
+# post-selection cases: name, n_mid, recall_clip, span_size, span_mode, pattern
+POST_CASES = [
+    ("post_unique_span32", 60000, -1, 32, "centered", "random"),
+    ("post_clip40_span5", 3000, 40, 5, "centered", "frequency"),
+    ("post_span0_identity", 2000, -1, 0, "centered", "random"),
+    ("post_edges_span7", 600, -1, 7, "centered", "edges"),
+    ("post_floor_span5", 3000, -1, 5, "floor", "random"),
+    ("post_floor_clip25_span4", 4000, 25, 4, "floor", "frequency"),
+]
+
+
+def post_select_cases(ReAttentionMethod) -> None:
+    """Golden vectors of the post-selection: ReAttentionMethod._global_unique and
+    _expand_spans (reattention.py:844-874) for the centered spans; for the floor
+    spans, _global_unique followed by the span arithmetic of
+    reattention_exact.py:578-581 (offsets arange(-span // 2, (span + 1) // 2),
+    clamp to the middle, unique), which lives inline in a larger method there."""
+    for (name, n_mid, clip, span, mode, pattern) in POST_CASES:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+        if pattern == "random":
+            idx = torch.randint(0, n_mid, (1, 8, 4, 64), generator=g)
+        elif pattern == "edges":
+            idx = torch.cat([torch.randint(0, 4, (40,), generator=g),
+                             torch.randint(n_mid - 4, n_mid, (40,), generator=g),
+                             torch.randint(0, n_mid, (40,), generator=g)])
+        else:  # distinct selection counts, so the recall_clip cut has no ties
+            pos = torch.randperm(n_mid, generator=g)[:100]
+            idx = torch.cat([pos[i:i + 1].repeat(i + 1) for i in range(100)])
+            idx = idx[torch.randperm(idx.numel(), generator=g)]
+        sel = ReAttentionMethod._global_unique(idx, clip)
+        if mode == "centered":
+            method = ReAttentionMethod(span_size=span, use_triton_kernel="off")
+            out = method._expand_spans(sel, n_mid)
+        else:
+            offsets = torch.arange(-span // 2, (span + 1) // 2)
+            ids = (sel[:, None] + offsets[None, :]).reshape(-1).clamp(0, n_mid - 1)
+            out = torch.unique(ids)
+        np.savez_compressed(HERE / f"{name}.npz", idx=idx.numpy().astype(np.int64),
+                            n_mid=np.array(n_mid), recall_clip=np.array(clip),
+                            span=np.array(span), mode=np.array(mode), out=out.numpy().astype(np.int64))
+        print(name, idx.numel(), "->", out.numel())
 
 
 if __name__ == "__main__":

@@ -8,7 +8,7 @@ import torch
 
 from oracle import reattention_topk as orc
 
-GOLDEN = sorted((Path(__file__).parent / "golden").glob("*.npz"))
+GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith("post_"))
 
 
 def load_case(path):
@@ -88,3 +88,15 @@ def test_blockmax_top1_and_top4_semantics():
     # block maxima: blk0 3.0@5, blk1 7.0@130 (first index), blk2 5.0@300, blk3 7.0@450
     # strict > insertion keeps the earlier 7.0 ahead; the merge keeps tie order
     assert top4.flatten().tolist() == [130, 450, 300, 5]
+
+
+POST = sorted((Path(__file__).resolve().parent / "golden").glob("post_*.npz"))
+
+
+@pytest.mark.parametrize("path", POST, ids=[p.stem for p in POST])
+def test_post_select_oracle_matches_reference(path):
+    z = np.load(path)
+    idx = torch.from_numpy(z["idx"])
+    sel = orc.global_unique(idx, int(z["recall_clip"]))
+    out = orc.expand_spans(sel, int(z["n_mid"]), int(z["span"]), str(z["mode"]))
+    assert torch.equal(out, torch.from_numpy(z["out"]))
