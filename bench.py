@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--workload", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--recall-type", default="qk", choices=["qk", "qkv", "qkv2"],
+                    help="value-norm weighting of the keys (qkv: L1, qkv2: L2)")
     return ap.parse_args()
 
 
@@ -67,13 +69,14 @@ def pick_workload(args, world):
     return W.WORKLOADS[name]
 
 
-def config_of(wl, world):
+def config_of(wl, world, recall_type="qk"):
     return {
         "workload": wl.name, "B": wl.B, "Hq": wl.Hq, "Hkv": wl.Hkv, "Sq": wl.Sq, "Sk": wl.Sk,
         "topk": wl.topk, "head_dim": wl.D, "rope_theta": wl.theta, "key_dtype": "bf16",
         "causal_offset": wl.causal_offset, "shards": world,
         "parallelism": "single GPU" if world == 1 else f"sequence-sharded x{world} (NCCL all-gather + device merge)",
         "l2": "inputs larger than L2 (cached keys %d MB per rank > 126 MB), no flush" % (wl.kv_bytes // world >> 20),
+        "recall_type": recall_type,
     }
 
 
@@ -161,7 +164,7 @@ def ncu_traffic(kernel: str, workload: str):
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_baseline(wl, max_seconds=20.0):
+def cpu_baseline(wl, max_seconds=20.0, recall_type="qk"):
     """The reference's dense CPU path (oracle restatement) on the host cores.
 
     Runs whole calls (or, when one call would exceed the budget, one KV head of
@@ -173,18 +176,25 @@ def cpu_baseline(wl, max_seconds=20.0):
     heads = wl.Hkv if wl.Sk * wl.Sq <= (1 << 17) * 8 else 1
     sub = wl.with_(Hkv=heads, Hq=heads * (wl.Hq // wl.Hkv))
     x = W.make_inputs(sub, "cpu")
-    orc.dense_topk(x["q"], x["k"], sub.topk, x["inv_freq"], 0, sub.causal_offset)  # warm-up
+    v = W.make_values(sub, "cpu") if recall_type != "qk" else None
+
+    def call():
+        w = orc.recall_weights(v, recall_type)
+        orc.dense_topk(x["q"], x["k"], sub.topk, x["inv_freq"], 0, sub.causal_offset, weights=w)
+
+    call()  # warm-up
     times = []
     t_budget = time.perf_counter()
     while len(times) < 5 and time.perf_counter() - t_budget < max_seconds:
         t0 = time.perf_counter()
-        orc.dense_topk(x["q"], x["k"], sub.topk, x["inv_freq"], 0, sub.causal_offset)
+        call()
         times.append(time.perf_counter() - t0)
     best = min(times)
     frac = heads / wl.Hkv
     value = wl.Sk * frac / best
     sample = (f"{'full call' if heads == wl.Hkv else f'{heads} of {wl.Hkv} KV heads'} of {wl.name} "
-              f"(un-rotate fp32, einsum, topk), best of {len(times)} after 1 warm-up")
+              f"(un-rotate fp32, {'value norms, ' if recall_type != 'qk' else ''}einsum, topk), "
+              f"best of {len(times)} after 1 warm-up")
     return {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
             "seconds_per_call": best / frac}
 
@@ -201,17 +211,24 @@ def run_reference(args):
     # bounded sample per step: one KV head (and its query group) of the workload
     sub = wl.with_(Hkv=1, Hq=wl.Hq // wl.Hkv)
     x = W.make_inputs(sub, "cpu")
+    rt = args.recall_type
+    v = W.make_values(sub, "cpu") if rt != "qk" else None
+
+    def call():
+        w = orc.recall_weights(v, rt)
+        orc.dense_topk(x["q"], x["k"], sub.topk, x["inv_freq"], 0, sub.causal_offset, weights=w)
+
     steps, warm = max(1, args.steps), max(0, args.warmup)
     est = None
     for _ in range(max(1, warm)):
         t0 = time.perf_counter()
-        orc.dense_topk(x["q"], x["k"], sub.topk, x["inv_freq"], 0, sub.causal_offset)
+        call()
         est = time.perf_counter() - t0
     # keep the whole run within a few minutes
     steps = min(steps, max(3, int(120.0 / max(est, 1e-3))))
     t0 = time.perf_counter()
     for _ in range(steps):
-        orc.dense_topk(x["q"], x["k"], sub.topk, x["inv_freq"], 0, sub.causal_offset)
+        call()
     dt = (time.perf_counter() - t0) / steps
     value = wl.Sk / wl.Hkv / dt  # KV tokens (all heads) per second
     sample = f"1 of {wl.Hkv} KV heads of {wl.name} per step (un-rotate fp32, einsum, topk); {steps} steps"
@@ -219,7 +236,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32 (tf32 MMA)",
-        "data": "synthetic", "config": config_of(wl, world),
+        "data": "synthetic", "config": config_of(wl, world, rt),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -249,12 +266,15 @@ def main():
     start, stop = shard_bounds(wl.Sk, rank, world)
     x = W.make_inputs(wl, dev, shard=(rank, world) if world > 1 else None)
     q, k, inv = x["q"], x["k"], x["inv_freq"]
+    rt = args.recall_type
+    v = W.make_values(wl, dev, start, stop) if rt != "qk" else None
 
-    def step(qq, kk):
+    def step(qq, kk, vv=v):
         if world == 1:
             return einsum_topk_func(qq, kk, wl.topk, inv_freq=inv, return_scores=True,
-                                    causal_offset=wl.causal_offset)
-        return sharded_einsum_topk(qq, kk, wl.topk, shard_start=start, inv_freq=inv, return_scores=True)
+                                    causal_offset=wl.causal_offset, values=vv, recall_type=rt)
+        return sharded_einsum_topk(qq, kk, wl.topk, shard_start=start, inv_freq=inv, return_scores=True,
+                                   v_shard=vv, recall_type=rt)
 
     def barrier():
         if world > 1:
@@ -338,6 +358,12 @@ def main():
     n_me = _lib.ctypes.c_int64(0)
     t_me = _lib.ctypes.c_double(0.0)
     lib.prism_profile_read(_lib.KERNEL_MERGE, _lib.ctypes.byref(n_me), _lib.ctypes.byref(t_me))
+    n_we = _lib.ctypes.c_int64(0)
+    t_we = _lib.ctypes.c_double(0.0)
+    lib.prism_profile_read(_lib.KERNEL_WEIGHT, _lib.ctypes.byref(n_we), _lib.ctypes.byref(t_we))
+    n_sa = _lib.ctypes.c_int64(0)
+    t_sa = _lib.ctypes.c_double(0.0)
+    lib.prism_profile_read(_lib.KERNEL_SCALE, _lib.ctypes.byref(n_sa), _lib.ctypes.byref(t_sa))
     score_ms = t_sc.value / max(1, n_sc.value)
     bytes_per_launch = (stop - start) * wl.B * wl.Hkv * wl.D * 2  # keys of this rank, read once
     peak, peak_kind = measured_peaks()
@@ -356,10 +382,14 @@ def main():
         sc_h = torch.empty((rows * wl.topk,), dtype=torch.float32).pin_memory()
         q_d = torch.empty_like(q)
         k_d = torch.empty_like(k)
+        v_h = v.cpu().pin_memory() if v is not None else None
+        v_d = torch.empty_like(v) if v is not None else None
         for _ in range(2):
             q_d.copy_(q_h, non_blocking=True)
             k_d.copy_(k_h, non_blocking=True)
-            oi, os_ = step(q_d, k_d)
+            if v_d is not None:
+                v_d.copy_(v_h, non_blocking=True)
+            oi, os_ = step(q_d, k_d, v_d)
             idx_h.copy_(oi.reshape(-1), non_blocking=True)
             sc_h.copy_(os_.reshape(-1), non_blocking=True)
         torch.cuda.synchronize()
@@ -371,7 +401,9 @@ def main():
         for _ in range(args.steps):
             q_d.copy_(q_h, non_blocking=True)
             k_d.copy_(k_h, non_blocking=True)
-            oi, os_ = step(q_d, k_d)
+            if v_d is not None:
+                v_d.copy_(v_h, non_blocking=True)
+            oi, os_ = step(q_d, k_d, v_d)
             idx_h.copy_(oi.reshape(-1), non_blocking=True)
             sc_h.copy_(os_.reshape(-1), non_blocking=True)
         e1.record()
@@ -380,13 +412,14 @@ def main():
         torch.cuda.synchronize()
         ems = max_over_ranks(e0.elapsed_time(e1))
         e2e = {"value": wl.Sk * args.steps / (ems * 1e-3), "unit": UNIT,
-               "h2d_bytes_per_step": int(q_h.numel() * q_h.element_size() + k_h.numel() * k_h.element_size()) * world,
+               "h2d_bytes_per_step": int(q_h.numel() * q_h.element_size() + k_h.numel() * k_h.element_size()
+                                         + (v_h.numel() * v_h.element_size() if v_h is not None else 0)) * world,
                "d2h_bytes_per_step": int(idx_h.numel() * 4 + sc_h.numel() * 4) * world,
                "ms_per_step": ems / args.steps}
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        base = cpu_baseline(wl)
+        base = cpu_baseline(wl, recall_type=rt)
 
     if world > 1:
         import torch.distributed as dist
@@ -399,7 +432,7 @@ def main():
         "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32 (tf32 MMA)",
         "data": "synthetic (seeded; see prism_test_b200/workloads.py)",
-        "config": config_of(wl, world),
+        "config": config_of(wl, world, rt),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind,
                      "traffic": ncu_traffic("score", wl.name),
@@ -409,6 +442,8 @@ def main():
             "score": t_sc.value / max(1, args.steps),
             "select": t_se.value / max(1, args.steps),
             "merge": t_me.value / max(1, args.steps),
+            "value_norms": t_we.value / max(1, args.steps),
+            "score_weighting": t_sa.value / max(1, args.steps),
         },
         "gpu_launches": int(launches),
         "timing": "CUDA graph of one call, replayed",

@@ -90,6 +90,47 @@ PRISM_API int prism_einsum_topk(const void* q, const void* k, const float* inv_f
 PRISM_API size_t prism_einsum_topk_workspace_size(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk,
                                         int32_t topk, int32_t mode);
 
+/* recall weightings of prism_einsum_topk_weighted (the reference's recall_type) */
+#define PRISM_RECALL_QK 0   /* "qk": unweighted, the same as prism_einsum_topk */
+#define PRISM_RECALL_QKV 1  /* "qkv": key j scaled by ||v_j||_1 */
+#define PRISM_RECALL_QKV2 2 /* "qkv2": key j scaled by ||v_j||_2 */
+
+/*
+ * prism_einsum_topk with the value-norm recall weighting: the score of key j
+ * is multiplied by the L1 (PRISM_RECALL_QKV) or L2 (PRISM_RECALL_QKV2) norm of
+ * value row j of the same KV head, computed in fp32 and rounded to `dtype`.
+ *
+ * Replaces ReAttentionMethod._apply_recall_weight
+ * (eval_harness/attention_methods/reattention.py:822-842, applied at :358 and
+ * in reattention_exact.py:547) — raw_k * values.norm(p, dim=-1, keepdim=True),
+ * a bf16/fp16 norm — followed by the selection prism_einsum_topk replaces.
+ * Scaling the raw key by a scalar and scaling its score by it are the same
+ * product; the weighting runs after scoring, on the score matrix.
+ *
+ *   v          [B, Hkv, Sk, Dv] elements of `dtype`: the value rows of the
+ *              same keys (the middle slice k covers). v_strides[3] == 1;
+ *              base and v_strides[0..2] 16-byte aligned; Dv % 8 == 0,
+ *              8 <= Dv <= 1024.
+ *   recall_weight  PRISM_RECALL_QK, PRISM_RECALL_QKV or PRISM_RECALL_QKV2
+ *              (with PRISM_RECALL_QK, v and v_strides are ignored).
+ *   workspace  at least prism_einsum_topk_weighted_workspace_size() bytes
+ *              (prism_einsum_topk's plus B * Hkv * Sk fp32 weights).
+ * Every other argument and the outputs are those of prism_einsum_topk;
+ * out_scores holds the weighted scores. A masked (-inf) score stays -inf.
+ */
+PRISM_API size_t prism_einsum_topk_weighted_workspace_size(int64_t B, int64_t Hq, int64_t Hkv,
+                                                           int64_t Sq, int64_t Sk, int32_t topk,
+                                                           int32_t mode, int32_t recall_weight);
+PRISM_API int prism_einsum_topk_weighted(const void* q, const void* k, const void* v,
+                                         const float* inv_freq, int dtype, int64_t B, int64_t Hq,
+                                         int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D,
+                                         int64_t Dv, const int64_t* q_strides,
+                                         const int64_t* k_strides, const int64_t* v_strides,
+                                         int64_t pos_offset, int64_t causal_offset,
+                                         int32_t recall_weight, int32_t topk, int32_t mode,
+                                         int64_t index_base, int32_t* out_idx, float* out_scores,
+                                         void* workspace, size_t workspace_bytes, void* stream);
+
 /*
  * Exact top-k over candidate lists: for each of `rows` rows, picks the topk
  * largest of n (score, index) pairs laid out with row stride ld (ld % 4 == 0,
@@ -200,6 +241,8 @@ PRISM_API int prism_read_status(void* workspace, int* status_out, void* stream);
 #define PRISM_KERNEL_SCORE 0  /* decode scorer (un-rotate + q·K^T) */
 #define PRISM_KERNEL_SELECT 1 /* exact top-k selection of a score matrix */
 #define PRISM_KERNEL_MERGE 2  /* top-k merge of gathered shard candidates */
+#define PRISM_KERNEL_WEIGHT 3 /* value-row norms of the weighted recall */
+#define PRISM_KERNEL_SCALE 4  /* weighting of the score matrix by those norms */
 PRISM_API int prism_profile_start(int32_t capacity);
 PRISM_API int prism_profile_stop(void);
 PRISM_API int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms);

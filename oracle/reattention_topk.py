@@ -20,6 +20,10 @@ path (RUSH-Intelligence/Prism-Test, eval_harness/attention_methods/):
                            einsum("bhqd,bhmd->bhqm") in fp32, then topk (sorted,
                            largest first); a causal mask (-inf) is applied before
                            topk when ``causal_offset`` is given
+* ``recall_weights``       ReAttentionMethod._apply_recall_weight, reattention.py:822-842:
+                           qkv -> ||v||_1, qkv2 -> ||v||_2 per key, as the
+                           values' dtype (``values.norm`` of a bf16/fp16 tensor);
+                           the weighted raw key is raw_k (fp32) * that weight
 * ``blockmax_topk``        the fused Triton kernels einsum_topk.py:21-161 with the
                            4-wide merge of bitonic_merge_wrapper.py:5-52: per
                            128-key block the row maximum (first index on ties),
@@ -89,10 +93,13 @@ def dense_scores(q: torch.Tensor, k_raw: torch.Tensor, causal_offset: Optional[i
 
 def dense_topk(q: torch.Tensor, k: torch.Tensor, topk: int, inv_freq: Optional[torch.Tensor] = None,
                pos_offset: int = 0, causal_offset: Optional[int] = None,
-               index_base: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
-    """(scores fp32, indices int64) of shape [B, Hq, Sq, topk], largest first."""
+               index_base: int = 0, weights: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(scores fp32, indices int64) of shape [B, Hq, Sq, topk], largest first.
+    ``weights`` [B, Hkv, Sk] (``recall_weights``) scale the raw keys."""
     q = q.cpu()
     k_raw = unrotate_keys(k.cpu(), inv_freq, pos_offset)
+    if weights is not None:
+        k_raw = k_raw * weights.cpu()[..., None]
     scores = dense_scores(q, k_raw, causal_offset)
     vals, idx = scores.topk(min(topk, scores.shape[-1]), dim=-1)
     return vals, idx + index_base
@@ -197,3 +204,16 @@ def expand_spans(sel: torch.Tensor, n_middle: int, span_size: int, mode: str = "
         offsets = torch.arange(-span_size // 2, (span_size + 1) // 2)
         ids = (sel[:, None] + offsets[None, :]).reshape(-1)
     return torch.unique(ids.clamp(0, n_middle - 1))
+
+
+def recall_weights(values: Optional[torch.Tensor], recall_type: str) -> Optional[torch.Tensor]:
+    """Per-key weights [B, Hkv, Sk] (fp32 holding values of the values' dtype) of
+    ReAttentionMethod._apply_recall_weight (reattention.py:822-842), or None for "qk".
+    The weighted raw key is ``raw_k * weights[..., None]``."""
+    if recall_type == "qk":
+        return None
+    if recall_type == "qkv":
+        return values.cpu().norm(p=1, dim=-1).to(torch.float32)
+    if recall_type == "qkv2":
+        return values.cpu().norm(p=2, dim=-1).to(torch.float32)
+    raise ValueError(f"Unsupported recall_type '{recall_type}'. Use one of: qk, qkv, qkv2.")

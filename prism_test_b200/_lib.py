@@ -27,6 +27,11 @@ MODE_EXACT = 0
 MODE_BLOCKMAX = 1
 SPAN_CENTERED = 0
 SPAN_FLOOR = 1
+KERNEL_WEIGHT = 3
+KERNEL_SCALE = 4
+RECALL_QK = 0
+RECALL_QKV = 1
+RECALL_QKV2 = 2
 
 # Every function the header declares: name -> (restype, argtypes)
 _c_i64 = ctypes.c_int64
@@ -39,6 +44,16 @@ SIGNATURES = {
         ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64), _c_i64,
         _c_i64, _c_i32, _c_i32, _c_i64,
         _vp, _vp, _vp, ctypes.c_size_t, _vp,
+    ]),
+    "prism_einsum_topk_weighted": (ctypes.c_int, [
+        _vp, _vp, _vp, _vp, ctypes.c_int,
+        _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+        ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64),
+        _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i64,
+        _vp, _vp, _vp, ctypes.c_size_t, _vp,
+    ]),
+    "prism_einsum_topk_weighted_workspace_size": (ctypes.c_size_t, [
+        _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32,
     ]),
     "prism_einsum_topk_workspace_size": (ctypes.c_size_t, [
         _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i32,

@@ -54,7 +54,7 @@ std::vector<cudaEvent_t> g_prof_pool;  // 2 * capacity events
 std::vector<ProfRec> g_prof_recs;
 bool g_prof_on = false;
 size_t g_prof_next = 0;
-int64_t g_prof_untimed[3] = {0, 0, 0};
+int64_t g_prof_untimed[5] = {0, 0, 0, 0, 0};
 
 // Runs `launch` (which enqueues one kernel on `stream`), counting it and, while
 // profiling is on, bracketing it with a pair of events from the pool.
@@ -86,6 +86,10 @@ size_t exact_workspace(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk) {
   return kStatusBytes + round_up(int64_t(scores_bytes(rows, Sk)), 256) +
          prism::select_workspace_bytes(rows, Sk);
 }
+// the value-norm weights of the weighted call follow, 256-byte aligned
+size_t weights_offset(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk) {
+  return size_t(round_up(int64_t(exact_workspace(B, Hq, Sq, Sk)), 256));
+}
 
 }  // namespace
 
@@ -107,13 +111,18 @@ size_t prism_einsum_topk_workspace_size(int64_t B, int64_t Hq, int64_t Sq, int64
   return exact_workspace(B, Hq, Sq, Sk);
 }
 
-int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int dtype, int64_t B,
-                      int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D,
-                      const int64_t* q_strides, const int64_t* k_strides, int64_t pos_offset,
-                      int64_t causal_offset, int32_t topk, int32_t mode, int64_t index_base,
-                      int32_t* out_idx, float* out_scores, void* workspace,
-                      size_t workspace_bytes, void* stream_ptr) {
-  g_last_error.clear();
+}  // extern "C"
+
+namespace {
+
+// Shared body of prism_einsum_topk and prism_einsum_topk_weighted: `weight`
+// (already validated) scales the score matrix between scoring and selection.
+int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dtype, int64_t B,
+                     int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D,
+                     const int64_t* q_strides, const int64_t* k_strides, int64_t pos_offset,
+                     int64_t causal_offset, int32_t topk, int32_t mode, int64_t index_base,
+                     int32_t* out_idx, float* out_scores, void* workspace,
+                     size_t workspace_bytes, void* stream_ptr, const prism::WeightArgs* weight) {
   if (!q || !k || !out_idx || !q_strides || !k_strides)
     return fail(PRISM_E_INVALID, "null pointer argument");
   if (dtype != PRISM_DTYPE_BF16 && dtype != PRISM_DTYPE_FP16)
@@ -149,7 +158,8 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
   if (Hq > prism::kDecodeMaxRows)
     return fail(PRISM_E_UNSUPPORTED, "more than %d query heads", prism::kDecodeMaxRows);
 
-  const size_t need = exact_workspace(B, Hq, Sq, Sk);
+  const size_t need = weight ? weights_offset(B, Hq, Sq, Sk) + prism::weight_workspace_bytes(B, Hkv, Sk)
+                            : exact_workspace(B, Hq, Sq, Sk);
   if (!workspace || workspace_bytes < need)
     return fail(PRISM_E_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
@@ -163,8 +173,27 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
   cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
 
-  // ---- scoring ----------------------------------------------------------------------
   const int nsm = num_sms_current_device();
+  // ---- value norms (streams V once) ------------------------------------------------
+  prism::WeightArgs wa{};
+  if (weight) {
+    wa = *weight;
+    wa.B = int(B);
+    wa.Hq = int(Hq);
+    wa.Hkv = int(Hkv);
+    wa.G = int(Hq / Hkv);
+    wa.Sq = int(Sq);
+    wa.Sk = Sk;
+    wa.scores = scores;
+    wa.ld = ld;
+    wa.w = reinterpret_cast<float*>(ws + weights_offset(B, Hq, Sq, Sk));
+    wa.status = status;
+    e = launch_counted(PRISM_KERNEL_WEIGHT, stream,
+                       [&] { return prism::launch_value_norms(wa, dtype, nsm, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "value norm kernel launch");
+  }
+
+  // ---- scoring ----------------------------------------------------------------------
   prism::DecodeArgs a{};
   a.q = q;
   a.k = k;
@@ -222,6 +251,15 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
     }
   }
 
+  // ---- value-norm weighting of the score matrix ----------------------------------------
+  // (a separate pass: loading the weights inside the issue-bound scorer's
+  // epilogue was measured slower than re-reading the scores here)
+  if (weight) {
+    e = launch_counted(PRISM_KERNEL_SCALE, stream,
+                       [&] { return prism::launch_scale_scores(wa, nsm, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "score weighting kernel launch");
+  }
+
   // ---- selection ------------------------------------------------------------------
   prism::SelectArgs s{};
   s.scores = scores;
@@ -245,6 +283,68 @@ int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int d
                      [&] { return prism::launch_select_topk(s, cand_ws, stream); });
   if (e != cudaSuccess) return cuda_fail(e, "select kernel launch");
   return PRISM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int dtype, int64_t B,
+                      int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D,
+                      const int64_t* q_strides, const int64_t* k_strides, int64_t pos_offset,
+                      int64_t causal_offset, int32_t topk, int32_t mode, int64_t index_base,
+                      int32_t* out_idx, float* out_scores, void* workspace,
+                      size_t workspace_bytes, void* stream_ptr) {
+  g_last_error.clear();
+  return einsum_topk_impl(q, k, inv_freq, dtype, B, Hq, Hkv, Sq, Sk, D, q_strides, k_strides,
+                          pos_offset, causal_offset, topk, mode, index_base, out_idx, out_scores,
+                          workspace, workspace_bytes, stream_ptr, nullptr);
+}
+
+size_t prism_einsum_topk_weighted_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
+                                                 int64_t Sk, int32_t topk, int32_t mode,
+                                                 int32_t recall_weight) {
+  const size_t base = prism_einsum_topk_workspace_size(B, Hq, Sq, Sk, topk, mode);
+  if (base == 0 || Hkv <= 0) return 0;
+  if (recall_weight == PRISM_RECALL_QK) return base;
+  if (recall_weight != PRISM_RECALL_QKV && recall_weight != PRISM_RECALL_QKV2) return 0;
+  return weights_offset(B, Hq, Sq, Sk) + prism::weight_workspace_bytes(B, Hkv, Sk);
+}
+
+int prism_einsum_topk_weighted(const void* q, const void* k, const void* v, const float* inv_freq,
+                               int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
+                               int64_t Sk, int64_t D, int64_t Dv, const int64_t* q_strides,
+                               const int64_t* k_strides, const int64_t* v_strides,
+                               int64_t pos_offset, int64_t causal_offset, int32_t recall_weight,
+                               int32_t topk, int32_t mode, int64_t index_base, int32_t* out_idx,
+                               float* out_scores, void* workspace, size_t workspace_bytes,
+                               void* stream_ptr) {
+  g_last_error.clear();
+  if (recall_weight != PRISM_RECALL_QK && recall_weight != PRISM_RECALL_QKV &&
+      recall_weight != PRISM_RECALL_QKV2)
+    return fail(PRISM_E_INVALID, "unknown recall_weight %d", recall_weight);
+  if (recall_weight == PRISM_RECALL_QK)
+    return einsum_topk_impl(q, k, inv_freq, dtype, B, Hq, Hkv, Sq, Sk, D, q_strides, k_strides,
+                            pos_offset, causal_offset, topk, mode, index_base, out_idx,
+                            out_scores, workspace, workspace_bytes, stream_ptr, nullptr);
+  if (!v || !v_strides) return fail(PRISM_E_INVALID, "null values pointer or strides");
+  if (Dv <= 0 || Dv % 8 != 0 || Dv > 1024)
+    return fail(PRISM_E_UNSUPPORTED, "value head_dim must be a multiple of 8 in [8, 1024], got %lld",
+                (long long)Dv);
+  if (v_strides[3] != 1) return fail(PRISM_E_INVALID, "values must have unit stride in the last dimension");
+  if ((reinterpret_cast<uintptr_t>(v) & 15u) != 0 || (v_strides[0] * 2) % 16 != 0 ||
+      (v_strides[1] * 2) % 16 != 0 || (v_strides[2] * 2) % 16 != 0)
+    return fail(PRISM_E_INVALID, "values base and batch/head/key strides must be 16-byte aligned");
+  prism::WeightArgs wa{};
+  wa.v = v;
+  wa.v_sb = v_strides[0];
+  wa.v_sh = v_strides[1];
+  wa.v_ss = v_strides[2];
+  wa.Dv = int(Dv);
+  wa.p = recall_weight == PRISM_RECALL_QKV ? 1 : 2;
+  return einsum_topk_impl(q, k, inv_freq, dtype, B, Hq, Hkv, Sq, Sk, D, q_strides, k_strides,
+                          pos_offset, causal_offset, topk, mode, index_base, out_idx, out_scores,
+                          workspace, workspace_bytes, stream_ptr, &wa);
 }
 
 size_t prism_topk_merge_workspace_size(int64_t rows, int64_t n) {
@@ -367,7 +467,7 @@ int prism_profile_start(int32_t capacity) {
   }
   g_prof_recs.clear();
   g_prof_next = 0;
-  g_prof_untimed[0] = g_prof_untimed[1] = g_prof_untimed[2] = 0;
+  for (int64_t& u : g_prof_untimed) u = 0;
   g_prof_on = capacity > 0;
   return PRISM_OK;
 }
@@ -379,7 +479,7 @@ int prism_profile_stop(void) {
 
 int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms) {
   g_last_error.clear();
-  if (!launches || !total_ms || kernel < 0 || kernel > 2)
+  if (!launches || !total_ms || kernel < 0 || kernel > PRISM_KERNEL_SCALE)
     return fail(PRISM_E_INVALID, "bad kernel id or null output");
   int64_t n = 0;
   double ms = 0.0;

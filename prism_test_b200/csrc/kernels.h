@@ -94,6 +94,27 @@ cudaError_t launch_post_select(const int32_t* idx, int64_t n_idx, int64_t n_mid,
 // {1, 4}, a.n % 128 == 0.
 cudaError_t launch_select_blockmax(const SelectArgs& a, cudaStream_t stream);
 
+// Value-norm weighting of a score matrix in place: scores[(b, hq, s), j] *=
+// dtype-rounded ||v[b, hq / G, j, :]||_p, p in {1, 2}. Value rows: unit stride,
+// row/head/batch strides and base 16-byte aligned, Dv % 8 == 0.
+// launch_value_norms writes w [B * Hkv, ld] (weight_workspace_bytes, 16-byte
+// aligned); launch_scale_scores then scales the scores [rows, ld] by it.
+struct WeightArgs {
+  const void* v;
+  int64_t v_sb, v_sh, v_ss;  // element strides of batch, KV head, key
+  int Dv;
+  int p;
+  int B, Hq, Hkv, G, Sq;
+  int64_t Sk;
+  float* scores;
+  int64_t ld;
+  float* w;
+  int* status;  // device status word (bounded waits report kStatusTimeout)
+};
+size_t weight_workspace_bytes(int64_t B, int64_t Hkv, int64_t Sk);
+cudaError_t launch_value_norms(const WeightArgs& a, int dtype, int num_sms, cudaStream_t stream);
+cudaError_t launch_scale_scores(const WeightArgs& a, int num_sms, cudaStream_t stream);
+
 // Sets the message prism_last_error() returns for the calling thread.
 void set_last_error(const char* msg);
 

@@ -21,6 +21,11 @@ defaults keep the reference call working unchanged:
 * ``causal_offset``: key ``j`` is visible to query row ``s`` iff
   ``j <= causal_offset + s`` (masked keys score ``-inf``).
 * ``index_base`` is added to every returned index (sequence shards).
+* ``recall_type`` ("qk" default, "qkv", "qkv2") with ``values`` fuses
+  ``ReAttentionMethod._apply_recall_weight`` (reattention.py:822-842): each key's
+  score is scaled by the L1 / L2 norm of its value row (the norm rounded to the
+  values' dtype, as ``values.norm`` returns it). Other recall types raise
+  ``ValueError`` with the reference's messages.
 * ``return_scores=True`` also returns the fp32 scores of the selected keys.
 
 Argument errors raise ``AssertionError`` like the reference's ``assert``
@@ -53,6 +58,29 @@ def _rows_contiguous_aligned(k: torch.Tensor) -> bool:
     return (k.stride(0) * esz) % 16 == 0 and (k.stride(1) * esz) % 16 == 0
 
 
+def _value_rows_aligned(v: torch.Tensor) -> bool:
+    if v.stride(-1) != 1 or v.data_ptr() % 16:
+        return False
+    esz = v.element_size()
+    return all((st * esz) % 16 == 0 for st in v.stride()[:3])
+
+
+def _recall_weight_code(recall_type: str) -> int:
+    """recall_type -> PRISM_RECALL_*, raising like ReAttentionMethod._apply_recall_weight
+    (reattention.py:822-842) for the types it rejects."""
+    codes = {"qk": _lib.RECALL_QK, "qkv": _lib.RECALL_QKV, "qkv2": _lib.RECALL_QKV2}
+    if recall_type in codes:
+        return codes[recall_type]
+    if recall_type in ("qk_pe", "qkv_pe", "qkv2_pe"):
+        raise ValueError(
+            f"Unsupported recall_type '{recall_type}' for the hook port: the "
+            "'_pe' variants score against position-encoded (rotated) "
+            "keys, but this port un-rotates the cache unconditionally "
+            "('_pe' variants are not implemented).",
+        )
+    raise ValueError(f"Unsupported recall_type '{recall_type}'. Use one of: qk, qkv, qkv2.")
+
+
 def einsum_topk_func(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -65,6 +93,8 @@ def einsum_topk_func(
     return_scores: bool = False,
     mode: str = "exact",
     out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+    values: Optional[torch.Tensor] = None,
+    recall_type: str = "qk",
 ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """Fused (un-rotate +) q·K^T + top-k on the GPU.
 
@@ -83,7 +113,11 @@ def einsum_topk_func(
     ``out=(indices, scores)`` writes into caller tensors instead (contiguous,
     int32 and fp32, ``batch * num_heads * seqlen_q * topk`` elements each) and
     returns them.
+
+    ``values`` : Tensor [batch, num_kv_heads, seqlen_k, head_dim_v], the value
+    rows of the same keys, needed by ``recall_type`` "qkv" / "qkv2".
     """
+    weight_code = _recall_weight_code(recall_type)
     batch, num_heads, seqlen_q, d = q.shape
     batch_k, num_heads_k, seqlen_k, dk = k.shape
     assert q.stride(-1) == 1 and k.stride(-1) == 1
@@ -110,10 +144,20 @@ def einsum_topk_func(
     else:
         raise AssertionError(f"unknown mode {mode!r}; use 'exact' or 'blockmax'")
 
+    if weight_code != _lib.RECALL_QK:
+        assert values is not None, f"recall_type {recall_type!r} needs values"
+        assert values.dim() == 4 and tuple(values.shape[:3]) == (batch, num_heads_k, seqlen_k), (
+            f"values must be [batch, num_kv_heads, seqlen_k, head_dim_v], got {tuple(values.shape)}"
+        )
+        assert values.dtype == q.dtype, "values must have the dtype of q and k"
+        assert values.device == q.device, "values must be on the device of q"
+
     lib = _lib.load()
     with torch.cuda.device(q.device):
         if not _rows_contiguous_aligned(k):
             k = k.contiguous()
+        if weight_code != _lib.RECALL_QK and not _value_rows_aligned(values):
+            values = values.contiguous()
         invf_ptr = None
         if inv_freq is not None:
             assert inv_freq.numel() == d // 2, "inv_freq must have head_dim // 2 entries"
@@ -135,18 +179,31 @@ def einsum_topk_func(
                 torch.empty((batch, num_heads, seqlen_q, topk), dtype=torch.float32, device=q.device)
                 if return_scores else None
             )
-        ws_bytes = lib.prism_einsum_topk_workspace_size(batch, num_heads, seqlen_q, seqlen_k, topk, mode_code)
+        ws_bytes = lib.prism_einsum_topk_weighted_workspace_size(
+            batch, num_heads, num_heads_k, seqlen_q, seqlen_k, topk, mode_code, weight_code)
         ws = torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=q.device)
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        rc = lib.prism_einsum_topk(
-            q.data_ptr(), k.data_ptr(), invf_ptr, _dtype_code(q.dtype),
-            batch, num_heads, num_heads_k, seqlen_q, seqlen_k, d,
-            _lib.i64_array(q.stride()), _lib.i64_array(k.stride()), int(pos_offset),
-            causal, int(topk), mode_code, int(index_base),
-            out_idx.data_ptr(), out_scores.data_ptr() if out_scores is not None else None,
-            ws.data_ptr(), ws.numel(), stream,
-        )
-        _lib.check(rc, "prism_einsum_topk")
+        if weight_code == _lib.RECALL_QK:
+            rc = lib.prism_einsum_topk(
+                q.data_ptr(), k.data_ptr(), invf_ptr, _dtype_code(q.dtype),
+                batch, num_heads, num_heads_k, seqlen_q, seqlen_k, d,
+                _lib.i64_array(q.stride()), _lib.i64_array(k.stride()), int(pos_offset),
+                causal, int(topk), mode_code, int(index_base),
+                out_idx.data_ptr(), out_scores.data_ptr() if out_scores is not None else None,
+                ws.data_ptr(), ws.numel(), stream,
+            )
+            _lib.check(rc, "prism_einsum_topk")
+        else:
+            rc = lib.prism_einsum_topk_weighted(
+                q.data_ptr(), k.data_ptr(), values.data_ptr(), invf_ptr, _dtype_code(q.dtype),
+                batch, num_heads, num_heads_k, seqlen_q, seqlen_k, d, values.shape[-1],
+                _lib.i64_array(q.stride()), _lib.i64_array(k.stride()),
+                _lib.i64_array(values.stride()), int(pos_offset), causal, weight_code,
+                int(topk), mode_code, int(index_base),
+                out_idx.data_ptr(), out_scores.data_ptr() if out_scores is not None else None,
+                ws.data_ptr(), ws.numel(), stream,
+            )
+            _lib.check(rc, "prism_einsum_topk_weighted")
         if _SYNC_CHECK:
             read_status(ws)
     if return_scores:

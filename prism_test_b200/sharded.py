@@ -64,6 +64,8 @@ def sharded_einsum_topk(
     return_scores: bool = False,
     local_topk: Optional[Callable] = None,
     merge: Optional[Callable] = None,
+    v_shard: Optional[torch.Tensor] = None,
+    recall_type: str = "qk",
 ):
     """Global exact top-k over a key sequence split across the ranks of ``group``.
 
@@ -71,9 +73,12 @@ def sharded_einsum_topk(
     at absolute position / global index ``shard_start``. Returns int32 indices
     ``[B, Hq, Sq, topk]`` (and fp32 scores) on every rank.
     ``local_topk`` / ``merge`` default to the CUDA kernels; tests substitute
-    CPU implementations to run the exchange over gloo.
+    CPU implementations to run the exchange over gloo. ``recall_type`` "qkv" /
+    "qkv2" weights each key by the norm of its value row in ``v_shard`` (the
+    same slice of the value cache), as ``einsum_topk_func`` does.
     """
     local_topk = local_topk or einsum_topk_func
+    extra = {} if recall_type == "qk" else dict(values=v_shard, recall_type=recall_type)
     world = dist.get_world_size(group)
     B, Hq, Sq, _ = q.shape
     rows = B * Hq * Sq
@@ -81,10 +86,10 @@ def sharded_einsum_topk(
     packed = torch.empty((2, rows, topk), dtype=torch.int32, device=q.device)
     if kl == topk and local_topk is einsum_topk_func:
         local_topk(q, k_shard, kl, inv_freq=inv_freq, pos_offset=shard_start, index_base=shard_start,
-                   out=(packed[1], packed[0].view(torch.float32)))
+                   out=(packed[1], packed[0].view(torch.float32)), **extra)
     else:
         idx, sc = local_topk(q, k_shard, kl, inv_freq=inv_freq, pos_offset=shard_start,
-                             index_base=shard_start, return_scores=True)
+                             index_base=shard_start, return_scores=True, **extra)
         packed[0, :, :kl] = sc.reshape(rows, kl).contiguous().view(torch.int32)
         packed[1, :, :kl] = idx.reshape(rows, kl)
         if kl < topk:  # a shard shorter than k contributes -inf padding

@@ -185,6 +185,24 @@ def make_keys(wl: Workload, device, q: torch.Tensor, inv_freq: torch.Tensor,
     return out
 
 
+def make_values(wl: Workload, device, start: int = 0, stop: Optional[int] = None,
+                seed: int = 0) -> torch.Tensor:
+    """Cached value rows [B, Hkv, stop - start, D] in ``wl.dtype`` for the
+    value-weighted recall (qkv / qkv2): normal rows, each scaled by exp(0.7 z),
+    z normal, so that the value norms vary by about 2x either way and change the
+    selection. Chunk-seeded like the keys, so a shard is a slice of the whole."""
+    stop = wl.Sk if stop is None else stop
+    out = torch.empty((wl.B, wl.Hkv, stop - start, wl.D), dtype=wl.dtype, device=device)
+    for c in range(start // CHUNK, (stop - 1) // CHUNK + 1):
+        g = _gen(device, seed * 1_000_003 + 7_000_001 + c)
+        n = min(CHUNK, wl.Sk - c * CHUNK)
+        x = torch.randn((wl.B, wl.Hkv, n, wl.D), generator=g, device=device, dtype=torch.float32)
+        x *= torch.exp(0.7 * torch.randn((wl.B, wl.Hkv, n, 1), generator=g, device=device))
+        a, b = max(start, c * CHUNK), min(stop, c * CHUNK + n)
+        out[:, :, a - start:b - start] = x[:, :, a - c * CHUNK:b - c * CHUNK].to(wl.dtype)
+    return out
+
+
 def make_inputs(wl: Workload, device, seed: int = 0, shard: Optional[tuple] = None) -> dict:
     """All inputs of one scorer call. ``shard=(rank, world)`` keeps only that
     rank's contiguous slice of the keys; ``pos_offset``/``index_base`` then give

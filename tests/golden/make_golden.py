@@ -5,7 +5,8 @@ code (RUSH-Intelligence/Prism-Test, imported read-only from a checkout given by
     eval_harness/attention_methods/_method_base.py  build_cos_sin,
         apply_rotary_pos_emb, undo_rotary_pos_emb
     eval_harness/attention_methods/reattention.py   ReAttentionMethod._dense_topk,
-        ReAttentionMethod._global_unique, ReAttentionMethod._expand_spans
+        ReAttentionMethod._global_unique, ReAttentionMethod._expand_spans,
+        ReAttentionMethod._apply_recall_weight
 
 For each case it draws seeded raw keys and queries, rotates the keys with the
 reference's RoPE (fp32), stores them as bf16 (the dtype the GPU path reads),
@@ -108,6 +109,53 @@ def main() -> None:
         )
         print(name, tuple(q.shape), tuple(k_cached.shape), "topk", topk)
     post_select_cases(ReAttentionMethod)
+    recall_weight_cases(ReAttentionMethod, apply_rotary_pos_emb, build_cos_sin, undo_rotary_pos_emb)
+
+
+# value-weighted recall cases: name, recall_type, B, Hq, Hkv, Sq, Sk, topk, theta, pos_offset, zero_rows
+RECALL_CASES = [
+    ("recall_qkv_gqa_decode", "qkv", 1, 8, 2, 1, 1000, 37, 5e5, 0, 0.0),
+    ("recall_qkv2_multirow", "qkv2", 2, 4, 4, 3, 700, 64, 1e4, 5000, 0.0),
+    ("recall_qkv2_zero_values", "qkv2", 1, 4, 2, 2, 640, 20, 5e5, 100, 0.05),
+]
+
+
+def recall_weight_cases(ReAttentionMethod, apply_rotary_pos_emb, build_cos_sin, undo_rotary_pos_emb) -> None:
+    """Golden vectors of the value-weighted recall: ReAttentionMethod.
+    _apply_recall_weight (reattention.py:822-842) on the fp32 un-rotated keys and
+    bf16 values, then _dense_topk (reattention.py:486-498). Value rows carry a
+    per-row scale (exp of a normal draw) so the weighting changes the selection;
+    ``zero_rows`` of them are zero (weight 0)."""
+    for (name, rt, B, Hq, Hkv, Sq, Sk, topk, theta, pos_offset, zero_rows) in RECALL_CASES:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+        D = 128
+        q = torch.randn(B, Hq, Sq, D, generator=g).to(torch.bfloat16)
+        k_raw = torch.randn(B, Hkv, Sk, D, generator=g)
+        v = torch.randn(B, Hkv, Sk, D, generator=g) * torch.exp(0.7 * torch.randn(B, Hkv, Sk, 1, generator=g))
+        if zero_rows > 0:
+            v[torch.rand(B, Hkv, Sk, generator=g) < zero_rows] = 0.0
+        v = v.to(torch.bfloat16)
+        inv_freq = 1.0 / (theta ** (torch.arange(0, D, 2, dtype=torch.int64).to(torch.float32) / D))
+        pos = torch.arange(pos_offset, pos_offset + Sk)
+        cos, sin = build_cos_sin(pos, inv_freq, torch.device("cpu"), torch.float32)
+        k_cached = apply_rotary_pos_emb(k_raw, cos, sin).to(torch.bfloat16)
+        raw_ref = undo_rotary_pos_emb(k_cached.float(), cos, sin)
+        method = ReAttentionMethod(mid_size=topk, recall_type=rt, use_triton_kernel="off")
+        recall_k = method._apply_recall_weight(raw_ref, v)
+        idx = method._dense_topk(q.float(), recall_k, Sk)
+        n_rep = Hq // Hkv
+        rk = recall_k[:, :, None].expand(B, Hkv, n_rep, Sk, D).reshape(B, Hq, Sk, D)
+        full = torch.einsum("bhqd,bhmd->bhqm", q.float(), rk.float())
+        vals = torch.gather(full, -1, idx)
+        np.savez_compressed(
+            HERE / f"{name}.npz",
+            q_bf16=bf16_bits(q), k_bf16=bf16_bits(k_cached), v_bf16=bf16_bits(v),
+            inv_freq=inv_freq.numpy(), rope=np.array(True), pos_offset=np.array(pos_offset),
+            causal_offset=np.array(-1), topk=np.array(topk), recall_type=np.array(rt),
+            idx=idx.numpy().astype(np.int64), scores=vals.numpy(),
+            raw_keys_ref=np.zeros(0, np.float32),
+        )
+        print(name, rt, tuple(q.shape), tuple(k_cached.shape), "topk", topk)
 
 
 # post-selection cases: name, n_mid, recall_clip, span_size, span_mode, pattern

@@ -16,12 +16,16 @@ import torch
 from oracle import reattention_topk as orc
 
 REL = 1e-3
+# Weighted recall (qkv / qkv2): the key weight is a value-row norm rounded to
+# bf16/fp16 like values.norm; a different fp32 summation order can move that
+# rounding by one step (2^-8 relative for bf16), so weighted scores get 4e-3.
+REL_WEIGHTED = 4e-3
 
 
 def check_parity(idx: torch.Tensor, scores: Optional[torch.Tensor], q: torch.Tensor, k: torch.Tensor,
                  topk: int, inv_freq: Optional[torch.Tensor] = None, pos_offset: int = 0,
                  causal_offset: Optional[int] = None, index_base: int = 0, rel: float = REL,
-                 by_head: bool = False) -> dict:
+                 by_head: bool = False, weights: Optional[torch.Tensor] = None) -> dict:
     """Assert the parity rules; returns a few statistics for reporting."""
     idx = idx.cpu().long() - index_base
     q = q.cpu()
@@ -35,6 +39,8 @@ def check_parity(idx: torch.Tensor, scores: Optional[torch.Tensor], q: torch.Ten
     inv = inv_freq.cpu() if inv_freq is not None else None
     for hk in range(Hkv):
         k_raw = orc.unrotate_keys(k[:, hk:hk + 1], inv, pos_offset)  # [B,1,Sk,D]
+        if weights is not None:  # recall_type qkv / qkv2: raw_k * ||v||
+            k_raw = k_raw * weights.cpu()[:, hk:hk + 1, :, None]
         qh = q[:, hk * G:(hk + 1) * G]
         full = orc.dense_scores(qh, k_raw, causal_offset)  # [B,G,Sq,Sk]
         tol = orc.score_tolerance(qh, k_raw, rel)  # [B,G,Sq,Sk]

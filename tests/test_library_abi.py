@@ -100,3 +100,58 @@ def test_error_maps_to_assertion():
         _lib.check(_lib.PRISM_E_INVALID, "x")
     with pytest.raises(pb.PrismLibraryError):
         _lib.check(_lib.PRISM_E_CUDA, "x")
+
+
+def _call_weighted(lib, **over):
+    args = dict(q=16, k=16, v=16, inv=None, dtype=0, B=1, Hq=4, Hkv=2, Sq=1, Sk=256, D=128, Dv=128,
+                qs=(512, 128, 128, 1), ks=(65536, 32768, 128, 1), vs=(65536, 32768, 128, 1), pos=0,
+                causal=-1, rw=_lib.RECALL_QKV2, topk=8, mode=0, base=0, oi=16, os=None, ws=256,
+                wsb=1 << 20, stream=None)
+    args.update(over)
+    return lib.prism_einsum_topk_weighted(
+        args["q"], args["k"], args["v"], args["inv"], args["dtype"], args["B"], args["Hq"], args["Hkv"],
+        args["Sq"], args["Sk"], args["D"], args["Dv"], _lib.i64_array(args["qs"]),
+        _lib.i64_array(args["ks"]), _lib.i64_array(args["vs"]), args["pos"], args["causal"], args["rw"],
+        args["topk"], args["mode"], args["base"], args["oi"], args["os"], args["ws"], args["wsb"],
+        args["stream"])
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(rw=3), _lib.PRISM_E_INVALID),                               # unknown weighting
+    (dict(v=None), _lib.PRISM_E_INVALID),
+    (dict(Dv=100, vs=(51200, 25600, 100, 1)), _lib.PRISM_E_UNSUPPORTED),  # Dv % 8
+    (dict(vs=(65536, 32768, 128, 2)), _lib.PRISM_E_INVALID),          # inner stride
+    (dict(v=8), _lib.PRISM_E_INVALID),                                # misaligned base
+    (dict(vs=(65536, 32768, 132, 1)), _lib.PRISM_E_INVALID),          # key stride not 16-byte
+    (dict(q=None), _lib.PRISM_E_INVALID),                             # shared checks still apply
+    (dict(wsb=100), _lib.PRISM_E_WORKSPACE),
+    (dict(rw=_lib.RECALL_QK, v=None, topk=0), _lib.PRISM_E_INVALID),  # qk ignores v
+])
+def test_weighted_argument_validation(lib, over, code):
+    rc = _call_weighted(lib, **over)
+    assert rc == code, (rc, _lib.last_error())
+    assert _lib.last_error()
+
+
+def test_recall_type_errors_match_reference():
+    # the messages of ReAttentionMethod._apply_recall_weight (reattention.py:834-842)
+    from prism_test_b200.kernels import _recall_weight_code
+    assert _recall_weight_code("qk") == _lib.RECALL_QK
+    assert _recall_weight_code("qkv") == _lib.RECALL_QKV
+    assert _recall_weight_code("qkv2") == _lib.RECALL_QKV2
+    with pytest.raises(ValueError, match="'_pe' variants are not implemented"):
+        _recall_weight_code("qkv2_pe")
+    with pytest.raises(ValueError, match="Use one of: qk, qkv, qkv2"):
+        _recall_weight_code("k")
+
+
+def test_weighted_workspace_size(lib):
+    base = lib.prism_einsum_topk_workspace_size(1, 32, 1, 131072, 4096, 0)
+    assert lib.prism_einsum_topk_weighted_workspace_size(1, 32, 8, 1, 131072, 4096, 0, _lib.RECALL_QK) == base
+    # weights [B * Hkv, Sk rounded to 4] fp32 after the 256-byte aligned base
+    want = (base + 255) // 256 * 256 + 8 * 131072 * 4
+    assert lib.prism_einsum_topk_weighted_workspace_size(1, 32, 8, 1, 131072, 4096, 0, _lib.RECALL_QKV2) == want
+    odd = lib.prism_einsum_topk_workspace_size(1, 4, 5, 1001, 3, 0)
+    got = lib.prism_einsum_topk_weighted_workspace_size(1, 4, 2, 5, 1001, 3, 0, _lib.RECALL_QKV)
+    assert got == (odd + 255) // 256 * 256 + (2 * 1004 * 4 + 255) // 256 * 256
+    assert lib.prism_einsum_topk_weighted_workspace_size(1, 4, 2, 5, 1001, 3, 0, 9) == 0

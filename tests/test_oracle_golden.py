@@ -8,7 +8,7 @@ import torch
 
 from oracle import reattention_topk as orc
 
-GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith("post_"))
+GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith(("post_", "recall_")))
 
 
 def load_case(path):
@@ -100,3 +100,32 @@ def test_post_select_oracle_matches_reference(path):
     sel = orc.global_unique(idx, int(z["recall_clip"]))
     out = orc.expand_spans(sel, int(z["n_mid"]), int(z["span"]), str(z["mode"]))
     assert torch.equal(out, torch.from_numpy(z["out"]))
+
+
+RECALL = sorted((Path(__file__).resolve().parent / "golden").glob("recall_*.npz"))
+
+
+def test_recall_golden_present():
+    assert len(RECALL) >= 3
+
+
+@pytest.mark.parametrize("path", RECALL, ids=[p.stem for p in RECALL])
+def test_recall_weight_oracle_matches_reference(path):
+    """orc.recall_weights + dense_topk against ReAttentionMethod._apply_recall_weight
+    + _dense_topk (reattention.py:822-842, 486-498): bit-identical."""
+    z = np.load(path)
+    c = load_case(path)
+    v = torch.from_numpy(z["v_bf16"].view(np.int16)).view(torch.bfloat16)
+    w = orc.recall_weights(v, str(z["recall_type"]))
+    vals, idx = orc.dense_topk(c["q"], c["k"], c["topk"], c["inv_freq"], c["pos_offset"], weights=w)
+    assert torch.equal(vals, c["scores"])
+    assert torch.equal(idx, c["idx"])
+
+
+def test_recall_weights_types():
+    v = torch.tensor([[[[3.0, -4.0], [0.0, 0.0]]]]).to(torch.bfloat16)
+    assert orc.recall_weights(v, "qk") is None
+    assert orc.recall_weights(v, "qkv").tolist() == [[[7.0, 0.0]]]
+    assert orc.recall_weights(v, "qkv2").tolist() == [[[5.0, 0.0]]]
+    with pytest.raises(ValueError):
+        orc.recall_weights(v, "qkv_pe")

@@ -18,9 +18,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _cpu_local(q, k, kl, inv_freq=None, pos_offset=0, index_base=0, return_scores=True):
+def _cpu_local(q, k, kl, inv_freq=None, pos_offset=0, index_base=0, return_scores=True, values=None,
+               recall_type="qk"):
     from oracle import reattention_topk as orc
-    vals, idx = orc.dense_topk(q, k, kl, inv_freq, pos_offset, None, index_base)
+    vals, idx = orc.dense_topk(q, k, kl, inv_freq, pos_offset, None, index_base,
+                               weights=orc.recall_weights(values, recall_type))
     return idx.to(torch.int32), vals
 
 
@@ -31,7 +33,7 @@ def _put_and_exit(q, item):
     os._exit(0)
 
 
-def _worker(rank, world, port, case, q, k_full, inv, topk, errq):
+def _worker(rank, world, port, case, q, k_full, inv, topk, errq, v_full=None):
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -42,10 +44,12 @@ def _worker(rank, world, port, case, q, k_full, inv, topk, errq):
         start, stop = shard_bounds(k_full.shape[2], rank, world)
         if case == "die" and rank == 1:
             os._exit(0)  # leaves between steps, before the exchange
+        rt = "qkv2" if case == "qkv2" else "qk"
+        v_shard = v_full[:, :, start:stop] if v_full is not None else None
         try:
             idx, sc = sharded_einsum_topk(q, k_full[:, :, start:stop], topk, shard_start=start,
                                           inv_freq=inv, return_scores=True, local_topk=_cpu_local,
-                                          merge=merge_candidates_torch)
+                                          merge=merge_candidates_torch, v_shard=v_shard, recall_type=rt)
         except Exception as e:  # noqa: BLE001
             if case == "die":
                 _put_and_exit(errq, ("ok-error", rank, type(e).__name__))
@@ -54,7 +58,8 @@ def _worker(rank, world, port, case, q, k_full, inv, topk, errq):
             _put_and_exit(errq, ("no-error", rank, ""))
         from oracle import reattention_topk as orc
         from tests.parity import check_parity
-        check_parity(idx, sc, q, k_full, topk, inv, 0)
+        w = orc.recall_weights(v_full, rt)
+        check_parity(idx, sc, q, k_full, topk, inv, 0, weights=w)
         errq.put(("ok", rank, ""))
         dist.destroy_process_group()
     except Exception:  # noqa: BLE001
@@ -69,10 +74,12 @@ def _run(world, case, Sk, topk, seed=0):
     from prism_test_b200.workloads import apply_rope, rope_cos_sin
     cos, sin = rope_cos_sin(torch.arange(Sk), inv)
     k = apply_rope(raw, cos, sin).to(torch.bfloat16)
+    v = (torch.randn(1, 2, Sk, 128, generator=g) * torch.exp(0.7 * torch.randn(1, 2, Sk, 1, generator=g))
+         ).to(torch.bfloat16) if case == "qkv2" else None
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q, k, inv, topk, errq)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q, k, inv, topk, errq, v)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -90,6 +97,13 @@ def _run(world, case, Sk, topk, seed=0):
 def test_sharded_matches_oracle(world, Sk, topk):
     res = _run(world, "ok", Sk, topk)
     assert sorted(r[1] for r in res) == list(range(world)), res
+    for status, rank, msg in res:
+        assert status == "ok", msg
+
+
+def test_sharded_value_weighted_matches_oracle():
+    res = _run(2, "qkv2", 1000, 60, seed=4)
+    assert sorted(r[1] for r in res) == [0, 1], res
     for status, rank, msg in res:
         assert status == "ok", msg
 
