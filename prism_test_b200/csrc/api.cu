@@ -233,6 +233,10 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
     e = launch_counted(PRISM_KERNEL_SCORE, stream,
                        [&] { return prism::launch_decode_scores_wide(a, dtype, nsm, stream); });
     if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
+  } else if (prism::prefill_tc_supported(a)) {
+    e = launch_counted(PRISM_KERNEL_SCORE, stream,
+                       [&] { return prism::launch_prefill_scores_tc(a, dtype, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "prefill score kernel launch");
   } else if (prism::decode_g4_supported(a)) {
     e = launch_counted(PRISM_KERNEL_SCORE, stream,
                        [&] { return prism::launch_decode_scores_g4(a, dtype, nsm, stream); });

@@ -56,6 +56,12 @@ bool decode_g4_supported(const DecodeArgs& a);
 cudaError_t launch_decode_scores_g4(const DecodeArgs& a, int dtype, int num_sms,
                                     cudaStream_t stream);
 
+// Tensor-core (tcgen05) scorer for raw keys (inv_freq == nullptr) and at least
+// kPrefillMinRows query rows per KV head; q rows 16-byte aligned.
+constexpr int kPrefillMinRows = 128;
+bool prefill_tc_supported(const DecodeArgs& a);
+cudaError_t launch_prefill_scores_tc(const DecodeArgs& a, int dtype, cudaStream_t stream);
+
 // --- exact per-row top-k selection over a score matrix ----------------------
 struct SelectArgs {
   const float* scores;      // [rows, ld]

@@ -41,4 +41,22 @@ cudaError_t make_key_tensor_map(CUtensorMap* map, const void* k, int dtype, int6
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+cudaError_t make_key_tensor_map_sw128(CUtensorMap* map, const void* k, int dtype, int64_t B,
+                                      int64_t Hkv, int64_t Sk, int64_t k_sb, int64_t k_sh) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (fn == nullptr) return cudaErrorNotSupported;
+  const bool batched = B > 1 && k_sb != 0;
+  cuuint64_t dims[4] = {128, cuuint64_t(Sk), cuuint64_t(Hkv), cuuint64_t(batched ? B : 1)};
+  cuuint64_t strides[3] = {256, cuuint64_t(k_sh) * 2,
+                           cuuint64_t(batched ? k_sb : k_sh * Hkv) * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 4, const_cast<void*>(k), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace prism

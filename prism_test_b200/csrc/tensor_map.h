@@ -19,4 +19,10 @@ cudaError_t make_key_tensor_map(CUtensorMap* map, const void* k, int dtype, int6
                                 int64_t Sk, int64_t k_sb, int64_t k_sh, int box_rows,
                                 int box_heads = 0);
 
+// The same key cache as a K-major tensor-core operand: box {64, 128, 1, 1} (64
+// dimensions x 128 positions of one KV head = one 16 KB atom per copy), written
+// to shared memory in the 128-byte swizzle mode.
+cudaError_t make_key_tensor_map_sw128(CUtensorMap* map, const void* k, int dtype, int64_t B,
+                                      int64_t Hkv, int64_t Sk, int64_t k_sb, int64_t k_sh);
+
 }  // namespace prism
