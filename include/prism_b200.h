@@ -38,6 +38,7 @@ extern "C" {
 /* selection modes */
 #define PRISM_MODE_EXACT 0    /* exact top-k of the fp32 scores (torch.topk semantics) */
 #define PRISM_MODE_BLOCKMAX 1 /* per-128-key-block maxima, top-1 / top-4 (Triton kernel semantics) */
+#define PRISM_MODE_EXACT_STREAM 2 /* exact, without a score matrix (prefill chunks; see below) */
 
 /* status codes */
 #define PRISM_OK 0
@@ -72,6 +73,15 @@ extern "C" {
  *              (invisible keys score -inf); < 0: no mask.
  *   topk       1 <= topk <= Sk, and topk <= 16384 (exact mode);
  *              topk in {1, 4} with Sq % 128 == 0 and Sk % 128 == 0 (blockmax mode).
+ *   mode       PRISM_MODE_EXACT, PRISM_MODE_BLOCKMAX or PRISM_MODE_EXACT_STREAM.
+ *              The streaming path gives the exact-mode result without writing
+ *              the B*Hq*Sq x Sk score matrix: per-row thresholds from a strided
+ *              key sample, the keys at or above them, a selection per row, and
+ *              an exact recompute of any row the threshold missed. Exact mode
+ *              takes it by itself when Sq >= 128, Sk >= 8192, topk <= 4096 and
+ *              the score matrix would be 2 GiB or more; it needs raw keys
+ *              (inv_freq NULL), at least 128 query rows per KV head, 16-byte
+ *              aligned query rows and topk <= 4096 (PRISM_E_UNSUPPORTED otherwise).
  *   index_base added to every output index (global index of key 0 of this shard).
  *   out_idx    [B, Hq, Sq, topk] int32, contiguous. Sorted by descending score,
  *              ties by ascending index.

@@ -25,6 +25,7 @@ KERNEL_SELECT = 1
 KERNEL_MERGE = 2
 MODE_EXACT = 0
 MODE_BLOCKMAX = 1
+MODE_EXACT_STREAM = 2
 SPAN_CENTERED = 0
 SPAN_FLOOR = 1
 KERNEL_WEIGHT = 3

@@ -86,6 +86,22 @@ size_t exact_workspace(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk) {
   return kStatusBytes + round_up(int64_t(scores_bytes(rows, Sk)), 256) +
          prism::select_workspace_bytes(rows, Sk);
 }
+// Exact mode switches to the streaming prefill path (no score matrix) when the
+// matrix would reach 2 GiB on a prefill-shaped call; PRISM_MODE_EXACT_STREAM
+// asks for it at any size.
+constexpr int64_t kStreamMinTopk = 4096;  // streaming path: topk <= this
+bool auto_stream(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk, int32_t topk) {
+  const double bytes = double(B) * double(Hq) * double(Sq) * double(round_up(Sk, 4)) * 4.0;
+  return Sq >= prism::kPrefillMinRows && topk <= kStreamMinTopk && Sk >= 8192 &&
+         bytes >= double(int64_t(1) << 31);
+}
+bool use_stream(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk, int32_t topk, int32_t mode) {
+  return mode == PRISM_MODE_EXACT_STREAM ||
+         (mode == PRISM_MODE_EXACT && auto_stream(B, Hq, Sq, Sk, topk));
+}
+size_t stream_workspace(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk, int32_t topk) {
+  return kStatusBytes + prism::prefill_stream_workspace_bytes(B * Hq * Sq, Sk, topk);
+}
 // the value-norm weights of the weighted call follow, 256-byte aligned
 size_t weights_offset(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk) {
   return size_t(round_up(int64_t(exact_workspace(B, Hq, Sq, Sk)), 256));
@@ -105,9 +121,13 @@ const char* prism_last_error(void) { return g_last_error.c_str(); }
 
 size_t prism_einsum_topk_workspace_size(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk,
                                         int32_t topk, int32_t mode) {
-  (void)topk;
   if (B <= 0 || Hq <= 0 || Sq <= 0 || Sk <= 0) return 0;
-  if (mode != PRISM_MODE_EXACT && mode != PRISM_MODE_BLOCKMAX) return 0;
+  if (mode != PRISM_MODE_EXACT && mode != PRISM_MODE_BLOCKMAX && mode != PRISM_MODE_EXACT_STREAM)
+    return 0;
+  if (use_stream(B, Hq, Sq, Sk, topk, mode)) {
+    if (topk < 1 || topk > kStreamMinTopk) return 0;
+    return stream_workspace(B, Hq, Sq, Sk, topk);
+  }
   return exact_workspace(B, Hq, Sq, Sk);
 }
 
@@ -138,7 +158,7 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
   if ((reinterpret_cast<uintptr_t>(k) & 15u) != 0 || (k_strides[0] * 2) % 16 != 0 ||
       (k_strides[1] * 2) % 16 != 0)
     return fail(PRISM_E_INVALID, "k base and batch/head strides must be 16-byte aligned");
-  if (mode != PRISM_MODE_EXACT && mode != PRISM_MODE_BLOCKMAX)
+  if (mode != PRISM_MODE_EXACT && mode != PRISM_MODE_BLOCKMAX && mode != PRISM_MODE_EXACT_STREAM)
     return fail(PRISM_E_INVALID, "unknown mode %d", mode);
   if (mode == PRISM_MODE_BLOCKMAX && topk != 1 && topk != 4)
     return fail(PRISM_E_INVALID, "blockmax mode supports topk 1 or 4, got %d", topk);
@@ -158,8 +178,28 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
   if (Hq > prism::kDecodeMaxRows)
     return fail(PRISM_E_UNSUPPORTED, "more than %d query heads", prism::kDecodeMaxRows);
 
-  const size_t need = weight ? weights_offset(B, Hq, Sq, Sk) + prism::weight_workspace_bytes(B, Hkv, Sk)
-                            : exact_workspace(B, Hq, Sq, Sk);
+  const bool streaming = use_stream(B, Hq, Sq, Sk, topk, mode);
+  if (streaming) {
+    if (topk > kStreamMinTopk)
+      return fail(PRISM_E_UNSUPPORTED, "the streaming prefill path takes topk <= %lld, got %d",
+                  (long long)kStreamMinTopk, topk);
+    if (inv_freq)
+      return fail(PRISM_E_UNSUPPORTED,
+                  "the streaming prefill path (score matrix of 2 GiB or more, or "
+                  "PRISM_MODE_EXACT_STREAM) takes raw keys: pass inv_freq = NULL");
+    if (weight)
+      return fail(PRISM_E_UNSUPPORTED, "value-weighted recall is not available on the streaming "
+                                       "prefill path");
+    if ((Hq / Hkv) * Sq < prism::kPrefillMinRows)
+      return fail(PRISM_E_UNSUPPORTED, "the streaming prefill path needs at least %d query rows "
+                                       "per KV head", prism::kPrefillMinRows);
+    if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0 || q_strides[0] % 8 || q_strides[1] % 8 ||
+        q_strides[2] % 8)
+      return fail(PRISM_E_INVALID, "the streaming prefill path needs 16-byte aligned query rows");
+  }
+  const size_t need = streaming ? stream_workspace(B, Hq, Sq, Sk, topk)
+                      : weight ? weights_offset(B, Hq, Sq, Sk) + prism::weight_workspace_bytes(B, Hkv, Sk)
+                               : exact_workspace(B, Hq, Sq, Sk);
   if (!workspace || workspace_bytes < need)
     return fail(PRISM_E_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
@@ -221,6 +261,15 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
   // specialised kernels take every query row of a KV head in one launch:
   // tensor-core tiles (keys as M for <= 16 rows per KV head, queries as M up
   // to 256 / Hkv rows), CUDA cores for <= 4
+  if (streaming) {  // thresholds, candidates, per-row selection, exact fallback: 6 kernels
+    e = launch_counted(PRISM_KERNEL_SCORE, stream, [&] {
+      return prism::launch_prefill_topk(a, dtype, topk, index_base, out_idx, out_scores,
+                                        ws + kStatusBytes, nsm, stream);
+    });
+    if (e != cudaSuccess) return cuda_fail(e, "streaming prefill launch");
+    g_launches.fetch_add(5, std::memory_order_relaxed);
+    return PRISM_OK;
+  }
   if (prism::decode_hp_supported(a, dtype)) {
     e = launch_counted(PRISM_KERNEL_SCORE, stream,
                        [&] { return prism::launch_decode_scores_hp(a, nsm, stream); });

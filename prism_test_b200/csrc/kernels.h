@@ -62,6 +62,24 @@ constexpr int kPrefillMinRows = 128;
 bool prefill_tc_supported(const DecodeArgs& a);
 cudaError_t launch_prefill_scores_tc(const DecodeArgs& a, int dtype, cudaStream_t stream);
 
+// Streaming prefill top-k (no score matrix): per-row thresholds from a strided
+// key sample (every kSampleStride-th key), then the candidates >= threshold,
+// then an exact selection per row with an exact recompute of rows whose
+// candidates fell outside [min(k, visible keys), cap].
+constexpr int kSampleStride = 16;
+cudaError_t launch_prefill_threshold_tc(const DecodeArgs& a, int dtype, int topk, float* thr,
+                                        cudaStream_t stream);
+cudaError_t launch_prefill_candidates_tc(const DecodeArgs& a, int dtype, const float* thr,
+                                         uint32_t* counts, uint64_t* cand, int64_t cap,
+                                         cudaStream_t stream);
+int64_t prefill_cand_cap(int64_t Sk, int topk);
+size_t prefill_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk);
+// The whole streaming path: thresholds, candidates, selection, fallback.
+// `ws` holds prefill_stream_workspace_bytes(rows, Sk, topk) bytes (256-aligned).
+cudaError_t launch_prefill_topk(const DecodeArgs& a, int dtype, int topk, int64_t index_base,
+                                int32_t* out_idx, float* out_scores, void* ws, int num_sms,
+                                cudaStream_t stream);
+
 // --- exact per-row top-k selection over a score matrix ----------------------
 struct SelectArgs {
   const float* scores;      // [rows, ld]
@@ -74,6 +92,7 @@ struct SelectArgs {
   int32_t* out_idx;         // [rows, k]
   float* out_scores;        // [rows, k] or nullptr
   int* status;
+  const int* rows_dyn;      // nullptr, or a device count: rows >= *rows_dyn are skipped
 };
 constexpr int kSelectMaxK = 16384;
 

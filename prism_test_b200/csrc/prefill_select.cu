@@ -1,0 +1,395 @@
+// Streaming top-k of the prefill chunk: the exact per-row selection over the
+// candidates that prefill_tc.cu's kCand pass left (keys scoring at or above a
+// sampled per-row threshold), so that the B * Hq * Sq x Sk score matrix is never
+// written. Result: the top-k of each row sorted like torch.topk (descending
+// score, ties by ascending index) — _dense_topk, reattention.py:486-498, with the
+// causal mask of the chunk; a row that sees fewer than k keys continues with its
+// masked keys (-inf) in ascending index order, as the score-matrix path does.
+//
+// prefill_select_kernel, one 256-thread CTA per row: the row's n candidates
+// (packed (order-preserving score key << 32) | ~index, so larger = earlier) are
+// loaded into shared memory and counting-sorted into 2048 fine bins, linear in
+// the score between the row's largest and smallest candidate (NaN, which ranks
+// first, in bin 0; linear in the value, not in the packed key, whose spacing
+// explodes around zero); a candidate's output position is its bin's start plus
+// the number of bin members above it. Rows whose candidate count lies
+// outside [min(k, visible keys), cap] (a threshold too high or too low for the
+// row), or whose fine bins hold more than kRankMax members (massive ties), are
+// listed for the exact fallback: all their scores recomputed on CUDA cores into
+// a scratch row, the library's general selection on those rows, and a copy of
+// the results into place. At most kFallbackRows rows per call can take the
+// fallback; more set kStatusCapacity.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace prism {
+namespace {
+
+constexpr int kPsThreads = 256;
+constexpr int kPsBins = 2048;
+constexpr int kPsRankMax = 64;
+constexpr int kFallbackRows = 64;
+
+struct PsArgs {
+  const uint64_t* cand;
+  const uint32_t* counts;
+  int64_t cap;
+  int k;
+  int64_t Sk;
+  int Sq;
+  int causal;
+  int64_t causal_offset;
+  int64_t index_base;
+  int32_t* out_idx;
+  float* out_scores;
+  int* nflag;
+  int32_t* flag_rows;
+  int* status;
+};
+
+__device__ __forceinline__ int64_t visible_keys(int64_t row, int Sq, int causal,
+                                                int64_t causal_offset, int64_t Sk) {
+  if (!causal) return Sk;
+  const int64_t v = causal_offset + row % Sq + 1;
+  return v < 0 ? 0 : (v < Sk ? v : Sk);
+}
+
+__device__ __forceinline__ void flag_row(const PsArgs& a, int64_t row) {
+  const int slot = atomicAdd(a.nflag, 1);
+  if (slot < kFallbackRows)
+    a.flag_rows[slot] = int32_t(row);
+  else
+    set_status(a.status, kStatusCapacity);
+}
+
+// exclusive block scan of one value per thread (256 threads)
+__device__ __forceinline__ uint32_t ps_scan(uint32_t v, uint32_t* wtot, uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wtot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < kPsThreads / 32 ? wtot[lane] : 0u;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < kPsThreads / 32) wtot[lane] = w;
+  }
+  __syncthreads();
+  const uint32_t r = (warp ? wtot[warp - 1] : 0u) + x - v;
+  *total = wtot[kPsThreads / 32 - 1];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint64_t* buf = reinterpret_cast<uint64_t*>(smem);                       // [cap]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(buf + a.cap);               // [kPsBins]
+  uint16_t* perm = reinterpret_cast<uint16_t*>(hist + kPsBins);            // [cap]
+  __shared__ uint32_t wtot[kPsThreads / 32];
+  __shared__ uint32_t s_kmax, s_kmin, s_big;  // max / min key of the finite scores
+
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const uint32_t n = a.counts[row];
+  const int64_t nvis = visible_keys(row, a.Sq, a.causal, a.causal_offset, a.Sk);
+  const uint32_t keff = uint32_t(nvis < a.k ? nvis : a.k);
+  int32_t* oi = a.out_idx + row * a.k;
+  float* os = a.out_scores ? a.out_scores + row * a.k : nullptr;
+  if (n > uint32_t(a.cap) || n < keff) {
+    if (tid == 0) flag_row(a, row);
+    return;
+  }
+  // masked keys after the visible ones (rows that see fewer than k keys)
+  for (uint32_t p = keff + tid; p < uint32_t(a.k); p += kPsThreads) {
+    oi[p] = int32_t(nvis + (p - keff) + a.index_base);
+    if (os) os[p] = -INFINITY;
+  }
+  if (keff == 0) return;
+  if (tid == 0) {
+    s_kmax = 0u;
+    s_kmin = 0xffffffffu;
+    s_big = 0u;
+  }
+  for (int i = tid; i < kPsBins; i += kPsThreads) hist[i] = 0u;
+  __syncthreads();
+  const uint64_t* src = a.cand + row * a.cap;
+  uint32_t kmx = 0u, kmn = 0xffffffffu;
+  for (uint32_t i = tid; i < n; i += kPsThreads) {
+    const uint64_t x = src[i];
+    buf[i] = x;
+    const uint32_t key = uint32_t(x >> 32);
+    if (key != 0xffffffffu) {  // NaN is binned apart
+      kmx = max(kmx, key);
+      kmn = min(kmn, key);
+    }
+  }
+  kmx = __reduce_max_sync(0xffffffffu, kmx);
+  kmn = __reduce_min_sync(0xffffffffu, kmn);
+  if (lane == 0) {
+    atomicMax(&s_kmax, kmx);
+    atomicMin(&s_kmin, kmn);
+  }
+  __syncthreads();
+  const float fmax = okey_to_float(s_kmax), fmin = okey_to_float(s_kmin);
+  const float scale = fmax > fmin ? float(kPsBins - 1) / (fmax - fmin) : 0.f;
+  // bin of a packed candidate: monotone non-increasing in its score
+  auto bin_of = [&](uint64_t x) -> uint32_t {
+    const uint32_t key = uint32_t(x >> 32);
+    if (key == 0xffffffffu) return 0u;
+    const float b = (fmax - okey_to_float(key)) * scale;
+    return b >= float(kPsBins - 1) ? uint32_t(kPsBins - 1) : (b > 0.f ? uint32_t(b) : 0u);
+  };
+  for (uint32_t i = tid; i < n; i += kPsThreads) atomicAdd(&hist[bin_of(buf[i])], 1u);
+  __syncthreads();
+  {
+    constexpr int kPer = kPsBins / kPsThreads;
+    uint32_t h[kPer], tot = 0, hmax = 0;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      h[u] = hist[kPer * tid + u];
+      tot += h[u];
+      hmax = max(hmax, h[u]);
+    }
+    hmax = __reduce_max_sync(0xffffffffu, hmax);
+    if (lane == 0) atomicMax(&s_big, hmax);
+    uint32_t total;
+    uint32_t ex = ps_scan(tot, wtot, &total);
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      hist[kPer * tid + u] = ex;  // start of bin
+      ex += h[u];
+    }
+  }
+  __syncthreads();
+  if (s_big > uint32_t(kPsRankMax)) {  // massive ties: exact recompute of the row
+    if (tid == 0) flag_row(a, row);
+    return;
+  }
+  for (uint32_t i = tid; i < n; i += kPsThreads) perm[atomicAdd(&hist[bin_of(buf[i])], 1u)] = uint16_t(i);
+  __syncthreads();  // hist[f] is now the end of bin f
+  // candidates in the bins that hold output positions [0, keff)
+  uint32_t fend = 0;  // first bin whose start is >= keff
+  {
+    uint32_t lo = 0, hi = kPsBins;  // smallest f with end(f) >= keff
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (hist[mid] >= keff) hi = mid; else lo = mid + 1;
+    }
+    fend = lo;
+  }
+  const uint32_t qend = hist[fend < kPsBins ? fend : kPsBins - 1];
+  for (uint32_t q = tid; q < qend; q += kPsThreads) {
+    const uint32_t i = perm[q];
+    const uint64_t x = buf[i];
+    const uint32_t f = bin_of(x);
+    const uint32_t s = f ? hist[f - 1] : 0u;
+    const uint32_t e = hist[f];
+    uint32_t p = s;
+    for (uint32_t j = s; j < e; ++j) p += buf[perm[j]] > x;
+    if (p < keff) {
+      oi[p] = int32_t(int64_t(~uint32_t(x)) + a.index_base);
+      if (os) os[p] = okey_to_float(uint32_t(x >> 32));
+    }
+  }
+}
+
+// Exact scores of the listed rows (CUDA cores): scratch[slot, j] for every key j
+// (masked keys -inf). Block 0 also publishes the number of listed rows it will
+// serve (min(nflag, kFallbackRows)).
+template <typename T>
+__global__ void __launch_bounds__(256)
+    fallback_scores_kernel(const DecodeArgs a, const int* nflag, const int32_t* flag_rows,
+                           int* nserve, float* scratch) {
+  __shared__ float qs[128];
+  const int nf = *nflag < kFallbackRows ? *nflag : kFallbackRows;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *nserve = nf;
+  const int slot = blockIdx.x;
+  if (slot >= nf) return;
+  const int64_t row = flag_rows[slot];
+  const int s = int(row % a.Sq);
+  const int64_t bhq = row / a.Sq;
+  const int hq = int(bhq % a.Hq), b = int(bhq / a.Hq);
+  const int kvh = hq / a.G;
+  const T* qr = static_cast<const T*>(a.q) + int64_t(b) * a.q_sb + int64_t(hq) * a.q_sh +
+                int64_t(s) * a.q_ss;
+  if (threadIdx.x < 128) qs[threadIdx.x] = to_f32<T>(qr[threadIdx.x]);
+  __syncthreads();
+  int64_t nvis = a.Sk;
+  if (a.causal) {
+    const int64_t v = a.causal_offset + s + 1;
+    nvis = v < 0 ? 0 : (v < a.Sk ? v : a.Sk);
+  }
+  const T* kb = static_cast<const T*>(a.k) + (a.B > 1 ? int64_t(b) * a.k_sb : 0) +
+                int64_t(kvh) * a.k_sh;
+  float* out = scratch + int64_t(slot) * a.ld;
+  for (int64_t j = threadIdx.x; j < a.Sk; j += 256) {
+    if (j >= nvis) {
+      out[j] = -INFINITY;
+      continue;
+    }
+    const uint4* kr = reinterpret_cast<const uint4*>(kb + j * 128);
+    float acc = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < 16; ++c) {
+      const uint4 u = kr[c];
+      float x0, x1, x2, x3, x4, x5, x6, x7;
+      Unpack<T>::run(u.x, x0, x1);
+      Unpack<T>::run(u.y, x2, x3);
+      Unpack<T>::run(u.z, x4, x5);
+      Unpack<T>::run(u.w, x6, x7);
+      const float* qq = qs + 8 * c;
+      acc = fmaf(qq[0], x0, acc);
+      acc = fmaf(qq[1], x1, acc);
+      acc = fmaf(qq[2], x2, acc);
+      acc = fmaf(qq[3], x3, acc);
+      acc = fmaf(qq[4], x4, acc);
+      acc = fmaf(qq[5], x5, acc);
+      acc = fmaf(qq[6], x6, acc);
+      acc = fmaf(qq[7], x7, acc);
+    }
+    out[j] = acc;
+  }
+}
+
+__global__ void fallback_scatter_kernel(const int* nserve, const int32_t* flag_rows, int k,
+                                        const int32_t* cidx, const float* csc, int32_t* out_idx,
+                                        float* out_scores) {
+  const int slot = blockIdx.x;
+  if (slot >= *nserve) return;
+  const int64_t row = flag_rows[slot];
+  for (int p = threadIdx.x; p < k; p += blockDim.x) {
+    out_idx[row * k + p] = cidx[int64_t(slot) * k + p];
+    if (out_scores) out_scores[row * k + p] = csc[int64_t(slot) * k + p];
+  }
+}
+
+size_t up256(size_t x) { return (x + 255) / 256 * 256; }
+
+struct PsLayout {
+  size_t thr, counts, cand, flags, flag_rows, scratch, sel_ws, cidx, csc, total;
+};
+
+PsLayout ps_layout(int64_t rows, int64_t Sk, int topk) {
+  PsLayout L{};
+  const int64_t cap = prefill_cand_cap(Sk, topk);
+  const int64_t ld = (Sk + 3) / 4 * 4;
+  size_t o = 0;
+  L.thr = o;
+  o += up256(size_t(rows) * 4);
+  L.counts = o;
+  o += up256(size_t(rows) * 4);
+  L.cand = o;
+  o += up256(size_t(rows) * size_t(cap) * 8);
+  L.flags = o;  // nflag, nserve
+  o += 256;
+  L.flag_rows = o;
+  o += up256(kFallbackRows * 4);
+  L.scratch = o;
+  o += up256(size_t(kFallbackRows) * size_t(ld) * 4);
+  L.sel_ws = o;
+  o += up256(select_workspace_bytes(kFallbackRows, Sk));
+  L.cidx = o;
+  o += up256(size_t(kFallbackRows) * size_t(topk) * 4);
+  L.csc = o;
+  o += up256(size_t(kFallbackRows) * size_t(topk) * 4);
+  L.total = o;
+  return L;
+}
+
+}  // namespace
+
+int64_t prefill_cand_cap(int64_t Sk, int topk) {
+  const int64_t c = 2 * int64_t(topk) + 2048;
+  return c < Sk ? c : Sk;
+}
+
+size_t prefill_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk) {
+  return ps_layout(rows, Sk, topk).total;
+}
+
+cudaError_t launch_prefill_topk(const DecodeArgs& d, int dtype, int topk, int64_t index_base,
+                                int32_t* out_idx, float* out_scores, void* ws, int num_sms,
+                                cudaStream_t stream) {
+  (void)num_sms;
+  const int64_t rows = int64_t(d.B) * d.Hq * d.Sq;
+  const PsLayout L = ps_layout(rows, d.Sk, topk);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  float* thr = reinterpret_cast<float*>(w + L.thr);
+  uint32_t* counts = reinterpret_cast<uint32_t*>(w + L.counts);
+  uint64_t* cand = reinterpret_cast<uint64_t*>(w + L.cand);
+  int* nflag = reinterpret_cast<int*>(w + L.flags);
+  int* nserve = nflag + 1;
+  int32_t* flag_rows = reinterpret_cast<int32_t*>(w + L.flag_rows);
+  float* scratch = reinterpret_cast<float*>(w + L.scratch);
+  int32_t* cidx = reinterpret_cast<int32_t*>(w + L.cidx);
+  float* csc = reinterpret_cast<float*>(w + L.csc);
+  const int64_t cap = prefill_cand_cap(d.Sk, topk);
+
+  cudaError_t e = cudaMemsetAsync(nflag, 0, 2 * sizeof(int), stream);
+  if (e != cudaSuccess) return e;
+  e = launch_prefill_threshold_tc(d, dtype, topk, thr, stream);
+  if (e != cudaSuccess) return e;
+  e = launch_prefill_candidates_tc(d, dtype, thr, counts, cand, cap, stream);
+  if (e != cudaSuccess) return e;
+
+  PsArgs p{};
+  p.cand = cand;
+  p.counts = counts;
+  p.cap = cap;
+  p.k = topk;
+  p.Sk = d.Sk;
+  p.Sq = d.Sq;
+  p.causal = d.causal;
+  p.causal_offset = d.causal_offset;
+  p.index_base = index_base;
+  p.out_idx = out_idx;
+  p.out_scores = out_scores;
+  p.nflag = nflag;
+  p.flag_rows = flag_rows;
+  p.status = d.status;
+  const size_t smem = size_t(cap) * 10 + kPsBins * 4;
+  e = cudaFuncSetAttribute(prefill_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(smem));
+  if (e != cudaSuccess) return e;
+  prefill_select_kernel<<<dim3(unsigned(rows)), kPsThreads, smem, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+
+  // exact fallback for the listed rows (kernels return at once when none are)
+  if (dtype == kBF16)
+    fallback_scores_kernel<__nv_bfloat16><<<kFallbackRows, 256, 0, stream>>>(d, nflag, flag_rows,
+                                                                            nserve, scratch);
+  else
+    fallback_scores_kernel<__half><<<kFallbackRows, 256, 0, stream>>>(d, nflag, flag_rows, nserve,
+                                                                     scratch);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  SelectArgs s{};
+  s.scores = scratch;
+  s.idx_in = nullptr;
+  s.rows = kFallbackRows;
+  s.n = d.Sk;
+  s.ld = d.ld;
+  s.k = topk;
+  s.index_base = index_base;
+  s.out_idx = cidx;
+  s.out_scores = csc;
+  s.status = d.status;
+  s.rows_dyn = nserve;
+  e = launch_select_topk(s, w + L.sel_ws, stream);
+  if (e != cudaSuccess) return e;
+  fallback_scatter_kernel<<<kFallbackRows, 256, 0, stream>>>(nserve, flag_rows, topk, cidx, csc,
+                                                             out_idx, out_scores);
+  return cudaGetLastError();
+}
+
+}  // namespace prism

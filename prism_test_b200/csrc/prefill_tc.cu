@@ -6,7 +6,7 @@
 // Work unit: one CTA takes 256 query rows of one (batch, KV head) — two M = 128
 // tiles of the rows (g, s) of the KV head's G query heads, g-major — and streams
 // that head's keys in N = 128 tiles up to the last key any of its rows can see.
-//   warp 0 (one lane): TMA producer, a 4-stage ring of 32 KB key tiles (two 16 KB
+//   warp 0 (one lane): TMA producer, a ring of 32 KB key tiles (two 16 KB
 //     128-byte-swizzled atoms: dimensions 0-63 and 64-127);
 //   warp 1: allocates 512 TMEM columns; one lane issues the MMAs: per key tile
 //     and query tile, 8 tcgen05.mma kind::f16 steps (M 128, N 128, K 16) into a
@@ -20,6 +20,20 @@
 // zero). 16-bit products are exact in the fp32 accumulator, so the scores equal
 // the fp32 einsum of the oracle up to summation order.
 //
+// Modes (the epilogue's work):
+//   kScores  writes the fp32 score matrix [rows, ld] (masked keys -inf) for the
+//            selection kernels;
+//   kSample  streams a strided sample of the keys (every kSampleStride-th) twice:
+//            pass 1 takes each row's sample minimum and maximum, pass 2 a
+//            128-bin histogram between them (per-row bins in shared memory);
+//            the row's threshold T is the lower edge of the bin holding sample
+//            rank m = 1.1 e + 4 sqrt(e) + 8, e = k * samples / keys visible
+//            (-inf when the row sees at most k keys);
+//   kCand    appends every visible key with score >= T, packed as
+//            (order-preserving score key << 32 | ~index), to the row's candidate
+//            list [rows, cap] and stores the row's count (which may exceed cap:
+//            the selection then recomputes that row exactly).
+//
 // Every mbarrier wait is bounded (2 s): on expiry the kernel records
 // kStatusTimeout, the roles leave their loops, and the TMEM is still freed.
 #include "common.cuh"
@@ -30,20 +44,30 @@
 namespace prism {
 namespace {
 
-constexpr int kPfStages = 4;
+enum PfMode : int { kScores = 0, kSample = 1, kCand = 2 };
+
 constexpr int kPfThreads = 320;
 constexpr int kPfEpiWarps = 8;
 constexpr uint32_t kAtomBytes = 128 * 128;       // 128 rows x 128 B
 constexpr uint32_t kTileBytes = 2 * kAtomBytes;  // 128 rows x 128 dims
 constexpr uint32_t kAOff = 0;                    // two query tiles
 constexpr uint32_t kBOff = 2 * kTileBytes;       // key stages
-constexpr uint32_t kBarOff = kBOff + kPfStages * kTileBytes;
-constexpr uint32_t kPfSmem = kBarOff + 256 + 1024;  // + alignment slack
+constexpr int kHistBins = 128;
+constexpr int kHistStride = 130;                 // u16 per row: 65 words, rows in distinct banks
 constexpr uint32_t kTmemCols = 512;
 
+template <int kMode>
+struct PfCfg {
+  static constexpr int kStages = kMode == kSample ? 2 : 4;
+  static constexpr uint32_t kHistOff = kBOff + kStages * kTileBytes;
+  static constexpr uint32_t kHistBytes = kMode == kSample ? 256 * kHistStride * 2 : 0;
+  static constexpr uint32_t kBarOff = kHistOff + kHistBytes;
+  static constexpr uint32_t kSmem = kBarOff + 256 + 1024;  // + alignment slack
+};
+
 struct PfBars {
-  uint64_t full[kPfStages];
-  uint64_t empty[kPfStages];
+  uint64_t full[4];
+  uint64_t empty[4];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t done;
@@ -57,9 +81,14 @@ struct PfArgs {
   int64_t q_sb, q_sh, q_ss;
   int causal;
   int64_t causal_offset;
-  float* scores;  // [B * Hq * Sq, ld]
+  float* scores;       // kScores: [B * Hq * Sq, ld]
   int64_t ld;
-  int pairs;      // CTAs per (batch, KV head)
+  float* thr;          // kSample (out) / kCand (in): [B * Hq * Sq]
+  uint32_t* counts;    // kCand: [B * Hq * Sq]
+  uint64_t* cand;      // kCand: [B * Hq * Sq, cap]
+  int64_t cap;
+  int topk;
+  int pairs;           // CTAs per (batch, KV head)
   int* status;
 };
 
@@ -69,15 +98,17 @@ __device__ __forceinline__ int64_t score_row(const PfArgs& a, int b, int h, int6
   return (int64_t(b) * a.Hq + int64_t(h) * a.G + g) * a.Sq + s;
 }
 
-template <bool kBF16>
+template <bool kBF16, int kMode>
 __global__ void __launch_bounds__(kPfThreads, 1)
-    prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const PfArgs a) {
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const PfArgs a) {
+  using Cfg = PfCfg<kMode>;
+  constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t pad = ((raw_u32 + 1023u) & ~1023u) - raw_u32;
   uint8_t* smem = smem_raw + pad;
   const uint32_t sbase = raw_u32 + pad;
-  PfBars* bars = reinterpret_cast<PfBars*>(smem + kBarOff);
+  PfBars* bars = reinterpret_cast<PfBars*>(smem + Cfg::kBarOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pair = blockIdx.x % a.pairs;
@@ -94,10 +125,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int64_t lim = a.causal_offset + smax + 1;
     nkeys = lim < nkeys ? lim : nkeys;
   }
-  const int nkt = int((nkeys + 127) / 128);
+  // key tiles per pass (sample tiles in kSample) and passes
+  const int64_t nitems = kMode == kSample ? (nkeys + kSampleStride - 1) / kSampleStride : nkeys;
+  const int ntile = int((nitems + 127) / 128);
+  const int npass = kMode == kSample ? 2 : 1;
+  const int nkt = ntile * npass;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPfStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
@@ -142,18 +177,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // ---- TMA producer ------------------------------------------------------------
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
+      const int kb = (a.B > 1) ? b : 0;
       for (int t = 0; t < nkt; ++t) {
-        const int s = t % kPfStages;
-        if (t >= kPfStages &&
-            !mbar_wait_bounded(&bars->empty[s], uint32_t((t / kPfStages - 1) & 1))) {
+        const int s = t % kStages;
+        if (t >= kStages &&
+            !mbar_wait_bounded(&bars->empty[s], uint32_t((t / kStages - 1) & 1))) {
           set_status(a.status, kStatusTimeout);
           break;
         }
+        const int tt = t % ntile;  // tile within the pass
         mbar_arrive_expect_tx(&bars->full[s], kTileBytes);
         uint8_t* dst = smem + kBOff + uint32_t(s) * kTileBytes;
-        const int kb = (a.B > 1) ? b : 0;
-        tma_load_4d(dst, &kmap, 0, t * 128, h, kb, &bars->full[s], pol);
-        tma_load_4d(dst + kAtomBytes, &kmap, 64, t * 128, h, kb, &bars->full[s], pol);
+        tma_load_4d(dst, &kmap, 0, tt * 128, h, kb, &bars->full[s], pol);
+        tma_load_4d(dst + kAtomBytes, &kmap, 64, tt * 128, h, kb, &bars->full[s], pol);
       }
     }
   } else if (warp == 1) {
@@ -162,8 +198,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       constexpr uint32_t idesc = idesc_kind_f16(kBF16, 128, 128);
       bool ok = true;
       for (int t = 0; t < nkt && ok; ++t) {
-        const int s = t % kPfStages, buf = t & 1;
-        ok = mbar_wait_bounded(&bars->full[s], uint32_t((t / kPfStages) & 1));
+        const int s = t % kStages, buf = t & 1;
+        ok = mbar_wait_bounded(&bars->full[s], uint32_t((t / kStages) & 1));
         if (ok && t >= 2) ok = mbar_wait_bounded(&bars->tempty[buf], uint32_t((t / 2 - 1) & 1));
         if (!ok) {
           set_status(a.status, kStatusTimeout);
@@ -190,16 +226,34 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   } else {
     // ---- epilogue ------------------------------------------------------------------
-    const int qt = (warp - 2) >> 2;      // query tile
-    const int quad = warp & 3;           // TMEM lanes [32 quad, 32 quad + 32)
-    const int64_t r = r0 + int64_t(qt) * 128 + quad * 32 + lane;
+    const int qt = (warp - 2) >> 2;  // query tile
+    const int quad = warp & 3;       // TMEM lanes [32 quad, 32 quad + 32)
+    const int rl = qt * 128 + quad * 32 + lane;  // row within the CTA
+    const int64_t r = r0 + rl;
     const bool rvalid = r < r1;
-    int64_t vis = INT64_MAX, row_off = 0;
+    int64_t nvis = 0, srow = 0;  // keys this row sees; its flattened score row
     if (rvalid) {
       const int64_t g = r / a.Sq, s = r - g * a.Sq;
-      if (a.causal) vis = a.causal_offset + s;
-      row_off = score_row(a, b, h, r) * a.ld;
+      nvis = a.causal ? a.causal_offset + s + 1 : a.Sk;
+      nvis = nvis < a.Sk ? nvis : a.Sk;
+      nvis = nvis > 0 ? nvis : 0;
+      srow = score_row(a, b, h, r);
     }
+    // per-mode row state
+    float mn = INFINITY, mx = -INFINITY, inv_w = 0.f;  // kSample
+    uint16_t* hist = nullptr;
+    if (kMode == kSample) {
+      hist = reinterpret_cast<uint16_t*>(smem + Cfg::kHistOff) + rl * kHistStride;
+      for (int i = 0; i < kHistStride / 2; ++i) reinterpret_cast<uint32_t*>(hist)[i] = 0u;
+    }
+    float thr = -INFINITY;  // kCand
+    uint32_t cnt = 0;
+    uint64_t* cl = nullptr;
+    if (kMode == kCand && rvalid) {
+      thr = a.thr[srow];
+      cl = a.cand + srow * a.cap;
+    }
+    const int64_t nsamp = (nvis + kSampleStride - 1) / kSampleStride;  // samples it sees
     for (int t = 0; t < nkt; ++t) {
       const int buf = t & 1;
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars->tfull[buf], uint32_t((t >> 1) & 1)))) {
@@ -216,19 +270,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tempty[buf]);
-      if (rvalid) {
-        const int64_t j0 = int64_t(t) * 128;
-        float* dst = a.scores + row_off + j0;
+      if (!rvalid) continue;
+      const int tt = t % ntile;
+      const int64_t j0 = int64_t(tt) * 128;  // first key (sample) of the tile
+      if (kMode == kScores) {
+        float* dst = a.scores + srow * a.ld + j0;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
             const int64_t j = j0 + c * 32 + i;
             float4 o;
-            o.x = j + 0 > vis ? -INFINITY : __uint_as_float(v[c][i + 0]);
-            o.y = j + 1 > vis ? -INFINITY : __uint_as_float(v[c][i + 1]);
-            o.z = j + 2 > vis ? -INFINITY : __uint_as_float(v[c][i + 2]);
-            o.w = j + 3 > vis ? -INFINITY : __uint_as_float(v[c][i + 3]);
+            o.x = j + 0 < nvis ? __uint_as_float(v[c][i + 0]) : -INFINITY;
+            o.y = j + 1 < nvis ? __uint_as_float(v[c][i + 1]) : -INFINITY;
+            o.z = j + 2 < nvis ? __uint_as_float(v[c][i + 2]) : -INFINITY;
+            o.w = j + 3 < nvis ? __uint_as_float(v[c][i + 3]) : -INFINITY;
             if (j + 4 <= a.Sk) {
               *reinterpret_cast<float4*>(dst + c * 32 + i) = o;
             } else {
@@ -238,11 +294,75 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
           }
         }
+      } else if (kMode == kSample) {
+        const int64_t lim = nsamp - j0;  // samples of this tile the row sees
+        if (t < ntile) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (c * 32 + i < lim) {
+                const float x = __uint_as_float(v[c][i]);
+                mn = fminf(mn, x);
+                mx = fmaxf(mx, x);
+              }
+            }
+          if (t == ntile - 1) inv_w = mx > mn ? float(kHistBins) / (mx - mn) : 0.f;
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (c * 32 + i < lim) {
+                const float x = __uint_as_float(v[c][i]);
+                int bin = int((x - mn) * inv_w);
+                bin = bin < 0 ? 0 : (bin > kHistBins - 1 ? kHistBins - 1 : bin);
+                hist[bin] = uint16_t(hist[bin] + 1);
+              }
+            }
+        }
+      } else {  // kCand
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x = __uint_as_float(v[c][i]);
+            const int64_t j = j0 + c * 32 + i;
+            if ((x >= thr || x != x) && j < nvis) {  // NaN ranks above every number
+              if (cnt < uint32_t(a.cap))
+                cl[cnt] = (uint64_t(float_to_okey(x)) << 32) | uint64_t(~uint32_t(j));
+              ++cnt;
+            }
+          }
       }
     }
-    // keys beyond the last visible tile are masked for every row of this CTA
-    if (rvalid && a.causal) {
-      for (int64_t j = int64_t(nkt) * 128; j < a.Sk; ++j) a.scores[row_off + j] = -INFINITY;
+    if (rvalid && kMode == kSample) {
+      float T = -INFINITY;
+      if (nvis > a.topk && nsamp > 0) {
+        const double e = double(a.topk) * double(nsamp) / double(nvis);
+        const double m = 1.1 * e + 4.0 * sqrt(e) + 8.0;
+        if (m < double(nsamp)) {
+          if (inv_w > 0.f) {
+            uint32_t acc = 0;
+            int bin = kHistBins - 1;
+            for (; bin > 0; --bin) {
+              acc += hist[bin];
+              if (double(acc) >= m) break;
+            }
+            const float w = (mx - mn) / float(kHistBins);
+            T = mn + float(bin) * w - w * (1.0f / 1024.0f);
+          } else {
+            T = mn;  // every sample equal
+          }
+        }
+      }
+      a.thr[srow] = T;
+    }
+    if (rvalid && kMode == kCand) a.counts[srow] = cnt;
+    // kScores: keys past the last tile any row of this CTA sees are masked
+    if (rvalid && kMode == kScores) {
+      float* dst = a.scores + srow * a.ld;
+      for (int64_t j = int64_t(ntile) * 128; j < a.Sk; ++j) dst[j] = -INFINITY;
     }
   }
   tc_fence_before();
@@ -253,18 +373,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   }
 }
 
-}  // namespace
-
-bool prefill_tc_supported(const DecodeArgs& a) {
-  return a.inv_freq == nullptr && int64_t(a.G) * a.Sq >= kPrefillMinRows &&
-         (a.q_ss % 8) == 0 && (a.q_sh % 8) == 0 && (a.q_sb % 8) == 0 &&
-         (reinterpret_cast<uintptr_t>(a.q) & 15u) == 0;
-}
-
-cudaError_t launch_prefill_scores_tc(const DecodeArgs& d, int dtype, cudaStream_t stream) {
-  CUtensorMap kmap;
-  cudaError_t e = make_key_tensor_map_sw128(&kmap, d.k, dtype, d.B, d.Hkv, d.Sk, d.k_sb, d.k_sh);
-  if (e != cudaSuccess) return e;
+PfArgs make_args(const DecodeArgs& d) {
   PfArgs a{};
   a.q = d.q;
   a.B = d.B;
@@ -282,12 +391,60 @@ cudaError_t launch_prefill_scores_tc(const DecodeArgs& d, int dtype, cudaStream_
   a.ld = d.ld;
   a.pairs = int((int64_t(d.G) * d.Sq + 255) / 256);
   a.status = d.status;
-  const int64_t grid = int64_t(a.pairs) * d.B * d.Hkv;
-  auto kern = dtype == kBF16 ? prefill_scores_kernel<true> : prefill_scores_kernel<false>;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPfSmem));
+  return a;
+}
+
+template <int kMode>
+cudaError_t launch_mode(const CUtensorMap& kmap, const PfArgs& a, int dtype, int64_t grid,
+                        cudaStream_t stream) {
+  auto kern = dtype == kBF16 ? prefill_tc_kernel<true, kMode> : prefill_tc_kernel<false, kMode>;
+  constexpr uint32_t smem = PfCfg<kMode>::kSmem;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  kern<<<dim3(unsigned(grid)), kPfThreads, kPfSmem, stream>>>(kmap, a);
+  kern<<<dim3(unsigned(grid)), kPfThreads, smem, stream>>>(kmap, a);
   return cudaGetLastError();
+}
+
+}  // namespace
+
+bool prefill_tc_supported(const DecodeArgs& a) {
+  return a.inv_freq == nullptr && int64_t(a.G) * a.Sq >= kPrefillMinRows &&
+         (a.q_ss % 8) == 0 && (a.q_sh % 8) == 0 && (a.q_sb % 8) == 0 &&
+         (reinterpret_cast<uintptr_t>(a.q) & 15u) == 0;
+}
+
+cudaError_t launch_prefill_scores_tc(const DecodeArgs& d, int dtype, cudaStream_t stream) {
+  CUtensorMap kmap;
+  cudaError_t e = make_key_tensor_map_sw128(&kmap, d.k, dtype, d.B, d.Hkv, d.Sk, d.k_sb, d.k_sh);
+  if (e != cudaSuccess) return e;
+  const PfArgs a = make_args(d);
+  return launch_mode<kScores>(kmap, a, dtype, int64_t(a.pairs) * d.B * d.Hkv, stream);
+}
+
+cudaError_t launch_prefill_threshold_tc(const DecodeArgs& d, int dtype, int topk, float* thr,
+                                        cudaStream_t stream) {
+  CUtensorMap smap;
+  cudaError_t e = make_key_tensor_map_sw128(&smap, d.k, dtype, d.B, d.Hkv, d.Sk, d.k_sb, d.k_sh,
+                                            kSampleStride);
+  if (e != cudaSuccess) return e;
+  PfArgs a = make_args(d);
+  a.thr = thr;
+  a.topk = topk;
+  return launch_mode<kSample>(smap, a, dtype, int64_t(a.pairs) * d.B * d.Hkv, stream);
+}
+
+cudaError_t launch_prefill_candidates_tc(const DecodeArgs& d, int dtype, const float* thr,
+                                         uint32_t* counts, uint64_t* cand, int64_t cap,
+                                         cudaStream_t stream) {
+  CUtensorMap kmap;
+  cudaError_t e = make_key_tensor_map_sw128(&kmap, d.k, dtype, d.B, d.Hkv, d.Sk, d.k_sb, d.k_sh);
+  if (e != cudaSuccess) return e;
+  PfArgs a = make_args(d);
+  a.thr = const_cast<float*>(thr);
+  a.counts = counts;
+  a.cand = cand;
+  a.cap = cap;
+  return launch_mode<kCand>(kmap, a, dtype, int64_t(a.pairs) * d.B * d.Hkv, stream);
 }
 
 }  // namespace prism

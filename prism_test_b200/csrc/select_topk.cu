@@ -496,6 +496,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   cg::cluster_group cluster = cg::this_cluster();
   const unsigned rank = cluster.block_rank();
   const int64_t row = blockIdx.x / kCluster;
+  if (a.rows_dyn != nullptr && row >= *a.rows_dyn) return;  // the whole cluster leaves
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const float* sc = a.scores + row * a.ld;
@@ -842,6 +843,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_row_kernel(const Sele
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
   const int64_t row = blockIdx.x;
+  if (a.rows_dyn != nullptr && row >= *a.rows_dyn) return;
   const int tid = threadIdx.x, lane = tid & 31;
   const float* sc = a.scores + row * a.ld;
   const int32_t* ix = a.idx_in ? a.idx_in + row * a.ld : nullptr;
@@ -1111,6 +1113,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void __launch_bounds__(kThreads, 1) select_topk_general_kernel(const SelectArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
+  if (a.rows_dyn != nullptr && int64_t(blockIdx.x) >= *a.rows_dyn) return;
   select_row_general(a, blockIdx.x, sm);
 }
 

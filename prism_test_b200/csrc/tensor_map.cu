@@ -42,12 +42,14 @@ cudaError_t make_key_tensor_map(CUtensorMap* map, const void* k, int dtype, int6
 }
 
 cudaError_t make_key_tensor_map_sw128(CUtensorMap* map, const void* k, int dtype, int64_t B,
-                                      int64_t Hkv, int64_t Sk, int64_t k_sb, int64_t k_sh) {
+                                      int64_t Hkv, int64_t Sk, int64_t k_sb, int64_t k_sh,
+                                      int key_stride) {
   PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
   if (fn == nullptr) return cudaErrorNotSupported;
   const bool batched = B > 1 && k_sb != 0;
-  cuuint64_t dims[4] = {128, cuuint64_t(Sk), cuuint64_t(Hkv), cuuint64_t(batched ? B : 1)};
-  cuuint64_t strides[3] = {256, cuuint64_t(k_sh) * 2,
+  const int64_t nkeys = (Sk + key_stride - 1) / key_stride;
+  cuuint64_t dims[4] = {128, cuuint64_t(nkeys), cuuint64_t(Hkv), cuuint64_t(batched ? B : 1)};
+  cuuint64_t strides[3] = {cuuint64_t(256) * cuuint64_t(key_stride), cuuint64_t(k_sh) * 2,
                            cuuint64_t(batched ? k_sb : k_sh * Hkv) * 2};
   cuuint32_t box[4] = {64, 128, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};

@@ -21,8 +21,10 @@ cudaError_t make_key_tensor_map(CUtensorMap* map, const void* k, int dtype, int6
 
 // The same key cache as a K-major tensor-core operand: box {64, 128, 1, 1} (64
 // dimensions x 128 positions of one KV head = one 16 KB atom per copy), written
-// to shared memory in the 128-byte swizzle mode.
+// to shared memory in the 128-byte swizzle mode. With key_stride s > 1 the map
+// covers only every s-th key (positions 0, s, 2s, ...): a strided sample.
 cudaError_t make_key_tensor_map_sw128(CUtensorMap* map, const void* k, int dtype, int64_t B,
-                                      int64_t Hkv, int64_t Sk, int64_t k_sb, int64_t k_sh);
+                                      int64_t Hkv, int64_t Sk, int64_t k_sb, int64_t k_sh,
+                                      int key_stride = 1);
 
 }  // namespace prism

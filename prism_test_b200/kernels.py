@@ -12,7 +12,10 @@ defaults keep the reference call working unchanged:
   what the reference's dense path ``ReAttentionMethod._dense_topk``
   (reattention.py:486-498) selects, sorted by descending score (torch.topk
   order). The reference Triton kernel's per-128-key block-maximum top-{1,4}
-  (``mode="blockmax"``) is a separate mode.
+  (``mode="blockmax"``) is a separate mode. ``mode="stream"`` gives the exact
+  result without a score matrix (raw keys, >= 128 query rows per KV head,
+  ``topk <= 4096``); exact mode switches to it by itself for prefill chunks whose
+  score matrix would reach 2 GiB.
 * Any ``seqlen_q >= 1``, any ``seqlen_k``, any ``1 <= topk <= min(seqlen_k, 16384)``
   in exact mode (the reference needs ``seqlen_q % 128 == 0``, ``seqlen_k % 128 == 0``
   and ``topk in {1, 4}``).
@@ -131,8 +134,8 @@ def einsum_topk_func(
     assert q.is_cuda and k.is_cuda, "All tensors must be sent to gpu"
     assert q.device == k.device, "q and k must be on the same device"
     assert d == 128, f"Only support d == 128, but find d={d}"
-    if mode == "exact":
-        mode_code = _lib.MODE_EXACT
+    if mode in ("exact", "stream"):
+        mode_code = _lib.MODE_EXACT if mode == "exact" else _lib.MODE_EXACT_STREAM
         assert 1 <= topk <= seqlen_k, f"need 1 <= topk <= seqlen_k, got topk={topk}, seqlen_k={seqlen_k}"
     elif mode == "blockmax":
         mode_code = _lib.MODE_BLOCKMAX
@@ -142,7 +145,7 @@ def einsum_topk_func(
         )
         assert topk == 1 or topk == 4, "Only support k == 1 or 4"
     else:
-        raise AssertionError(f"unknown mode {mode!r}; use 'exact' or 'blockmax'")
+        raise AssertionError(f"unknown mode {mode!r}; use 'exact', 'stream' or 'blockmax'")
 
     if weight_code != _lib.RECALL_QK:
         assert values is not None, f"recall_type {recall_type!r} needs values"

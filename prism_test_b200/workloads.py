@@ -11,7 +11,8 @@ generated on the target device:
 * cached keys = RoPE(raw keys) at absolute positions ``0 .. Sk-1`` with the HF
   ``rotate_half`` layout and fp32 angles ``fp32(pos) * inv_freq`` — the keys the
   reference un-rotates in ``ReAttentionMethod._unrotate_keys``
-  (eval_harness/attention_methods/reattention.py:743-793) — stored in bf16.
+  (eval_harness/attention_methods/reattention.py:743-793) — stored in bf16;
+  the prefill chunk keeps raw keys (no RoPE), as the exact method's cache does.
 
 Key generation is chunked along the sequence with a per-chunk seed, so a
 sequence shard ``[start, stop)`` can be generated on its own rank and equals
@@ -44,6 +45,7 @@ class Workload:
     planted_per_qhead: int = 0
     planted_sigma: float = 6.0
     D: int = 128
+    rope: bool = True                 # cached keys RoPE-rotated (else raw, pre-RoPE)
 
     @property
     def kv_bytes(self) -> int:
@@ -61,9 +63,10 @@ WORKLOADS: Dict[str, Workload] = {
     # decode top-k at 128K keys (single GPU headline)
     "decode-128k": Workload("decode-128k", 1, 32, 8, 1, 131072, 5e5, 4096,
                             outlier_channels=4, planted_per_qhead=16, planted_sigma=6.0),
-    # prefill chunk: 4096 query rows against 128K keys, causal
+    # prefill chunk: 4096 query rows against 128K keys, causal; raw (pre-RoPE) keys,
+    # as the exact method's cache holds them (reattention_exact.py:545-547)
     "prefill-chunk-128k": Workload("prefill-chunk-128k", 1, 32, 8, 4096, 131072, 5e5, 2048,
-                                   causal_offset=126976),
+                                   causal_offset=126976, rope=False),
     # 1M-key decode, sequence-sharded over N GPUs
     "decode-1m-sharded": Workload("decode-1m-sharded", 1, 32, 8, 1, 1 << 20, 5e5, 8192,
                                   planted_per_qhead=64, planted_sigma=5.0),
@@ -180,8 +183,10 @@ def make_keys(wl: Workload, device, q: torch.Tensor, inv_freq: torch.Tensor,
                         z = wl.planted_sigma * sigma / qv.norm()
                         n = raw[b, hk, p - c0]
                         raw[b, hk, p - c0] = z * qn + (n - (n @ qn) * qn)
-        cos, sin = rope_cos_sin(torch.arange(c0, c1, device=device), inv_freq)
-        out[:, :, c0 - start:c1 - start] = apply_rope(raw, cos, sin).to(wl.dtype)
+        if wl.rope:
+            cos, sin = rope_cos_sin(torch.arange(c0, c1, device=device), inv_freq)
+            raw = apply_rope(raw, cos, sin)
+        out[:, :, c0 - start:c1 - start] = raw.to(wl.dtype)
     return out
 
 
@@ -216,7 +221,8 @@ def make_inputs(wl: Workload, device, seed: int = 0, shard: Optional[tuple] = No
         assert per * world == wl.Sk, "Sk must divide evenly over the shards"
         start, stop = rank * per, (rank + 1) * per
     k = make_keys(wl, device, q, inv_freq.to(device), start, stop, seed)
-    return dict(q=q, k=k, inv_freq=inv_freq.to(device), pos_offset=start, index_base=start,
+    return dict(q=q, k=k, inv_freq=inv_freq.to(device) if wl.rope else None, pos_offset=start,
+                index_base=start,
                 topk=wl.topk, causal_offset=wl.causal_offset, start=start, stop=stop)
 
 

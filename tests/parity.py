@@ -82,3 +82,49 @@ def check_parity(idx: torch.Tensor, scores: Optional[torch.Tensor], q: torch.Ten
         stats["swapped"] += int(diff.sum()) // 2
         stats["rows"] += B * G * Sq
     return stats
+
+
+def check_rows_parity(idx: torch.Tensor, scores: torch.Tensor, q: torch.Tensor, k: torch.Tensor,
+                      topk: int, rows, causal_offset: Optional[int] = None, rel: float = REL) -> int:
+    """The parity rules on selected flattened rows (b, hq, s) only, for shapes whose
+    full oracle does not fit in memory; keys raw (no RoPE). Returns near-tie swaps."""
+    B, Hq, Sq, _ = q.shape
+    Hkv, Sk = k.shape[1], k.shape[2]
+    G = Hq // Hkv
+    idx = idx.reshape(B * Hq * Sq, topk)
+    scores = scores.reshape(B * Hq * Sq, topk)
+    swaps = 0
+    for row in rows:
+        s = row % Sq
+        b, hq = divmod(row // Sq, Hq)
+        qv = q[b, hq, s].float().cpu()
+        kk = k[b, hq // G].float().cpu()
+        full = kk @ qv                                            # [Sk]
+        tol = rel * qv.norm() * kk.norm(dim=-1)                   # [Sk]
+        if causal_offset is not None:
+            full[causal_offset + s + 1:] = float("-inf")
+        mine = idx[row].long().cpu()
+        sc = scores[row].float().cpu()
+        assert int(mine.min()) >= 0 and int(mine.max()) < Sk, f"row {row}: index out of range"
+        assert mine.unique().numel() == topk, f"row {row}: duplicate indices"
+        ref_at = full[mine]
+        finite = torch.isfinite(ref_at)
+        lim = torch.maximum(rel * ref_at.abs(), tol[mine])
+        ok = torch.where(finite, (sc - ref_at).abs() <= lim, sc == ref_at)
+        assert bool(ok.all()), f"row {row}: {int((~ok).sum())} scores off"
+        d = sc[1:] - sc[:-1]
+        assert bool((d <= 0).all()), f"row {row}: scores not sorted"
+        ref_vals, ref_idx = full.topk(topk)
+        kth = ref_vals[-1]
+        tol_k = max(float(rel * kth.abs()), float(tol[ref_idx[-1]]))
+        in_ref = torch.zeros(Sk, dtype=torch.bool)
+        in_ref[ref_idx] = True
+        in_mine = torch.zeros(Sk, dtype=torch.bool)
+        in_mine[mine] = True
+        diff = in_ref ^ in_mine
+        near = (full - kth).abs() <= tol_k
+        both_inf = torch.isinf(full) & torch.isinf(kth) & (full == kth)
+        bad = diff & ~(near | both_inf)
+        assert not bool(bad.any()), f"row {row}: index sets differ beyond near-ties"
+        swaps += int(diff.sum()) // 2
+    return swaps

@@ -39,3 +39,16 @@ def test_prefill_tc_strided_queries(cuda_device):
     idx, sc = einsum_topk_func(q, k, 64, return_scores=True)
     torch.cuda.synchronize()
     check_parity(idx, sc, q.contiguous(), k, 64)
+
+
+def test_prefill_tc_causal_tail_masked(cuda_device):
+    # causal offset 0: the first CTA's rows see only the first keys, so most key
+    # tiles are never scored for them and must read as masked
+    g = torch.Generator(device=cuda_device).manual_seed(12)
+    q = torch.randn(1, 4, 128, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    k = torch.randn(1, 2, 3000, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    idx, sc = einsum_topk_func(q, k, 40, causal_offset=0, return_scores=True)
+    torch.cuda.synchronize()
+    check_parity(idx, sc, q, k, 40, None, 0, 0, by_head=True)
+    # masked keys follow the visible ones in ascending index order
+    assert idx[0, 0, 0, :5].tolist() == [0, 1, 2, 3, 4]
