@@ -140,15 +140,26 @@ class ClockSampler:
                 "reasons": names, "samples": len(self.samples)}
 
 
-def measured_peaks():
+def measured_peaks(kind: str = "hbm_gbs"):
+    """A measured peak (hbm_gbs, bf16_tflops or bf16_tflops_sustained) and its source."""
+    fallback = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         try:
             d = json.loads(p.read_text())
-            return float(d["hbm_gbs"]), "measured"
+            return float(d[kind]), "measured"
         except Exception:  # noqa: BLE001
             pass
-    return 6650.0, "fallback"
+    return fallback[kind], "fallback"
+
+
+def prefill_flops(wl) -> float:
+    """Algorithmic FLOPs of one prefill-chunk call: 2 * D per (query row, visible key)."""
+    vis = 0
+    for s in range(wl.Sq):
+        n = wl.Sk if wl.causal_offset is None else min(wl.Sk, wl.causal_offset + s + 1)
+        vis += max(0, n)
+    return 2.0 * wl.D * wl.B * wl.Hq * vis
 
 
 def ncu_traffic(kernel: str, workload: str):
@@ -164,6 +175,25 @@ def ncu_traffic(kernel: str, workload: str):
 
 
 # ---------------------------------------------------------------- CPU baseline
+def cpu_sample_plan(wl, whole_heads: int):
+    """(sub-workload, fraction of the whole call it is, description) of a bounded CPU
+    sample. Prefill chunks (Sq >= 128): the 128 query rows of the last 32 positions of
+    one KV head's group (the rows that see the most keys), extrapolated linearly over
+    the rows — the full score matrix would not fit in host memory. Otherwise
+    `whole_heads` KV heads with their query groups."""
+    if wl.Sq >= 128:
+        G = wl.Hq // wl.Hkv
+        rows = 32
+        causal = None if wl.causal_offset is None else wl.causal_offset + wl.Sq - rows
+        sub = wl.with_(Hkv=1, Hq=G, Sq=rows, causal_offset=causal, planted_per_qhead=0)
+        frac = G * rows / (wl.B * wl.Hq * wl.Sq)
+        return sub, frac, (f"{G * rows} of {wl.B * wl.Hq * wl.Sq} query rows (the last {rows} "
+                           f"positions of one KV head group), extrapolated")
+    sub = wl.with_(Hkv=whole_heads, Hq=whole_heads * (wl.Hq // wl.Hkv))
+    frac = whole_heads / wl.Hkv
+    return sub, frac, ("full call" if whole_heads == wl.Hkv else f"{whole_heads} of {wl.Hkv} KV heads")
+
+
 def cpu_baseline(wl, max_seconds=20.0, recall_type="qk"):
     """The reference's dense CPU path (oracle restatement) on the host cores.
 
@@ -174,7 +204,7 @@ def cpu_baseline(wl, max_seconds=20.0, recall_type="qk"):
     torch.set_num_threads(os.cpu_count() or 1)
     cores = torch.get_num_threads()
     heads = wl.Hkv if wl.Sk * wl.Sq <= (1 << 17) * 8 else 1
-    sub = wl.with_(Hkv=heads, Hq=heads * (wl.Hq // wl.Hkv))
+    sub, frac, what = cpu_sample_plan(wl, heads)
     x = W.make_inputs(sub, "cpu")
     v = W.make_values(sub, "cpu") if recall_type != "qk" else None
 
@@ -190,11 +220,10 @@ def cpu_baseline(wl, max_seconds=20.0, recall_type="qk"):
         call()
         times.append(time.perf_counter() - t0)
     best = min(times)
-    frac = heads / wl.Hkv
     value = wl.Sk * frac / best
-    sample = (f"{'full call' if heads == wl.Hkv else f'{heads} of {wl.Hkv} KV heads'} of {wl.name} "
-              f"(un-rotate fp32, {'value norms, ' if recall_type != 'qk' else ''}einsum, topk), "
-              f"best of {len(times)} after 1 warm-up")
+    sample = (f"{what} of {wl.name} "
+              f"({'un-rotate fp32, ' if wl.rope else ''}{'value norms, ' if recall_type != 'qk' else ''}"
+              f"einsum, topk), best of {len(times)} after 1 warm-up")
     return {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
             "seconds_per_call": best / frac}
 
@@ -209,7 +238,7 @@ def run_reference(args):
     torch.set_num_threads(os.cpu_count() or 1)
     cores = torch.get_num_threads()
     # bounded sample per step: one KV head (and its query group) of the workload
-    sub = wl.with_(Hkv=1, Hq=wl.Hq // wl.Hkv)
+    sub, frac, what = cpu_sample_plan(wl, 1)
     x = W.make_inputs(sub, "cpu")
     rt = args.recall_type
     v = W.make_values(sub, "cpu") if rt != "qk" else None
@@ -230,8 +259,9 @@ def run_reference(args):
     for _ in range(steps):
         call()
     dt = (time.perf_counter() - t0) / steps
-    value = wl.Sk / wl.Hkv / dt  # KV tokens (all heads) per second
-    sample = f"1 of {wl.Hkv} KV heads of {wl.name} per step (un-rotate fp32, einsum, topk); {steps} steps"
+    value = wl.Sk * frac / dt  # KV tokens (the whole call) per second
+    sample = (f"{what} of {wl.name} per step ({'un-rotate fp32, ' if wl.rope else ''}einsum, topk); "
+              f"{steps} steps")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": dt * 1e3, "higher_is_better": True,
@@ -364,10 +394,25 @@ def main():
     n_sa = _lib.ctypes.c_int64(0)
     t_sa = _lib.ctypes.c_double(0.0)
     lib.prism_profile_read(_lib.KERNEL_SCALE, _lib.ctypes.byref(n_sa), _lib.ctypes.byref(t_sa))
+    n_th = _lib.ctypes.c_int64(0)
+    t_th = _lib.ctypes.c_double(0.0)
+    lib.prism_profile_read(_lib.KERNEL_THRESHOLD, _lib.ctypes.byref(n_th), _lib.ctypes.byref(t_th))
     score_ms = t_sc.value / max(1, n_sc.value)
-    bytes_per_launch = (stop - start) * wl.B * wl.Hkv * wl.D * 2  # keys of this rank, read once
-    peak, peak_kind = measured_peaks()
-    achieved = bytes_per_launch / (score_ms * 1e-3) / 1e9
+    prefill = wl.Sq >= 128 and inv is None  # the tcgen05 path: tensor-bound
+    if prefill:
+        work_per_launch = prefill_flops(wl)
+        peak, peak_kind = measured_peaks("bf16_tflops_sustained")
+        achieved = work_per_launch / (score_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "unit": "TFLOP/s", "flops_per_launch": work_per_launch,
+                "kernel": "prefill candidate pass (tcgen05 kind::f16 M128 N128, TMEM accumulators, "
+                          "threshold epilogue)",
+                "peak_note": "sustained bf16 GEMM peak: the kernel runs inside a long step loop"}
+    else:
+        work_per_launch = (stop - start) * wl.B * wl.Hkv * wl.D * 2  # keys of this rank, read once
+        peak, peak_kind = measured_peaks()
+        achieved = work_per_launch / (score_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "unit": "GB/s", "bytes_per_launch": work_per_launch,
+                "kernel": "decode scorer (TMA ring, fused inverse RoPE, fp32 q·K^T)"}
     achieved = max_over_ranks(-achieved) * -1.0 if world > 1 else achieved  # slowest rank
 
     value = wl.Sk * args.steps / (ms * 1e-3)
@@ -430,20 +475,20 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32 (tf32 MMA)",
+        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None,
+        "dtype": "bf16 in, fp32 accumulate (tcgen05)" if prefill else "f32 (tf32 MMA)",
         "data": "synthetic (seeded; see prism_test_b200/workloads.py)",
         "config": config_of(wl, world, rt),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_source": peak_kind,
-                     "traffic": ncu_traffic("score", wl.name),
-                     "kernel": "decode scorer (TMA ring, fused inverse RoPE, fp32 q·K^T)",
-                     "bytes_per_launch": bytes_per_launch, "launch_ms": score_ms},
+        "roofline": dict(roof, achieved=achieved, peak=peak, frac=achieved / peak,
+                         peak_source=peak_kind, traffic=ncu_traffic("score", wl.name),
+                         launch_ms=score_ms),
         "kernels_ms_per_step": {
             "score": t_sc.value / max(1, args.steps),
             "select": t_se.value / max(1, args.steps),
             "merge": t_me.value / max(1, args.steps),
             "value_norms": t_we.value / max(1, args.steps),
             "score_weighting": t_sa.value / max(1, args.steps),
+            "threshold": t_th.value / max(1, args.steps),
         },
         "gpu_launches": int(launches),
         "timing": "CUDA graph of one call, replayed",

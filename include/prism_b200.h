@@ -253,6 +253,7 @@ PRISM_API int prism_read_status(void* workspace, int* status_out, void* stream);
 #define PRISM_KERNEL_MERGE 2  /* top-k merge of gathered shard candidates */
 #define PRISM_KERNEL_WEIGHT 3 /* value-row norms of the weighted recall */
 #define PRISM_KERNEL_SCALE 4  /* weighting of the score matrix by those norms */
+#define PRISM_KERNEL_THRESHOLD 5 /* sampled per-row thresholds of the streaming prefill path */
 PRISM_API int prism_profile_start(int32_t capacity);
 PRISM_API int prism_profile_stop(void);
 PRISM_API int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms);

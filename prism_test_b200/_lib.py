@@ -30,6 +30,7 @@ SPAN_CENTERED = 0
 SPAN_FLOOR = 1
 KERNEL_WEIGHT = 3
 KERNEL_SCALE = 4
+KERNEL_THRESHOLD = 5
 RECALL_QK = 0
 RECALL_QKV = 1
 RECALL_QKV2 = 2

@@ -54,7 +54,7 @@ std::vector<cudaEvent_t> g_prof_pool;  // 2 * capacity events
 std::vector<ProfRec> g_prof_recs;
 bool g_prof_on = false;
 size_t g_prof_next = 0;
-int64_t g_prof_untimed[5] = {0, 0, 0, 0, 0};
+int64_t g_prof_untimed[6] = {0, 0, 0, 0, 0, 0};
 
 // Runs `launch` (which enqueues one kernel on `stream`), counting it and, while
 // profiling is on, bracketing it with a pair of events from the pool.
@@ -261,13 +261,20 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
   // specialised kernels take every query row of a KV head in one launch:
   // tensor-core tiles (keys as M for <= 16 rows per KV head, queries as M up
   // to 256 / Hkv rows), CUDA cores for <= 4
-  if (streaming) {  // thresholds, candidates, per-row selection, exact fallback: 6 kernels
-    e = launch_counted(PRISM_KERNEL_SCORE, stream, [&] {
-      return prism::launch_prefill_topk(a, dtype, topk, index_base, out_idx, out_scores,
-                                        ws + kStatusBytes, nsm, stream);
+  if (streaming) {  // thresholds, candidates, per-row selection + exact fallback
+    void* pws = ws + kStatusBytes;
+    e = launch_counted(PRISM_KERNEL_THRESHOLD, stream,
+                       [&] { return prism::prefill_stream_threshold(a, dtype, topk, pws, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "prefill threshold launch");
+    e = launch_counted(PRISM_KERNEL_SCORE, stream,
+                       [&] { return prism::prefill_stream_candidates(a, dtype, topk, pws, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "prefill candidate launch");
+    e = launch_counted(PRISM_KERNEL_SELECT, stream, [&] {
+      return prism::prefill_stream_select(a, dtype, topk, index_base, out_idx, out_scores, pws,
+                                          stream);
     });
-    if (e != cudaSuccess) return cuda_fail(e, "streaming prefill launch");
-    g_launches.fetch_add(5, std::memory_order_relaxed);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill select launch");
+    g_launches.fetch_add(3, std::memory_order_relaxed);  // the select phase launches 4 kernels
     return PRISM_OK;
   }
   if (prism::decode_hp_supported(a, dtype)) {
@@ -532,7 +539,7 @@ int prism_profile_stop(void) {
 
 int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms) {
   g_last_error.clear();
-  if (!launches || !total_ms || kernel < 0 || kernel > PRISM_KERNEL_SCALE)
+  if (!launches || !total_ms || kernel < 0 || kernel > PRISM_KERNEL_THRESHOLD)
     return fail(PRISM_E_INVALID, "bad kernel id or null output");
   int64_t n = 0;
   double ms = 0.0;

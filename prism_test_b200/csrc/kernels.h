@@ -74,11 +74,17 @@ cudaError_t launch_prefill_candidates_tc(const DecodeArgs& a, int dtype, const f
                                          cudaStream_t stream);
 int64_t prefill_cand_cap(int64_t Sk, int topk);
 size_t prefill_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk);
-// The whole streaming path: thresholds, candidates, selection, fallback.
-// `ws` holds prefill_stream_workspace_bytes(rows, Sk, topk) bytes (256-aligned).
-cudaError_t launch_prefill_topk(const DecodeArgs& a, int dtype, int topk, int64_t index_base,
-                                int32_t* out_idx, float* out_scores, void* ws, int num_sms,
-                                cudaStream_t stream);
+// The streaming path in three phases on one workspace `ws` of
+// prefill_stream_workspace_bytes(rows, Sk, topk) bytes (256-aligned):
+// thresholds (one tcgen05 launch), candidates (one tcgen05 launch), selection
+// (the per-row select and the exact fallback: four launches).
+cudaError_t prefill_stream_threshold(const DecodeArgs& a, int dtype, int topk, void* ws,
+                                     cudaStream_t stream);
+cudaError_t prefill_stream_candidates(const DecodeArgs& a, int dtype, int topk, void* ws,
+                                      cudaStream_t stream);
+cudaError_t prefill_stream_select(const DecodeArgs& a, int dtype, int topk, int64_t index_base,
+                                  int32_t* out_idx, float* out_scores, void* ws,
+                                  cudaStream_t stream);
 
 // --- exact per-row top-k selection over a score matrix ----------------------
 struct SelectArgs {

@@ -99,7 +99,9 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
 
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31;
-  const uint32_t n = a.counts[row];
+  // the row's candidates: n0 from the front of its list, n1 from the back
+  const uint32_t n0 = a.counts[2 * row], n1 = a.counts[2 * row + 1];
+  const uint32_t n = n0 + n1;
   const int64_t nvis = visible_keys(row, a.Sq, a.causal, a.causal_offset, a.Sk);
   const uint32_t keff = uint32_t(nvis < a.k ? nvis : a.k);
   int32_t* oi = a.out_idx + row * a.k;
@@ -124,7 +126,7 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
   const uint64_t* src = a.cand + row * a.cap;
   uint32_t kmx = 0u, kmn = 0xffffffffu;
   for (uint32_t i = tid; i < n; i += kPsThreads) {
-    const uint64_t x = src[i];
+    const uint64_t x = i < n0 ? src[i] : src[a.cap - 1 - (i - n0)];
     buf[i] = x;
     const uint32_t key = uint32_t(x >> 32);
     if (key != 0xffffffffu) {  // NaN is binned apart
@@ -286,7 +288,7 @@ PsLayout ps_layout(int64_t rows, int64_t Sk, int topk) {
   L.thr = o;
   o += up256(size_t(rows) * 4);
   L.counts = o;
-  o += up256(size_t(rows) * 4);
+  o += up256(size_t(rows) * 8);
   L.cand = o;
   o += up256(size_t(rows) * size_t(cap) * 8);
   L.flags = o;  // nflag, nserve
@@ -316,35 +318,63 @@ size_t prefill_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk) {
   return ps_layout(rows, Sk, topk).total;
 }
 
-cudaError_t launch_prefill_topk(const DecodeArgs& d, int dtype, int topk, int64_t index_base,
-                                int32_t* out_idx, float* out_scores, void* ws, int num_sms,
-                                cudaStream_t stream) {
-  (void)num_sms;
+namespace {
+struct PsPtrs {
+  float* thr;
+  uint32_t* counts;
+  uint64_t* cand;
+  int* nflag;
+  int* nserve;
+  int32_t* flag_rows;
+  float* scratch;
+  void* sel_ws;
+  int32_t* cidx;
+  float* csc;
+  int64_t cap;
+};
+PsPtrs ps_ptrs(const DecodeArgs& d, int topk, void* ws) {
   const int64_t rows = int64_t(d.B) * d.Hq * d.Sq;
   const PsLayout L = ps_layout(rows, d.Sk, topk);
   uint8_t* w = static_cast<uint8_t*>(ws);
-  float* thr = reinterpret_cast<float*>(w + L.thr);
-  uint32_t* counts = reinterpret_cast<uint32_t*>(w + L.counts);
-  uint64_t* cand = reinterpret_cast<uint64_t*>(w + L.cand);
-  int* nflag = reinterpret_cast<int*>(w + L.flags);
-  int* nserve = nflag + 1;
-  int32_t* flag_rows = reinterpret_cast<int32_t*>(w + L.flag_rows);
-  float* scratch = reinterpret_cast<float*>(w + L.scratch);
-  int32_t* cidx = reinterpret_cast<int32_t*>(w + L.cidx);
-  float* csc = reinterpret_cast<float*>(w + L.csc);
-  const int64_t cap = prefill_cand_cap(d.Sk, topk);
+  PsPtrs p;
+  p.thr = reinterpret_cast<float*>(w + L.thr);
+  p.counts = reinterpret_cast<uint32_t*>(w + L.counts);
+  p.cand = reinterpret_cast<uint64_t*>(w + L.cand);
+  p.nflag = reinterpret_cast<int*>(w + L.flags);
+  p.nserve = p.nflag + 1;
+  p.flag_rows = reinterpret_cast<int32_t*>(w + L.flag_rows);
+  p.scratch = reinterpret_cast<float*>(w + L.scratch);
+  p.sel_ws = w + L.sel_ws;
+  p.cidx = reinterpret_cast<int32_t*>(w + L.cidx);
+  p.csc = reinterpret_cast<float*>(w + L.csc);
+  p.cap = prefill_cand_cap(d.Sk, topk);
+  return p;
+}
+}  // namespace
 
-  cudaError_t e = cudaMemsetAsync(nflag, 0, 2 * sizeof(int), stream);
+cudaError_t prefill_stream_threshold(const DecodeArgs& d, int dtype, int topk, void* ws,
+                                     cudaStream_t stream) {
+  const PsPtrs p = ps_ptrs(d, topk, ws);
+  cudaError_t e = cudaMemsetAsync(p.nflag, 0, 2 * sizeof(int), stream);
   if (e != cudaSuccess) return e;
-  e = launch_prefill_threshold_tc(d, dtype, topk, thr, stream);
-  if (e != cudaSuccess) return e;
-  e = launch_prefill_candidates_tc(d, dtype, thr, counts, cand, cap, stream);
-  if (e != cudaSuccess) return e;
+  return launch_prefill_threshold_tc(d, dtype, topk, p.thr, stream);
+}
 
+cudaError_t prefill_stream_candidates(const DecodeArgs& d, int dtype, int topk, void* ws,
+                                      cudaStream_t stream) {
+  const PsPtrs p = ps_ptrs(d, topk, ws);
+  return launch_prefill_candidates_tc(d, dtype, p.thr, p.counts, p.cand, p.cap, stream);
+}
+
+cudaError_t prefill_stream_select(const DecodeArgs& d, int dtype, int topk, int64_t index_base,
+                                  int32_t* out_idx, float* out_scores, void* ws,
+                                  cudaStream_t stream) {
+  const PsPtrs w = ps_ptrs(d, topk, ws);
+  const int64_t rows = int64_t(d.B) * d.Hq * d.Sq;
   PsArgs p{};
-  p.cand = cand;
-  p.counts = counts;
-  p.cap = cap;
+  p.cand = w.cand;
+  p.counts = w.counts;
+  p.cap = w.cap;
   p.k = topk;
   p.Sk = d.Sk;
   p.Sq = d.Sq;
@@ -353,12 +383,12 @@ cudaError_t launch_prefill_topk(const DecodeArgs& d, int dtype, int topk, int64_
   p.index_base = index_base;
   p.out_idx = out_idx;
   p.out_scores = out_scores;
-  p.nflag = nflag;
-  p.flag_rows = flag_rows;
+  p.nflag = w.nflag;
+  p.flag_rows = w.flag_rows;
   p.status = d.status;
-  const size_t smem = size_t(cap) * 10 + kPsBins * 4;
-  e = cudaFuncSetAttribute(prefill_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           int(smem));
+  const size_t smem = size_t(w.cap) * 10 + kPsBins * 4;
+  cudaError_t e = cudaFuncSetAttribute(prefill_select_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   prefill_select_kernel<<<dim3(unsigned(rows)), kPsThreads, smem, stream>>>(p);
   e = cudaGetLastError();
@@ -366,29 +396,29 @@ cudaError_t launch_prefill_topk(const DecodeArgs& d, int dtype, int topk, int64_
 
   // exact fallback for the listed rows (kernels return at once when none are)
   if (dtype == kBF16)
-    fallback_scores_kernel<__nv_bfloat16><<<kFallbackRows, 256, 0, stream>>>(d, nflag, flag_rows,
-                                                                            nserve, scratch);
+    fallback_scores_kernel<__nv_bfloat16><<<kFallbackRows, 256, 0, stream>>>(
+        d, w.nflag, w.flag_rows, w.nserve, w.scratch);
   else
-    fallback_scores_kernel<__half><<<kFallbackRows, 256, 0, stream>>>(d, nflag, flag_rows, nserve,
-                                                                     scratch);
+    fallback_scores_kernel<__half><<<kFallbackRows, 256, 0, stream>>>(d, w.nflag, w.flag_rows,
+                                                                     w.nserve, w.scratch);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   SelectArgs s{};
-  s.scores = scratch;
+  s.scores = w.scratch;
   s.idx_in = nullptr;
   s.rows = kFallbackRows;
   s.n = d.Sk;
   s.ld = d.ld;
   s.k = topk;
   s.index_base = index_base;
-  s.out_idx = cidx;
-  s.out_scores = csc;
+  s.out_idx = w.cidx;
+  s.out_scores = w.csc;
   s.status = d.status;
-  s.rows_dyn = nserve;
-  e = launch_select_topk(s, w + L.sel_ws, stream);
+  s.rows_dyn = w.nserve;
+  e = launch_select_topk(s, w.sel_ws, stream);
   if (e != cudaSuccess) return e;
-  fallback_scatter_kernel<<<kFallbackRows, 256, 0, stream>>>(nserve, flag_rows, topk, cidx, csc,
-                                                             out_idx, out_scores);
+  fallback_scatter_kernel<<<kFallbackRows, 256, 0, stream>>>(w.nserve, w.flag_rows, topk, w.cidx,
+                                                             w.csc, out_idx, out_scores);
   return cudaGetLastError();
 }
 

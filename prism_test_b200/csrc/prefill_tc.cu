@@ -32,7 +32,11 @@
 //   kCand    appends every visible key with score >= T, packed as
 //            (order-preserving score key << 32 | ~index), to the row's candidate
 //            list [rows, cap] and stores the row's count (which may exceed cap:
-//            the selection then recomputes that row exactly).
+//            the selection then recomputes that row exactly). Per 16 scores a
+//            thread builds the bit mask of hits (a compare and an OR each), parks
+//            the 16 values in its own row of shared memory, and walks the set bits
+//            reading the hits back by index — registers cannot be indexed, and
+//            about 3 % of the scores are hits.
 //
 // Every mbarrier wait is bounded (2 s): on expiry the kernel records
 // kStatusTimeout, the roles leave their loops, and the TMEM is still freed.
@@ -46,8 +50,6 @@ namespace {
 
 enum PfMode : int { kScores = 0, kSample = 1, kCand = 2 };
 
-constexpr int kPfThreads = 320;
-constexpr int kPfEpiWarps = 8;
 constexpr uint32_t kAtomBytes = 128 * 128;       // 128 rows x 128 B
 constexpr uint32_t kTileBytes = 2 * kAtomBytes;  // 128 rows x 128 dims
 constexpr uint32_t kAOff = 0;                    // two query tiles
@@ -56,11 +58,20 @@ constexpr int kHistBins = 128;
 constexpr int kHistStride = 130;                 // u16 per row: 65 words, rows in distinct banks
 constexpr uint32_t kTmemCols = 512;
 
+constexpr int kStageStride = 16;  // floats per thread in the kCand staging rows
+
 template <int kMode>
 struct PfCfg {
+  // epilogue warps per (query tile, TMEM quadrant): each takes 128 / kSplit columns
+  static constexpr int kSplit = kMode == kSample ? 1 : 2;
+  static constexpr int kEpiWarps = 8 * kSplit;
+  static constexpr int kThreads = 64 + kEpiWarps * 32;
+  static constexpr int kChunks = 4 / kSplit;  // 32-column TMEM loads per thread and tile
   static constexpr int kStages = kMode == kSample ? 2 : 4;
   static constexpr uint32_t kHistOff = kBOff + kStages * kTileBytes;
-  static constexpr uint32_t kHistBytes = kMode == kSample ? 256 * kHistStride * 2 : 0;
+  static constexpr uint32_t kHistBytes =
+      kMode == kSample ? 256 * kHistStride * 2
+                       : (kMode == kCand ? kEpiWarps * 32 * kStageStride * 4 : 0);
   static constexpr uint32_t kBarOff = kHistOff + kHistBytes;
   static constexpr uint32_t kSmem = kBarOff + 256 + 1024;  // + alignment slack
 };
@@ -84,8 +95,8 @@ struct PfArgs {
   float* scores;       // kScores: [B * Hq * Sq, ld]
   int64_t ld;
   float* thr;          // kSample (out) / kCand (in): [B * Hq * Sq]
-  uint32_t* counts;    // kCand: [B * Hq * Sq]
-  uint64_t* cand;      // kCand: [B * Hq * Sq, cap]
+  uint32_t* counts;    // kCand: [B * Hq * Sq, 2] (front and back list of each row)
+  uint64_t* cand;      // kCand: [B * Hq * Sq, cap], filled from both ends
   int64_t cap;
   int topk;
   int pairs;           // CTAs per (batch, KV head)
@@ -99,7 +110,7 @@ __device__ __forceinline__ int64_t score_row(const PfArgs& a, int b, int h, int6
 }
 
 template <bool kBF16, int kMode>
-__global__ void __launch_bounds__(kPfThreads, 1)
+__global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const PfArgs a) {
   using Cfg = PfCfg<kMode>;
   constexpr int kStages = Cfg::kStages;
@@ -138,7 +149,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->tfull[i], 1);
-      mbar_init(&bars->tempty[i], kPfEpiWarps);
+      mbar_init(&bars->tempty[i], Cfg::kEpiWarps);
     }
     mbar_init(&bars->done, 1);
     fence_mbar_init();
@@ -151,7 +162,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   // dimensions [8c, 8c + 8) lands in atom c / 8 at row i, chunk (c % 8) ^ (i % 8)
   {
     const uint16_t* qg = static_cast<const uint16_t*>(a.q);
-    for (int e = threadIdx.x; e < 256 * 16; e += kPfThreads) {
+    for (int e = threadIdx.x; e < 256 * 16; e += Cfg::kThreads) {
       const int i = e >> 4, c = e & 15;
       const int64_t r = r0 + i;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -226,8 +237,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   } else {
     // ---- epilogue ------------------------------------------------------------------
-    const int qt = (warp - 2) >> 2;  // query tile
-    const int quad = warp & 3;       // TMEM lanes [32 quad, 32 quad + 32)
+    constexpr int kCols = 128 / Cfg::kSplit;
+    const int ew = warp - 2;
+    const int quad = warp & 3;         // TMEM lanes [32 quad, 32 quad + 32)
+    const int qt = (ew >> 2) & 1;      // query tile
+    const int half = ew >> 3;          // column part: [half * kCols, +kCols) of each tile
     const int rl = qt * 128 + quad * 32 + lane;  // row within the CTA
     const int64_t r = r0 + rl;
     const bool rvalid = r < r1;
@@ -249,9 +263,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     float thr = -INFINITY;  // kCand
     uint32_t cnt = 0;
     uint64_t* cl = nullptr;
-    if (kMode == kCand && rvalid) {
-      thr = a.thr[srow];
-      cl = a.cand + srow * a.cap;
+    float* stage = nullptr;
+    if (kMode == kCand) {
+      stage = reinterpret_cast<float*>(smem + Cfg::kHistOff) + (ew * 32 + lane) * kStageStride;
+      if (rvalid) {
+        thr = a.thr[srow];
+        cl = a.cand + srow * a.cap;
+      }
     }
     const int64_t nsamp = (nvis + kSampleStride - 1) / kSampleStride;  // samples it sees
     for (int t = 0; t < nkt; ++t) {
@@ -261,22 +279,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t v[4][32];
+      uint32_t v[Cfg::kChunks][32];
       const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16) + uint32_t(buf) * 256 +
-                             uint32_t(qt) * 128;
+                             uint32_t(qt) * 128 + uint32_t(half * kCols);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(taddr + uint32_t(c) * 32, v[c]);
+      for (int c = 0; c < Cfg::kChunks; ++c) tmem_ld32(taddr + uint32_t(c) * 32, v[c]);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tempty[buf]);
       if (!rvalid) continue;
       const int tt = t % ntile;
-      const int64_t j0 = int64_t(tt) * 128;  // first key (sample) of the tile
-      if (kMode == kScores) {
+      const int64_t j0 = int64_t(tt) * 128 + half * kCols;  // first key (sample) of this part
+      if constexpr (kMode == kScores) {
         float* dst = a.scores + srow * a.ld + j0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < Cfg::kChunks; ++c) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
             const int64_t j = j0 + c * 32 + i;
@@ -294,7 +312,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
           }
         }
-      } else if (kMode == kSample) {
+      } else if constexpr (kMode == kSample) {
         const int64_t lim = nsamp - j0;  // samples of this tile the row sees
         if (t < ntile) {
 #pragma unroll
@@ -322,18 +340,50 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
         }
       } else {  // kCand
+        const uint32_t cap = uint32_t(a.cap);
+        // half 0 fills the row's list from the front, half 1 from the back
+        auto emit = [&](float x, uint32_t j) {
+          if (cnt < cap) {
+            const uint32_t slot = half ? cap - 1u - cnt : cnt;
+            cl[slot] = (uint64_t(float_to_okey(x)) << 32) | uint64_t(~j);
+          }
+          ++cnt;
+        };
+        const bool all_vis = j0 + kCols <= nvis;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < Cfg::kChunks; ++c) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float x = __uint_as_float(v[c][i]);
-            const int64_t j = j0 + c * 32 + i;
-            if ((x >= thr || x != x) && j < nvis) {  // NaN ranks above every number
-              if (cnt < uint32_t(a.cap))
-                cl[cnt] = (uint64_t(float_to_okey(x)) << 32) | uint64_t(~uint32_t(j));
-              ++cnt;
+          for (int hh = 0; hh < 2; ++hh) {
+            const int o = 16 * hh;  // these 16 values: v[c][o .. o + 15]
+            uint32_t m = 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)  // NaN (unordered) counts as a hit: it ranks first
+              if (!(__uint_as_float(v[c][o + i]) < thr)) m |= 1u << i;
+            if (!all_vis) {
+              const int64_t lim = nvis - (j0 + 32 * c + o);
+              m &= lim >= 16 ? 0xffffu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
+            }
+            if (m == 0) continue;
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<uint4*>(stage + i) =
+                  make_uint4(v[c][o + i], v[c][o + i + 1], v[c][o + i + 2], v[c][o + i + 3]);
+            const uint32_t jb = uint32_t(j0 + 32 * c + o);
+            // the first two hits without a loop (their shared loads overlap), then the rest
+            const int i1 = __ffs(m) - 1;
+            const uint32_t m2 = m & (m - 1);
+            const int i2 = m2 ? __ffs(m2) - 1 : i1;
+            const float x1 = stage[i1], x2 = stage[i2];
+            emit(x1, jb + uint32_t(i1));
+            if (m2) emit(x2, jb + uint32_t(i2));
+            uint32_t m3 = m2 & (m2 - 1);
+            while (m3) {
+              const int i = __ffs(m3) - 1;
+              m3 &= m3 - 1;
+              emit(stage[i], jb + uint32_t(i));
             }
           }
+        }
       }
     }
     if (rvalid && kMode == kSample) {
@@ -358,9 +408,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       a.thr[srow] = T;
     }
-    if (rvalid && kMode == kCand) a.counts[srow] = cnt;
+    if (rvalid && kMode == kCand) a.counts[2 * srow + half] = cnt;
     // kScores: keys past the last tile any row of this CTA sees are masked
-    if (rvalid && kMode == kScores) {
+    if (rvalid && kMode == kScores && half == 0) {
       float* dst = a.scores + srow * a.ld;
       for (int64_t j = int64_t(ntile) * 128; j < a.Sk; ++j) dst[j] = -INFINITY;
     }
@@ -401,7 +451,7 @@ cudaError_t launch_mode(const CUtensorMap& kmap, const PfArgs& a, int dtype, int
   constexpr uint32_t smem = PfCfg<kMode>::kSmem;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  kern<<<dim3(unsigned(grid)), kPfThreads, smem, stream>>>(kmap, a);
+  kern<<<dim3(unsigned(grid)), PfCfg<kMode>::kThreads, smem, stream>>>(kmap, a);
   return cudaGetLastError();
 }
 
