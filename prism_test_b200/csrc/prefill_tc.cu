@@ -58,7 +58,8 @@ constexpr int kHistBins = 128;
 constexpr int kHistStride = 130;                 // u16 per row: 65 words, rows in distinct banks
 constexpr uint32_t kTmemCols = 512;
 
-constexpr int kStageStride = 16;  // floats per thread in the kCand staging rows
+constexpr int kStageStride = 20;  // floats per thread in the kCand staging rows (16 used;
+                                   // 20 keeps a warp's 16-byte stores bank-conflict free)
 
 template <int kMode>
 struct PfCfg {
@@ -67,7 +68,7 @@ struct PfCfg {
   static constexpr int kEpiWarps = 8 * kSplit;
   static constexpr int kThreads = 64 + kEpiWarps * 32;
   static constexpr int kChunks = 4 / kSplit;  // 32-column TMEM loads per thread and tile
-  static constexpr int kStages = kMode == kSample ? 2 : 4;
+  static constexpr int kStages = kMode == kScores ? 4 : (kMode == kSample ? 2 : 3);
   static constexpr uint32_t kHistOff = kBOff + kStages * kTileBytes;
   static constexpr uint32_t kHistBytes =
       kMode == kSample ? 256 * kHistStride * 2
@@ -102,6 +103,14 @@ struct PfArgs {
   int pairs;           // CTAs per (batch, KV head)
   int* status;
 };
+
+// Shifts the sign bit of d in at the bottom of m: m = (m << 1) | (d >> 31), one
+// funnel shift.
+__device__ __forceinline__ uint32_t push_sign(uint32_t m, float d) {
+  uint32_t r;
+  asm("shf.l.wrap.b32 %0, %1, %2, 1;" : "=r"(r) : "r"(__float_as_uint(d)), "r"(m));
+  return r;
+}
 
 // flattened score row of row r (g-major) of KV head h in batch b
 __device__ __forceinline__ int64_t score_row(const PfArgs& a, int b, int h, int64_t r) {
@@ -355,10 +364,18 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const int o = 16 * hh;  // these 16 values: v[c][o .. o + 15]
+            // bit i of m = sign of (x_i - T), i.e. x_i < T: the values go in from the
+            // last, two subtractions per packed instruction. x - T is never -0, and a
+            // NaN x gives the canonical NaN (sign 0), so NaN is a hit: it ranks first.
             uint32_t m = 0;
 #pragma unroll
-            for (int i = 0; i < 16; ++i)  // NaN (unordered) counts as a hit: it ranks first
-              if (!(__uint_as_float(v[c][o + i]) < thr)) m |= 1u << i;
+            for (int i = 14; i >= 0; i -= 2) {
+              const float2 d = __fadd2_rn(
+                  make_float2(__uint_as_float(v[c][o + i]), __uint_as_float(v[c][o + i + 1])),
+                  make_float2(-thr, -thr));
+              m = push_sign(push_sign(m, d.y), d.x);
+            }
+            m = ~m & 0xffffu;  // hits
             if (!all_vis) {
               const int64_t lim = nvis - (j0 + 32 * c + o);
               m &= lim >= 16 ? 0xffffu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
