@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
     }
     // per-mode row state
     float mn = INFINITY, mx = -INFINITY, inv_w = 0.f;  // kSample
-    uint16_t* hist = nullptr;
+    uint16_t* hist = nullptr;  // kSample: the row's 128 bins (only this thread's)
     if (kMode == kSample) {
       hist = reinterpret_cast<uint16_t*>(smem + Cfg::kHistOff) + rl * kHistStride;
       for (int i = 0; i < kHistStride / 2; ++i) reinterpret_cast<uint32_t*>(hist)[i] = 0u;
@@ -351,11 +351,13 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
       } else {  // kCand
         const uint32_t cap = uint32_t(a.cap);
         // half 0 fills the row's list from the front, half 1 from the back
+        // branch-free append: past the capacity the last slot is overwritten (the
+        // row is then recomputed exactly, its list unused)
+        uint64_t* const lbase = half ? cl + (cap - 1u) : cl;
+        const int64_t lstep = half ? -1 : 1;
         auto emit = [&](float x, uint32_t j) {
-          if (cnt < cap) {
-            const uint32_t slot = half ? cap - 1u - cnt : cnt;
-            cl[slot] = (uint64_t(float_to_okey(x)) << 32) | uint64_t(~j);
-          }
+          const uint32_t slot = cnt < cap - 1u ? cnt : cap - 1u;
+          lbase[lstep * int64_t(slot)] = (uint64_t(float_to_okey(x)) << 32) | uint64_t(~j);
           ++cnt;
         };
         const bool all_vis = j0 + kCols <= nvis;

@@ -67,6 +67,9 @@ WORKLOADS: Dict[str, Workload] = {
     # as the exact method's cache holds them (reattention_exact.py:545-547)
     "prefill-chunk-128k": Workload("prefill-chunk-128k", 1, 32, 8, 4096, 131072, 5e5, 2048,
                                    causal_offset=126976, rope=False),
+    # the same chunk cut to its last 512 query rows (profiling-sized)
+    "prefill-chunk-128k-512rows": Workload("prefill-chunk-128k-512rows", 1, 32, 8, 512, 131072,
+                                           5e5, 2048, causal_offset=130560, rope=False),
     # 1M-key decode, sequence-sharded over N GPUs
     "decode-1m-sharded": Workload("decode-1m-sharded", 1, 32, 8, 1, 1 << 20, 5e5, 8192,
                                   planted_per_qhead=64, planted_sigma=5.0),
