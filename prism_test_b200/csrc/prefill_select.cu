@@ -91,8 +91,10 @@ __device__ __forceinline__ uint32_t ps_scan(uint32_t v, uint32_t* wtot, uint32_t
 
 __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  uint64_t* buf = reinterpret_cast<uint64_t*>(smem);                       // [cap]
-  uint32_t* hist = reinterpret_cast<uint32_t*>(buf + a.cap);               // [kPsBins]
+  // candidates' score keys only (their indices are re-read from the row's list,
+  // which is still in L2, for ties and for the output): 6 bytes per candidate
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem);                      // [cap]
+  uint32_t* hist = keys + a.cap;                                           // [kPsBins]
   uint16_t* perm = reinterpret_cast<uint16_t*>(hist + kPsBins);            // [cap]
   __shared__ uint32_t wtot[kPsThreads / 32];
   __shared__ uint32_t s_kmax, s_kmin, s_big;  // max / min key of the finite scores
@@ -124,11 +126,11 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
   for (int i = tid; i < kPsBins; i += kPsThreads) hist[i] = 0u;
   __syncthreads();
   const uint64_t* src = a.cand + row * a.cap;
+  auto cand_at = [&](uint32_t i) { return i < n0 ? src[i] : src[a.cap - 1 - (i - n0)]; };
   uint32_t kmx = 0u, kmn = 0xffffffffu;
   for (uint32_t i = tid; i < n; i += kPsThreads) {
-    const uint64_t x = i < n0 ? src[i] : src[a.cap - 1 - (i - n0)];
-    buf[i] = x;
-    const uint32_t key = uint32_t(x >> 32);
+    const uint32_t key = uint32_t(cand_at(i) >> 32);
+    keys[i] = key;
     if (key != 0xffffffffu) {  // NaN is binned apart
       kmx = max(kmx, key);
       kmn = min(kmn, key);
@@ -143,14 +145,13 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
   __syncthreads();
   const float fmax = okey_to_float(s_kmax), fmin = okey_to_float(s_kmin);
   const float scale = fmax > fmin ? float(kPsBins - 1) / (fmax - fmin) : 0.f;
-  // bin of a packed candidate: monotone non-increasing in its score
-  auto bin_of = [&](uint64_t x) -> uint32_t {
-    const uint32_t key = uint32_t(x >> 32);
+  // bin of a score key: monotone non-increasing in the score
+  auto bin_of = [&](uint32_t key) -> uint32_t {
     if (key == 0xffffffffu) return 0u;
     const float b = (fmax - okey_to_float(key)) * scale;
     return b >= float(kPsBins - 1) ? uint32_t(kPsBins - 1) : (b > 0.f ? uint32_t(b) : 0u);
   };
-  for (uint32_t i = tid; i < n; i += kPsThreads) atomicAdd(&hist[bin_of(buf[i])], 1u);
+  for (uint32_t i = tid; i < n; i += kPsThreads) atomicAdd(&hist[bin_of(keys[i])], 1u);
   __syncthreads();
   {
     constexpr int kPer = kPsBins / kPsThreads;
@@ -176,7 +177,7 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
     if (tid == 0) flag_row(a, row);
     return;
   }
-  for (uint32_t i = tid; i < n; i += kPsThreads) perm[atomicAdd(&hist[bin_of(buf[i])], 1u)] = uint16_t(i);
+  for (uint32_t i = tid; i < n; i += kPsThreads) perm[atomicAdd(&hist[bin_of(keys[i])], 1u)] = uint16_t(i);
   __syncthreads();  // hist[f] is now the end of bin f
   // candidates in the bins that hold output positions [0, keff)
   uint32_t fend = 0;  // first bin whose start is >= keff
@@ -191,15 +192,26 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
   const uint32_t qend = hist[fend < kPsBins ? fend : kPsBins - 1];
   for (uint32_t q = tid; q < qend; q += kPsThreads) {
     const uint32_t i = perm[q];
-    const uint64_t x = buf[i];
-    const uint32_t f = bin_of(x);
+    const uint32_t kx = keys[i];
+    const uint32_t f = bin_of(kx);
     const uint32_t s = f ? hist[f - 1] : 0u;
     const uint32_t e = hist[f];
-    uint32_t p = s;
-    for (uint32_t j = s; j < e; ++j) p += buf[perm[j]] > x;
+    uint32_t p = s, ties = 0;
+    for (uint32_t j = s; j < e; ++j) {
+      const uint32_t ky = keys[perm[j]];
+      p += ky > kx;
+      ties += ky == kx;  // this candidate included
+    }
+    const uint64_t x = cand_at(i);
+    if (ties > 1) {  // equal scores: the lower index goes first
+      for (uint32_t j = s; j < e; ++j) {
+        const uint32_t pj = perm[j];
+        if (pj != i && keys[pj] == kx) p += cand_at(pj) > x;
+      }
+    }
     if (p < keff) {
       oi[p] = int32_t(int64_t(~uint32_t(x)) + a.index_base);
-      if (os) os[p] = okey_to_float(uint32_t(x >> 32));
+      if (os) os[p] = okey_to_float(kx);
     }
   }
 }
@@ -386,7 +398,7 @@ cudaError_t prefill_stream_select(const DecodeArgs& d, int dtype, int topk, int6
   p.nflag = w.nflag;
   p.flag_rows = w.flag_rows;
   p.status = d.status;
-  const size_t smem = size_t(w.cap) * 10 + kPsBins * 4;
+  const size_t smem = size_t(w.cap) * 6 + kPsBins * 4;
   cudaError_t e = cudaFuncSetAttribute(prefill_select_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;

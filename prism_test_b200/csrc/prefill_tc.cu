@@ -23,9 +23,10 @@
 // Modes (the epilogue's work):
 //   kScores  writes the fp32 score matrix [rows, ld] (masked keys -inf) for the
 //            selection kernels;
-//   kSample  streams a strided sample of the keys (every kSampleStride-th) twice:
-//            pass 1 takes each row's sample minimum and maximum, pass 2 a
-//            128-bin histogram between them (per-row bins in shared memory);
+//   kSample  streams a strided sample of the keys (every kSampleStride-th): pass
+//            1 takes each row's minimum and maximum over the first quarter of the
+//            sample, pass 2 a 128-bin histogram of the whole sample between them
+//            (values outside in the end bins; per-row bins in shared memory);
 //            the row's threshold T is the lower edge of the bin holding sample
 //            rank m = 1.1 e + 4 sqrt(e) + 8, e = k * samples / keys visible
 //            (-inf when the row sees at most k keys);
@@ -148,8 +149,11 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
   // key tiles per pass (sample tiles in kSample) and passes
   const int64_t nitems = kMode == kSample ? (nkeys + kSampleStride - 1) / kSampleStride : nkeys;
   const int ntile = int((nitems + 127) / 128);
-  const int npass = kMode == kSample ? 2 : 1;
-  const int nkt = ntile * npass;
+  // kSample: pass 1 (range) over the first quarter of the sample tiles, pass 2
+  // (histogram) over all of them; tile t of the loop is sample tile tile_of(t)
+  const int q1 = kMode == kSample ? (ntile + 3) / 4 : 0;
+  const int nkt = ntile + q1;
+  auto tile_of = [&](int t) { return t < q1 ? t : t - q1; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
           set_status(a.status, kStatusTimeout);
           break;
         }
-        const int tt = t % ntile;  // tile within the pass
+        const int tt = tile_of(t);  // tile within the pass
         mbar_arrive_expect_tx(&bars->full[s], kTileBytes);
         uint8_t* dst = smem + kBOff + uint32_t(s) * kTileBytes;
         tma_load_4d(dst, &kmap, 0, tt * 128, h, kb, &bars->full[s], pol);
@@ -298,7 +302,7 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tempty[buf]);
       if (!rvalid) continue;
-      const int tt = t % ntile;
+      const int tt = tile_of(t);
       const int64_t j0 = int64_t(tt) * 128 + half * kCols;  // first key (sample) of this part
       if constexpr (kMode == kScores) {
         float* dst = a.scores + srow * a.ld + j0;
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
         }
       } else if constexpr (kMode == kSample) {
         const int64_t lim = nsamp - j0;  // samples of this tile the row sees
-        if (t < ntile) {
+        if (t < q1) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -334,7 +338,7 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
                 mx = fmaxf(mx, x);
               }
             }
-          if (t == ntile - 1) inv_w = mx > mn ? float(kHistBins) / (mx - mn) : 0.f;
+          if (t == q1 - 1) inv_w = mx > mn ? float(kHistBins) / (mx - mn) : 0.f;
         } else {
 #pragma unroll
           for (int c = 0; c < 4; ++c)

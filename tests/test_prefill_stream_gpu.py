@@ -78,3 +78,14 @@ def test_stream_full_prefill_chunk_sampled_rows(cuda_device, monkeypatch):
     n = wl.B * wl.Hq * wl.Sq
     rows = sorted(set(list(range(0, n, n // 96)) + [1, 4095, 4096, n - 1]))
     check_rows_parity(idx, sc, x["q"], x["k"], wl.topk, rows, wl.causal_offset)
+
+
+def test_stream_duplicate_keys_tie_by_index(cuda_device):
+    # every key appears three times: equal scores must come out lowest index first
+    g = torch.Generator(device=cuda_device).manual_seed(21)
+    q = torch.randn(1, 8, 128, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    base = torch.randn(1, 2, 3000, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    k = base.repeat_interleave(3, dim=2)[:, :, :8192].contiguous()
+    a = einsum_topk_func(q, k, 600, return_scores=True, mode="stream")
+    b = einsum_topk_func(q, k, 600, return_scores=True, mode="exact")
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
