@@ -142,6 +142,40 @@ PRISM_API int prism_einsum_topk_weighted(const void* q, const void* k, const voi
                                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Attention over the selected view: the step after the recall selection in the
+ * exact method. Replaces ReAttentionExactMethod._chunk_attention's gather of
+ * the [global | recalled | local] view from the raw cache, its RoPE of keys and
+ * queries at their positions (eval_harness/attention_methods/
+ * reattention_exact.py:453-508) and the eager path of _attend (:650-661):
+ * softmax(q k^T * scale) v in fp32, keys at absolute positions above a query's
+ * masked, a query that sees no key giving zeros (the reference's nan_to_num).
+ *
+ *   q          [B, Hq, Sq, D] raw (pre-RoPE) queries of `dtype`, q_strides in
+ *              elements, q_strides[3] == 1, other strides multiples of 4.
+ *   k, v       [B, Hkv, S, D] raw cache; rows contiguous (strides[2] == D,
+ *              strides[3] == 1), base and strides 8-byte aligned.
+ *   key_pos    int64 [nsel] device array: absolute positions of the view (its
+ *              order is the view's order). A position outside [0, S) is skipped
+ *              and reported in the status word (prism_read_status).
+ *   q_pos      int64 [Sq] device array: absolute positions of the query rows.
+ *   inv_freq   [D/2] fp32 or NULL (no rotation).
+ *   pe_original  1: RoPE at the absolute positions; 0: keys at 0 .. nsel-1 and
+ *              query row i at nsel - Sq + i (the contiguous re-rotation).
+ *   D          must be 128.
+ *   out        [B, Hq, Sq, D] contiguous, `dtype`.
+ *   workspace  prism_sparse_attention_workspace_size(B, Hq, Sq) bytes (256-aligned):
+ *              the status block and the per-split partial softmax states.
+ */
+PRISM_API int prism_sparse_attention(const void* q, const void* k, const void* v,
+                                     const int64_t* key_pos, int64_t nsel, const int64_t* q_pos,
+                                     const float* inv_freq, int32_t pe_original, float scale,
+                                     int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
+                                     int64_t S, int64_t D, const int64_t* q_strides,
+                                     const int64_t* k_strides, const int64_t* v_strides, void* out,
+                                     void* workspace, size_t workspace_bytes, void* stream);
+PRISM_API size_t prism_sparse_attention_workspace_size(int64_t B, int64_t Hq, int64_t Sq);
+
+/*
  * Exact top-k over candidate lists: for each of `rows` rows, picks the topk
  * largest of n (score, index) pairs laid out with row stride ld (ld % 4 == 0,
  * 16-byte aligned rows) and writes them sorted like prism_einsum_topk.
@@ -254,6 +288,7 @@ PRISM_API int prism_read_status(void* workspace, int* status_out, void* stream);
 #define PRISM_KERNEL_WEIGHT 3 /* value-row norms of the weighted recall */
 #define PRISM_KERNEL_SCALE 4  /* weighting of the score matrix by those norms */
 #define PRISM_KERNEL_THRESHOLD 5 /* sampled per-row thresholds of the streaming prefill path */
+#define PRISM_KERNEL_ATTN 6   /* attention over the selected view */
 PRISM_API int prism_profile_start(int32_t capacity);
 PRISM_API int prism_profile_stop(void);
 PRISM_API int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms);

@@ -24,6 +24,9 @@ path (RUSH-Intelligence/Prism-Test, eval_harness/attention_methods/):
                            qkv -> ||v||_1, qkv2 -> ||v||_2 per key, as the
                            values' dtype (``values.norm`` of a bf16/fp16 tensor);
                            the weighted raw key is raw_k (fp32) * that weight
+* ``sparse_attention``     ReAttentionExactMethod._chunk_attention's gather + RoPE
+                           (reattention_exact.py:453-508) and the eager path of
+                           _attend (:650-661), in fp32
 * ``blockmax_topk``        the fused Triton kernels einsum_topk.py:21-161 with the
                            4-wide merge of bitonic_merge_wrapper.py:5-52: per
                            128-key block the row maximum (first index on ties),
@@ -217,3 +220,36 @@ def recall_weights(values: Optional[torch.Tensor], recall_type: str) -> Optional
     if recall_type == "qkv2":
         return values.cpu().norm(p=2, dim=-1).to(torch.float32)
     raise ValueError(f"Unsupported recall_type '{recall_type}'. Use one of: qk, qkv, qkv2.")
+
+
+def sparse_attention(q: torch.Tensor, k_full: torch.Tensor, v_full: torch.Tensor, key_pos: torch.Tensor,
+                     q_pos: torch.Tensor, inv_freq: Optional[torch.Tensor], pe_original: bool,
+                     scale: float) -> torch.Tensor:
+    """Attention over the selected view, fp32 [B, Hq, Sq, D].
+
+    reattention_exact.py:453-508: sel_k / sel_v gathered at the absolute positions
+    ``key_pos``; RoPE positions ``key_pos`` / ``q_pos`` (pe_original) or
+    ``arange(view_len)`` / its last Sq (contiguous); then _attend's eager path
+    (:650-661): repeat_kv, (q k^T) * scale, keys with key_pos > q_pos masked to -inf,
+    fp32 softmax, nan_to_num (a row that sees nothing gives zeros), times v."""
+    key_pos = key_pos.cpu().long()
+    q_pos = q_pos.cpu().long()
+    sel_k = k_full.cpu().float()[:, :, key_pos]
+    sel_v = v_full.cpu().float()[:, :, key_pos]
+    qf = q.cpu().float()
+    view_len, q_len = key_pos.numel(), qf.shape[2]
+    if inv_freq is not None:
+        pe_k = key_pos if pe_original else torch.arange(view_len)
+        pe_q = q_pos if pe_original else torch.arange(view_len - q_len, view_len)
+        cos_k, sin_k = build_cos_sin(pe_k, inv_freq.cpu())
+        sel_k = apply_rotary_pos_emb(sel_k, cos_k, sin_k)
+        cos_q, sin_q = build_cos_sin(pe_q, inv_freq.cpu())
+        qf = apply_rotary_pos_emb(qf, cos_q, sin_q)
+    n_rep = max(1, qf.shape[1] // sel_k.shape[1])
+    kk = repeat_kv(sel_k, n_rep)
+    vv = repeat_kv(sel_v, n_rep)
+    attn = torch.matmul(qf, kk.transpose(2, 3)) * scale
+    attn = attn.masked_fill(key_pos[None, :] > q_pos[:, None], float("-inf"))
+    attn = torch.softmax(attn, dim=-1, dtype=torch.float32)
+    attn = torch.nan_to_num(attn, nan=0.0)
+    return torch.matmul(attn, vv)

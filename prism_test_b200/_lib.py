@@ -31,6 +31,7 @@ SPAN_FLOOR = 1
 KERNEL_WEIGHT = 3
 KERNEL_SCALE = 4
 KERNEL_THRESHOLD = 5
+KERNEL_ATTN = 6
 RECALL_QK = 0
 RECALL_QKV = 1
 RECALL_QKV2 = 2
@@ -60,6 +61,13 @@ SIGNATURES = {
     "prism_einsum_topk_workspace_size": (ctypes.c_size_t, [
         _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i32,
     ]),
+    "prism_sparse_attention": (ctypes.c_int, [
+        _vp, _vp, _vp, _vp, _c_i64, _vp, _vp, _c_i32, ctypes.c_float, ctypes.c_int,
+        _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+        ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64),
+        _vp, _vp, ctypes.c_size_t, _vp,
+    ]),
+    "prism_sparse_attention_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64]),
     "prism_topk_merge": (ctypes.c_int, [
         _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i32, _vp, _vp, _vp, ctypes.c_size_t, _vp,
     ]),

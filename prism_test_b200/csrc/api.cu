@@ -54,7 +54,7 @@ std::vector<cudaEvent_t> g_prof_pool;  // 2 * capacity events
 std::vector<ProfRec> g_prof_recs;
 bool g_prof_on = false;
 size_t g_prof_next = 0;
-int64_t g_prof_untimed[6] = {0, 0, 0, 0, 0, 0};
+int64_t g_prof_untimed[7] = {0, 0, 0, 0, 0, 0, 0};
 
 // Runs `launch` (which enqueues one kernel on `stream`), counting it and, while
 // profiling is on, bracketing it with a pair of events from the pool.
@@ -407,6 +407,83 @@ int prism_einsum_topk_weighted(const void* q, const void* k, const void* v, cons
                           workspace, workspace_bytes, stream_ptr, &wa);
 }
 
+size_t prism_sparse_attention_workspace_size(int64_t B, int64_t Hq, int64_t Sq) {
+  if (B <= 0 || Hq <= 0 || Sq <= 0) return 0;
+  return kStatusBytes + prism::sparse_attn_workspace_bytes(B, Hq, Sq);
+}
+
+int prism_sparse_attention(const void* q, const void* k, const void* v, const int64_t* key_pos,
+                           int64_t nsel, const int64_t* q_pos, const float* inv_freq,
+                           int32_t pe_original, float scale, int dtype, int64_t B, int64_t Hq,
+                           int64_t Hkv, int64_t Sq, int64_t S, int64_t D,
+                           const int64_t* q_strides, const int64_t* k_strides,
+                           const int64_t* v_strides, void* out, void* workspace,
+                           size_t workspace_bytes, void* stream_ptr) {
+  g_last_error.clear();
+  if (!q || !k || !v || !key_pos || !q_pos || !out || !q_strides || !k_strides || !v_strides)
+    return fail(PRISM_E_INVALID, "null pointer argument");
+  if (dtype != PRISM_DTYPE_BF16 && dtype != PRISM_DTYPE_FP16)
+    return fail(PRISM_E_INVALID, "dtype must be PRISM_DTYPE_BF16 or PRISM_DTYPE_FP16");
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || S <= 0 || nsel <= 0)
+    return fail(PRISM_E_INVALID, "all of B, Hq, Hkv, Sq, S, nsel must be positive");
+  if (Hq % Hkv != 0) return fail(PRISM_E_INVALID, "num_heads must be divisible by num_heads_k");
+  if (D != prism::kHeadDim) return fail(PRISM_E_UNSUPPORTED, "head_dim must be 128, got %lld", (long long)D);
+  if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1)
+    return fail(PRISM_E_INVALID, "q, k and v must have unit stride in the last dimension");
+  if (k_strides[2] != D || v_strides[2] != D)
+    return fail(PRISM_E_INVALID, "key and value rows must be contiguous (stride(-2) == head_dim)");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+       reinterpret_cast<uintptr_t>(v)) & 7u)
+    return fail(PRISM_E_INVALID, "q, k and v must be 8-byte aligned");
+  for (int i = 0; i < 3; ++i)
+    if (q_strides[i] % 4 || k_strides[i] % 4 || v_strides[i] % 4)
+      return fail(PRISM_E_INVALID, "q, k and v strides must be multiples of 4 elements");
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0)
+    return fail(PRISM_E_INVALID, "out must be 16-byte aligned");
+  const size_t need = prism_sparse_attention_workspace_size(B, Hq, Sq);
+  if (!workspace || workspace_bytes < need)
+    return fail(PRISM_E_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(PRISM_E_INVALID, "workspace must be 256-byte aligned");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* status = reinterpret_cast<int*>(ws);
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
+  prism::SparseAttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.key_pos = key_pos;
+  a.q_pos = q_pos;
+  a.inv_freq = inv_freq;
+  a.pe_original = pe_original ? 1 : 0;
+  a.scale = scale;
+  a.B = int(B);
+  a.Hq = int(Hq);
+  a.Hkv = int(Hkv);
+  a.G = int(Hq / Hkv);
+  a.Sq = int(Sq);
+  a.S = S;
+  a.nsel = nsel;
+  a.q_sb = q_strides[0];
+  a.q_sh = q_strides[1];
+  a.q_ss = q_strides[2];
+  a.k_sb = k_strides[0];
+  a.k_sh = k_strides[1];
+  a.v_sb = v_strides[0];
+  a.v_sh = v_strides[1];
+  a.out = out;
+  a.status = status;
+  const int nsm = num_sms_current_device();
+  e = launch_counted(PRISM_KERNEL_ATTN, stream, [&] {
+    return prism::launch_sparse_attn(a, dtype, ws + kStatusBytes, nsm, stream);
+  });
+  if (e != cudaSuccess) return cuda_fail(e, "sparse attention launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);  // partial + combine
+  return PRISM_OK;
+}
+
 size_t prism_topk_merge_workspace_size(int64_t rows, int64_t n) {
   if (rows < 0 || n <= 0) return 0;
   return prism::select_workspace_bytes(rows, n);
@@ -539,7 +616,7 @@ int prism_profile_stop(void) {
 
 int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms) {
   g_last_error.clear();
-  if (!launches || !total_ms || kernel < 0 || kernel > PRISM_KERNEL_THRESHOLD)
+  if (!launches || !total_ms || kernel < 0 || kernel > PRISM_KERNEL_ATTN)
     return fail(PRISM_E_INVALID, "bad kernel id or null output");
   int64_t n = 0;
   double ms = 0.0;

@@ -146,6 +146,32 @@ size_t weight_workspace_bytes(int64_t B, int64_t Hkv, int64_t Sk);
 cudaError_t launch_value_norms(const WeightArgs& a, int dtype, int num_sms, cudaStream_t stream);
 cudaError_t launch_scale_scores(const WeightArgs& a, int num_sms, cudaStream_t stream);
 
+// Attention over a selected view (sparse_attn.cu): gathered keys/values at the
+// view's absolute positions key_pos[nsel], RoPE at the view's positions (if
+// inv_freq), causal by absolute position, fp32 softmax; split over the view.
+constexpr int kSparseMaxSplits = 64;
+struct SparseAttnArgs {
+  const void* q;          // [B, Hq, Sq, 128]
+  const void* k;          // [B, Hkv, S, 128], rows contiguous
+  const void* v;          // [B, Hkv, S, 128], rows contiguous
+  const int64_t* key_pos; // [nsel] absolute positions of the view (< S)
+  const int64_t* q_pos;   // [Sq] absolute positions of the query rows
+  const float* inv_freq;  // [64] or nullptr (no rotation)
+  int pe_original;        // RoPE at absolute positions (1) or at 0 .. nsel-1 with the queries last (0)
+  float scale;
+  int B, Hq, Hkv, G, Sq;
+  int64_t S, nsel;
+  int64_t q_sb, q_sh, q_ss, k_sb, k_sh, v_sb, v_sh;
+  void* out;              // [B, Hq, Sq, 128] contiguous, dtype of q
+  int* status;
+  float* part_m;          // workspace (set by the launcher)
+  float* part_l;
+  float* part_acc;
+};
+size_t sparse_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq);
+cudaError_t launch_sparse_attn(SparseAttnArgs a, int dtype, void* ws, int num_sms,
+                               cudaStream_t stream);
+
 // Sets the message prism_last_error() returns for the calling thread.
 void set_last_error(const char* msg);
 

@@ -1,0 +1,296 @@
+// Attention over the selected [global | recalled | local] view — the step after
+// the recall selection in the exact method: ReAttentionExactMethod._chunk_attention
+// gathers the view's keys and values from the raw (pre-RoPE) cache by absolute
+// position, rotates keys and queries at their RoPE positions and attends
+// (eval_harness/attention_methods/reattention_exact.py:453-508), with the eager
+// path of _attend (:650-661): softmax(q k^T * scale) v in fp32, keys past a
+// query's absolute position masked, fully masked rows giving zeros.
+//
+// sparse_attn_partial_kernel: a CTA takes up to kRB query rows (g-major rows of
+// one (batch, KV head)) and one split of the view; each of its 8 warps walks the
+// split's keys j = warp, warp + 8, ...: the key and value rows are gathered with
+// one coalesced 8-byte load per lane (lane L holds dimensions 4L .. 4L+3), the
+// key is rotated at its RoPE position in registers (lanes L and L ^ 16 hold the
+// two halves of a rotation pair; each computes two of the pair group's four
+// angles and they swap them), dotted with every query row (fp32, warp
+// reduction), and folded into the row's online softmax (running max, sum and
+// the unnormalised value accumulator). The warps' states are merged in shared
+// memory and the CTA writes one partial (m, l, acc[128]) per row and split.
+// sparse_attn_combine_kernel merges the splits of each row and writes the output.
+#include "common.cuh"
+#include "kernels.h"
+#include "rope_sincos.cuh"
+
+namespace prism {
+namespace {
+
+constexpr int kSaWarps = 8;
+constexpr int kRB = 8;  // query rows per CTA
+
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  float4 f;
+  Unpack<T>::run(u.x, f.x, f.y);
+  Unpack<T>::run(u.y, f.z, f.w);
+  return f;
+}
+
+template <typename T>
+__device__ __forceinline__ void store4(T* p, float4 f);
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float4 f) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(f.x, f.y), b = __floats2bfloat162_rn(f.z, f.w);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+template <>
+__device__ __forceinline__ void store4<__half>(__half* p, float4 f) {
+  __half2 a = __floats2half2_rn(f.x, f.y), b = __floats2half2_rn(f.z, f.w);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+// RoPE of the lane's 4 dimensions at position pe: lanes L < 16 hold x_i (i in
+// [4L, 4L+4)), lanes L + 16 hold x_{i+64}; out_i = x_i c_i - x_{i+64} s_i,
+// out_{i+64} = x_{i+64} c_i + x_i s_i (apply_rotary_pos_emb, _method_base.py:324-333).
+__device__ __forceinline__ float4 rope4(float4 x, float pe, const float* inv_lane, int lane) {
+  // this lane computes the angles of 2 of its group's 4 frequencies, the partner the other 2
+  const int base = (lane & 16) ? 2 : 0;
+  float s0, c0, s1, c1;
+  rope_sincos_fast(__fmul_rn(pe, inv_lane[base]), s0, c0);
+  rope_sincos_fast(__fmul_rn(pe, inv_lane[base + 1]), s1, c1);
+  const float os0 = __shfl_xor_sync(0xffffffffu, s0, 16), oc0 = __shfl_xor_sync(0xffffffffu, c0, 16);
+  const float os1 = __shfl_xor_sync(0xffffffffu, s1, 16), oc1 = __shfl_xor_sync(0xffffffffu, c1, 16);
+  float sn[4], cs[4];
+  if (lane & 16) {
+    sn[0] = os0; cs[0] = oc0; sn[1] = os1; cs[1] = oc1; sn[2] = s0; cs[2] = c0; sn[3] = s1; cs[3] = c1;
+  } else {
+    sn[0] = s0; cs[0] = c0; sn[1] = s1; cs[1] = c1; sn[2] = os0; cs[2] = oc0; sn[3] = os1; cs[3] = oc1;
+  }
+  float4 p;  // partner half
+  p.x = __shfl_xor_sync(0xffffffffu, x.x, 16);
+  p.y = __shfl_xor_sync(0xffffffffu, x.y, 16);
+  p.z = __shfl_xor_sync(0xffffffffu, x.z, 16);
+  p.w = __shfl_xor_sync(0xffffffffu, x.w, 16);
+  const float sg = (lane & 16) ? 1.f : -1.f;
+  float4 o;
+  o.x = fmaf(sg * p.x, sn[0], x.x * cs[0]);
+  o.y = fmaf(sg * p.y, sn[1], x.y * cs[1]);
+  o.z = fmaf(sg * p.z, sn[2], x.z * cs[2]);
+  o.w = fmaf(sg * p.w, sn[3], x.w * cs[3]);
+  return o;
+}
+
+__device__ __forceinline__ float dot4(float4 a, float4 b) {
+  return fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, a.w * b.w)));
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+template <typename T, bool kRope>
+__global__ void __launch_bounds__(kSaWarps * 32)
+    sparse_attn_partial_kernel(const SparseAttnArgs a) {
+  __shared__ float s_m[kSaWarps][kRB], s_l[kSaWarps][kRB];
+  __shared__ float4 s_acc[kSaWarps][kRB][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t R = int64_t(a.G) * a.Sq;  // query rows of a KV head
+  const int nrb = int((R + kRB - 1) / kRB);
+  const int rb = blockIdx.x % nrb;
+  const int bh = blockIdx.x / nrb;
+  const int b = bh / a.Hkv, h = bh - b * a.Hkv;
+  const int split = blockIdx.y, nsplit = gridDim.y;
+  const int64_t per = (a.nsel + nsplit - 1) / nsplit;
+  const int64_t j0 = int64_t(split) * per;
+  const int64_t j1 = j0 + per < a.nsel ? j0 + per : a.nsel;
+
+  // this lane's frequencies: i = (4 * lane) mod 64 + 0..3
+  float inv_lane[4] = {0.f, 0.f, 0.f, 0.f};
+  if (kRope) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) inv_lane[e] = a.inv_freq[(4 * lane + e) & 63];
+  }
+  const int64_t r0 = int64_t(rb) * kRB;
+  const int nrows = int(R - r0 < kRB ? R - r0 : kRB);
+
+  // rotated queries (fp32, 4 dims per lane) and their absolute positions
+  float4 q[kRB];
+  int64_t qabs[kRB];
+#pragma unroll
+  for (int r = 0; r < kRB; ++r) {
+    q[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    qabs[r] = -1;
+    if (r < nrows) {
+      const int64_t rr = r0 + r, g = rr / a.Sq, s = rr - g * a.Sq;
+      const T* qr = static_cast<const T*>(a.q) + int64_t(b) * a.q_sb +
+                    (int64_t(h) * a.G + g) * a.q_sh + s * a.q_ss;
+      qabs[r] = a.q_pos[s];
+      const float pe = a.pe_original ? float(qabs[r]) : float(a.nsel - a.Sq + s);
+      q[r] = load4<T>(qr + 4 * lane);
+      if (kRope) q[r] = rope4(q[r], pe, inv_lane, lane);
+      q[r].x *= a.scale;
+      q[r].y *= a.scale;
+      q[r].z *= a.scale;
+      q[r].w *= a.scale;
+    }
+  }
+  float m[kRB], l[kRB];
+  float4 acc[kRB];
+#pragma unroll
+  for (int r = 0; r < kRB; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+    acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const T* kb = static_cast<const T*>(a.k) + (a.B > 1 ? int64_t(b) * a.k_sb : 0) + int64_t(h) * a.k_sh;
+  const T* vb = static_cast<const T*>(a.v) + (a.B > 1 ? int64_t(b) * a.v_sb : 0) + int64_t(h) * a.v_sh;
+  for (int64_t j = j0 + warp; j < j1; j += kSaWarps) {
+    const int64_t p = a.key_pos[j];
+    if (p < 0 || p >= a.S) {  // a position outside the cache: skipped and reported
+      if (lane == 0) set_status(a.status, kStatusBounds);
+      continue;
+    }
+    const float4 kv = load4<T>(kb + p * 128 + 4 * lane);
+    const float4 vv = load4<T>(vb + p * 128 + 4 * lane);
+    const float pe = a.pe_original ? float(p) : float(j);
+    const float4 kr = kRope ? rope4(kv, pe, inv_lane, lane) : kv;
+#pragma unroll
+    for (int r = 0; r < kRB; ++r) {
+      if (r >= nrows) break;
+      if (p > qabs[r]) continue;  // causal by absolute position (uniform across the warp)
+      const float sc = warp_sum(dot4(q[r], kr));
+      const float mn = fmaxf(m[r], sc);
+      const float corr = __expf(m[r] - mn);  // m = -inf at first: corr = 0
+      const float e = __expf(sc - mn);
+      l[r] = fmaf(l[r], corr, e);
+      acc[r].x = fmaf(acc[r].x, corr, e * vv.x);
+      acc[r].y = fmaf(acc[r].y, corr, e * vv.y);
+      acc[r].z = fmaf(acc[r].z, corr, e * vv.z);
+      acc[r].w = fmaf(acc[r].w, corr, e * vv.w);
+      m[r] = mn;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kRB; ++r) {
+    if (lane == 0) {
+      s_m[warp][r] = m[r];
+      s_l[warp][r] = l[r];
+    }
+    s_acc[warp][r][lane] = acc[r];
+  }
+  __syncthreads();
+  // merge the warps: warp w merges rows w, w + 8, ... (one row per warp here)
+  for (int r = warp; r < nrows; r += kSaWarps) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kSaWarps; ++w) M = fmaxf(M, s_m[w][r]);
+    float L = 0.f;
+    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kSaWarps; ++w) {
+        const float f = __expf(s_m[w][r] - M);
+        L = fmaf(s_l[w][r], f, L);
+        const float4 x = s_acc[w][r][lane];
+        A.x = fmaf(x.x, f, A.x);
+        A.y = fmaf(x.y, f, A.y);
+        A.z = fmaf(x.z, f, A.z);
+        A.w = fmaf(x.w, f, A.w);
+      }
+    }
+    const int64_t rr = r0 + r, g = rr / a.Sq, s = rr - g * a.Sq;
+    const int64_t orow = (int64_t(b) * a.Hq + int64_t(h) * a.G + g) * a.Sq + s;
+    const int64_t slot = orow * nsplit + split;
+    if (lane == 0) {
+      a.part_m[slot] = M;
+      a.part_l[slot] = L;
+    }
+    reinterpret_cast<float4*>(a.part_acc + slot * 128)[lane] = A;
+  }
+}
+
+template <typename T>
+__global__ void sparse_attn_combine_kernel(const SparseAttnArgs a, int nsplit) {
+  const int64_t row = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = int64_t(a.B) * a.Hq * a.Sq;
+  if (row >= rows) return;
+  float M = -INFINITY;
+  for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, a.part_m[row * nsplit + sp]);
+  float L = 0.f;
+  float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (M != -INFINITY) {
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const int64_t slot = row * nsplit + sp;
+      const float f = __expf(a.part_m[slot] - M);
+      L = fmaf(a.part_l[slot], f, L);
+      const float4 x = reinterpret_cast<const float4*>(a.part_acc + slot * 128)[lane];
+      A.x = fmaf(x.x, f, A.x);
+      A.y = fmaf(x.y, f, A.y);
+      A.z = fmaf(x.z, f, A.z);
+      A.w = fmaf(x.w, f, A.w);
+    }
+  }
+  // a row that sees no key gets zeros (the reference's nan_to_num of 0/0)
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  A.x *= inv;
+  A.y *= inv;
+  A.z *= inv;
+  A.w *= inv;
+  store4<T>(static_cast<T*>(a.out) + row * 128 + 4 * lane, A);
+}
+
+int sa_splits(const SparseAttnArgs& a, int num_sms) {
+  const int64_t R = int64_t(a.G) * a.Sq;
+  const int64_t ctas = int64_t(a.B) * a.Hkv * ((R + kRB - 1) / kRB);
+  int64_t s = (int64_t(num_sms) * 4 + ctas - 1) / ctas;  // about four CTAs per SM
+  const int64_t maxs = (a.nsel + 255) / 256;            // at least 256 keys per split
+  s = s < maxs ? s : maxs;
+  s = s < kSparseMaxSplits ? s : kSparseMaxSplits;
+  return int(s < 1 ? 1 : s);
+}
+
+}  // namespace
+
+size_t sparse_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq) {
+  const size_t rows = size_t(B) * size_t(Hq) * size_t(Sq);
+  return (rows * kSparseMaxSplits * (2 + 128) * sizeof(float) + 255) / 256 * 256;
+}
+
+cudaError_t launch_sparse_attn(SparseAttnArgs a, int dtype, void* ws, int num_sms,
+                               cudaStream_t stream) {
+  const int nsplit = sa_splits(a, num_sms);
+  const size_t rows = size_t(a.B) * size_t(a.Hq) * size_t(a.Sq);
+  float* w = static_cast<float*>(ws);
+  a.part_m = w;
+  a.part_l = w + rows * kSparseMaxSplits;
+  a.part_acc = w + 2 * rows * kSparseMaxSplits;
+  const int64_t R = int64_t(a.G) * a.Sq;
+  const dim3 grid(unsigned(int64_t(a.B) * a.Hkv * ((R + kRB - 1) / kRB)), unsigned(nsplit));
+  const unsigned cgrid = unsigned((rows + 7) / 8);
+  const bool rope = a.inv_freq != nullptr;
+  if (dtype == kBF16) {
+    if (rope)
+      sparse_attn_partial_kernel<__nv_bfloat16, true><<<grid, kSaWarps * 32, 0, stream>>>(a);
+    else
+      sparse_attn_partial_kernel<__nv_bfloat16, false><<<grid, kSaWarps * 32, 0, stream>>>(a);
+    sparse_attn_combine_kernel<__nv_bfloat16><<<cgrid, 256, 0, stream>>>(a, nsplit);
+  } else {
+    if (rope)
+      sparse_attn_partial_kernel<__half, true><<<grid, kSaWarps * 32, 0, stream>>>(a);
+    else
+      sparse_attn_partial_kernel<__half, false><<<grid, kSaWarps * 32, 0, stream>>>(a);
+    sparse_attn_combine_kernel<__half><<<cgrid, 256, 0, stream>>>(a, nsplit);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace prism

@@ -321,3 +321,63 @@ def post_select(topk_idx: torch.Tensor, n_middle: int, recall_clip: int = -1, sp
         _lib.check(rc, "prism_post_select")
         n = int(out_count.item())
     return out_pos[:n].to(torch.int64)
+
+
+def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, key_pos: torch.Tensor, *,
+                     q_pos: Optional[torch.Tensor] = None, inv_freq: Optional[torch.Tensor] = None,
+                     pe_original: bool = True, scale: Optional[float] = None) -> torch.Tensor:
+    """Attention over the selected view, on the GPU (C ABI ``prism_sparse_attention``).
+
+    The step after the recall selection in ReAttentionExactMethod._chunk_attention
+    (eval_harness/attention_methods/reattention_exact.py:453-508 and the eager path of
+    ``_attend``, :650-661): the view's keys and values are gathered from the raw cache
+    ``k``, ``v`` [B, Hkv, S, 128] at the absolute positions ``key_pos`` [nsel], keys and
+    queries ``q`` [B, Hq, Sq, 128] are rotated at their RoPE positions (absolute with
+    ``pe_original``, else contiguous with the queries last), and
+    ``softmax(q k^T * scale) v`` is taken in fp32 with keys past a query's absolute
+    position ``q_pos`` masked (default: the last Sq positions of the cache). Returns
+    [B, Hq, Sq, 128] in q's dtype; a query that sees no key gives zeros.
+    """
+    B, Hq, Sq, D = q.shape
+    Bk, Hkv, S, Dk = k.shape
+    assert v.shape == k.shape and Bk == B and Dk == D, "q, k, v shapes disagree"
+    assert q.dtype == k.dtype == v.dtype and q.dtype in (torch.float16, torch.bfloat16), (
+        "q, k and v must share one dtype, fp16 or bf16")
+    assert q.is_cuda and k.device == q.device and v.device == q.device, "all tensors on one GPU"
+    assert Hq % Hkv == 0, "num_heads must be divisible by num_heads_k"
+    assert D == 128, f"Only support d == 128, but find d={D}"
+    dev = q.device
+    key_pos = key_pos.to(device=dev, dtype=torch.int64).contiguous()
+    if q_pos is None:
+        q_pos = torch.arange(S - Sq, S, device=dev, dtype=torch.int64)
+    q_pos = q_pos.to(device=dev, dtype=torch.int64).contiguous()
+    assert q_pos.numel() == Sq, "q_pos needs one position per query row"
+    if scale is None:
+        scale = D ** -0.5
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        if k.stride(-2) != D or k.stride(-1) != 1:
+            k = k.contiguous()
+        if v.stride(-2) != D or v.stride(-1) != 1:
+            v = v.contiguous()
+        if any(s % 4 for s in q.stride()[:3]) or q.stride(-1) != 1:
+            q = q.contiguous()
+        invf = None
+        if inv_freq is not None:
+            inv_freq = inv_freq.to(device=dev, dtype=torch.float32).contiguous()
+            assert inv_freq.numel() == D // 2, "inv_freq must have head_dim // 2 entries"
+            invf = inv_freq.data_ptr()
+        out = torch.empty((B, Hq, Sq, D), dtype=q.dtype, device=dev)
+        ws_bytes = lib.prism_sparse_attention_workspace_size(B, Hq, Sq)
+        ws = torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=dev)
+        rc = lib.prism_sparse_attention(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), key_pos.data_ptr(), key_pos.numel(),
+            q_pos.data_ptr(), invf, 1 if pe_original else 0, float(scale), _dtype_code(q.dtype),
+            B, Hq, Hkv, Sq, S, D, _lib.i64_array(q.stride()), _lib.i64_array(k.stride()),
+            _lib.i64_array(v.stride()), out.data_ptr(), ws.data_ptr(), ws.numel(),
+            torch.cuda.current_stream(dev).cuda_stream,
+        )
+        _lib.check(rc, "prism_sparse_attention")
+        if _SYNC_CHECK:
+            read_status(ws)
+    return out

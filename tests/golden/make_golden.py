@@ -7,6 +7,7 @@ code (RUSH-Intelligence/Prism-Test, imported read-only from a checkout given by
     eval_harness/attention_methods/reattention.py   ReAttentionMethod._dense_topk,
         ReAttentionMethod._global_unique, ReAttentionMethod._expand_spans,
         ReAttentionMethod._apply_recall_weight
+    eval_harness/attention_methods/reattention_exact.py  ReAttentionExactMethod._attend
 
 For each case it draws seeded raw keys and queries, rotates the keys with the
 reference's RoPE (fp32), stores them as bf16 (the dtype the GPU path reads),
@@ -110,6 +111,8 @@ def main() -> None:
         print(name, tuple(q.shape), tuple(k_cached.shape), "topk", topk)
     post_select_cases(ReAttentionMethod)
     recall_weight_cases(ReAttentionMethod, apply_rotary_pos_emb, build_cos_sin, undo_rotary_pos_emb)
+    from eval_harness.attention_methods.reattention_exact import ReAttentionExactMethod  # noqa: E402
+    sparse_attention_cases(ReAttentionExactMethod, apply_rotary_pos_emb, build_cos_sin)
 
 
 # value-weighted recall cases: name, recall_type, B, Hq, Hkv, Sq, Sk, topk, theta, pos_offset, zero_rows
@@ -199,6 +202,61 @@ def post_select_cases(ReAttentionMethod) -> None:
                             n_mid=np.array(n_mid), recall_clip=np.array(clip),
                             span=np.array(span), mode=np.array(mode), out=out.numpy().astype(np.int64))
         print(name, idx.numel(), "->", out.numel())
+
+
+# attention over a selected view: name, B, Hq, Hkv, Sq, S, n_mid_selected, local, pe_original, pattern
+ATTN_CASES = [
+    ("attn_decode_pe_original", 1, 8, 2, 1, 3000, 300, 256, True, "view"),
+    ("attn_chunk_contiguous", 2, 4, 2, 16, 2000, 200, 128, False, "view"),
+    ("attn_rows_without_keys", 1, 4, 1, 3, 40, 0, 0, True, "late_keys"),
+]
+
+
+def sparse_attention_cases(ReAttentionExactMethod, apply_rotary_pos_emb, build_cos_sin) -> None:
+    """Golden vectors of the attention over the selected view: the gather and RoPE of
+    ReAttentionExactMethod._chunk_attention (reattention_exact.py:453-508), run here on
+    fp32 copies of bf16 tensors with the reference's build_cos_sin /
+    apply_rotary_pos_emb, then its own _attend with the eager path
+    (use_flash_attn='off', :650-661)."""
+    method = ReAttentionExactMethod(use_flash_attn="off")
+    for (name, B, Hq, Hkv, Sq, S, n_sel_mid, local, pe_original, pattern) in ATTN_CASES:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+        D = 128
+        q = torch.randn(B, Hq, Sq, D, generator=g).to(torch.bfloat16)
+        k = torch.randn(B, Hkv, S, D, generator=g).to(torch.bfloat16)
+        v = torch.randn(B, Hkv, S, D, generator=g).to(torch.bfloat16)
+        pos_c = torch.arange(S - Sq, S)
+        if pattern == "view":  # [global 32 | recalled middle | local tail]
+            gsz = 32
+            mid = torch.randperm(S - gsz - local, generator=g)[:n_sel_mid] + gsz
+            key_pos = torch.cat([torch.arange(gsz), mid.sort().values, torch.arange(S - local, S)])
+        else:  # keys only after the first query rows: those rows see nothing
+            pos_c = torch.tensor([5, 15, 25])
+            key_pos = torch.arange(10, 21)
+        inv_freq = 1.0 / (5e5 ** (torch.arange(0, D, 2, dtype=torch.int64).to(torch.float32) / D))
+        gather = key_pos.view(1, 1, -1, 1).expand(B, Hkv, -1, D)
+        sel_k = torch.gather(k.float(), 2, gather)
+        sel_v = torch.gather(v.float(), 2, gather)
+        view_len = key_pos.numel()
+        if pe_original:
+            pe_key_pos, pe_q_pos = key_pos, pos_c
+        else:
+            pe_key_pos = torch.arange(view_len)
+            pe_q_pos = torch.arange(view_len - Sq, view_len)
+        cos_k, sin_k = build_cos_sin(pe_key_pos, inv_freq, torch.device("cpu"), torch.float32)
+        sel_k = apply_rotary_pos_emb(sel_k, cos_k, sin_k)
+        cos_q, sin_q = build_cos_sin(pe_q_pos, inv_freq, torch.device("cpu"), torch.float32)
+        q_rot = apply_rotary_pos_emb(q.float(), cos_q, sin_q)
+        scale = D ** -0.5
+        out = method._attend(q_rot, sel_k, sel_v, pos_c, key_pos, scale)
+        np.savez_compressed(
+            HERE / f"{name}.npz",
+            q_bf16=bf16_bits(q), k_bf16=bf16_bits(k), v_bf16=bf16_bits(v),
+            key_pos=key_pos.numpy().astype(np.int64), q_pos=pos_c.numpy().astype(np.int64),
+            inv_freq=inv_freq.numpy(), pe_original=np.array(pe_original), scale=np.array(scale),
+            out=out.numpy(),
+        )
+        print(name, tuple(q.shape), "view", view_len, "pe_original", pe_original)
 
 
 if __name__ == "__main__":

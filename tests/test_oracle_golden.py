@@ -8,7 +8,7 @@ import torch
 
 from oracle import reattention_topk as orc
 
-GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith(("post_", "recall_")))
+GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith(("post_", "recall_", "attn_")))
 
 
 def load_case(path):
@@ -129,3 +129,29 @@ def test_recall_weights_types():
     assert orc.recall_weights(v, "qkv2").tolist() == [[[5.0, 0.0]]]
     with pytest.raises(ValueError):
         orc.recall_weights(v, "qkv_pe")
+
+
+ATTN = sorted((Path(__file__).resolve().parent / "golden").glob("attn_*.npz"))
+
+
+def _attn_case(path):
+    z = np.load(path)
+    t = lambda key: torch.from_numpy(z[key].view(np.int16)).view(torch.bfloat16)  # noqa: E731
+    return (t("q_bf16"), t("k_bf16"), t("v_bf16"), torch.from_numpy(z["key_pos"]),
+            torch.from_numpy(z["q_pos"]), torch.from_numpy(z["inv_freq"]), bool(z["pe_original"]),
+            float(z["scale"]), torch.from_numpy(z["out"]))
+
+
+def test_attn_golden_present():
+    assert len(ATTN) >= 3
+
+
+@pytest.mark.parametrize("path", ATTN, ids=[p.stem for p in ATTN])
+def test_sparse_attention_oracle_matches_reference(path):
+    """orc.sparse_attention against the reference's gather + RoPE + _attend eager path
+    (reattention_exact.py:453-508, 650-661)."""
+    q, k, v, kp, qp, inv, pe_orig, scale, want = _attn_case(path)
+    got = orc.sparse_attention(q, k, v, kp, qp, inv, pe_orig, scale)
+    torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-6)
+    if "rows_without_keys" in path.stem:
+        assert bool((got[:, :, 0] == 0).all())  # the first query row sees no key

@@ -13,7 +13,7 @@ from tests.parity import check_parity
 
 pytestmark = pytest.mark.gpu
 
-GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith(("post_", "recall_")))
+GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith(("post_", "recall_", "attn_")))
 
 
 def _golden(path, dev):
