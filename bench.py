@@ -53,7 +53,79 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--recall-type", default="qk", choices=["qk", "qkv", "qkv2"],
                     help="value-norm weighting of the keys (qkv: L1, qkv2: L2)")
+    ap.add_argument("--stage", default="recall", choices=["recall", "attention"],
+                    help="attention: time the attention over a selected view instead of the recall")
     return ap.parse_args()
+
+
+def run_attention(args):
+    """Attention over a selected view on one GPU: the step after the recall in the
+    exact method. The view of a decode step on the workload's cache: 32 global
+    positions, 4096 recalled middle positions, the 4096-position local window."""
+    from prism_test_b200 import _lib, sparse_attention
+    from prism_test_b200 import workloads as W
+    dev = torch.device("cuda", 0)
+    wl = W.WORKLOADS[args.workload or "decode-128k"]
+    lib = _lib.load()
+    g = torch.Generator(device=dev).manual_seed(1)
+    q = torch.randn(wl.B, wl.Hq, 1, wl.D, generator=g, device=dev).to(wl.dtype)
+    k = torch.randn(wl.B, wl.Hkv, wl.Sk, wl.D, generator=g, device=dev).to(wl.dtype)
+    v = torch.randn(wl.B, wl.Hkv, wl.Sk, wl.D, generator=g, device=dev).to(wl.dtype)
+    loc, glob, mid = 4096, 32, 4096
+    middle = torch.randperm(wl.Sk - glob - loc, generator=g, device=dev)[:mid].sort().values + glob
+    key_pos = torch.cat([torch.arange(glob, device=dev), middle,
+                         torch.arange(wl.Sk - loc, wl.Sk, device=dev)])
+    inv = W.rope_inv_freq(wl.D, wl.theta).to(dev)
+    step = lambda: sparse_attention(q, k, v, key_pos, inv_freq=inv, pe_original=True)  # noqa: E731
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    lib.prism_profile_start(2 * args.steps + 16)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    lib.prism_profile_stop()
+    n_a = _lib.ctypes.c_int64(0)
+    t_a = _lib.ctypes.c_double(0.0)
+    lib.prism_profile_read(_lib.KERNEL_ATTN, _lib.ctypes.byref(n_a), _lib.ctypes.byref(t_a))
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    nsel = key_pos.numel()
+    bytes_per_call = nsel * wl.B * wl.Hkv * wl.D * 2 * 2  # gathered key and value rows
+    launch_ms = t_a.value / max(1, n_a.value)
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_per_call / (launch_ms * 1e-3) / 1e9
+    line = {
+        "metric": "view KV tokens attended/sec", "value": nsel * args.steps / (ms * 1e-3),
+        "unit": "KV tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (bf16 in)", "data": "synthetic",
+        "config": {"workload": wl.name, "stage": "attention over the selected view",
+                   "view": {"global": glob, "recalled": mid, "local": loc}, "q_len": 1},
+        "roofline": {"bound": "hbm", "unit": "GB/s", "bytes_per_launch": bytes_per_call,
+                     "achieved": achieved, "peak": peak, "frac": achieved / peak,
+                     "peak_source": peak_kind, "launch_ms": launch_ms},
+        "gpu_launches": 2 * args.steps, "timing": "CUDA graph of one call, replayed",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def dist_env():
@@ -279,6 +351,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.stage == "attention":
+        return run_attention(args)
     world, rank, local = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")

@@ -6,10 +6,11 @@
 // path of _attend (:650-661): softmax(q k^T * scale) v in fp32, keys past a
 // query's absolute position masked, fully masked rows giving zeros.
 //
-// sparse_attn_partial_kernel: a CTA takes up to kRB query rows (g-major rows of
-// one (batch, KV head)) and one split of the view; each of its 8 warps walks the
-// split's keys j = warp, warp + 8, ...: the key and value rows are gathered with
-// one coalesced 8-byte load per lane (lane L holds dimensions 4L .. 4L+3), the
+// sparse_attn_partial_kernel: a CTA takes up to kRB (4 or 8) query rows (g-major rows of
+// one (batch, KV head)) and one split of the view; each of its 8 warps walks a
+// contiguous share of the split's keys, 8 at a time (their rows all requested
+// before the first is used): the key and value rows are gathered with one
+// coalesced 8-byte load per lane (lane L holds dimensions 4L .. 4L+3), the
 // key is rotated at its RoPE position in registers (lanes L and L ^ 16 hold the
 // two halves of a rotation pair; each computes two of the pair group's four
 // angles and they swap them), dotted with every query row (fp32, warp
@@ -25,7 +26,7 @@ namespace prism {
 namespace {
 
 constexpr int kSaWarps = 8;
-constexpr int kRB = 8;  // query rows per CTA
+constexpr int kU = 8;  // key rows per warp in flight
 
 template <typename T>
 __device__ __forceinline__ float4 load4(const T* p) {
@@ -96,8 +97,9 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
-template <typename T, bool kRope>
-__global__ void __launch_bounds__(kSaWarps * 32)
+// kRB: query rows per CTA (4 for decode's GQA groups, 8 otherwise)
+template <typename T, bool kRope, int kRB>
+__global__ void __launch_bounds__(kSaWarps * 32, kRB == 4 ? 2 : 1)
     sparse_attn_partial_kernel(const SparseAttnArgs a) {
   __shared__ float s_m[kSaWarps][kRB], s_l[kSaWarps][kRB];
   __shared__ float4 s_acc[kSaWarps][kRB][32];
@@ -152,30 +154,52 @@ __global__ void __launch_bounds__(kSaWarps * 32)
   }
   const T* kb = static_cast<const T*>(a.k) + (a.B > 1 ? int64_t(b) * a.k_sb : 0) + int64_t(h) * a.k_sh;
   const T* vb = static_cast<const T*>(a.v) + (a.B > 1 ? int64_t(b) * a.v_sb : 0) + int64_t(h) * a.v_sh;
-  for (int64_t j = j0 + warp; j < j1; j += kSaWarps) {
-    const int64_t p = a.key_pos[j];
-    if (p < 0 || p >= a.S) {  // a position outside the cache: skipped and reported
-      if (lane == 0) set_status(a.status, kStatusBounds);
-      continue;
-    }
-    const float4 kv = load4<T>(kb + p * 128 + 4 * lane);
-    const float4 vv = load4<T>(vb + p * 128 + 4 * lane);
-    const float pe = a.pe_original ? float(p) : float(j);
-    const float4 kr = kRope ? rope4(kv, pe, inv_lane, lane) : kv;
+  // the warp's contiguous share of the split, kU keys at a time: one load brings
+  // the kU positions (lane u holds key jb + u), then all kU key and value rows are
+  // requested before the first is used, so kU gathers per warp are in flight
+  const int64_t wper = (j1 - j0 + kSaWarps - 1) / kSaWarps;
+  const int64_t w0 = j0 + int64_t(warp) * wper;
+  const int64_t w1 = w0 + wper < j1 ? w0 + wper : j1;
+  for (int64_t jb = w0; jb < w1; jb += kU) {
+    const int64_t mine = jb + lane;
+    const int64_t pos = lane < kU && mine < w1 ? a.key_pos[mine] : -1;
+    uint2 kraw[kU], vraw[kU];  // packed 16-bit rows: half the registers of fp32
+    int pu[kU];                // positions (< S < 2^31)
 #pragma unroll
-    for (int r = 0; r < kRB; ++r) {
-      if (r >= nrows) break;
-      if (p > qabs[r]) continue;  // causal by absolute position (uniform across the warp)
-      const float sc = warp_sum(dot4(q[r], kr));
-      const float mn = fmaxf(m[r], sc);
-      const float corr = __expf(m[r] - mn);  // m = -inf at first: corr = 0
-      const float e = __expf(sc - mn);
-      l[r] = fmaf(l[r], corr, e);
-      acc[r].x = fmaf(acc[r].x, corr, e * vv.x);
-      acc[r].y = fmaf(acc[r].y, corr, e * vv.y);
-      acc[r].z = fmaf(acc[r].z, corr, e * vv.z);
-      acc[r].w = fmaf(acc[r].w, corr, e * vv.w);
-      m[r] = mn;
+    for (int u = 0; u < kU; ++u) {
+      const int64_t pp = __shfl_sync(0xffffffffu, pos, u);
+      const bool ok = jb + u < w1 && pp >= 0 && pp < a.S;
+      if (jb + u < w1 && !ok && lane == 0) set_status(a.status, kStatusBounds);  // skipped
+      pu[u] = ok ? int(pp) : -1;
+      kraw[u] = ok ? *reinterpret_cast<const uint2*>(kb + pp * 128 + 4 * lane) : make_uint2(0u, 0u);
+      vraw[u] = ok ? *reinterpret_cast<const uint2*>(vb + pp * 128 + 4 * lane) : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t p = pu[u];
+      if (p < 0) continue;  // past the share, or a position outside the cache
+      const float pe = a.pe_original ? float(p) : float(jb + u);
+      float4 kf, vf;
+      Unpack<T>::run(kraw[u].x, kf.x, kf.y);
+      Unpack<T>::run(kraw[u].y, kf.z, kf.w);
+      Unpack<T>::run(vraw[u].x, vf.x, vf.y);
+      Unpack<T>::run(vraw[u].y, vf.z, vf.w);
+      const float4 kr = kRope ? rope4(kf, pe, inv_lane, lane) : kf;
+#pragma unroll
+      for (int r = 0; r < kRB; ++r) {
+        if (r >= nrows) break;
+        if (p > qabs[r]) continue;  // causal by absolute position (uniform across the warp)
+        const float sc = warp_sum(dot4(q[r], kr));
+        const float mn = fmaxf(m[r], sc);
+        const float corr = __expf(m[r] - mn);  // m = -inf at first: corr = 0
+        const float e = __expf(sc - mn);
+        l[r] = fmaf(l[r], corr, e);
+        acc[r].x = fmaf(acc[r].x, corr, e * vf.x);
+        acc[r].y = fmaf(acc[r].y, corr, e * vf.y);
+        acc[r].z = fmaf(acc[r].z, corr, e * vf.z);
+        acc[r].w = fmaf(acc[r].w, corr, e * vf.w);
+        m[r] = mn;
+      }
     }
   }
 #pragma unroll
@@ -248,14 +272,28 @@ __global__ void sparse_attn_combine_kernel(const SparseAttnArgs a, int nsplit) {
   store4<T>(static_cast<T*>(a.out) + row * 128 + 4 * lane, A);
 }
 
+int sa_rows(const SparseAttnArgs& a) { return int64_t(a.G) * a.Sq <= 4 ? 4 : 8; }
+
 int sa_splits(const SparseAttnArgs& a, int num_sms) {
   const int64_t R = int64_t(a.G) * a.Sq;
-  const int64_t ctas = int64_t(a.B) * a.Hkv * ((R + kRB - 1) / kRB);
+  const int rb = sa_rows(a);
+  const int64_t ctas = int64_t(a.B) * a.Hkv * ((R + rb - 1) / rb);
   int64_t s = (int64_t(num_sms) * 4 + ctas - 1) / ctas;  // about four CTAs per SM
   const int64_t maxs = (a.nsel + 255) / 256;            // at least 256 keys per split
   s = s < maxs ? s : maxs;
   s = s < kSparseMaxSplits ? s : kSparseMaxSplits;
   return int(s < 1 ? 1 : s);
+}
+
+template <typename T, bool kRope>
+void launch_partial(const SparseAttnArgs& a, int nsplit, cudaStream_t stream) {
+  const int64_t R = int64_t(a.G) * a.Sq;
+  const int rb = sa_rows(a);
+  const dim3 grid(unsigned(int64_t(a.B) * a.Hkv * ((R + rb - 1) / rb)), unsigned(nsplit));
+  if (rb == 4)
+    sparse_attn_partial_kernel<T, kRope, 4><<<grid, kSaWarps * 32, 0, stream>>>(a);
+  else
+    sparse_attn_partial_kernel<T, kRope, 8><<<grid, kSaWarps * 32, 0, stream>>>(a);
 }
 
 }  // namespace
@@ -273,21 +311,19 @@ cudaError_t launch_sparse_attn(SparseAttnArgs a, int dtype, void* ws, int num_sm
   a.part_m = w;
   a.part_l = w + rows * kSparseMaxSplits;
   a.part_acc = w + 2 * rows * kSparseMaxSplits;
-  const int64_t R = int64_t(a.G) * a.Sq;
-  const dim3 grid(unsigned(int64_t(a.B) * a.Hkv * ((R + kRB - 1) / kRB)), unsigned(nsplit));
   const unsigned cgrid = unsigned((rows + 7) / 8);
   const bool rope = a.inv_freq != nullptr;
   if (dtype == kBF16) {
     if (rope)
-      sparse_attn_partial_kernel<__nv_bfloat16, true><<<grid, kSaWarps * 32, 0, stream>>>(a);
+      launch_partial<__nv_bfloat16, true>(a, nsplit, stream);
     else
-      sparse_attn_partial_kernel<__nv_bfloat16, false><<<grid, kSaWarps * 32, 0, stream>>>(a);
+      launch_partial<__nv_bfloat16, false>(a, nsplit, stream);
     sparse_attn_combine_kernel<__nv_bfloat16><<<cgrid, 256, 0, stream>>>(a, nsplit);
   } else {
     if (rope)
-      sparse_attn_partial_kernel<__half, true><<<grid, kSaWarps * 32, 0, stream>>>(a);
+      launch_partial<__half, true>(a, nsplit, stream);
     else
-      sparse_attn_partial_kernel<__half, false><<<grid, kSaWarps * 32, 0, stream>>>(a);
+      launch_partial<__half, false>(a, nsplit, stream);
     sparse_attn_combine_kernel<__half><<<cgrid, 256, 0, stream>>>(a, nsplit);
   }
   return cudaGetLastError();
