@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--recall-type", default="qk", choices=["qk", "qkv", "qkv2"],
                     help="value-norm weighting of the keys (qkv: L1, qkv2: L2)")
+    ap.add_argument("--chunks", type=int, default=0,
+                    help="sharded path: groups of KV heads whose exchange is pipelined "
+                         "(0: 2 when the KV heads split evenly, else 1)")
     ap.add_argument("--stage", default="recall", choices=["recall", "attention"],
                     help="attention: time the attention over a selected view instead of the recall")
     return ap.parse_args()
@@ -146,7 +149,8 @@ def config_of(wl, world, recall_type="qk"):
         "workload": wl.name, "B": wl.B, "Hq": wl.Hq, "Hkv": wl.Hkv, "Sq": wl.Sq, "Sk": wl.Sk,
         "topk": wl.topk, "head_dim": wl.D, "rope_theta": wl.theta, "key_dtype": "bf16",
         "causal_offset": wl.causal_offset, "shards": world,
-        "parallelism": "single GPU" if world == 1 else f"sequence-sharded x{world} (NCCL all-gather + device merge)",
+        "parallelism": "single GPU" if world == 1 else
+                       f"sequence-sharded x{world} (NCCL all-gather pipelined over KV-head groups + device merge)",
         "l2": "inputs larger than L2 (cached keys %d MB per rank > 126 MB), no flush" % (wl.kv_bytes // world >> 20),
         "recall_type": recall_type,
     }
@@ -372,13 +376,14 @@ def main():
     q, k, inv = x["q"], x["k"], x["inv_freq"]
     rt = args.recall_type
     v = W.make_values(wl, dev, start, stop) if rt != "qk" else None
+    chunks = args.chunks or (2 if wl.Hkv % 2 == 0 else 1)
 
     def step(qq, kk, vv=v):
         if world == 1:
             return einsum_topk_func(qq, kk, wl.topk, inv_freq=inv, return_scores=True,
                                     causal_offset=wl.causal_offset, values=vv, recall_type=rt)
         return sharded_einsum_topk(qq, kk, wl.topk, shard_start=start, inv_freq=inv, return_scores=True,
-                                   v_shard=vv, recall_type=rt)
+                                   v_shard=vv, recall_type=rt, chunks=chunks)
 
     def barrier():
         if world > 1:

@@ -163,8 +163,9 @@ PRISM_API int prism_einsum_topk_weighted(const void* q, const void* k, const voi
  *              query row i at nsel - Sq + i (the contiguous re-rotation).
  *   D          must be 128.
  *   out        [B, Hq, Sq, D] contiguous, `dtype`.
- *   workspace  prism_sparse_attention_workspace_size(B, Hq, Sq) bytes (256-aligned):
- *              the status block and the per-split partial softmax states.
+ *   workspace  prism_sparse_attention_workspace_size(B, Hq, Sq, nsel) bytes
+ *              (256-aligned): the status block, the per-split partial softmax
+ *              states and a table of the view's RoPE angles.
  */
 PRISM_API int prism_sparse_attention(const void* q, const void* k, const void* v,
                                      const int64_t* key_pos, int64_t nsel, const int64_t* q_pos,
@@ -173,7 +174,8 @@ PRISM_API int prism_sparse_attention(const void* q, const void* k, const void* v
                                      int64_t S, int64_t D, const int64_t* q_strides,
                                      const int64_t* k_strides, const int64_t* v_strides, void* out,
                                      void* workspace, size_t workspace_bytes, void* stream);
-PRISM_API size_t prism_sparse_attention_workspace_size(int64_t B, int64_t Hq, int64_t Sq);
+PRISM_API size_t prism_sparse_attention_workspace_size(int64_t B, int64_t Hq, int64_t Sq,
+                                                       int64_t nsel);
 
 /*
  * Exact top-k over candidate lists: for each of `rows` rows, picks the topk

@@ -67,7 +67,7 @@ SIGNATURES = {
         ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64),
         _vp, _vp, ctypes.c_size_t, _vp,
     ]),
-    "prism_sparse_attention_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64]),
+    "prism_sparse_attention_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "prism_topk_merge": (ctypes.c_int, [
         _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i32, _vp, _vp, _vp, ctypes.c_size_t, _vp,
     ]),

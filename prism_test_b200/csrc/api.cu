@@ -407,9 +407,9 @@ int prism_einsum_topk_weighted(const void* q, const void* k, const void* v, cons
                           workspace, workspace_bytes, stream_ptr, &wa);
 }
 
-size_t prism_sparse_attention_workspace_size(int64_t B, int64_t Hq, int64_t Sq) {
-  if (B <= 0 || Hq <= 0 || Sq <= 0) return 0;
-  return kStatusBytes + prism::sparse_attn_workspace_bytes(B, Hq, Sq);
+size_t prism_sparse_attention_workspace_size(int64_t B, int64_t Hq, int64_t Sq, int64_t nsel) {
+  if (B <= 0 || Hq <= 0 || Sq <= 0 || nsel <= 0) return 0;
+  return kStatusBytes + prism::sparse_attn_workspace_bytes(B, Hq, Sq, nsel);
 }
 
 int prism_sparse_attention(const void* q, const void* k, const void* v, const int64_t* key_pos,
@@ -440,7 +440,7 @@ int prism_sparse_attention(const void* q, const void* k, const void* v, const in
       return fail(PRISM_E_INVALID, "q, k and v strides must be multiples of 4 elements");
   if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0)
     return fail(PRISM_E_INVALID, "out must be 16-byte aligned");
-  const size_t need = prism_sparse_attention_workspace_size(B, Hq, Sq);
+  const size_t need = prism_sparse_attention_workspace_size(B, Hq, Sq, nsel);
   if (!workspace || workspace_bytes < need)
     return fail(PRISM_E_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
@@ -480,7 +480,7 @@ int prism_sparse_attention(const void* q, const void* k, const void* v, const in
     return prism::launch_sparse_attn(a, dtype, ws + kStatusBytes, nsm, stream);
   });
   if (e != cudaSuccess) return cuda_fail(e, "sparse attention launch");
-  g_launches.fetch_add(1, std::memory_order_relaxed);  // partial + combine
+  g_launches.fetch_add(inv_freq ? 2 : 1, std::memory_order_relaxed);  // table, partial, combine
   return PRISM_OK;
 }
 

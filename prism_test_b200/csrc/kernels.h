@@ -149,7 +149,7 @@ cudaError_t launch_scale_scores(const WeightArgs& a, int num_sms, cudaStream_t s
 // Attention over a selected view (sparse_attn.cu): gathered keys/values at the
 // view's absolute positions key_pos[nsel], RoPE at the view's positions (if
 // inv_freq), causal by absolute position, fp32 softmax; split over the view.
-constexpr int kSparseMaxSplits = 64;
+constexpr int kSparseMaxSplits = 128;
 struct SparseAttnArgs {
   const void* q;          // [B, Hq, Sq, 128]
   const void* k;          // [B, Hkv, S, 128], rows contiguous
@@ -167,8 +167,9 @@ struct SparseAttnArgs {
   float* part_m;          // workspace (set by the launcher)
   float* part_l;
   float* part_acc;
+  const float2* table;    // [nsel][64] (cos, sin) of the view's RoPE angles (launcher)
 };
-size_t sparse_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq);
+size_t sparse_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t nsel);
 cudaError_t launch_sparse_attn(SparseAttnArgs a, int dtype, void* ws, int num_sms,
                                cudaStream_t stream);
 

@@ -973,6 +973,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_row_kernel(const Sele
 // binary searches in the other runs in global memory instead (slow, same result).
 constexpr int kMergeMaxRuns = 16;
 constexpr int kMergeSumm = 128;
+constexpr int kMergeParts = 4;  // CTAs per row of the run merge
 
 __device__ __forceinline__ uint64_t run_cand(const int32_t* runs, int r, int64_t rows, int64_t row,
                                              int64_t run_len, int64_t j) {
@@ -985,7 +986,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                       int k, int32_t* __restrict__ out_idx, float* __restrict__ out_scores) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
-  const int64_t row = blockIdx.x;
+  // kMergeParts CTAs per row: each finds the same candidates and sorts them, and
+  // writes its own part of the output positions
+  const int64_t row = blockIdx.x / kMergeParts;
+  const unsigned part = blockIdx.x % kMergeParts;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   auto cand_at = [&](int r, int64_t j) { return run_cand(runs, r, rows, row, run_len, j); };
   uint64_t* summ = reinterpret_cast<uint64_t*>(sm.hist);  // [nruns][kMergeSumm]
@@ -1061,7 +1065,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // rank every prefix candidate against the other runs in global memory
     int32_t* oi = out_idx + row * k;
     float* os = out_scores ? out_scores + row * k : nullptr;
-    for (uint32_t e = tid; e < total; e += kThreads) {
+    for (uint32_t e = part * kThreads + tid; e < total; e += kMergeParts * kThreads) {
       int r = 0;
       while (e >= sm.roff[r + 1]) ++r;
       const uint32_t j = e - sm.roff[r];
@@ -1107,7 +1111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   a.k = k;
   a.out_idx = out_idx;
   a.out_scores = out_scores;
-  replicated_sort_store(a, row, sm, total, uint32_t(thr >> 32), sm.kmax, 0, 1);
+  replicated_sort_store(a, row, sm, total, uint32_t(thr >> 32), sm.kmax, part, kMergeParts);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) select_topk_general_kernel(const SelectArgs a) {
@@ -1136,8 +1140,8 @@ cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int6
   cudaError_t e = cudaFuncSetAttribute(merge_runs_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  merge_runs_kernel<<<dim3(unsigned(rows)), kThreads, smem, stream>>>(runs, nruns, rows, run_len, k,
-                                                                      out_idx, out_scores);
+  merge_runs_kernel<<<dim3(unsigned(rows * kMergeParts)), kThreads, smem, stream>>>(
+      runs, nruns, rows, run_len, k, out_idx, out_scores);
   return cudaGetLastError();
 }
 

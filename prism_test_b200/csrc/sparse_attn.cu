@@ -87,6 +87,38 @@ __device__ __forceinline__ float4 rope4(float4 x, float pe, const float* inv_lan
   return o;
 }
 
+// x[i] of a small register array with a lane-dependent i, by selects (no local memory)
+template <int N, typename V>
+__device__ __forceinline__ V pick(const V (&x)[N], int i) {
+  V r = x[0];
+#pragma unroll
+  for (int k = 1; k < N; ++k) r = i == k ? x[k] : r;
+  return r;
+}
+template <int N>
+__device__ __forceinline__ int pu_at(const int (&x)[N], int i) { return pick<N, int>(x, i); }
+template <int N>
+__device__ __forceinline__ int64_t qabs_at(const int64_t (&x)[N], int i) { return pick<N, int64_t>(x, i); }
+
+// RoPE of the lane's 4 dimensions from a table row of (cos, sin) per frequency
+// (64 float2): lanes L < 16 hold x_i, lanes L + 16 hold x_{i+64}, i = 4 (L mod 16) + e.
+__device__ __forceinline__ float4 rope4_table(float4 x, const float2* row, int lane) {
+  const float4* t = reinterpret_cast<const float4*>(row + ((4 * lane) & 63));
+  const float4 cs01 = t[0], cs23 = t[1];  // (c0, s0, c1, s1), (c2, s2, c3, s3)
+  float4 p;  // partner half
+  p.x = __shfl_xor_sync(0xffffffffu, x.x, 16);
+  p.y = __shfl_xor_sync(0xffffffffu, x.y, 16);
+  p.z = __shfl_xor_sync(0xffffffffu, x.z, 16);
+  p.w = __shfl_xor_sync(0xffffffffu, x.w, 16);
+  const float sg = (lane & 16) ? 1.f : -1.f;
+  float4 o;
+  o.x = fmaf(sg * p.x, cs01.y, x.x * cs01.x);
+  o.y = fmaf(sg * p.y, cs01.w, x.y * cs01.z);
+  o.z = fmaf(sg * p.z, cs23.y, x.z * cs23.x);
+  o.w = fmaf(sg * p.w, cs23.w, x.w * cs23.z);
+  return o;
+}
+
 __device__ __forceinline__ float dot4(float4 a, float4 b) {
   return fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, a.w * b.w)));
 }
@@ -154,17 +186,24 @@ __global__ void __launch_bounds__(kSaWarps * 32, kRB == 4 ? 2 : 1)
   }
   const T* kb = static_cast<const T*>(a.k) + (a.B > 1 ? int64_t(b) * a.k_sb : 0) + int64_t(h) * a.k_sh;
   const T* vb = static_cast<const T*>(a.v) + (a.B > 1 ? int64_t(b) * a.v_sb : 0) + int64_t(h) * a.v_sh;
-  // the warp's contiguous share of the split, kU keys at a time: one load brings
-  // the kU positions (lane u holds key jb + u), then all kU key and value rows are
-  // requested before the first is used, so kU gathers per warp are in flight
+  // the warp's contiguous share of the split, kU = 32 / kRB keys at a time: one
+  // load brings the kU positions (lane u holds key jb + u), then all kU key and
+  // value rows are requested before the first is used. The kU x kRB dot products
+  // are reduced across the warp together (a transposed butterfly: 31 shuffles for
+  // 32 sums; lane l ends with the score of key l / kRB for row l % kRB), so each
+  // lane runs the softmax bookkeeping of one (key, row) pair, and the group's
+  // running maximum is folded in once per row.
+  constexpr int kU = 32 / kRB;
+  float lpart = 0.f;  // this lane's share of l[lane % kRB]
+  const int my_u = lane / kRB, my_r = lane % kRB;
   const int64_t wper = (j1 - j0 + kSaWarps - 1) / kSaWarps;
   const int64_t w0 = j0 + int64_t(warp) * wper;
   const int64_t w1 = w0 + wper < j1 ? w0 + wper : j1;
   for (int64_t jb = w0; jb < w1; jb += kU) {
     const int64_t mine = jb + lane;
     const int64_t pos = lane < kU && mine < w1 ? a.key_pos[mine] : -1;
-    uint2 kraw[kU], vraw[kU];  // packed 16-bit rows: half the registers of fp32
-    int pu[kU];                // positions (< S < 2^31)
+    uint2 kraw[kU], vraw[kU];  // packed 16-bit rows
+    int pu[kU];                // positions (< S < 2^31); -1: no key
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const int64_t pp = __shfl_sync(0xffffffffu, pos, u);
@@ -174,34 +213,71 @@ __global__ void __launch_bounds__(kSaWarps * 32, kRB == 4 ? 2 : 1)
       kraw[u] = ok ? *reinterpret_cast<const uint2*>(kb + pp * 128 + 4 * lane) : make_uint2(0u, 0u);
       vraw[u] = ok ? *reinterpret_cast<const uint2*>(vb + pp * 128 + 4 * lane) : make_uint2(0u, 0u);
     }
+    // partial dot products: d[u * kRB + r] = this lane's 4 dimensions of q_r . k_u
+    float d[32];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
-      const int64_t p = pu[u];
-      if (p < 0) continue;  // past the share, or a position outside the cache
-      const float pe = a.pe_original ? float(p) : float(jb + u);
-      float4 kf, vf;
+      float4 kf;
       Unpack<T>::run(kraw[u].x, kf.x, kf.y);
       Unpack<T>::run(kraw[u].y, kf.z, kf.w);
+      if (kRope) kf = rope4_table(kf, a.table + (jb + u < w1 ? (jb + u) : w0) * 64, lane);
+#pragma unroll
+      for (int r = 0; r < kRB; ++r) d[u * kRB + r] = dot4(q[r], kf);
+    }
+    // transposed butterfly: lane l ends with the full sum of d[l]
+#pragma unroll
+    for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
+      const bool up = lane & o;
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) {
+        const float send = up ? d[i] : d[i + n / 2];
+        const float keep = up ? d[i + n / 2] : d[i];
+        d[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    const int pk = pu_at(pu, my_u);  // position of this lane's key
+    const bool live = pk >= 0 && my_r < nrows && int64_t(pk) <= qabs_at(qabs, my_r);
+    const float sc = live ? d[0] : -INFINITY;
+    // the group's maximum per row (lanes with the same row differ in bits >= log2(kRB))
+    float gm = sc;
+#pragma unroll
+    for (int o = kRB; o < 32; o <<= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+    float corr_r[kRB];
+#pragma unroll
+    for (int r = 0; r < kRB; ++r) {
+      const float mn = fmaxf(m[r], __shfl_sync(0xffffffffu, gm, r));
+      corr_r[r] = mn == -INFINITY ? 1.f : __expf(m[r] - mn);
+      m[r] = mn;
+    }
+    const float e = live ? __expf(sc - pick<kRB, float>(m, my_r)) : 0.f;
+    lpart = fmaf(lpart, pick<kRB, float>(corr_r, my_r), e);
+#pragma unroll
+    for (int r = 0; r < kRB; ++r) {
+      acc[r].x *= corr_r[r];
+      acc[r].y *= corr_r[r];
+      acc[r].z *= corr_r[r];
+      acc[r].w *= corr_r[r];
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      float4 vf;
       Unpack<T>::run(vraw[u].x, vf.x, vf.y);
       Unpack<T>::run(vraw[u].y, vf.z, vf.w);
-      const float4 kr = kRope ? rope4(kf, pe, inv_lane, lane) : kf;
 #pragma unroll
       for (int r = 0; r < kRB; ++r) {
-        if (r >= nrows) break;
-        if (p > qabs[r]) continue;  // causal by absolute position (uniform across the warp)
-        const float sc = warp_sum(dot4(q[r], kr));
-        const float mn = fmaxf(m[r], sc);
-        const float corr = __expf(m[r] - mn);  // m = -inf at first: corr = 0
-        const float e = __expf(sc - mn);
-        l[r] = fmaf(l[r], corr, e);
-        acc[r].x = fmaf(acc[r].x, corr, e * vf.x);
-        acc[r].y = fmaf(acc[r].y, corr, e * vf.y);
-        acc[r].z = fmaf(acc[r].z, corr, e * vf.z);
-        acc[r].w = fmaf(acc[r].w, corr, e * vf.w);
-        m[r] = mn;
+        const float eu = __shfl_sync(0xffffffffu, e, u * kRB + r);
+        acc[r].x = fmaf(eu, vf.x, acc[r].x);
+        acc[r].y = fmaf(eu, vf.y, acc[r].y);
+        acc[r].z = fmaf(eu, vf.z, acc[r].z);
+        acc[r].w = fmaf(eu, vf.w, acc[r].w);
       }
     }
   }
+  // l[r]: the lanes of row r hold its parts
+#pragma unroll
+  for (int o = kRB; o < 32; o <<= 1) lpart += __shfl_xor_sync(0xffffffffu, lpart, o);
+#pragma unroll
+  for (int r = 0; r < kRB; ++r) l[r] = __shfl_sync(0xffffffffu, lpart, r);
 #pragma unroll
   for (int r = 0; r < kRB; ++r) {
     if (lane == 0) {
@@ -272,7 +348,27 @@ __global__ void sparse_attn_combine_kernel(const SparseAttnArgs a, int nsplit) {
   store4<T>(static_cast<T*>(a.out) + row * 128 + 4 * lane, A);
 }
 
+// (cos, sin) of every view position's 64 RoPE angles, fp32(pe) * inv_freq[i]
+// evaluated with the accurate reduction of rope_sincos.cuh: [nsel][64] float2
+__global__ void rope_table_kernel(const SparseAttnArgs a, float2* table) {
+  const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= a.nsel * 64) return;
+  const int64_t j = e >> 6;
+  const int i = int(e & 63);
+  const float pe = a.pe_original ? float(a.key_pos[j]) : float(j);
+  float sn, cs;
+  rope_sincos(__fmul_rn(pe, a.inv_freq[i]), sn, cs);
+  table[e] = make_float2(cs, sn);
+}
+
 int sa_rows(const SparseAttnArgs& a) { return int64_t(a.G) * a.Sq <= 4 ? 4 : 8; }
+
+// splits of the view the workspace holds room for: up to kSparseMaxSplits, and
+// at most 8192 (row, split) partials beyond one per row
+int64_t split_cap(int64_t rows) {
+  const int64_t c = 8192 / (rows > 0 ? rows : 1);
+  return c < 1 ? 1 : (c < kSparseMaxSplits ? c : kSparseMaxSplits);
+}
 
 int sa_splits(const SparseAttnArgs& a, int num_sms) {
   const int64_t R = int64_t(a.G) * a.Sq;
@@ -281,7 +377,8 @@ int sa_splits(const SparseAttnArgs& a, int num_sms) {
   int64_t s = (int64_t(num_sms) * 4 + ctas - 1) / ctas;  // about four CTAs per SM
   const int64_t maxs = (a.nsel + 255) / 256;            // at least 256 keys per split
   s = s < maxs ? s : maxs;
-  s = s < kSparseMaxSplits ? s : kSparseMaxSplits;
+  const int64_t cap = split_cap(int64_t(a.B) * a.Hq * a.Sq);
+  s = s < cap ? s : cap;
   return int(s < 1 ? 1 : s);
 }
 
@@ -298,19 +395,28 @@ void launch_partial(const SparseAttnArgs& a, int nsplit, cudaStream_t stream) {
 
 }  // namespace
 
-size_t sparse_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq) {
+size_t sparse_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t nsel) {
   const size_t rows = size_t(B) * size_t(Hq) * size_t(Sq);
-  return (rows * kSparseMaxSplits * (2 + 128) * sizeof(float) + 255) / 256 * 256;
+  return (rows * size_t(split_cap(int64_t(rows))) * (2 + 128) * sizeof(float) + 255) / 256 * 256 +
+         (size_t(nsel) * 64 * sizeof(float2) + 255) / 256 * 256;
 }
 
 cudaError_t launch_sparse_attn(SparseAttnArgs a, int dtype, void* ws, int num_sms,
                                cudaStream_t stream) {
   const int nsplit = sa_splits(a, num_sms);
   const size_t rows = size_t(a.B) * size_t(a.Hq) * size_t(a.Sq);
+  const size_t cap = size_t(split_cap(int64_t(rows)));
   float* w = static_cast<float*>(ws);
   a.part_m = w;
-  a.part_l = w + rows * kSparseMaxSplits;
-  a.part_acc = w + 2 * rows * kSparseMaxSplits;
+  a.part_l = w + rows * cap;
+  a.part_acc = w + 2 * rows * cap;
+  float2* table = reinterpret_cast<float2*>(
+      static_cast<uint8_t*>(ws) + (rows * cap * (2 + 128) * sizeof(float) + 255) / 256 * 256);
+  if (a.inv_freq != nullptr) {
+    const int64_t n = a.nsel * 64;
+    rope_table_kernel<<<unsigned((n + 255) / 256), 256, 0, stream>>>(a, table);
+    a.table = table;
+  }
   const unsigned cgrid = unsigned((rows + 7) / 8);
   const bool rope = a.inv_freq != nullptr;
   if (dtype == kBF16) {

@@ -368,7 +368,7 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, key_pos:
             assert inv_freq.numel() == D // 2, "inv_freq must have head_dim // 2 entries"
             invf = inv_freq.data_ptr()
         out = torch.empty((B, Hq, Sq, D), dtype=q.dtype, device=dev)
-        ws_bytes = lib.prism_sparse_attention_workspace_size(B, Hq, Sq)
+        ws_bytes = lib.prism_sparse_attention_workspace_size(B, Hq, Sq, key_pos.numel())
         ws = torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=dev)
         rc = lib.prism_sparse_attention(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), key_pos.data_ptr(), key_pos.numel(),

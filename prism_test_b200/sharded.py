@@ -13,6 +13,11 @@ contiguous key slice ``[r*Sk/N, (r+1)*Sk/N)`` of every KV head and:
    the gathered buffer in place): the global top-k is always contained in the
    union of the local top-k lists.
 
+With ``chunks`` > 1 the KV heads are taken in that many groups: a group's local
+top-k is all-gathered asynchronously (NCCL on its own stream) while the next
+group is scored, so only the last group's exchange is exposed; the merges run at
+the end, one per group.
+
 Every rank ends with the global result, equal to ``torch.topk`` over the whole
 sequence (``ReAttentionMethod._dense_topk``, reattention.py:486-498), ties
 broken toward lower global indices.
@@ -35,13 +40,14 @@ def shard_bounds(Sk_total: int, rank: int, world: int):
     return rank * per, (rank + 1) * per
 
 
-def _all_gather(packed: torch.Tensor, world: int, group) -> torch.Tensor:
+def _all_gather(packed: torch.Tensor, world: int, group, async_op: bool = False):
+    """[world, *packed.shape] gathered buffer (and the async work handle, or None)."""
     out = torch.empty((world, *packed.shape), dtype=packed.dtype, device=packed.device)
     if dist.get_backend(group) == "nccl":
-        dist.all_gather_into_tensor(out, packed, group=group)
+        work = dist.all_gather_into_tensor(out, packed, group=group, async_op=async_op)
     else:
-        dist.all_gather(list(out.unbind(0)), packed, group=group)
-    return out
+        work = dist.all_gather(list(out.unbind(0)), packed, group=group, async_op=async_op)
+    return (out, work) if async_op else out
 
 
 def merge_candidates_torch(cand_s: torch.Tensor, cand_i: torch.Tensor, topk: int):
@@ -66,6 +72,7 @@ def sharded_einsum_topk(
     merge: Optional[Callable] = None,
     v_shard: Optional[torch.Tensor] = None,
     recall_type: str = "qk",
+    chunks: int = 1,
 ):
     """Global exact top-k over a key sequence split across the ranks of ``group``.
 
@@ -75,11 +82,46 @@ def sharded_einsum_topk(
     ``local_topk`` / ``merge`` default to the CUDA kernels; tests substitute
     CPU implementations to run the exchange over gloo. ``recall_type`` "qkv" /
     "qkv2" weights each key by the norm of its value row in ``v_shard`` (the
-    same slice of the value cache), as ``einsum_topk_func`` does.
+    same slice of the value cache), as ``einsum_topk_func`` does. ``chunks``
+    (dividing Hkv) pipelines the exchange over groups of KV heads.
     """
     local_topk = local_topk or einsum_topk_func
-    extra = {} if recall_type == "qk" else dict(values=v_shard, recall_type=recall_type)
     world = dist.get_world_size(group)
+    B, Hq, Sq, _ = q.shape
+    Hkv = k_shard.shape[1]
+    if chunks < 1 or Hkv % chunks:
+        raise ValueError(f"chunks={chunks} must divide the {Hkv} KV heads")
+    hk, hq = Hkv // chunks, Hq // chunks
+    pending = []
+    for c in range(chunks):
+        qc = q[:, c * hq:(c + 1) * hq]
+        kc = k_shard[:, c * hk:(c + 1) * hk]
+        extra = {} if recall_type == "qk" else dict(values=v_shard[:, c * hk:(c + 1) * hk],
+                                                     recall_type=recall_type)
+        packed = _local_packed(local_topk, qc, kc, topk, inv_freq, shard_start, extra)
+        pending.append(_all_gather(packed, world, group, async_op=True))
+    outs_i, outs_s = [], []
+    for gathered, work in pending:
+        if work is not None:
+            work.wait()
+        rows = gathered.shape[2]
+        if merge is None:
+            out_i, out_s = topk_merge_runs(gathered, topk)  # [world, 2, rows, topk]: sorted runs
+        else:
+            cand_s = gathered[:, 0].permute(1, 0, 2).reshape(rows, world * topk).contiguous().view(torch.float32)
+            cand_i = gathered[:, 1].permute(1, 0, 2).reshape(rows, world * topk).contiguous()
+            out_i, out_s = merge(cand_s, cand_i, topk)
+        outs_i.append(out_i.reshape(B, hq, Sq, topk))
+        outs_s.append(out_s.reshape(B, hq, Sq, topk))
+    out_i = outs_i[0] if chunks == 1 else torch.cat(outs_i, dim=1)
+    if return_scores:
+        return out_i, (outs_s[0] if chunks == 1 else torch.cat(outs_s, dim=1))
+    return out_i
+
+
+def _local_packed(local_topk, q, k_shard, topk, inv_freq, shard_start, extra) -> torch.Tensor:
+    """This rank's exact local top-k as an int32 [2, rows, topk] buffer (score bits,
+    global indices), sorted; a shard shorter than topk is padded with -inf."""
     B, Hq, Sq, _ = q.shape
     rows = B * Hq * Sq
     kl = min(topk, k_shard.shape[2])
@@ -95,14 +137,4 @@ def sharded_einsum_topk(
         if kl < topk:  # a shard shorter than k contributes -inf padding
             packed[0, :, kl:] = torch.tensor(float("-inf"), dtype=torch.float32).view(torch.int32).item()
             packed[1, :, kl:] = torch.iinfo(torch.int32).max
-    gathered = _all_gather(packed, world, group)  # [world, 2, rows, topk]: sorted runs
-    if merge is None:
-        out_i, out_s = topk_merge_runs(gathered, topk)
-    else:
-        cand_s = gathered[:, 0].permute(1, 0, 2).reshape(rows, world * topk).contiguous().view(torch.float32)
-        cand_i = gathered[:, 1].permute(1, 0, 2).reshape(rows, world * topk).contiguous()
-        out_i, out_s = merge(cand_s, cand_i, topk)
-    out_i = out_i.reshape(B, Hq, Sq, topk)
-    if return_scores:
-        return out_i, out_s.reshape(B, Hq, Sq, topk)
-    return out_i
+    return packed

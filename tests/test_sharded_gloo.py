@@ -45,11 +45,13 @@ def _worker(rank, world, port, case, q, k_full, inv, topk, errq, v_full=None):
         if case == "die" and rank == 1:
             os._exit(0)  # leaves between steps, before the exchange
         rt = "qkv2" if case == "qkv2" else "qk"
+        chunks = 2 if case == "chunks2" else 1
         v_shard = v_full[:, :, start:stop] if v_full is not None else None
         try:
             idx, sc = sharded_einsum_topk(q, k_full[:, :, start:stop], topk, shard_start=start,
                                           inv_freq=inv, return_scores=True, local_topk=_cpu_local,
-                                          merge=merge_candidates_torch, v_shard=v_shard, recall_type=rt)
+                                          merge=merge_candidates_torch, v_shard=v_shard, recall_type=rt,
+                                          chunks=chunks)
         except Exception as e:  # noqa: BLE001
             if case == "die":
                 _put_and_exit(errq, ("ok-error", rank, type(e).__name__))
@@ -103,6 +105,14 @@ def test_sharded_matches_oracle(world, Sk, topk):
 
 def test_sharded_value_weighted_matches_oracle():
     res = _run(2, "qkv2", 1000, 60, seed=4)
+    assert sorted(r[1] for r in res) == [0, 1], res
+    for status, rank, msg in res:
+        assert status == "ok", msg
+
+
+def test_sharded_chunked_exchange_matches_oracle():
+    # two groups of KV heads, each exchanged on its own (asynchronous) all-gather
+    res = _run(2, "chunks2", 1000, 50, seed=6)
     assert sorted(r[1] for r in res) == [0, 1], res
     for status, rank, msg in res:
         assert status == "ok", msg
