@@ -125,7 +125,8 @@ def run_attention(args):
         "roofline": {"bound": "hbm", "unit": "GB/s", "bytes_per_launch": bytes_per_call,
                      "achieved": achieved, "peak": peak, "frac": achieved / peak,
                      "peak_source": peak_kind, "launch_ms": launch_ms},
-        "gpu_launches": 2 * args.steps, "timing": "CUDA graph of one call, replayed",
+        # per call: the RoPE angle table, the split partials, the split merge
+        "gpu_launches": 3 * args.steps, "timing": "CUDA graph of one call, replayed",
     }
     print(json.dumps(line), flush=True)
     return 0

@@ -10,6 +10,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
@@ -61,15 +62,19 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return LIB_PATH
     nvcc = nvcc_path()
     BUILD_DIR.mkdir(exist_ok=True)
-    objs = []
+    cmds, objs = [], []
     for src in _sources():
         obj = BUILD_DIR / (src.stem + ".o")
         cmd = [nvcc, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd), file=sys.stderr)
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
         objs.append(str(obj))
+    # one nvcc per source file, in parallel
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as pool:
+        for res in pool.map(lambda c: subprocess.run(c, check=True), cmds):
+            del res
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *objs]
     subprocess.run(cmd, check=True)

@@ -11,13 +11,15 @@
 // contiguous share of the split's keys, 8 at a time (their rows all requested
 // before the first is used): the key and value rows are gathered with one
 // coalesced 8-byte load per lane (lane L holds dimensions 4L .. 4L+3), the
-// key is rotated at its RoPE position in registers (lanes L and L ^ 16 hold the
-// two halves of a rotation pair; each computes two of the pair group's four
-// angles and they swap them), dotted with every query row (fp32, warp
-// reduction), and folded into the row's online softmax (running max, sum and
-// the unnormalised value accumulator). The warps' states are merged in shared
-// memory and the CTA writes one partial (m, l, acc[128]) per row and split.
+// key is rotated from the view's angle table (rope_table_kernel: (cos, sin) of
+// every position and frequency; lanes L and L ^ 16 hold the two halves of a
+// rotation pair), dotted with every query row (fp32, warp reduction), and folded
+// into the row's online softmax (running max, sum and the unnormalised value
+// accumulator). The warps' states are merged in shared memory and the CTA writes
+// one partial (m, l, acc[128]) per row and split.
 // sparse_attn_combine_kernel merges the splits of each row and writes the output.
+// The partial and combine kernels are dependent launches: each starts while its
+// predecessor drains and waits (griddepcontrol.wait) before reading its output.
 #include "common.cuh"
 #include "kernels.h"
 #include "rope_sincos.cuh"
@@ -26,7 +28,6 @@ namespace prism {
 namespace {
 
 constexpr int kSaWarps = 8;
-constexpr int kU = 8;  // key rows per warp in flight
 
 template <typename T>
 __device__ __forceinline__ float4 load4(const T* p) {
@@ -123,12 +124,6 @@ __device__ __forceinline__ float dot4(float4 a, float4 b) {
   return fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, a.w * b.w)));
 }
 
-__device__ __forceinline__ float warp_sum(float x) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-  return x;
-}
-
 // kRB: query rows per CTA (4 for decode's GQA groups, 8 otherwise)
 template <typename T, bool kRope, int kRB>
 __global__ void __launch_bounds__(kSaWarps * 32, kRB == 4 ? 2 : 1)
@@ -176,6 +171,10 @@ __global__ void __launch_bounds__(kSaWarps * 32, kRB == 4 ? 2 : 1)
       q[r].w *= a.scale;
     }
   }
+  // the angle table (a dependent launch after rope_table_kernel) is complete and
+  // visible after this; the combine kernel may launch now
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   float m[kRB], l[kRB];
   float4 acc[kRB];
 #pragma unroll
@@ -317,28 +316,78 @@ __global__ void __launch_bounds__(kSaWarps * 32, kRB == 4 ? 2 : 1)
   }
 }
 
-template <typename T>
-__global__ void sparse_attn_combine_kernel(const SparseAttnArgs a, int nsplit) {
-  const int64_t row = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+// Merge of the splits: kWpr warps per row (8 when the row has many splits, 1
+// otherwise). Every warp of the row takes the row maximum over all splits (one
+// load per lane), then folds its splits sp = sub, sub + kWpr, ... four at a time
+// with all their loads in flight; the row's warps are summed in shared memory.
+template <typename T, int kWpr>
+__global__ void __launch_bounds__(256) sparse_attn_combine_kernel(const SparseAttnArgs a, int nsplit) {
+  constexpr int kRpc = 8 / kWpr;  // rows per CTA
+  __shared__ float s_l[8];
+  __shared__ float4 s_acc[8][32];
+  // programmatic dependent launch: the partials are complete and visible after this
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = warp % kWpr;
+  const int64_t row = int64_t(blockIdx.x) * kRpc + warp / kWpr;
   const int64_t rows = int64_t(a.B) * a.Hq * a.Sq;
-  if (row >= rows) return;
+  const bool ok = row < rows;
+  const int64_t base = row * nsplit;
   float M = -INFINITY;
-  for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, a.part_m[row * nsplit + sp]);
+  if (ok) {
+#pragma unroll
+    for (int t = 0; t < kSparseMaxSplits / 32; ++t)
+      if (lane + 32 * t < nsplit) M = fmaxf(M, a.part_m[base + lane + 32 * t]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   float L = 0.f;
   float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (M != -INFINITY) {
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const int64_t slot = row * nsplit + sp;
-      const float f = __expf(a.part_m[slot] - M);
-      L = fmaf(a.part_l[slot], f, L);
-      const float4 x = reinterpret_cast<const float4*>(a.part_acc + slot * 128)[lane];
-      A.x = fmaf(x.x, f, A.x);
-      A.y = fmaf(x.y, f, A.y);
-      A.z = fmaf(x.z, f, A.z);
-      A.w = fmaf(x.w, f, A.w);
+  if (ok && M != -INFINITY) {
+    for (int sp0 = sub; sp0 < nsplit; sp0 += 4 * kWpr) {
+      float mm[4], ll[4];
+      float4 xx[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int sp = sp0 + u * kWpr;
+        mm[u] = -INFINITY;
+        ll[u] = 0.f;
+        xx[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (sp < nsplit) {
+          mm[u] = a.part_m[base + sp];
+          ll[u] = a.part_l[base + sp];
+          xx[u] = reinterpret_cast<const float4*>(a.part_acc + (base + sp) * 128)[lane];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float f = __expf(mm[u] - M);
+        L = fmaf(ll[u], f, L);
+        A.x = fmaf(xx[u].x, f, A.x);
+        A.y = fmaf(xx[u].y, f, A.y);
+        A.z = fmaf(xx[u].z, f, A.z);
+        A.w = fmaf(xx[u].w, f, A.w);
+      }
     }
   }
+  if (kWpr > 1) {
+    if (lane == 0) s_l[warp] = L;
+    s_acc[warp][lane] = A;
+    __syncthreads();
+    if (sub != 0) return;
+    L = 0.f;
+    A = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kWpr; ++w) {
+      L += s_l[warp + w];
+      const float4 x = s_acc[warp + w][lane];
+      A.x += x.x;
+      A.y += x.y;
+      A.z += x.z;
+      A.w += x.w;
+    }
+  }
+  if (!ok) return;
   // a row that sees no key gets zeros (the reference's nan_to_num of 0/0)
   const float inv = L > 0.f ? 1.f / L : 0.f;
   A.x *= inv;
@@ -351,6 +400,7 @@ __global__ void sparse_attn_combine_kernel(const SparseAttnArgs a, int nsplit) {
 // (cos, sin) of every view position's 64 RoPE angles, fp32(pe) * inv_freq[i]
 // evaluated with the accurate reduction of rope_sincos.cuh: [nsel][64] float2
 __global__ void rope_table_kernel(const SparseAttnArgs a, float2* table) {
+  asm volatile("griddepcontrol.launch_dependents;");
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (e >= a.nsel * 64) return;
   const int64_t j = e >> 6;
@@ -382,15 +432,56 @@ int sa_splits(const SparseAttnArgs& a, int num_sms) {
   return int(s < 1 ? 1 : s);
 }
 
+// A launch that may begin while the previous kernel in the stream is finishing
+// (programmatic dependent launch); the kernel's griddepcontrol.wait orders its
+// reads of that kernel's output.
+template <typename... P, typename... A>
+cudaError_t launch_dependent(void (*kern)(P...), dim3 grid, dim3 block, bool pdl,
+                             cudaStream_t stream, A... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// The partial kernel follows the angle table with a dependent launch when there
+// is one (it reads only the caller's inputs before its wait); without RoPE it
+// follows the caller's own work and launches normally.
 template <typename T, bool kRope>
-void launch_partial(const SparseAttnArgs& a, int nsplit, cudaStream_t stream) {
+cudaError_t launch_partial(const SparseAttnArgs& a, int nsplit, cudaStream_t stream) {
   const int64_t R = int64_t(a.G) * a.Sq;
   const int rb = sa_rows(a);
   const dim3 grid(unsigned(int64_t(a.B) * a.Hkv * ((R + rb - 1) / rb)), unsigned(nsplit));
   if (rb == 4)
-    sparse_attn_partial_kernel<T, kRope, 4><<<grid, kSaWarps * 32, 0, stream>>>(a);
-  else
-    sparse_attn_partial_kernel<T, kRope, 8><<<grid, kSaWarps * 32, 0, stream>>>(a);
+    return launch_dependent(sparse_attn_partial_kernel<T, kRope, 4>, grid, dim3(kSaWarps * 32), kRope,
+                            stream, a);
+  return launch_dependent(sparse_attn_partial_kernel<T, kRope, 8>, grid, dim3(kSaWarps * 32), kRope,
+                          stream, a);
+}
+
+template <typename T>
+cudaError_t launch_combine(const SparseAttnArgs& a, int nsplit, cudaStream_t stream) {
+  const int64_t rows = int64_t(a.B) * a.Hq * a.Sq;
+  if (nsplit > 4)
+    return launch_dependent(sparse_attn_combine_kernel<T, 8>, dim3(unsigned(rows)), dim3(256), true,
+                            stream, a, nsplit);
+  return launch_dependent(sparse_attn_combine_kernel<T, 1>, dim3(unsigned((rows + 7) / 8)), dim3(256),
+                          true, stream, a, nsplit);
+}
+
+template <typename T>
+cudaError_t launch_attn(const SparseAttnArgs& a, int nsplit, cudaStream_t stream) {
+  cudaError_t e = a.inv_freq != nullptr ? launch_partial<T, true>(a, nsplit, stream)
+                                        : launch_partial<T, false>(a, nsplit, stream);
+  if (e != cudaSuccess) return e;
+  return launch_combine<T>(a, nsplit, stream);
 }
 
 }  // namespace
@@ -417,21 +508,9 @@ cudaError_t launch_sparse_attn(SparseAttnArgs a, int dtype, void* ws, int num_sm
     rope_table_kernel<<<unsigned((n + 255) / 256), 256, 0, stream>>>(a, table);
     a.table = table;
   }
-  const unsigned cgrid = unsigned((rows + 7) / 8);
-  const bool rope = a.inv_freq != nullptr;
-  if (dtype == kBF16) {
-    if (rope)
-      launch_partial<__nv_bfloat16, true>(a, nsplit, stream);
-    else
-      launch_partial<__nv_bfloat16, false>(a, nsplit, stream);
-    sparse_attn_combine_kernel<__nv_bfloat16><<<cgrid, 256, 0, stream>>>(a, nsplit);
-  } else {
-    if (rope)
-      launch_partial<__half, true>(a, nsplit, stream);
-    else
-      launch_partial<__half, false>(a, nsplit, stream);
-    sparse_attn_combine_kernel<__half><<<cgrid, 256, 0, stream>>>(a, nsplit);
-  }
+  const cudaError_t e = dtype == kBF16 ? launch_attn<__nv_bfloat16>(a, nsplit, stream)
+                                        : launch_attn<__half>(a, nsplit, stream);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
