@@ -10,8 +10,9 @@ processed per second, all heads), whole job.
 * N = 1 runs ``decode-128k``: one decode step, 32 query / 8 KV heads,
   head_dim 128, 131072 RoPE'd bf16 keys, k = 4096 per query head.
 * N > 1 (one process per GPU, launched by torchrun) runs ``decode-1m-sharded``:
-  1,048,576 keys split evenly over the N ranks (strong scaling), k = 8192, the
-  per-rank candidates all-gathered with NCCL and merged on every GPU.
+  1,048,576 keys split evenly over the N ranks (strong scaling), k = 8192; every
+  rank's merge kernel reads the other ranks' sorted runs from their GPUs over
+  NVLink (peer-mapped buffers; ``--exchange nccl``: NCCL all-gather, then merge).
 
 A step is one full call of the op on resident inputs; W untimed steps, then K
 steps timed with CUDA events between barriers, max over ranks. The key cache
@@ -56,6 +57,9 @@ def parse():
     ap.add_argument("--chunks", type=int, default=0,
                     help="sharded path: groups of KV heads whose exchange is pipelined "
                          "(0: 2 when the KV heads split evenly, else 1)")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="sharded path: peer: runs read over NVLink from peer-mapped buffers; "
+                         "nccl: all-gather of the runs, then a local merge")
     ap.add_argument("--stage", default="recall", choices=["recall", "attention"],
                     help="attention: time the attention over a selected view instead of the recall")
     return ap.parse_args()
@@ -145,13 +149,16 @@ def pick_workload(args, world):
     return W.WORKLOADS[name]
 
 
-def config_of(wl, world, recall_type="qk"):
+def config_of(wl, world, recall_type="qk", exchange="nccl"):
     return {
         "workload": wl.name, "B": wl.B, "Hq": wl.Hq, "Hkv": wl.Hkv, "Sq": wl.Sq, "Sk": wl.Sk,
         "topk": wl.topk, "head_dim": wl.D, "rope_theta": wl.theta, "key_dtype": "bf16",
         "causal_offset": wl.causal_offset, "shards": world,
         "parallelism": "single GPU" if world == 1 else
-                       f"sequence-sharded x{world} (NCCL all-gather pipelined over KV-head groups + device merge)",
+                       f"sequence-sharded x{world} (" + (
+                           "peer-mapped exchange over NVLink: each rank's merge kernel reads the other ranks' "
+                           "runs from their GPUs" if exchange == "peer" else
+                           "NCCL all-gather pipelined over KV-head groups + device merge") + ")",
         "l2": "inputs larger than L2 (cached keys %d MB per rank > 126 MB), no flush" % (wl.kv_bytes // world >> 20),
         "recall_type": recall_type,
     }
@@ -377,14 +384,18 @@ def main():
     q, k, inv = x["q"], x["k"], x["inv_freq"]
     rt = args.recall_type
     v = W.make_values(wl, dev, start, stop) if rt != "qk" else None
-    chunks = args.chunks or (2 if wl.Hkv % 2 == 0 else 1)
+    exchange = None
+    if world > 1 and args.exchange == "peer":
+        from prism_test_b200.peer_exchange import PeerExchange
+        exchange = PeerExchange(wl.B * wl.Hq * wl.Sq, wl.topk, dev)
+    chunks = 1 if exchange is not None else (args.chunks or (2 if wl.Hkv % 2 == 0 else 1))
 
     def step(qq, kk, vv=v):
         if world == 1:
             return einsum_topk_func(qq, kk, wl.topk, inv_freq=inv, return_scores=True,
                                     causal_offset=wl.causal_offset, values=vv, recall_type=rt)
         return sharded_einsum_topk(qq, kk, wl.topk, shard_start=start, inv_freq=inv, return_scores=True,
-                                   v_shard=vv, recall_type=rt, chunks=chunks)
+                                   v_shard=vv, recall_type=rt, chunks=chunks, exchange=exchange)
 
     def barrier():
         if world > 1:
@@ -546,6 +557,10 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = cpu_baseline(wl, recall_type=rt)
 
+    exchange_status = None
+    if exchange is not None:
+        exchange_status = max_over_ranks(float(exchange.status()))
+        exchange.close()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -558,7 +573,7 @@ def main():
         "scaling": "weak" if world == 1 else "strong", "vs_baseline": None,
         "dtype": "bf16 in, fp32 accumulate (tcgen05)" if prefill else "f32 (tf32 MMA)",
         "data": "synthetic (seeded; see prism_test_b200/workloads.py)",
-        "config": config_of(wl, world, rt),
+        "config": config_of(wl, world, rt, "peer" if exchange is not None else "nccl"),
         "roofline": dict(roof, achieved=achieved, peak=peak, frac=achieved / peak,
                          peak_source=peak_kind, traffic=ncu_traffic("score", wl.name),
                          launch_ms=score_ms),
@@ -576,6 +591,8 @@ def main():
         "e2e": e2e,
         "cpu_baseline": base,
     }
+    if exchange_status is not None:
+        line["exchange_status"] = int(exchange_status)  # 0: every bounded peer wait succeeded
     print(json.dumps(line), flush=True)
     return 0
 

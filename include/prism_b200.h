@@ -216,6 +216,48 @@ PRISM_API int prism_topk_merge_runs(const int32_t* runs, int32_t nruns, int64_t 
                                     float* out_scores, void* stream);
 
 /*
+ * Peer exchange of the sequence-sharded path over NVLink. It has no counterpart
+ * in the reference (which is single-GPU); with prism_peer_merge it replaces the
+ * all-gather of the ranks' local top-k runs plus prism_topk_merge_runs, i.e. the
+ * torch.topk over the union (reattention.py:497) of a sequence split over GPUs.
+ * One process per GPU. Every rank owns one exchange buffer of
+ * prism_peer_buffer_bytes(rows, topk) bytes: a PRISM_PEER_HEADER_BYTES header
+ * (its first int32 is the status word prism_read_status reads), then the rank's
+ * run, int32 [2, rows, topk] (fp32 score bits, global indices) at offset
+ * PRISM_PEER_HEADER_BYTES, laid out as prism_einsum_topk's out_scores / out_idx.
+ *   prism_peer_alloc   cudaMalloc + zero + an IPC handle (PRISM_IPC_HANDLE_BYTES)
+ *                      to hand to the other ranks (any host transport).
+ *   prism_peer_open    maps another rank's buffer from its handle;
+ *                      prism_peer_close unmaps it, prism_peer_free frees one's own.
+ * A step on every rank, on one stream, in the same order on all ranks:
+ *   1. write the local top-k into the own buffer's run;
+ *   2. prism_peer_publish: advances the rank's step counter and marks its run
+ *      ready in every rank's header (one warp, release stores over NVLink);
+ *   3. prism_peer_merge: waits until every rank's run of the step is ready, merges
+ *      the runs straight from the peers' memory into out_idx / out_scores
+ *      [rows, topk] (same result as prism_topk_merge_runs), then tells every rank
+ *      its run was read; with wait_acks != 0 its last CTA also waits until every
+ *      rank has read this rank's run, so step 1 of the next step may overwrite it.
+ * bufs is a HOST array of the world buffers as mapped in this process (the own
+ * one at bufs[rank]), each 256-byte aligned; world <= PRISM_PEER_MAX_RANKS.
+ * Steps are counted on the device, so the calls can be captured in a CUDA graph.
+ * Every wait gives up after timeout_ns (<= 0: 2 s) and sets status 1; the
+ * exchange must then be rebuilt (new buffers on every rank).
+ */
+#define PRISM_IPC_HANDLE_BYTES 64
+#define PRISM_PEER_HEADER_BYTES 512
+#define PRISM_PEER_MAX_RANKS 16
+PRISM_API size_t prism_peer_buffer_bytes(int64_t rows, int32_t topk);
+PRISM_API int prism_peer_alloc(size_t bytes, void** buf, void* ipc_handle);
+PRISM_API int prism_peer_open(const void* ipc_handle, void** buf);
+PRISM_API int prism_peer_close(void* buf);
+PRISM_API int prism_peer_free(void* buf);
+PRISM_API int prism_peer_publish(void* const* bufs, int32_t world, int32_t rank, void* stream);
+PRISM_API int prism_peer_merge(void* const* bufs, int32_t world, int32_t rank, int64_t rows,
+                               int32_t topk, int32_t wait_acks, int64_t timeout_ns,
+                               int32_t* out_idx, float* out_scores, void* stream);
+
+/*
  * prism_topk_merge without a workspace, for callers that cannot allocate device
  * memory (no cudaMalloc / cudaFree / allocating library call anywhere in the
  * call). It has no counterpart in the reference. Same arguments, kernel and

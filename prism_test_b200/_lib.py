@@ -35,6 +35,9 @@ KERNEL_ATTN = 6
 RECALL_QK = 0
 RECALL_QKV = 1
 RECALL_QKV2 = 2
+IPC_HANDLE_BYTES = 64
+PEER_HEADER_BYTES = 512
+PEER_MAX_RANKS = 16
 
 # Every function the header declares: name -> (restype, argtypes)
 _c_i64 = ctypes.c_int64
@@ -82,6 +85,15 @@ SIGNATURES = {
         _vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _vp, _vp, _vp, ctypes.c_size_t, _vp,
     ]),
     "prism_post_select_workspace_size": (ctypes.c_size_t, [_c_i64, _c_i32]),
+    "prism_peer_buffer_bytes": (ctypes.c_size_t, [_c_i64, _c_i32]),
+    "prism_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]),
+    "prism_peer_open": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
+    "prism_peer_close": (ctypes.c_int, [_vp]),
+    "prism_peer_free": (ctypes.c_int, [_vp]),
+    "prism_peer_publish": (ctypes.c_int, [ctypes.POINTER(_vp), _c_i32, _c_i32, _vp]),
+    "prism_peer_merge": (ctypes.c_int, [
+        ctypes.POINTER(_vp), _c_i32, _c_i32, _c_i64, _c_i32, _c_i32, _c_i64, _vp, _vp, _vp,
+    ]),
     "prism_read_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), _vp]),
     "prism_profile_start": (ctypes.c_int, [_c_i32]),
     "prism_profile_stop": (ctypes.c_int, []),

@@ -637,6 +637,123 @@ int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms) {
 
 int64_t prism_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+// ---- peer exchange of the sequence-sharded path -------------------------------------
+static_assert(PRISM_PEER_HEADER_BYTES == prism::kPeerHeaderBytes, "peer header size");
+static_assert(PRISM_PEER_MAX_RANKS == prism::kPeerMaxRanks, "peer rank limit");
+
+size_t prism_peer_buffer_bytes(int64_t rows, int32_t topk) {
+  if (rows < 1 || topk < 1) return 0;
+  return prism::kPeerHeaderBytes + size_t(rows) * size_t(topk) * 2 * sizeof(int32_t);
+}
+
+int prism_peer_alloc(size_t bytes, void** buf, void* ipc_handle) {
+  g_last_error.clear();
+  if (!buf || !ipc_handle) return fail(PRISM_E_INVALID, "null pointer argument");
+  if (bytes < prism::kPeerHeaderBytes) return fail(PRISM_E_INVALID, "buffer smaller than its header");
+  static_assert(sizeof(cudaIpcMemHandle_t) == PRISM_IPC_HANDLE_BYTES, "IPC handle size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "allocating the exchange buffer");
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "preparing the exchange buffer");
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *buf = p;
+  return PRISM_OK;
+}
+
+int prism_peer_open(const void* ipc_handle, void** buf) {
+  g_last_error.clear();
+  if (!buf || !ipc_handle) return fail(PRISM_E_INVALID, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "mapping a peer's exchange buffer");
+  *buf = p;
+  return PRISM_OK;
+}
+
+int prism_peer_close(void* buf) {
+  g_last_error.clear();
+  if (!buf) return fail(PRISM_E_INVALID, "null pointer argument");
+  cudaError_t e = cudaIpcCloseMemHandle(buf);
+  if (e != cudaSuccess) return cuda_fail(e, "unmapping a peer's exchange buffer");
+  return PRISM_OK;
+}
+
+int prism_peer_free(void* buf) {
+  g_last_error.clear();
+  if (!buf) return fail(PRISM_E_INVALID, "null pointer argument");
+  cudaError_t e = cudaFree(buf);
+  if (e != cudaSuccess) return cuda_fail(e, "freeing the exchange buffer");
+  return PRISM_OK;
+}
+
+}  // extern "C"
+
+namespace {
+int peer_sync(void* const* bufs, int32_t world, int32_t rank, prism::PeerSync& sync) {
+  if (!bufs) return fail(PRISM_E_INVALID, "null pointer argument");
+  if (world < 1 || world > prism::kPeerMaxRanks)
+    return fail(PRISM_E_UNSUPPORTED, "1 to %d ranks are supported, got %d", prism::kPeerMaxRanks, world);
+  if (rank < 0 || rank >= world) return fail(PRISM_E_INVALID, "rank %d outside [0, %d)", rank, world);
+  sync = prism::PeerSync{};
+  for (int r = 0; r < world; ++r) {
+    if (!bufs[r]) return fail(PRISM_E_INVALID, "null exchange buffer of rank %d", r);
+    if (reinterpret_cast<uintptr_t>(bufs[r]) & 255u)
+      return fail(PRISM_E_INVALID, "exchange buffer of rank %d is not 256-byte aligned", r);
+    sync.peer[r] = static_cast<prism::PeerHeader*>(bufs[r]);
+  }
+  sync.self = sync.peer[rank];
+  sync.rank = rank;
+  return PRISM_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int prism_peer_publish(void* const* bufs, int32_t world, int32_t rank, void* stream_ptr) {
+  g_last_error.clear();
+  prism::PeerSync sync;
+  const int rc = peer_sync(bufs, world, rank, sync);
+  if (rc != PRISM_OK) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  cudaError_t e = launch_counted(PRISM_KERNEL_MERGE, stream, [&] {
+    return prism::launch_peer_publish(sync, world, stream);
+  });
+  if (e != cudaSuccess) return cuda_fail(e, "publish kernel launch");
+  return PRISM_OK;
+}
+
+int prism_peer_merge(void* const* bufs, int32_t world, int32_t rank, int64_t rows, int32_t topk,
+                     int32_t wait_acks, int64_t timeout_ns, int32_t* out_idx, float* out_scores,
+                     void* stream_ptr) {
+  g_last_error.clear();
+  prism::PeerSync sync;
+  const int rc = peer_sync(bufs, world, rank, sync);
+  if (rc != PRISM_OK) return rc;
+  if (!out_idx) return fail(PRISM_E_INVALID, "null pointer argument");
+  if (rows < 1 || topk < 1) return fail(PRISM_E_INVALID, "need rows >= 1 and topk >= 1");
+  if (topk > prism::kSelectMaxK)
+    return fail(PRISM_E_UNSUPPORTED, "topk above %d is not supported", prism::kSelectMaxK);
+  sync.wait_acks = wait_acks != 0;
+  sync.timeout_ns = timeout_ns > 0 ? timeout_ns : int64_t(prism::kWaitTimeoutNs);
+  prism::RunSet rs{};
+  for (int r = 0; r < world; ++r)
+    rs.run[r] = reinterpret_cast<const int32_t*>(static_cast<const uint8_t*>(bufs[r]) + prism::kPeerHeaderBytes);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  cudaError_t e = launch_counted(PRISM_KERNEL_MERGE, stream, [&] {
+    return prism::launch_merge_runs(rs, world, rows, topk, topk, out_idx, out_scores, sync, stream);
+  });
+  if (e != cudaSuccess) return cuda_fail(e, "peer merge kernel launch");
+  return PRISM_OK;
+}
+
 int prism_read_status(void* workspace, int* status_out, void* stream_ptr) {
   g_last_error.clear();
   if (!workspace || !status_out) return fail(PRISM_E_INVALID, "null pointer argument");

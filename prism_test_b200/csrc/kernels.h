@@ -108,10 +108,40 @@ int64_t select_cand_cap(int64_t n);
 size_t select_workspace_bytes(int64_t rows, int64_t n);
 cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t stream);
 
-// Top-k of the union of nruns sorted runs [nruns, rows, run_len, 2] of (fp32
-// score bits, int32 index) pairs, run_len >= k, k <= 16384.
+// Top-k of the union of nruns sorted runs, run r an int32 [2, rows, run_len]
+// buffer (fp32 score bits, int32 indices), run_len >= k, k <= 16384. The first
+// form takes the runs back to back ([nruns, 2, rows, run_len]).
 cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int64_t run_len, int k,
                               int32_t* out_idx, float* out_scores, cudaStream_t stream);
+
+// --- peer exchange of the sequence-sharded path (NVLink, peer-mapped memory) ----
+// Every rank owns one exchange buffer: this header, then its run [2, rows, topk]
+// at kPeerHeaderBytes. Every rank maps every other rank's buffer.
+constexpr int kPeerMaxRanks = 16;
+constexpr size_t kPeerHeaderBytes = 512;
+struct PeerHeader {
+  int32_t status;               // kStatus* of this rank's exchange kernels (first word)
+  uint32_t done;                // merge CTAs of the current step that finished reading
+  uint64_t step;                // this rank's exchange step (advanced by the publish)
+  uint64_t ready[kPeerMaxRanks];  // ready[r] == s: rank r's run of step s is complete
+  uint64_t ack[kPeerMaxRanks];    // ack[r] == s: rank r has read this rank's run of step s
+};
+static_assert(sizeof(PeerHeader) <= kPeerHeaderBytes, "peer header too large");
+constexpr int kMergeRunsMax = 16;
+struct RunSet {
+  const int32_t* run[kMergeRunsMax];
+};
+struct PeerSync {
+  PeerHeader* self;                 // nullptr: a plain merge, no exchange
+  PeerHeader* peer[kPeerMaxRanks];  // every rank's header, as mapped here
+  int rank;
+  int wait_acks;                    // the merge's last CTA waits for every rank's ack
+  int64_t timeout_ns;               // bound of every wait
+};
+cudaError_t launch_merge_runs(const RunSet& rs, int nruns, int64_t rows, int64_t run_len, int k,
+                              int32_t* out_idx, float* out_scores, const PeerSync& sync,
+                              cudaStream_t stream);
+cudaError_t launch_peer_publish(const PeerSync& sync, int world, cudaStream_t stream);
 
 // Post-selection: sorted union of the selected middle positions (optionally the
 // recall_clip most frequent), each widened to [p + lo, p + hi) and clamped to

@@ -959,37 +959,54 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_row_kernel(const Sele
 }
 
 // ---- top-k of the union of sorted runs (the sharded path's merge) --------------------
-// Runs are int32 [nruns, 2, rows, run_len]: per run a plane of fp32 score bits and a
+// Run r is int32 [2, rows, run_len] at rs.run[r]: a plane of fp32 score bits and a
 // plane of global indices, each row sorted by descending score then ascending
-// index (what every rank's prism_einsum_topk returns). Candidates are compared as
+// index (what every rank's prism_einsum_topk returns); the runs may sit in other
+// GPUs' memory (peer-mapped exchange buffers). Candidates are compared as
 // (key << 32) | ~index. A summary of every run — its entries at positions s-1,
 // 2s-1, ... with s = max(1, k / 128) — bounds from below how many of its entries
 // are at or above a value (s per summary entry at or above it). The threshold T is
 // the largest summary entry whose bound, summed over the runs, reaches k: the
 // global k-th candidate is at or above T, and fewer than k + (N + 1) s candidates
 // are, however the top keys are split over the runs. Those prefixes are staged in
-// shared memory and counting-sorted exactly like the selection's candidates. If
-// ties at T make the prefixes exceed 16384 entries, each candidate is ranked by
-// binary searches in the other runs in global memory instead (slow, same result).
-constexpr int kMergeMaxRuns = 16;
+// shared memory and every staged candidate is ranked by binary searches in the
+// other runs' prefixes (ties between equal candidates: lower run first); the
+// candidates ranked below k are the output, each written to its rank. If ties at
+// T make the prefixes exceed 16384 entries, the binary searches run in global
+// memory instead (slow, same result).
+constexpr int kMergeMaxRuns = kMergeRunsMax;
 constexpr int kMergeSumm = 128;
 constexpr int kMergeParts = 4;  // CTAs per row of the run merge
 
-__device__ __forceinline__ uint64_t run_cand(const int32_t* runs, int r, int64_t rows, int64_t row,
-                                             int64_t run_len, int64_t j) {
-  const int32_t* s = runs + ((int64_t(r) * 2) * rows + row) * run_len + j;
+__device__ __forceinline__ uint64_t run_cand(const int32_t* const* runs, int r, int64_t rows,
+                                             int64_t row, int64_t run_len, int64_t j) {
+  const int32_t* s = runs[r] + row * run_len + j;
   return (uint64_t(float_to_okey(__int_as_float(s[0]))) << 32) | uint64_t(~uint32_t(s[rows * run_len]));
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    merge_runs_kernel(const int32_t* __restrict__ runs, int nruns, int64_t rows, int64_t run_len,
-                      int k, int32_t* __restrict__ out_idx, float* __restrict__ out_scores) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
-  // kMergeParts CTAs per row: each finds the same candidates and sorts them, and
-  // writes its own part of the output positions
-  const int64_t row = blockIdx.x / kMergeParts;
-  const unsigned part = blockIdx.x % kMergeParts;
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Spins until *p == want or timeout_ns of %globaltimer pass (false).
+__device__ bool wait_flag_eq(const uint64_t* p, uint64_t want, int64_t timeout_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_sys(p) != want) {
+    if (int64_t(globaltimer_ns() - t0) > timeout_ns) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
+__device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, int64_t run_len, int k,
+                          int32_t* __restrict__ out_idx, float* __restrict__ out_scores,
+                          SelectSmem& sm, int64_t row, unsigned part) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   auto cand_at = [&](int r, int64_t j) { return run_cand(runs, r, rows, row, run_len, j); };
   uint64_t* summ = reinterpret_cast<uint64_t*>(sm.hist);  // [nruns][kMergeSumm]
@@ -997,15 +1014,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- threshold from the run summaries ----------------------------------------------------
   const int64_t sstep = k / kMergeSumm > 1 ? k / kMergeSumm : 1;
   const int nsum = int(run_len / sstep < kMergeSumm ? run_len / sstep : kMergeSumm);
-  if (tid == 0) {
-    sm.rthr = 0;
-    sm.kmax = 0;
+  if (tid == 0) sm.rthr = 0;
+  {
+    // each CTA of the row's cluster loads a quarter of the summary entries and
+    // copies the rest from its cluster peers' shared memory
+    cg::cluster_group cluster = cg::this_cluster();
+    const int ns = nruns * nsum;
+    for (int e = ns * int(part) / kMergeParts + tid; e < ns * int(part + 1) / kMergeParts; e += kThreads) {
+      const int r = e / nsum, i = e - r * nsum;
+      summ[r * kMergeSumm + i] = cand_at(r, (int64_t(i) + 1) * sstep - 1);
+    }
+    cluster.sync();
+    for (unsigned c = 0; c < unsigned(kMergeParts); ++c) {
+      if (c == part) continue;
+      const uint64_t* src = cluster.map_shared_rank(summ, c);
+      for (int e = ns * int(c) / kMergeParts + tid; e < ns * int(c + 1) / kMergeParts; e += kThreads) {
+        const int at = (e / nsum) * kMergeSumm + e % nsum;
+        summ[at] = src[at];
+      }
+    }
+    cluster.sync();  // every CTA holds every summary; nobody reads a peer's copy any more
   }
-  for (int e = tid; e < nruns * nsum; e += kThreads) {
-    const int r = e / nsum, i = e - r * nsum;
-    summ[r * kMergeSumm + i] = cand_at(r, (int64_t(i) + 1) * sstep - 1);
-  }
-  __syncthreads();
   for (int e = tid; e < nruns * nsum; e += kThreads) {
     const uint64_t v = summ[(e / nsum) * kMergeSumm + e % nsum];
     int64_t c = 0;
@@ -1034,9 +1063,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   const uint64_t thr = sm.rthr;
-  // prefix of each run at or above T: warp r narrows the boundary 32-fold per step
+  // prefix of each run at or above T: warp r narrows the boundary 32-fold per step,
+  // starting from the window its summary leaves (c summary entries >= T: the
+  // boundary lies in [c * sstep, (c + 1) * sstep - 1], or beyond the summarised part)
   if (warp < nruns) {
-    int64_t lo = 0, hi = run_len;  // entries [0, lo) are >= T, entries [hi, run_len) are < T
+    const uint64_t* sw = summ + warp * kMergeSumm;
+    int ns_ge = 0;
+    for (int i = lane; i < nsum; i += 32) ns_ge += sw[i] >= thr ? 1 : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ns_ge += __shfl_xor_sync(0xffffffffu, ns_ge, o);
+    int64_t lo = int64_t(ns_ge) * sstep;  // entries [0, lo) are >= T, entries [hi, run_len) are < T
+    int64_t hi = ns_ge < nsum ? (int64_t(ns_ge) + 1) * sstep - 1 : run_len;
+    if (hi > run_len) hi = run_len;
     while (lo < hi) {
       const int64_t step = (hi - lo + 31) / 32;
       const int64_t p = lo + int64_t(lane) * step;
@@ -1060,58 +1098,114 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   const uint32_t total = sm.roff[nruns];
+  const bool staged = total <= uint32_t(kCap);  // the same on every CTA of the cluster
+  if (staged) {
+    // each CTA of the row's cluster loads a quarter of the staged entries (so each
+    // entry is read once, from wherever the run lives), then copies the other
+    // quarters from its cluster peers' shared memory
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t q0 = uint32_t(uint64_t(total) * part / kMergeParts);
+    const uint32_t q1 = uint32_t(uint64_t(total) * (part + 1) / kMergeParts);
+    for (int r = 0; r < nruns; ++r) {
+      const uint32_t o = sm.roff[r], e1 = min(o + sm.rlen[r], q1);
+      for (uint32_t e = max(o, q0) + tid; e < e1; e += kThreads) sm.buf[e] = cand_at(r, e - o);
+    }
+    cluster.sync();  // every quarter is staged
+    for (unsigned c = 0; c < unsigned(kMergeParts); ++c) {
+      if (c == part) continue;
+      const uint64_t* src = cluster.map_shared_rank(sm.buf, c);
+      const uint32_t c1 = uint32_t(uint64_t(total) * (c + 1) / kMergeParts);
+      for (uint32_t e = uint32_t(uint64_t(total) * c / kMergeParts) + tid; e < c1; e += kThreads)
+        sm.buf[e] = src[e];
+    }
+    cluster.sync();  // every CTA holds all entries; nobody reads a peer's copy any more
+  }
+  // rank every prefix candidate: its position in its run plus, in every other run,
+  // the entries ahead of it (ties: lower run first)
+  int32_t* oi = out_idx + row * k;
+  float* os = out_scores ? out_scores + row * k : nullptr;
+  for (uint32_t e = part * kThreads + tid; e < total; e += kMergeParts * kThreads) {
+    int r = 0;
+    while (e >= sm.roff[r + 1]) ++r;
+    const uint32_t j = e - sm.roff[r];
+    const uint64_t x = staged ? sm.buf[e] : cand_at(r, j);
+    uint32_t p = j;
+    for (int q = 0; q < nruns; ++q) {
+      if (q == r) continue;
+      const uint64_t* bq = sm.buf + sm.roff[q];
+      uint32_t lo = 0, hi = sm.rlen[q];
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        const uint64_t v = staged ? bq[mid] : cand_at(q, mid);
+        if (v > x || (q < r && v == x)) lo = mid + 1;
+        else hi = mid;
+      }
+      p += lo;
+    }
+    if (p < uint32_t(k)) {
+      oi[p] = int32_t(~uint32_t(x));
+      if (os) os[p] = okey_to_float(uint32_t(x >> 32));
+    }
+  }
+}
 
-  if (total > uint32_t(kCap)) {
-    // rank every prefix candidate against the other runs in global memory
-    int32_t* oi = out_idx + row * k;
-    float* os = out_scores ? out_scores + row * k : nullptr;
-    for (uint32_t e = part * kThreads + tid; e < total; e += kMergeParts * kThreads) {
-      int r = 0;
-      while (e >= sm.roff[r + 1]) ++r;
-      const uint32_t j = e - sm.roff[r];
-      const uint64_t x = cand_at(r, j);
-      uint32_t p = j;
-      for (int q = 0; q < nruns; ++q) {
-        if (q == r) continue;
-        uint32_t lo = 0, hi = sm.rlen[q];  // entries of run q ahead of x (ties: lower run first)
-        while (lo < hi) {
-          const uint32_t mid = (lo + hi) >> 1;
-          const uint64_t v = cand_at(q, mid);
-          if (v > x || (q < r && v == x)) lo = mid + 1;
-          else hi = mid;
-        }
-        p += lo;
-      }
-      if (p < uint32_t(k)) {
-        oi[p] = int32_t(~uint32_t(x));
-        if (os) os[p] = okey_to_float(uint32_t(x >> 32));
-      }
-    }
-    return;
+// With sync.self set, the merge is the read side of the peer exchange: every CTA
+// first waits until each rank has published the current step (ready flags in
+// this rank's header), and the last CTA to finish tells every rank that this
+// rank has read its run (ack flags), then (wait_acks) waits until every rank has
+// read this rank's run, so that the next step may overwrite it. All waits are
+// bounded by sync.timeout_ns and report kStatusTimeout in this rank's header; a
+// CTA whose wait expired merges whatever the buffers hold (every access stays in
+// bounds, and every CTA of a cluster takes the same cluster barriers).
+__global__ void __cluster_dims__(kMergeParts, 1, 1) __launch_bounds__(kThreads, 1)
+    merge_runs_kernel(const RunSet rs, int nruns, int64_t rows, int64_t run_len, int k,
+                      int32_t* __restrict__ out_idx, float* __restrict__ out_scores,
+                      const PeerSync sync) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
+  // kMergeParts CTAs per row: each finds the same candidates, and ranks and writes
+  // its own share of them
+  const int64_t row = blockIdx.x / kMergeParts;
+  const unsigned part = blockIdx.x % kMergeParts;
+  const int tid = threadIdx.x;
+  __shared__ const int32_t* s_runs[kMergeMaxRuns];  // the run pointers, indexed by run
+  if (tid < nruns) s_runs[tid] = rs.run[tid];
+  PeerHeader* self = sync.self;
+  uint64_t step = 0;
+  if (self != nullptr) {
+    step = self->step;
+    if (tid < nruns && !wait_flag_eq(&self->ready[tid], step, sync.timeout_ns))
+      set_status(&self->status, kStatusTimeout);
   }
-  uint32_t kmx = 0;
-  for (int r = 0; r < nruns; ++r) {
-    const uint32_t o = sm.roff[r], n = sm.rlen[r];
-    for (uint32_t j = tid; j < n; j += kThreads) {
-      const uint64_t v = cand_at(r, j);
-      sm.buf[o + j] = v;
-      kmx = max(kmx, uint32_t(v >> 32));
-    }
-  }
-  kmx = __reduce_max_sync(0xffffffffu, kmx);
-  if (lane == 0) atomicMax(&sm.kmax, kmx);
-  __syncthreads();  // the summaries in hist are no longer needed
-  for (int i = tid; i < kFineBins; i += kThreads) sm.hist[i] = 0u;
-  if (tid == 0) sm.big = 0;
   __syncthreads();
-  SelectArgs a{};
-  a.idx_in = runs;  // indices are the runs' own (no index_base)
-  a.rows = rows;
-  a.n = run_len;
-  a.k = k;
-  a.out_idx = out_idx;
-  a.out_scores = out_scores;
-  replicated_sort_store(a, row, sm, total, uint32_t(thr >> 32), sm.kmax, part, kMergeParts);
+  merge_row(s_runs, nruns, rows, run_len, k, out_idx, out_scores, sm, row, part);
+  if (self == nullptr) return;
+  __syncthreads();  // this CTA's reads of the runs are complete
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(&self->done, 1u) == gridDim.x - 1) {
+      self->done = 0;
+      __threadfence_system();
+      for (int r = 0; r < nruns; ++r) st_release_sys(&sync.peer[r]->ack[sync.rank], step);
+      if (sync.wait_acks) {
+        for (int r = 0; r < nruns; ++r)
+          if (!wait_flag_eq(&self->ack[r], step, sync.timeout_ns)) {
+            set_status(&self->status, kStatusTimeout);
+            break;
+          }
+      }
+    }
+  }
+}
+
+// Publish side of the peer exchange: advances this rank's step and marks its run
+// of that step ready in every rank's header (including its own). One warp.
+__global__ void peer_publish_kernel(const PeerSync sync, int world) {
+  const uint64_t s = sync.self->step + 1;
+  __syncwarp();
+  if (threadIdx.x == 0) sync.self->step = s;
+  __threadfence_system();
+  if (int(threadIdx.x) < world) st_release_sys(&sync.peer[threadIdx.x]->ready[sync.rank], s);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) select_topk_general_kernel(const SelectArgs a) {
@@ -1132,8 +1226,9 @@ size_t select_workspace_bytes(int64_t rows, int64_t n) {
   return size_t(rows) * size_t(select_cand_cap(n)) * sizeof(uint64_t);
 }
 
-cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int64_t run_len, int k,
-                              int32_t* out_idx, float* out_scores, cudaStream_t stream) {
+cudaError_t launch_merge_runs(const RunSet& rs, int nruns, int64_t rows, int64_t run_len, int k,
+                              int32_t* out_idx, float* out_scores, const PeerSync& sync,
+                              cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   if (nruns < 1 || nruns > kMergeMaxRuns) return cudaErrorInvalidValue;
   const size_t smem = sizeof(SelectSmem);
@@ -1141,7 +1236,21 @@ cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int6
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   merge_runs_kernel<<<dim3(unsigned(rows * kMergeParts)), kThreads, smem, stream>>>(
-      runs, nruns, rows, run_len, k, out_idx, out_scores);
+      rs, nruns, rows, run_len, k, out_idx, out_scores, sync);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int64_t run_len, int k,
+                              int32_t* out_idx, float* out_scores, cudaStream_t stream) {
+  if (nruns < 1 || nruns > kMergeMaxRuns) return cudaErrorInvalidValue;
+  RunSet rs{};
+  for (int r = 0; r < nruns; ++r) rs.run[r] = runs + int64_t(r) * 2 * rows * run_len;
+  return launch_merge_runs(rs, nruns, rows, run_len, k, out_idx, out_scores, PeerSync{}, stream);
+}
+
+cudaError_t launch_peer_publish(const PeerSync& sync, int world, cudaStream_t stream) {
+  if (world < 1 || world > kPeerMaxRanks || sync.self == nullptr) return cudaErrorInvalidValue;
+  peer_publish_kernel<<<1, 32, 0, stream>>>(sync, world);
   return cudaGetLastError();
 }
 

@@ -18,6 +18,12 @@ top-k is all-gathered asynchronously (NCCL on its own stream) while the next
 group is scored, so only the last group's exchange is exposed; the merges run at
 the end, one per group.
 
+With ``exchange`` (a :class:`~prism_test_b200.peer_exchange.PeerExchange`) steps 2
+and 3 go over peer-mapped memory instead: the local top-k is written into the
+rank's exchange buffer and each rank's merge kernel reads the other ranks' runs
+straight from their GPUs over NVLink, after a device-side ready flag per rank (no
+NCCL call, no gathered copy).
+
 Every rank ends with the global result, equal to ``torch.topk`` over the whole
 sequence (``ReAttentionMethod._dense_topk``, reattention.py:486-498), ties
 broken toward lower global indices.
@@ -73,6 +79,7 @@ def sharded_einsum_topk(
     v_shard: Optional[torch.Tensor] = None,
     recall_type: str = "qk",
     chunks: int = 1,
+    exchange=None,
 ):
     """Global exact top-k over a key sequence split across the ranks of ``group``.
 
@@ -83,7 +90,9 @@ def sharded_einsum_topk(
     CPU implementations to run the exchange over gloo. ``recall_type`` "qkv" /
     "qkv2" weights each key by the norm of its value row in ``v_shard`` (the
     same slice of the value cache), as ``einsum_topk_func`` does. ``chunks``
-    (dividing Hkv) pipelines the exchange over groups of KV heads.
+    (dividing Hkv) pipelines the exchange over groups of KV heads. ``exchange``
+    (a ``PeerExchange`` built for ``B * Hq * Sq`` rows and ``topk``) exchanges the
+    runs over peer-mapped memory instead of NCCL; ``chunks`` must then be 1.
     """
     local_topk = local_topk or einsum_topk_func
     world = dist.get_world_size(group)
@@ -92,6 +101,19 @@ def sharded_einsum_topk(
     if chunks < 1 or Hkv % chunks:
         raise ValueError(f"chunks={chunks} must divide the {Hkv} KV heads")
     hk, hq = Hkv // chunks, Hq // chunks
+    if exchange is not None:
+        if chunks != 1:
+            raise ValueError("the peer exchange takes the KV heads in one group (chunks=1)")
+        rows = B * Hq * Sq
+        if (exchange.rows, exchange.topk) != (rows, topk):
+            raise ValueError(f"exchange built for {exchange.rows} x {exchange.topk}, call needs {rows} x {topk}")
+        extra = {} if recall_type == "qk" else dict(values=v_shard, recall_type=recall_type)
+        _local_packed(local_topk, q, k_shard, topk, inv_freq, shard_start, extra, dest=exchange.run)
+        out_i = torch.empty((rows, topk), dtype=torch.int32, device=q.device)
+        out_s = torch.empty((rows, topk), dtype=torch.float32, device=q.device)
+        exchange.merge(out_i, out_s)
+        out_i, out_s = out_i.reshape(B, Hq, Sq, topk), out_s.reshape(B, Hq, Sq, topk)
+        return (out_i, out_s) if return_scores else out_i
     pending = []
     for c in range(chunks):
         qc = q[:, c * hq:(c + 1) * hq]
@@ -119,13 +141,14 @@ def sharded_einsum_topk(
     return out_i
 
 
-def _local_packed(local_topk, q, k_shard, topk, inv_freq, shard_start, extra) -> torch.Tensor:
+def _local_packed(local_topk, q, k_shard, topk, inv_freq, shard_start, extra, dest=None) -> torch.Tensor:
     """This rank's exact local top-k as an int32 [2, rows, topk] buffer (score bits,
-    global indices), sorted; a shard shorter than topk is padded with -inf."""
+    global indices), sorted; a shard shorter than topk is padded with -inf.
+    Written into ``dest`` when given."""
     B, Hq, Sq, _ = q.shape
     rows = B * Hq * Sq
     kl = min(topk, k_shard.shape[2])
-    packed = torch.empty((2, rows, topk), dtype=torch.int32, device=q.device)
+    packed = dest if dest is not None else torch.empty((2, rows, topk), dtype=torch.int32, device=q.device)
     if kl == topk and local_topk is einsum_topk_func:
         local_topk(q, k_shard, kl, inv_freq=inv_freq, pos_offset=shard_start, index_base=shard_start,
                    out=(packed[1], packed[0].view(torch.float32)), **extra)

@@ -155,3 +155,28 @@ def test_weighted_workspace_size(lib):
     got = lib.prism_einsum_topk_weighted_workspace_size(1, 4, 2, 5, 1001, 3, 0, _lib.RECALL_QKV)
     assert got == (odd + 255) // 256 * 256 + (2 * 1004 * 4 + 255) // 256 * 256
     assert lib.prism_einsum_topk_weighted_workspace_size(1, 4, 2, 5, 1001, 3, 0, 9) == 0
+
+
+def test_peer_exchange_validation(lib):
+    # argument checks of the peer exchange entry points run before any CUDA call
+    assert lib.prism_peer_buffer_bytes(32, 8192) == _lib.PEER_HEADER_BYTES + 32 * 8192 * 8
+    assert lib.prism_peer_buffer_bytes(0, 8) == 0
+    fake = (ctypes.c_void_p * 3)(1 << 20, 2 << 20, 3 << 20)  # never dereferenced
+    assert lib.prism_peer_publish(fake, 0, 0, None) == _lib.PRISM_E_UNSUPPORTED
+    assert lib.prism_peer_publish(fake, _lib.PEER_MAX_RANKS + 1, 0, None) == _lib.PRISM_E_UNSUPPORTED
+    assert lib.prism_peer_publish(fake, 3, 3, None) == _lib.PRISM_E_INVALID
+    assert lib.prism_peer_publish(None, 3, 0, None) == _lib.PRISM_E_INVALID
+    mis = (ctypes.c_void_p * 2)(1 << 20, (2 << 20) + 8)
+    assert lib.prism_peer_publish(mis, 2, 0, None) == _lib.PRISM_E_INVALID
+    nul = (ctypes.c_void_p * 2)(1 << 20, None)
+    assert lib.prism_peer_publish(nul, 2, 0, None) == _lib.PRISM_E_INVALID
+    out = 4 << 20
+    assert lib.prism_peer_merge(fake, 3, 0, 4, 16, 1, 0, None, None, None) == _lib.PRISM_E_INVALID
+    assert lib.prism_peer_merge(fake, 3, 0, 0, 16, 1, 0, out, None, None) == _lib.PRISM_E_INVALID
+    assert lib.prism_peer_merge(fake, 3, 0, 4, 16385, 1, 0, out, None, None) == _lib.PRISM_E_UNSUPPORTED
+    h = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+    assert lib.prism_peer_alloc(1 << 20, None, h) == _lib.PRISM_E_INVALID
+    assert lib.prism_peer_alloc(100, ctypes.byref(ctypes.c_void_p()), h) == _lib.PRISM_E_INVALID
+    assert lib.prism_peer_open(None, ctypes.byref(ctypes.c_void_p())) == _lib.PRISM_E_INVALID
+    assert lib.prism_peer_close(None) == _lib.PRISM_E_INVALID
+    assert lib.prism_peer_free(None) == _lib.PRISM_E_INVALID
