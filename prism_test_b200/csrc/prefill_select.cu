@@ -7,8 +7,8 @@
 // masked keys (-inf) in ascending index order, as the score-matrix path does.
 //
 // prefill_select_kernel, one 256-thread CTA per row: the row's n candidates
-// (packed (order-preserving score key << 32) | ~index, so larger = earlier) are
-// loaded into shared memory and counting-sorted into 2048 fine bins, linear in
+// (packed (fp32 score bits << 32) | ~index) are loaded into shared memory as
+// order-preserving score keys and counting-sorted into 2048 fine bins, linear in
 // the score between the row's largest and smallest candidate (NaN, which ranks
 // first, in bin 0; linear in the value, not in the packed key, whose spacing
 // explodes around zero); a candidate's output position is its bin's start plus
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
   auto cand_at = [&](uint32_t i) { return i < n0 ? src[i] : src[a.cap - 1 - (i - n0)]; };
   uint32_t kmx = 0u, kmn = 0xffffffffu;
   for (uint32_t i = tid; i < n; i += kPsThreads) {
-    const uint32_t key = uint32_t(cand_at(i) >> 32);
+    const uint32_t key = float_to_okey(__uint_as_float(uint32_t(cand_at(i) >> 32)));
     keys[i] = key;
     if (key != 0xffffffffu) {  // NaN is binned apart
       kmx = max(kmx, key);
@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
     if (ties > 1) {  // equal scores: the lower index goes first
       for (uint32_t j = s; j < e; ++j) {
         const uint32_t pj = perm[j];
-        if (pj != i && keys[pj] == kx) p += cand_at(pj) > x;
+        if (pj != i && keys[pj] == kx) p += uint32_t(cand_at(pj)) > uint32_t(x);  // lower index
       }
     }
     if (p < keff) {

@@ -31,13 +31,15 @@
 //            rank m = 1.1 e + 4 sqrt(e) + 8, e = k * samples / keys visible
 //            (-inf when the row sees at most k keys);
 //   kCand    appends every visible key with score >= T, packed as
-//            (order-preserving score key << 32 | ~index), to the row's candidate
-//            list [rows, cap] and stores the row's count (which may exceed cap:
-//            the selection then recomputes that row exactly). Per 16 scores a
-//            thread builds the bit mask of hits (a compare and an OR each), parks
-//            the 16 values in its own row of shared memory, and walks the set bits
-//            reading the hits back by index — registers cannot be indexed, and
-//            about 3 % of the scores are hits.
+//            (fp32 score bits << 32 | ~index), to the row's candidate list
+//            [rows, cap] and stores the row's count (which may exceed cap: the
+//            selection then recomputes that row exactly). Per 32 scores a thread
+//            builds the bit mask of hits (a subtraction and a funnel shift each),
+//            parks the 32 values in shared memory (transposed: 16-byte chunk q of
+//            thread t at (q * threads + t) * 16, so a warp's stores are
+//            conflict-free), and walks the set bits reading the hits back by
+//            index — registers cannot be indexed, and about 3 % of the scores
+//            are hits.
 //
 // Every mbarrier wait is bounded (2 s): on expiry the kernel records
 // kStatusTimeout, the roles leave their loops, and the TMEM is still freed.
@@ -59,8 +61,6 @@ constexpr int kHistBins = 128;
 constexpr int kHistStride = 130;                 // u16 per row: 65 words, rows in distinct banks
 constexpr uint32_t kTmemCols = 512;
 
-constexpr int kStageStride = 20;  // floats per thread in the kCand staging rows (16 used;
-                                   // 20 keeps a warp's 16-byte stores bank-conflict free)
 
 template <int kMode>
 struct PfCfg {
@@ -73,7 +73,7 @@ struct PfCfg {
   static constexpr uint32_t kHistOff = kBOff + kStages * kTileBytes;
   static constexpr uint32_t kHistBytes =
       kMode == kSample ? 256 * kHistStride * 2
-                       : (kMode == kCand ? kEpiWarps * 32 * kStageStride * 4 : 0);
+                       : (kMode == kCand ? kEpiWarps * 32 * 32 * 4 : 0);  // 32 values per thread
   static constexpr uint32_t kBarOff = kHistOff + kHistBytes;
   static constexpr uint32_t kSmem = kBarOff + 256 + 1024;  // + alignment slack
 };
@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
     uint64_t* cl = nullptr;
     float* stage = nullptr;
     if (kMode == kCand) {
-      stage = reinterpret_cast<float*>(smem + Cfg::kHistOff) + (ew * 32 + lane) * kStageStride;
+      stage = reinterpret_cast<float*>(smem + Cfg::kHistOff) + (ew * 32 + lane) * 4;
       if (rvalid) {
         thr = a.thr[srow];
         cl = a.cand + srow * a.cap;
@@ -353,58 +353,41 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
             }
         }
       } else {  // kCand
+        // half 0 fills the row's list from the front, half 1 from the back; a
+        // chunk whose hits would pass the capacity writes none of them (the count
+        // still grows, and the row is then recomputed exactly)
+        constexpr int kQStride = Cfg::kEpiWarps * 32 * 4;  // floats between staged chunks
         const uint32_t cap = uint32_t(a.cap);
-        // half 0 fills the row's list from the front, half 1 from the back
-        // branch-free append: past the capacity the last slot is overwritten (the
-        // row is then recomputed exactly, its list unused)
-        uint64_t* const lbase = half ? cl + (cap - 1u) : cl;
-        const int64_t lstep = half ? -1 : 1;
-        auto emit = [&](float x, uint32_t j) {
-          const uint32_t slot = cnt < cap - 1u ? cnt : cap - 1u;
-          lbase[lstep * int64_t(slot)] = (uint64_t(float_to_okey(x)) << 32) | uint64_t(~j);
-          ++cnt;
-        };
         const bool all_vis = j0 + kCols <= nvis;
 #pragma unroll
         for (int c = 0; c < Cfg::kChunks; ++c) {
+          // bit i of m = sign of (x_i - T), i.e. x_i < T, the values going in from
+          // the last. x - T is never -0, and a NaN x gives the canonical NaN (sign
+          // 0), so NaN is a hit: it ranks first.
+          uint32_t m = 0;
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int o = 16 * hh;  // these 16 values: v[c][o .. o + 15]
-            // bit i of m = sign of (x_i - T), i.e. x_i < T: the values go in from the
-            // last, two subtractions per packed instruction. x - T is never -0, and a
-            // NaN x gives the canonical NaN (sign 0), so NaN is a hit: it ranks first.
-            uint32_t m = 0;
+          for (int i = 31; i >= 0; --i) m = push_sign(m, __uint_as_float(v[c][i]) - thr);
+          m = ~m;  // hits
+          if (!all_vis) {
+            const int64_t lim = nvis - (j0 + 32 * c);
+            m &= lim >= 32 ? 0xffffffffu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
+          }
 #pragma unroll
-            for (int i = 14; i >= 0; i -= 2) {
-              const float2 d = __fadd2_rn(
-                  make_float2(__uint_as_float(v[c][o + i]), __uint_as_float(v[c][o + i + 1])),
-                  make_float2(-thr, -thr));
-              m = push_sign(push_sign(m, d.y), d.x);
-            }
-            m = ~m & 0xffffu;  // hits
-            if (!all_vis) {
-              const int64_t lim = nvis - (j0 + 32 * c + o);
-              m &= lim >= 16 ? 0xffffu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
-            }
-            if (m == 0) continue;
-#pragma unroll
-            for (int i = 0; i < 16; i += 4)
-              *reinterpret_cast<uint4*>(stage + i) =
-                  make_uint4(v[c][o + i], v[c][o + i + 1], v[c][o + i + 2], v[c][o + i + 3]);
-            const uint32_t jb = uint32_t(j0 + 32 * c + o);
-            // the first two hits without a loop (their shared loads overlap), then the rest
-            const int i1 = __ffs(m) - 1;
-            const uint32_t m2 = m & (m - 1);
-            const int i2 = m2 ? __ffs(m2) - 1 : i1;
-            const float x1 = stage[i1], x2 = stage[i2];
-            emit(x1, jb + uint32_t(i1));
-            if (m2) emit(x2, jb + uint32_t(i2));
-            uint32_t m3 = m2 & (m2 - 1);
-            while (m3) {
-              const int i = __ffs(m3) - 1;
-              m3 &= m3 - 1;
-              emit(stage[i], jb + uint32_t(i));
-            }
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<uint4*>(stage + q * kQStride) =
+                make_uint4(v[c][4 * q], v[c][4 * q + 1], v[c][4 * q + 2], v[c][4 * q + 3]);
+          const uint32_t nh = __popc(m);
+          uint32_t mm = cnt + nh <= cap ? m : 0u;
+          int32_t off = half ? int32_t(cap - 1u - cnt) : int32_t(cnt);
+          const int32_t dir = half ? -1 : 1;
+          cnt += nh;
+          const uint32_t jb = ~uint32_t(j0 + 32 * c);  // ~(jb + i) = jb - i
+          while (mm) {
+            const int i = __ffs(mm) - 1;
+            mm &= mm - 1;
+            const uint32_t xb = __float_as_uint(stage[(i >> 2) * kQStride + (i & 3)]);
+            cl[off] = (uint64_t(xb) << 32) | uint64_t(jb - uint32_t(i));
+            off += dir;
           }
         }
       }
