@@ -364,9 +364,15 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
           // bit i of m = sign of (x_i - T), i.e. x_i < T, the values going in from
           // the last. x - T is never -0, and a NaN x gives the canonical NaN (sign
           // 0), so NaN is a hit: it ranks first.
-          uint32_t m = 0;
+          // Four independent chains of eight (one byte each), so the funnel shifts
+          // do not wait on one another.
+          uint32_t mb[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-          for (int i = 31; i >= 0; --i) m = push_sign(m, __uint_as_float(v[c][i]) - thr);
+          for (int i = 7; i >= 0; --i)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) mb[q] = push_sign(mb[q], __uint_as_float(v[c][8 * q + i]) - thr);
+          uint32_t m = __byte_perm(__byte_perm(mb[0], mb[1], 0x0040), __byte_perm(mb[2], mb[3], 0x0040),
+                                   0x5410);
           m = ~m;  // hits
           if (!all_vis) {
             const int64_t lim = nvis - (j0 + 32 * c);
