@@ -20,6 +20,8 @@
 // resolved in column order.
 #include <cooperative_groups.h>
 
+#include <cstddef>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -977,6 +979,10 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_row_kernel(const Sele
 constexpr int kMergeMaxRuns = kMergeRunsMax;
 constexpr int kMergeSumm = 128;
 constexpr int kMergeParts = 4;  // CTAs per row of the run merge
+// the merge keeps kCap 4-byte score keys in hist and perm, which lie back to back
+static_assert(offsetof(SelectSmem, perm) == offsetof(SelectSmem, hist) + sizeof(uint32_t) * kFineBins &&
+                  sizeof(uint32_t) * kFineBins + sizeof(uint16_t) * kCap >= sizeof(uint32_t) * kCap,
+              "score-key staging does not fit hist + perm");
 
 __device__ __forceinline__ uint64_t run_cand(const int32_t* const* runs, int r, int64_t rows,
                                              int64_t row, int64_t run_len, int64_t j) {
@@ -1119,24 +1125,60 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
         sm.buf[e] = src[e];
     }
     cluster.sync();  // every CTA holds all entries; nobody reads a peer's copy any more
+    // the score keys alone, for the binary searches (4-byte probes; the index
+    // word is read only when two score keys are equal)
+    uint32_t* sk = reinterpret_cast<uint32_t*>(sm.hist);  // hist and perm: kCap words
+    for (uint32_t e = tid; e < total; e += kThreads) sk[e] = uint32_t(sm.buf[e] >> 32);
+    __syncthreads();
   }
   // rank every prefix candidate: its position in its run plus, in every other run,
   // the entries ahead of it (ties: lower run first)
   int32_t* oi = out_idx + row * k;
   float* os = out_scores ? out_scores + row * k : nullptr;
+  if (staged) {
+    const uint32_t* sk = reinterpret_cast<const uint32_t*>(sm.hist);
+    for (uint32_t e = part * kThreads + tid; e < total; e += kMergeParts * kThreads) {
+      int r = 0;
+      while (e >= sm.roff[r + 1]) ++r;
+      const uint32_t j = e - sm.roff[r];
+      const uint32_t xs = sk[e], xi = uint32_t(sm.buf[e]);
+      uint32_t p = j;
+      for (int q = 0; q < nruns; ++q) {
+        if (q == r) continue;
+        const uint32_t o = sm.roff[q];
+        uint32_t lo = 0, hi = sm.rlen[q];
+        while (lo < hi) {
+          const uint32_t mid = (lo + hi) >> 1;
+          const uint32_t vs = sk[o + mid];
+          bool ahead = vs > xs;
+          if (vs == xs) {
+            const uint32_t vi = uint32_t(sm.buf[o + mid]);
+            ahead = vi > xi || (q < r && vi == xi);
+          }
+          if (ahead) lo = mid + 1;
+          else hi = mid;
+        }
+        p += lo;
+      }
+      if (p < uint32_t(k)) {
+        oi[p] = int32_t(~xi);
+        if (os) os[p] = okey_to_float(xs);
+      }
+    }
+    return;
+  }
   for (uint32_t e = part * kThreads + tid; e < total; e += kMergeParts * kThreads) {
     int r = 0;
     while (e >= sm.roff[r + 1]) ++r;
     const uint32_t j = e - sm.roff[r];
-    const uint64_t x = staged ? sm.buf[e] : cand_at(r, j);
+    const uint64_t x = cand_at(r, j);
     uint32_t p = j;
     for (int q = 0; q < nruns; ++q) {
       if (q == r) continue;
-      const uint64_t* bq = sm.buf + sm.roff[q];
       uint32_t lo = 0, hi = sm.rlen[q];
       while (lo < hi) {
         const uint32_t mid = (lo + hi) >> 1;
-        const uint64_t v = staged ? bq[mid] : cand_at(q, mid);
+        const uint64_t v = cand_at(q, mid);
         if (v > x || (q < r && v == x)) lo = mid + 1;
         else hi = mid;
       }
