@@ -8,10 +8,10 @@
 //
 // prefill_select_kernel, one 256-thread CTA per row: the row's n candidates
 // (packed (fp32 score bits << 32) | ~index) are loaded into shared memory as
-// order-preserving score keys and counting-sorted into 2048 fine bins, linear in
-// the score between the row's largest and smallest candidate (NaN, which ranks
-// first, in bin 0; linear in the value, not in the packed key, whose spacing
-// explodes around zero); a candidate's output position is its bin's start plus
+// order-preserving score keys and counting-sorted into 2048 fine bins between the
+// row's largest and smallest candidate, logarithmic in the distance above the
+// smallest (NaN, which ranks first, in bin 0; computed from the value, not from
+// the packed key, whose spacing explodes around zero); a candidate's output position is its bin's start plus
 // the number of bin members above it. Rows whose candidate count lies
 // outside [min(k, visible keys), cap] (a threshold too high or too low for the
 // row), or whose fine bins hold more than kRankMax members (massive ties), are
@@ -144,12 +144,27 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
   }
   __syncthreads();
   const float fmax = okey_to_float(s_kmax), fmin = okey_to_float(s_kmin);
-  const float scale = fmax > fmin ? float(kPsBins - 1) / (fmax - fmin) : 0.f;
-  // bin of a score key: monotone non-increasing in the score
+  // Bins logarithmic in the distance above the smallest candidate: a candidate x
+  // goes to bin 2047 - floor((bits(y) - bits(c)) * 2047 / (bits(range + c) - bits(c))),
+  // y = (x - fmin) + c, c = range / 64. The bit pattern of a positive float grows
+  // with its value and about linearly in its log, so the bins are narrow just above
+  // the threshold, where the candidates crowd (a score tail thins out roughly
+  // exponentially), and wide near the top; every step is a rounded subtraction or
+  // addition of a constant, so the bin never increases with the score.
+  const float range = fmax - fmin;
+  const float c0 = range * (1.0f / 64.0f);
+  const uint32_t b0 = __float_as_uint(c0);
+  const uint32_t btop = __float_as_uint(range + c0);
+  uint32_t mult = 0u;  // 0: one bin (equal or non-finite candidates: the massive-tie path)
+  if (range > 0.f && range <= 3.0e38f && btop > b0) {
+    const double m = double(kPsBins - 1) * 4294967296.0 / double(btop - b0);
+    mult = m >= 4294967295.0 ? 0xffffffffu : uint32_t(m);
+  }
+  // bin of a score key: monotone non-increasing in the score, NaN in bin 0
   auto bin_of = [&](uint32_t key) -> uint32_t {
     if (key == 0xffffffffu) return 0u;
-    const float b = (fmax - okey_to_float(key)) * scale;
-    return b >= float(kPsBins - 1) ? uint32_t(kPsBins - 1) : (b > 0.f ? uint32_t(b) : 0u);
+    const float y = (okey_to_float(key) - fmin) + c0;
+    return uint32_t(kPsBins - 1) - __umulhi(__float_as_uint(y) - b0, mult);
   };
   for (uint32_t i = tid; i < n; i += kPsThreads) atomicAdd(&hist[bin_of(keys[i])], 1u);
   __syncthreads();
