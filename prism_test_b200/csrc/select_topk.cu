@@ -979,6 +979,11 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_row_kernel(const Sele
 constexpr int kMergeMaxRuns = kMergeRunsMax;
 constexpr int kMergeSumm = 128;
 constexpr int kMergeParts = 4;  // CTAs per row of the run merge
+constexpr uint32_t kTreeCap = 12288;  // entries per merge-tree ping-pong buffer (2 x 96 KB)
+// the merge tree's two buffers of kTreeCap entries span buf, hist and perm (back to back)
+static_assert(offsetof(SelectSmem, buf) == 0 && offsetof(SelectSmem, hist) == sizeof(uint64_t) * kCap &&
+                  offsetof(SelectSmem, perm) + sizeof(uint16_t) * kCap >= 2 * sizeof(uint64_t) * kTreeCap,
+              "merge tree buffers do not fit buf + hist + perm");
 // the merge keeps kCap 4-byte score keys in hist and perm, which lie back to back
 static_assert(offsetof(SelectSmem, perm) == offsetof(SelectSmem, hist) + sizeof(uint32_t) * kFineBins &&
                   sizeof(uint32_t) * kFineBins + sizeof(uint16_t) * kCap >= sizeof(uint32_t) * kCap,
@@ -1008,6 +1013,87 @@ __device__ bool wait_flag_eq(const uint64_t* p, uint64_t want, int64_t timeout_n
     __nanosleep(64);
   }
   return true;
+}
+
+// ---- merge-path tree over the staged prefixes ----------------------------------
+// The staged prefixes of the runs lie back to back (run r at roff[r]); every
+// level merges adjacent lists pairwise into the other buffer at the same
+// offsets (list m of level l + 1 = runs [m 2^(l+1), (m+1) 2^(l+1))). A thread
+// takes an even share of a level's output positions, finds where its first
+// position splits the two inputs (the co-rank: a binary search along the merge
+// path) and merges sequentially from there. Equal keys: the lower run first,
+// i.e. the first input of a pair. The last level writes only the output
+// positions below k of this CTA's share straight to the result.
+// Merged positions [d0, d1) of X[0, a) and Y[0, b) (both descending): emit(d, key).
+template <typename Emit>
+__device__ __forceinline__ void merge_path_range(const uint64_t* X, uint32_t a, const uint64_t* Y, uint32_t b,
+                                                 uint32_t d0, uint32_t d1, Emit&& emit) {
+  uint32_t lo = d0 > b ? d0 - b : 0u, hi = d0 < a ? d0 : a;
+  while (lo < hi) {  // the number of X entries among the first d0 outputs
+    const uint32_t mid = (lo + hi) >> 1;
+    if (X[mid] >= Y[d0 - mid - 1]) lo = mid + 1;
+    else hi = mid;
+  }
+  uint32_t i = lo, j = d0 - lo;
+  uint64_t xv = i < a ? X[i] : 0ull, yv = j < b ? Y[j] : 0ull;
+  for (uint32_t d = d0; d < d1; ++d) {
+    const bool take_x = j >= b || (i < a && xv >= yv);
+    emit(d, take_x ? xv : yv);
+    if (take_x) {
+      ++i;
+      xv = i < a ? X[i] : 0ull;
+    } else {
+      ++j;
+      yv = j < b ? Y[j] : 0ull;
+    }
+  }
+}
+
+// Runs the levels on the staged prefixes (in buffer A = smem entries [0, kTreeCap))
+// and writes result positions [p0, p1) of the row.
+__device__ void merge_tree(uint64_t* bufs, const uint32_t* roff, int nruns, uint32_t total, uint32_t p0,
+                           uint32_t p1, int32_t* oi, float* os) {
+  const int tid = threadIdx.x;
+  int levels = 0;
+  while ((1 << levels) < nruns) ++levels;
+  uint64_t* src = bufs;
+  uint64_t* dst = bufs + kTreeCap;
+  auto to_result = [&](uint32_t d, uint64_t x) {
+    oi[d] = int32_t(~uint32_t(x));
+    if (os) os[d] = okey_to_float(uint32_t(x >> 32));
+  };
+  if (levels == 0) {
+    for (uint32_t d = p0 + tid; d < p1; d += kThreads) to_result(d, src[d]);
+    return;
+  }
+  for (int l = 0; l < levels; ++l) {
+    const bool last = l == levels - 1;
+    const uint32_t s0 = last ? p0 : 0u, s1 = last ? p1 : total;  // positions of this level to make
+    const uint32_t per = (s1 - s0 + kThreads - 1) / kThreads;
+    uint32_t pos = s0 + min(s1 - s0, per * uint32_t(tid));
+    const uint32_t end = min(s1, pos + per);
+    while (pos < end) {
+      int m = 0;  // the pair (list of level l + 1) holding position pos
+      while (((m + 1) << (l + 1)) < nruns && roff[(m + 1) << (l + 1)] <= pos) ++m;
+      const int x0 = m << (l + 1);
+      const int x1 = min(x0 + (1 << l), nruns), y1 = min(x0 + (2 << l), nruns);
+      const uint32_t po = roff[x0], a = roff[x1] - po, b = roff[y1] - roff[x1];
+      const uint32_t seg = min(end, po + a + b);
+      if (last) {
+        merge_path_range(src + po, a, src + po + a, b, pos - po, seg - po,
+                         [&](uint32_t d, uint64_t x) { to_result(po + d, x); });
+      } else {
+        uint64_t* out = dst + po;
+        merge_path_range(src + po, a, src + po + a, b, pos - po, seg - po,
+                         [&](uint32_t d, uint64_t x) { out[d] = x; });
+      }
+      pos = seg;
+    }
+    __syncthreads();
+    uint64_t* t = src;
+    src = dst;
+    dst = t;
+  }
 }
 
 __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, int64_t run_len, int k,
@@ -1125,6 +1211,14 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
         sm.buf[e] = src[e];
     }
     cluster.sync();  // every CTA holds all entries; nobody reads a peer's copy any more
+    if (total <= kTreeCap) {
+      // this CTA makes a quarter of the k result positions (the last level)
+      const uint32_t kk = min(uint32_t(k), total);
+      merge_tree(reinterpret_cast<uint64_t*>(&sm), sm.roff, nruns, total,
+                 uint32_t(uint64_t(kk) * part / kMergeParts), uint32_t(uint64_t(kk) * (part + 1) / kMergeParts),
+                 out_idx + row * k, out_scores ? out_scores + row * k : nullptr);
+      return;
+    }
     // the score keys alone, for the binary searches (4-byte probes; the index
     // word is read only when two score keys are equal)
     uint32_t* sk = reinterpret_cast<uint32_t*>(sm.hist);  // hist and perm: kCap words
