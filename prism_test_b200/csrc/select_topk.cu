@@ -1400,20 +1400,32 @@ cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t 
     select_topk_general_kernel<<<dim3(unsigned(a.rows)), kThreads, smem, stream>>>(a);
     return cudaGetLastError();
   }
+  // A dependent launch (programmatic stream serialization): the kernel may be
+  // scheduled while the scorer before it drains; it reads nothing the scorer
+  // writes before its griddepcontrol.wait. Not with rows_dyn, which a kernel
+  // before it writes and which is read first.
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = at;
+  cfg.numAttrs = a.rows_dyn == nullptr ? 1 : 0;
   if (a.rows >= kRowKernelMinRows) {
     cudaError_t e = cudaFuncSetAttribute(select_topk_row_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    select_topk_row_kernel<<<dim3(unsigned(a.rows)), kThreads, smem, stream>>>(a);
-    return cudaGetLastError();
+    cfg.gridDim = dim3(unsigned(a.rows));
+    return cudaLaunchKernelEx(&cfg, select_topk_row_kernel, a);
   }
   const bool resident = a.n <= kPass;
   auto kern = resident ? select_topk_cluster_kernel<true> : select_topk_cluster_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  kern<<<dim3(unsigned(a.rows * kCluster)), kThreads, smem, stream>>>(
-      a, static_cast<uint64_t*>(cand_ws), select_cand_cap(a.n));
-  return cudaGetLastError();
+  cfg.gridDim = dim3(unsigned(a.rows * kCluster));
+  return cudaLaunchKernelEx(&cfg, kern, a, static_cast<uint64_t*>(cand_ws), select_cand_cap(a.n));
 }
 
 }  // namespace prism
