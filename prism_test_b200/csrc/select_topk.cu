@@ -521,6 +521,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   __syncthreads();
   cluster_arrive();  // every CTA has started and initialised its shared memory
   grid_dependency_wait();
+  asm volatile("griddepcontrol.launch_dependents;");  // e.g. the publish of the peer exchange
   uint32_t kv[kKeys];
   if (kResident) load_keys(sc, my_base, a.n, kv);
 
@@ -860,6 +861,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_row_kernel(const Sele
   }
   __syncthreads();
   grid_dependency_wait();
+  asm volatile("griddepcontrol.launch_dependents;");
 
   // ---- sample: 8 consecutive columns of every 128, at a hashed offset ----------------
   const int64_t ngroups = (a.n + 127) / 128;
@@ -1306,6 +1308,7 @@ __global__ void __cluster_dims__(kMergeParts, 1, 1) __launch_bounds__(kThreads, 
   const int tid = threadIdx.x;
   __shared__ const int32_t* s_runs[kMergeMaxRuns];  // the run pointers, indexed by run
   if (tid < nruns) s_runs[tid] = rs.run[tid];
+  grid_dependency_wait();  // a dependent launch after the publish (peer exchange)
   PeerHeader* self = sync.self;
   uint64_t step = 0;
   if (self != nullptr) {
@@ -1337,6 +1340,10 @@ __global__ void __cluster_dims__(kMergeParts, 1, 1) __launch_bounds__(kThreads, 
 // Publish side of the peer exchange: advances this rank's step and marks its run
 // of that step ready in every rank's header (including its own). One warp.
 __global__ void peer_publish_kernel(const PeerSync sync, int world) {
+  // a dependent launch: the merge may be scheduled now; the local top-k before
+  // this kernel is complete and visible after the wait
+  asm volatile("griddepcontrol.launch_dependents;");
+  grid_dependency_wait();
   const uint64_t s = sync.self->step + 1;
   __syncwarp();
   if (threadIdx.x == 0) sync.self->step = s;
@@ -1371,9 +1378,19 @@ cudaError_t launch_merge_runs(const RunSet& rs, int nruns, int64_t rows, int64_t
   cudaError_t e = cudaFuncSetAttribute(merge_runs_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  merge_runs_kernel<<<dim3(unsigned(rows * kMergeParts)), kThreads, smem, stream>>>(
-      rs, nruns, rows, run_len, k, out_idx, out_scores, sync);
-  return cudaGetLastError();
+  // the peer merge follows the publish as a dependent launch (it reads the step
+  // the publish wrote only after its griddepcontrol.wait)
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(unsigned(rows * kMergeParts));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = at;
+  cfg.numAttrs = sync.self != nullptr ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, merge_runs_kernel, rs, nruns, rows, run_len, k, out_idx, out_scores, sync);
 }
 
 cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int64_t run_len, int k,
@@ -1386,8 +1403,17 @@ cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int6
 
 cudaError_t launch_peer_publish(const PeerSync& sync, int world, cudaStream_t stream) {
   if (world < 1 || world > kPeerMaxRanks || sync.self == nullptr) return cudaErrorInvalidValue;
-  peer_publish_kernel<<<1, 32, 0, stream>>>(sync, world);
-  return cudaGetLastError();
+  // a dependent launch after the local top-k
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = stream;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, peer_publish_kernel, sync, world);
 }
 
 cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t stream) {
