@@ -26,6 +26,31 @@ def _cpu_local(q, k, kl, inv_freq=None, pos_offset=0, index_base=0, return_score
     return idx.to(torch.int32), vals
 
 
+class _HostExchange:
+    """Stand-in for PeerExchange on the CPU (the same interface: the local top-k is
+    written into ``run``, then ``merge`` fills the outputs), exchanging the runs
+    with a gloo all-gather and merging with the host merge; the peer-mapped GPU
+    buffers themselves are tested in tests/test_peer_exchange_gpu.py."""
+
+    def __init__(self, rows, topk):
+        self.rows, self.topk = rows, topk
+        self.run = torch.zeros((2, rows, topk), dtype=torch.int32)
+        self.merges = 0
+
+    def merge(self, out_idx, out_scores):
+        from prism_test_b200.sharded import merge_candidates_torch
+        world = dist.get_world_size()
+        runs = [torch.empty_like(self.run) for _ in range(world)]
+        dist.all_gather(runs, self.run)
+        g = torch.stack(runs)  # [world, 2, rows, topk]
+        cand_s = g[:, 0].permute(1, 0, 2).reshape(self.rows, -1).contiguous().view(torch.float32)
+        cand_i = g[:, 1].permute(1, 0, 2).reshape(self.rows, -1).contiguous()
+        i, s = merge_candidates_torch(cand_s, cand_i, self.topk)
+        out_idx.copy_(i)
+        out_scores.copy_(s)
+        self.merges += 1
+
+
 def _put_and_exit(q, item):
     q.put(item)
     q.close()
@@ -47,11 +72,24 @@ def _worker(rank, world, port, case, q, k_full, inv, topk, errq, v_full=None):
         rt = "qkv2" if case == "qkv2" else "qk"
         chunks = 2 if case == "chunks2" else 1
         v_shard = v_full[:, :, start:stop] if v_full is not None else None
+        exchange = None
+        if case == "exchange":
+            rows = q.shape[0] * q.shape[1] * q.shape[2]
+            exchange = _HostExchange(rows, topk)
+            for bad in (dict(chunks=2), dict(topk=topk - 1)):  # rejected before any exchange
+                try:
+                    sharded_einsum_topk(q, k_full[:, :, start:stop], bad.get("topk", topk), shard_start=start,
+                                        inv_freq=inv, local_topk=_cpu_local, exchange=exchange,
+                                        chunks=bad.get("chunks", 1))
+                except ValueError:
+                    pass
+                else:
+                    raise AssertionError(f"{bad} was not rejected")
         try:
             idx, sc = sharded_einsum_topk(q, k_full[:, :, start:stop], topk, shard_start=start,
                                           inv_freq=inv, return_scores=True, local_topk=_cpu_local,
                                           merge=merge_candidates_torch, v_shard=v_shard, recall_type=rt,
-                                          chunks=chunks)
+                                          chunks=chunks, exchange=exchange)
         except Exception as e:  # noqa: BLE001
             if case == "die":
                 _put_and_exit(errq, ("ok-error", rank, type(e).__name__))
@@ -113,6 +151,15 @@ def test_sharded_value_weighted_matches_oracle():
 def test_sharded_chunked_exchange_matches_oracle():
     # two groups of KV heads, each exchanged on its own (asynchronous) all-gather
     res = _run(2, "chunks2", 1000, 50, seed=6)
+    assert sorted(r[1] for r in res) == [0, 1], res
+    for status, rank, msg in res:
+        assert status == "ok", msg
+
+
+def test_sharded_exchange_path_matches_oracle():
+    # the exchange= path of sharded_einsum_topk (local top-k written into the
+    # exchange's run, one merge call), with a host stand-in for the peer buffers
+    res = _run(2, "exchange", 1000, 50, seed=8)
     assert sorted(r[1] for r in res) == [0, 1], res
     for status, rank, msg in res:
         assert status == "ok", msg
