@@ -188,4 +188,24 @@ __device__ __forceinline__ float to_f32<__half>(__half v) {
   return __half2float(v);
 }
 
+// Launches kern<<<grid, block, smem, stream>>>(args...), as a programmatic
+// dependent launch when pdl: the kernel may be scheduled while the previous
+// kernel in the stream drains, and must read that kernel's output only after
+// its griddepcontrol.wait.
+template <typename... P, typename... A>
+cudaError_t launch_maybe_dependent(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, bool pdl,
+                                   cudaStream_t stream, A... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 }  // namespace prism

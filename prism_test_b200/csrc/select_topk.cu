@@ -1380,17 +1380,9 @@ cudaError_t launch_merge_runs(const RunSet& rs, int nruns, int64_t rows, int64_t
   if (e != cudaSuccess) return e;
   // the peer merge follows the publish as a dependent launch (it reads the step
   // the publish wrote only after its griddepcontrol.wait)
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3(unsigned(rows * kMergeParts));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cfg.attrs = at;
-  cfg.numAttrs = sync.self != nullptr ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, merge_runs_kernel, rs, nruns, rows, run_len, k, out_idx, out_scores, sync);
+  return launch_maybe_dependent(merge_runs_kernel, dim3(unsigned(rows * kMergeParts)), dim3(kThreads), smem,
+                                sync.self != nullptr, stream, rs, nruns, rows, run_len, k, out_idx,
+                                out_scores, sync);
 }
 
 cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int64_t run_len, int k,
@@ -1404,16 +1396,7 @@ cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int6
 cudaError_t launch_peer_publish(const PeerSync& sync, int world, cudaStream_t stream) {
   if (world < 1 || world > kPeerMaxRanks || sync.self == nullptr) return cudaErrorInvalidValue;
   // a dependent launch after the local top-k
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3(1);
-  cfg.blockDim = dim3(32);
-  cfg.stream = stream;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, peer_publish_kernel, sync, world);
+  return launch_maybe_dependent(peer_publish_kernel, dim3(1), dim3(32), 0, true, stream, sync, world);
 }
 
 cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t stream) {
@@ -1430,28 +1413,20 @@ cudaError_t launch_select_topk(const SelectArgs& a, void* cand_ws, cudaStream_t 
   // scheduled while the scorer before it drains; it reads nothing the scorer
   // writes before its griddepcontrol.wait. Not with rows_dyn, which a kernel
   // before it writes and which is read first.
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cfg.attrs = at;
-  cfg.numAttrs = a.rows_dyn == nullptr ? 1 : 0;
+  const bool pdl = a.rows_dyn == nullptr;
   if (a.rows >= kRowKernelMinRows) {
     cudaError_t e = cudaFuncSetAttribute(select_topk_row_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    cfg.gridDim = dim3(unsigned(a.rows));
-    return cudaLaunchKernelEx(&cfg, select_topk_row_kernel, a);
+    return launch_maybe_dependent(select_topk_row_kernel, dim3(unsigned(a.rows)), dim3(kThreads), smem, pdl,
+                                  stream, a);
   }
   const bool resident = a.n <= kPass;
   auto kern = resident ? select_topk_cluster_kernel<true> : select_topk_cluster_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  cfg.gridDim = dim3(unsigned(a.rows * kCluster));
-  return cudaLaunchKernelEx(&cfg, kern, a, static_cast<uint64_t*>(cand_ws), select_cand_cap(a.n));
+  return launch_maybe_dependent(kern, dim3(unsigned(a.rows * kCluster)), dim3(kThreads), smem, pdl, stream, a,
+                                static_cast<uint64_t*>(cand_ws), select_cand_cap(a.n));
 }
 
 }  // namespace prism

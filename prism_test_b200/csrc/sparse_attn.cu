@@ -432,25 +432,6 @@ int sa_splits(const SparseAttnArgs& a, int num_sms) {
   return int(s < 1 ? 1 : s);
 }
 
-// A launch that may begin while the previous kernel in the stream is finishing
-// (programmatic dependent launch); the kernel's griddepcontrol.wait orders its
-// reads of that kernel's output.
-template <typename... P, typename... A>
-cudaError_t launch_dependent(void (*kern)(P...), dim3 grid, dim3 block, bool pdl,
-                             cudaStream_t stream, A... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, args...);
-}
-
 // The partial kernel follows the angle table with a dependent launch when there
 // is one (it reads only the caller's inputs before its wait); without RoPE it
 // follows the caller's own work and launches normally.
@@ -460,9 +441,9 @@ cudaError_t launch_partial(const SparseAttnArgs& a, int nsplit, cudaStream_t str
   const int rb = sa_rows(a);
   const dim3 grid(unsigned(int64_t(a.B) * a.Hkv * ((R + rb - 1) / rb)), unsigned(nsplit));
   if (rb == 4)
-    return launch_dependent(sparse_attn_partial_kernel<T, kRope, 4>, grid, dim3(kSaWarps * 32), kRope,
+    return launch_maybe_dependent(sparse_attn_partial_kernel<T, kRope, 4>, grid, dim3(kSaWarps * 32), 0, kRope,
                             stream, a);
-  return launch_dependent(sparse_attn_partial_kernel<T, kRope, 8>, grid, dim3(kSaWarps * 32), kRope,
+  return launch_maybe_dependent(sparse_attn_partial_kernel<T, kRope, 8>, grid, dim3(kSaWarps * 32), 0, kRope,
                           stream, a);
 }
 
@@ -470,10 +451,10 @@ template <typename T>
 cudaError_t launch_combine(const SparseAttnArgs& a, int nsplit, cudaStream_t stream) {
   const int64_t rows = int64_t(a.B) * a.Hq * a.Sq;
   if (nsplit > 4)
-    return launch_dependent(sparse_attn_combine_kernel<T, 8>, dim3(unsigned(rows)), dim3(256), true,
+    return launch_maybe_dependent(sparse_attn_combine_kernel<T, 8>, dim3(unsigned(rows)), dim3(256), 0, true,
                             stream, a, nsplit);
-  return launch_dependent(sparse_attn_combine_kernel<T, 1>, dim3(unsigned((rows + 7) / 8)), dim3(256),
-                          true, stream, a, nsplit);
+  return launch_maybe_dependent(sparse_attn_combine_kernel<T, 1>, dim3(unsigned((rows + 7) / 8)), dim3(256), 0,
+                                true, stream, a, nsplit);
 }
 
 template <typename T>
