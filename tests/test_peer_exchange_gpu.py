@@ -78,6 +78,8 @@ def _runs(nruns, rows, run_len, seed, kind="normal", pad=0):
     (3, 5, 4000, 2500, "normal", 0),      # runs longer than k
     (4, 3, 1000, 1000, "normal", 600),    # duplicate (-inf, INT32_MAX) padding in every run
     (2, 2, 16384, 16384, "flat", 0),      # ties beyond the staging capacity
+    (2, 3, 12800, 12800, "normal", 0),    # more staged entries than the merge tree holds
+    (7, 4, 3000, 2900, "ties", 40),       # an odd number of runs: a list without a partner
 ])
 def test_merge_runs_edge_cases(cuda_device, nruns, rows, run_len, topk, kind, pad):
     v, idx = _runs(nruns, rows, run_len, seed=nruns * 1000 + topk, kind=kind, pad=pad)
