@@ -198,6 +198,7 @@ struct SparseAttnArgs {
   float* part_l;
   float* part_acc;
   const float2* table;    // [nsel][64] (cos, sin) of the view's RoPE angles (launcher)
+  const float* qrot;      // [B * Hq * Sq][128] rotated, scaled fp32 queries (launcher, with RoPE)
 };
 size_t sparse_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t nsel);
 cudaError_t launch_sparse_attn(SparseAttnArgs a, int dtype, void* ws, int num_sms,

@@ -57,37 +57,6 @@ __device__ __forceinline__ void store4<__half>(__half* p, float4 f) {
   *reinterpret_cast<uint2*>(p) = u;
 }
 
-// RoPE of the lane's 4 dimensions at position pe: lanes L < 16 hold x_i (i in
-// [4L, 4L+4)), lanes L + 16 hold x_{i+64}; out_i = x_i c_i - x_{i+64} s_i,
-// out_{i+64} = x_{i+64} c_i + x_i s_i (apply_rotary_pos_emb, _method_base.py:324-333).
-__device__ __forceinline__ float4 rope4(float4 x, float pe, const float* inv_lane, int lane) {
-  // this lane computes the angles of 2 of its group's 4 frequencies, the partner the other 2
-  const int base = (lane & 16) ? 2 : 0;
-  float s0, c0, s1, c1;
-  rope_sincos_fast(__fmul_rn(pe, inv_lane[base]), s0, c0);
-  rope_sincos_fast(__fmul_rn(pe, inv_lane[base + 1]), s1, c1);
-  const float os0 = __shfl_xor_sync(0xffffffffu, s0, 16), oc0 = __shfl_xor_sync(0xffffffffu, c0, 16);
-  const float os1 = __shfl_xor_sync(0xffffffffu, s1, 16), oc1 = __shfl_xor_sync(0xffffffffu, c1, 16);
-  float sn[4], cs[4];
-  if (lane & 16) {
-    sn[0] = os0; cs[0] = oc0; sn[1] = os1; cs[1] = oc1; sn[2] = s0; cs[2] = c0; sn[3] = s1; cs[3] = c1;
-  } else {
-    sn[0] = s0; cs[0] = c0; sn[1] = s1; cs[1] = c1; sn[2] = os0; cs[2] = oc0; sn[3] = os1; cs[3] = oc1;
-  }
-  float4 p;  // partner half
-  p.x = __shfl_xor_sync(0xffffffffu, x.x, 16);
-  p.y = __shfl_xor_sync(0xffffffffu, x.y, 16);
-  p.z = __shfl_xor_sync(0xffffffffu, x.z, 16);
-  p.w = __shfl_xor_sync(0xffffffffu, x.w, 16);
-  const float sg = (lane & 16) ? 1.f : -1.f;
-  float4 o;
-  o.x = fmaf(sg * p.x, sn[0], x.x * cs[0]);
-  o.y = fmaf(sg * p.y, sn[1], x.y * cs[1]);
-  o.z = fmaf(sg * p.z, sn[2], x.z * cs[2]);
-  o.w = fmaf(sg * p.w, sn[3], x.w * cs[3]);
-  return o;
-}
-
 // x[i] of a small register array with a lane-dependent i, by selects (no local memory)
 template <int N, typename V>
 __device__ __forceinline__ V pick(const V (&x)[N], int i) {
@@ -141,16 +110,11 @@ __global__ void __launch_bounds__(kSaWarps * 32, kRB == 4 ? 2 : 1)
   const int64_t j0 = int64_t(split) * per;
   const int64_t j1 = j0 + per < a.nsel ? j0 + per : a.nsel;
 
-  // this lane's frequencies: i = (4 * lane) mod 64 + 0..3
-  float inv_lane[4] = {0.f, 0.f, 0.f, 0.f};
-  if (kRope) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) inv_lane[e] = a.inv_freq[(4 * lane + e) & 63];
-  }
   const int64_t r0 = int64_t(rb) * kRB;
   const int nrows = int(R - r0 < kRB ? R - r0 : kRB);
 
-  // rotated queries (fp32, 4 dims per lane) and their absolute positions
+  // the queries (fp32, 4 dims per lane; with RoPE rotated and scaled by the
+  // table kernel, read after the wait) and their absolute positions
   float4 q[kRB];
   int64_t qabs[kRB];
 #pragma unroll
@@ -159,22 +123,33 @@ __global__ void __launch_bounds__(kSaWarps * 32, kRB == 4 ? 2 : 1)
     qabs[r] = -1;
     if (r < nrows) {
       const int64_t rr = r0 + r, g = rr / a.Sq, s = rr - g * a.Sq;
-      const T* qr = static_cast<const T*>(a.q) + int64_t(b) * a.q_sb +
-                    (int64_t(h) * a.G + g) * a.q_sh + s * a.q_ss;
       qabs[r] = a.q_pos[s];
-      const float pe = a.pe_original ? float(qabs[r]) : float(a.nsel - a.Sq + s);
-      q[r] = load4<T>(qr + 4 * lane);
-      if (kRope) q[r] = rope4(q[r], pe, inv_lane, lane);
-      q[r].x *= a.scale;
-      q[r].y *= a.scale;
-      q[r].z *= a.scale;
-      q[r].w *= a.scale;
+      if (!kRope) {
+        const T* qr = static_cast<const T*>(a.q) + int64_t(b) * a.q_sb +
+                      (int64_t(h) * a.G + g) * a.q_sh + s * a.q_ss;
+        q[r] = load4<T>(qr + 4 * lane);
+        q[r].x *= a.scale;
+        q[r].y *= a.scale;
+        q[r].z *= a.scale;
+        q[r].w *= a.scale;
+      }
     }
   }
-  // the angle table (a dependent launch after rope_table_kernel) is complete and
-  // visible after this; the combine kernel may launch now
+  // the angle table and the rotated queries (a dependent launch after
+  // rope_table_kernel) are complete and visible after this; the combine kernel
+  // may launch now
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
+  if (kRope) {
+#pragma unroll
+    for (int r = 0; r < kRB; ++r) {
+      if (r < nrows) {
+        const int64_t rr = r0 + r, g = rr / a.Sq, s = rr - g * a.Sq;
+        const int64_t orow = (int64_t(b) * a.Hq + int64_t(h) * a.G + g) * a.Sq + s;
+        q[r] = reinterpret_cast<const float4*>(a.qrot + orow * 128)[lane];
+      }
+    }
+  }
   float m[kRB], l[kRB];
   float4 acc[kRB];
 #pragma unroll
@@ -398,17 +373,36 @@ __global__ void __launch_bounds__(256) sparse_attn_combine_kernel(const SparseAt
 }
 
 // (cos, sin) of every view position's 64 RoPE angles, fp32(pe) * inv_freq[i]
-// evaluated with the accurate reduction of rope_sincos.cuh: [nsel][64] float2
-__global__ void rope_table_kernel(const SparseAttnArgs a, float2* table) {
+// evaluated with the accurate reduction of rope_sincos.cuh: [nsel][64] float2;
+// the threads past the table rotate the query rows at their positions and scale
+// them: qrot[row][i], qrot[row][i + 64] (fp32), row = (b * Hq + hq) * Sq + s.
+template <typename T>
+__global__ void rope_table_kernel(const SparseAttnArgs a, float2* table, float* qrot) {
   asm volatile("griddepcontrol.launch_dependents;");
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (e >= a.nsel * 64) return;
-  const int64_t j = e >> 6;
-  const int i = int(e & 63);
-  const float pe = a.pe_original ? float(a.key_pos[j]) : float(j);
+  const int64_t ntab = a.nsel * 64;
+  const int64_t rows = int64_t(a.B) * a.Hq * a.Sq;
+  if (e < ntab) {
+    const int64_t j = e >> 6;
+    const int i = int(e & 63);
+    const float pe = a.pe_original ? float(a.key_pos[j]) : float(j);
+    float sn, cs;
+    rope_sincos(__fmul_rn(pe, a.inv_freq[i]), sn, cs);
+    table[e] = make_float2(cs, sn);
+    return;
+  }
+  const int64_t f = e - ntab;
+  if (f >= rows * 64) return;
+  const int64_t row = f >> 6;
+  const int i = int(f & 63);
+  const int64_t s = row % a.Sq, bh = row / a.Sq, hq = bh % a.Hq, b = bh / a.Hq;
+  const T* qr = static_cast<const T*>(a.q) + b * a.q_sb + hq * a.q_sh + s * a.q_ss;
+  const float x0 = to_f32(qr[i]), x1 = to_f32(qr[i + 64]);
+  const float pe = a.pe_original ? float(a.q_pos[s]) : float(a.nsel - a.Sq + s);
   float sn, cs;
   rope_sincos(__fmul_rn(pe, a.inv_freq[i]), sn, cs);
-  table[e] = make_float2(cs, sn);
+  qrot[row * 128 + i] = (x0 * cs - x1 * sn) * a.scale;
+  qrot[row * 128 + i + 64] = (x1 * cs + x0 * sn) * a.scale;
 }
 
 int sa_rows(const SparseAttnArgs& a) { return int64_t(a.G) * a.Sq <= 4 ? 4 : 8; }
@@ -470,7 +464,7 @@ cudaError_t launch_attn(const SparseAttnArgs& a, int nsplit, cudaStream_t stream
 size_t sparse_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Sq, int64_t nsel) {
   const size_t rows = size_t(B) * size_t(Hq) * size_t(Sq);
   return (rows * size_t(split_cap(int64_t(rows))) * (2 + 128) * sizeof(float) + 255) / 256 * 256 +
-         (size_t(nsel) * 64 * sizeof(float2) + 255) / 256 * 256;
+         (size_t(nsel) * 64 * sizeof(float2) + 255) / 256 * 256 + rows * 128 * sizeof(float);
 }
 
 cudaError_t launch_sparse_attn(SparseAttnArgs a, int dtype, void* ws, int num_sms,
@@ -482,12 +476,18 @@ cudaError_t launch_sparse_attn(SparseAttnArgs a, int dtype, void* ws, int num_sm
   a.part_m = w;
   a.part_l = w + rows * cap;
   a.part_acc = w + 2 * rows * cap;
-  float2* table = reinterpret_cast<float2*>(
-      static_cast<uint8_t*>(ws) + (rows * cap * (2 + 128) * sizeof(float) + 255) / 256 * 256);
+  const size_t tab_off = (rows * cap * (2 + 128) * sizeof(float) + 255) / 256 * 256;
+  float2* table = reinterpret_cast<float2*>(static_cast<uint8_t*>(ws) + tab_off);
+  float* qrot = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + tab_off +
+                                         (size_t(a.nsel) * 64 * sizeof(float2) + 255) / 256 * 256);
   if (a.inv_freq != nullptr) {
-    const int64_t n = a.nsel * 64;
-    rope_table_kernel<<<unsigned((n + 255) / 256), 256, 0, stream>>>(a, table);
+    const int64_t n = (a.nsel + int64_t(rows)) * 64;
+    if (dtype == kBF16)
+      rope_table_kernel<__nv_bfloat16><<<unsigned((n + 255) / 256), 256, 0, stream>>>(a, table, qrot);
+    else
+      rope_table_kernel<__half><<<unsigned((n + 255) / 256), 256, 0, stream>>>(a, table, qrot);
     a.table = table;
+    a.qrot = qrot;
   }
   const cudaError_t e = dtype == kBF16 ? launch_attn<__nv_bfloat16>(a, nsplit, stream)
                                         : launch_attn<__half>(a, nsplit, stream);
