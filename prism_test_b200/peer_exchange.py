@@ -68,18 +68,28 @@ class PeerExchange:
             handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
             _lib.check(lib.prism_peer_alloc(nbytes, ctypes.byref(own), handle), "prism_peer_alloc")
             self._own = own.value
-            handles = [None] * self.world
-            dist.all_gather_object(handles, handle.raw, group=group)
-            ptrs = []
-            for r, h in enumerate(handles):
-                if r == self.rank:
-                    ptrs.append(self._own)
-                    continue
-                p = ctypes.c_void_p()
-                hb = ctypes.create_string_buffer(h, _lib.IPC_HANDLE_BYTES)
-                _lib.check(lib.prism_peer_open(hb, ctypes.byref(p)), "prism_peer_open")
-                self._opened.append(p.value)
-                ptrs.append(p.value)
+            try:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, handle.raw, group=group)
+                ptrs = []
+                for r, h in enumerate(handles):
+                    if r == self.rank:
+                        ptrs.append(self._own)
+                        continue
+                    p = ctypes.c_void_p()
+                    hb = ctypes.create_string_buffer(h, _lib.IPC_HANDLE_BYTES)
+                    _lib.check(lib.prism_peer_open(hb, ctypes.byref(p)), "prism_peer_open")
+                    self._opened.append(p.value)
+                    ptrs.append(p.value)
+            except BaseException:
+                # undo this rank's mappings and buffer; the other ranks see the
+                # failure as an error of their next collective
+                for p in self._opened:
+                    lib.prism_peer_close(ctypes.c_void_p(p))
+                self._opened = []
+                lib.prism_peer_free(ctypes.c_void_p(self._own))
+                self._own = None
+                raise
         self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
         # this rank's run, int32 [2, rows, topk]: fp32 score bits, global indices
         self.run = torch.as_tensor(
