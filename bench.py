@@ -60,9 +60,76 @@ def parse():
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="sharded path: peer: runs read over NVLink from peer-mapped buffers; "
                          "nccl: all-gather of the runs, then a local merge")
-    ap.add_argument("--stage", default="recall", choices=["recall", "attention"],
-                    help="attention: time the attention over a selected view instead of the recall")
+    ap.add_argument("--stage", default="recall", choices=["recall", "attention", "merge"],
+                    help="attention: time the attention over a selected view instead of the recall; "
+                         "merge: time the sharded path's run merge for N ranks on one GPU (--runs)")
+    ap.add_argument("--runs", type=int, default=8,
+                    help="merge stage: number of sorted runs (the ranks of the sharded decode)")
     return ap.parse_args()
+
+
+def run_merge(args):
+    """The sharded path's run merge on one GPU: the top-k of --runs sorted runs per row,
+    each the local top-k of one rank of decode-1m-sharded (32 rows, k = 8192, distinct
+    global indices, scores of a normal score tail), in the gathered layout
+    [runs, 2, rows, k]. The work of each rank's merge kernel in the N-GPU step, without
+    the interconnect."""
+    from prism_test_b200 import _lib, topk_merge_runs
+    from prism_test_b200 import workloads as W
+    dev = torch.device("cuda", 0)
+    wl = W.WORKLOADS[args.workload or "decode-1m-sharded"]
+    nruns, rows, k = args.runs, wl.B * wl.Hq * wl.Sq, wl.topk
+    g = torch.Generator(device=dev).manual_seed(3)
+    s = torch.randn(nruns, rows, k, generator=g, device=dev).sort(dim=-1, descending=True).values
+    idx = (torch.arange(nruns * k, device=dev, dtype=torch.int32).view(nruns, 1, k)
+           .expand(nruns, rows, k).contiguous())
+    runs = torch.stack([s.view(torch.int32), idx], dim=1).contiguous()
+    lib = _lib.load()
+    step = lambda: topk_merge_runs(runs, k)  # noqa: E731
+    for _ in range(max(3, args.warmup)):
+        oi, os_ = step()
+    torch.cuda.synchronize()
+    ref = s.permute(1, 0, 2).reshape(rows, -1).topk(k, dim=-1).values
+    if not torch.equal(os_, ref):
+        raise SystemExit("run merge result differs from torch.topk over the union")
+    lib.prism_profile_start(args.steps + 16)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    lib.prism_profile_stop()
+    n_m = _lib.ctypes.c_int64(0)
+    t_m = _lib.ctypes.c_double(0.0)
+    lib.prism_profile_read(_lib.KERNEL_MERGE, _lib.ctypes.byref(n_m), _lib.ctypes.byref(t_m))
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    line = {
+        "metric": "run-merge candidates/sec", "value": nruns * rows * k * args.steps / (ms * 1e-3),
+        "unit": "candidates/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u64 keys (fp32 score, int32 index)", "data": "synthetic",
+        "config": {"workload": wl.name, "stage": "run merge", "runs": nruns, "rows": rows, "topk": k},
+        "launch_ms": t_m.value / max(1, n_m.value),
+        "gpu_launches": args.steps, "timing": "CUDA graph of one call, replayed",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def run_attention(args):
@@ -365,6 +432,8 @@ def main():
         return run_reference(args)
     if args.stage == "attention":
         return run_attention(args)
+    if args.stage == "merge":
+        return run_merge(args)
     world, rank, local = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
