@@ -1110,8 +1110,9 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
   const int nsum = int(run_len / sstep < kMergeSumm ? run_len / sstep : kMergeSumm);
   if (tid == 0) sm.rthr = 0;
   {
-    // each CTA of the row's cluster loads a quarter of the summary entries and
-    // copies the rest from its cluster peers' shared memory
+    // each CTA of the row's cluster loads a quarter of the summary entries (scattered
+    // words, which may cross the interconnect) and copies the rest from its cluster
+    // peers' shared memory
     cg::cluster_group cluster = cg::this_cluster();
     const int ns = nruns * nsum;
     for (int e = ns * int(part) / kMergeParts + tid; e < ns * int(part + 1) / kMergeParts; e += kThreads) {
@@ -1169,6 +1170,14 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
     int64_t lo = int64_t(ns_ge) * sstep;  // entries [0, lo) are >= T, entries [hi, run_len) are < T
     int64_t hi = ns_ge < nsum ? (int64_t(ns_ge) + 1) * sstep - 1 : run_len;
     if (hi > run_len) hi = run_len;
+    if (hi - lo <= 64) {
+      // the whole window in one round: entries lo + lane and lo + 32 + lane
+      const int64_t p0 = lo + lane, p1 = lo + 32 + lane;
+      const bool g0 = p0 < hi && cand_at(warp, p0) >= thr;
+      const bool g1 = p1 < hi && cand_at(warp, p1) >= thr;
+      lo += __popc(__ballot_sync(0xffffffffu, g0)) + __popc(__ballot_sync(0xffffffffu, g1));
+      hi = lo;
+    }
     while (lo < hi) {
       const int64_t step = (hi - lo + 31) / 32;
       const int64_t p = lo + int64_t(lane) * step;
