@@ -264,10 +264,15 @@ PRISM_API int prism_peer_merge(void* const* bufs, int32_t world, int32_t rank, i
  * results as prism_topk_merge; the per-row candidate buffers live in one static
  * device array of PRISM_NOALLOC_SCRATCH_BYTES per device, so the request must
  * satisfy rows * min(n, 16384) * 8 <= PRISM_NOALLOC_SCRATCH_BYTES (e.g. 64 rows
- * of any length); larger requests return PRISM_E_WORKSPACE.
+ * of any length); larger requests return PRISM_E_WORKSPACE. Only requests of
+ * fewer than 64 rows write the scratch (one 4-CTA cluster per row, exact path);
+ * 64 rows or more run one CTA per row with its candidates in shared memory, but
+ * the same size rule applies to them.
  *   - The first call on a device, made with that device current, looks the
  *     scratch address up (cudaGetSymbolAddress) and caches it; make that first
- *     call before any stream capture starts on the device.
+ *     call before any stream capture starts on the device. The cached address
+ *     does not survive cudaDeviceReset of that device: do not call this entry
+ *     point on a device after resetting it in the same process.
  *   - Nothing in the scratch needs to start at zero.
  *   - All calls on one device share the scratch: calls whose executions overlap
  *     (different streams, concurrent host threads) race and give wrong results.

@@ -13,6 +13,14 @@
 // array's address up once with cudaGetSymbolAddress and caches it. That first
 // call may make the CUDA runtime load this module on the device, so make it
 // before any stream capture is started on that device, e.g. once at start-up.
+// The cached address belongs to the device's current context: after a
+// cudaDeviceReset of that device it is stale, so the entry point must not be
+// called on a device that was reset in the same process.
+//
+// Only requests of fewer than 64 rows write the scratch (one 4-CTA cluster per
+// row; its exact path appends each row's candidates to the row's slice). From 64
+// rows on, one CTA per row keeps its candidates in shared memory; the size rule
+// below is applied to every request all the same.
 //
 // Nothing in the scratch has to start at zero: the selection kernel counts its
 // candidate slots in shared memory and writes every slot before reading it.

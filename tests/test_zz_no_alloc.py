@@ -1,17 +1,21 @@
 """prism_topk_merge_noalloc: the merge entry point whose candidate buffers live in a
 static device array instead of a caller workspace.
 
+Callers that cannot allocate device memory (a fixed device-memory budget owned by
+another allocator, or a path where cudaMalloc's implicit synchronisation is not
+acceptable) use this entry point; these tests check that it returns what the
+workspace merge returns.
+
 Collected last on purpose: its GPU test must also pass after every other test has
 run in the same process (and, run alone, in a fresh one).
 """
-import ctypes
-
 import pytest
 import torch
 
 from prism_test_b200 import _lib, topk_merge
 
 SCRATCH_BYTES = 8 << 20
+KPASS = 131072  # columns the select cluster holds in registers; longer rows take the exact path
 
 
 @pytest.fixture(scope="module")
@@ -33,13 +37,37 @@ def _noalloc(lib, s, i, topk, stream=None):
     return out_idx, out_scores
 
 
-def _shard_candidates(rows, shards, per_shard, seed, device):
-    """Per-shard sorted top lists with global indices, as after the all-gather."""
+def _distinct_rows(rows, n, seed):
+    """Scores that are distinct within each row (so torch.topk has one answer) and
+    candidate indices that are a per-row permutation of 3 * column."""
     g = torch.Generator().manual_seed(seed)
-    s = torch.randn(rows, shards, per_shard, generator=g).sort(dim=-1, descending=True).values
-    base = torch.arange(shards).view(1, shards, 1) * (per_shard * 16)
-    i = (base + torch.randperm(per_shard * 16, generator=g)[:per_shard].view(1, 1, per_shard)).expand(rows, -1, -1)
-    return (s.reshape(rows, -1).contiguous().to(device), i.reshape(rows, -1).to(torch.int32).contiguous().to(device))
+    s = torch.stack([torch.randperm(n, generator=g) for _ in range(rows)]).to(torch.float32)
+    s = s * (1.0 / n) - 0.5
+    i = (torch.stack([torch.randperm(n, generator=g) for _ in range(rows)]) * 3).to(torch.int32)
+    return s.contiguous(), i.contiguous()
+
+
+def _cluster_sampled_mask(n):
+    """Columns the cluster select's 1/8 threshold sample reads (white-box): thread t
+    of CTA r samples columns r*32768 + (u*1024 + t)*4 + e for (u, e) in
+    (0, 0), (2, 1), (4, 2), (6, 3)."""
+    t = torch.arange(1024)
+    cols = [r * 32768 + (u * 1024 + t) * 4 + e for r in range(4) for u, e in ((0, 0), (2, 1), (4, 2), (6, 3))]
+    cols = torch.cat(cols)
+    m = torch.zeros(n, dtype=torch.bool)
+    m[cols[cols < n]] = True
+    return m
+
+
+def _sample_defeating_rows(rows, n, seed):
+    """Distinct scores whose sampled columns all lie below the rest: the sampled
+    threshold admits every unsampled column, far more than the 16384 candidates
+    the fast path holds, so the kernel takes its exact path."""
+    s, i = _distinct_rows(rows, n, seed)
+    m = _cluster_sampled_mask(n)
+    assert int((~m).sum()) > 16384
+    s = torch.where(m[None, :], s, s + 2.0)
+    return s.contiguous(), i
 
 
 def test_noalloc_rejects_requests_beyond_the_scratch(lib):
@@ -55,16 +83,38 @@ def test_noalloc_rejects_requests_beyond_the_scratch(lib):
     assert lib.prism_topk_merge_noalloc(16, 16, 4, 64, 62, 10, 16, None, None) == _lib.PRISM_E_INVALID
 
 
+def test_noalloc_scratch_bound_of_the_test_cases():
+    # the exact-path cases below fill most of the scratch without passing its limit
+    assert 63 * 16384 * 8 <= SCRATCH_BYTES < 64 * 16384 * 8 + 1
+    assert 8 * 16384 * 8 <= SCRATCH_BYTES
+
+
 @pytest.mark.gpu
 def test_noalloc_matches_workspace_merge_twice_in_a_row(cuda_device, lib):
-    # 8 shards x 8192 sorted candidates for 64 rows (the 1M-key sharded decode
-    # merge has 32), exactly the 8 MiB scratch limit; then a small case
-    big = _shard_candidates(64, 8, 8192, seed=11, device=cuda_device)
-    small_s = torch.randn(5, 1000, generator=torch.Generator().manual_seed(12)).to(cuda_device)
-    small_i = torch.arange(small_s.shape[1], dtype=torch.int32, device=cuda_device).expand(5, -1).contiguous()
-    cases = [(big[0], big[1], 8192), (small_s, small_i, 37)]
+    # Cases that write the static scratch (fewer than 64 rows, so one 4-CTA cluster
+    # per row; the exact path appends every row's candidates to its scratch slice):
+    #   rows longer than the 131072 columns a cluster holds in registers, one of them
+    #   63 rows x 16384 candidates (63 * 16384 * 8 B, next to the 8 MiB limit), and
+    #   rows whose threshold sample is defeated, so the fast path falls back.
+    # Then cases that leave it alone: 64 rows (one CTA per row) and a short row
+    # set that the fast path resolves in shared memory.
+    torch.manual_seed(0)
+    cases = []
+    s, i = _distinct_rows(8, 2 * KPASS, seed=21)
+    cases.append((s, i, 4096))
+    s, i = _distinct_rows(63, KPASS + KPASS // 2, seed=22)
+    cases.append((s, i, 16384))
+    s, i = _sample_defeating_rows(8, 100000, seed=23)
+    cases.append((s, i, 3000))
+    s, i = _distinct_rows(64, 65536, seed=24)
+    cases.append((s, i, 8192))
+    s, i = _distinct_rows(5, 1000, seed=25)
+    cases.append((s, i, 37))
+    cases = [(s.to(cuda_device), i.to(cuda_device), k) for s, i, k in cases]
 
-    # two calls in a row on one stream, no synchronisation in between
+    # every case twice, one after the other on one stream and without
+    # synchronising: each call after the first finds the scratch full of the
+    # previous call's candidates
     got = [_noalloc(lib, s, i, k) for s, i, k in cases]
     got_again = [_noalloc(lib, s, i, k) for s, i, k in cases]
     torch.cuda.synchronize()
@@ -73,6 +123,8 @@ def test_noalloc_matches_workspace_merge_twice_in_a_row(cuda_device, lib):
         torch.cuda.synchronize()
         assert torch.equal(gi, ri) and torch.equal(gi2, ri)
         assert torch.equal(gs, rs) and torch.equal(gs2, rs)
-        # and against torch.topk (scores exact; index sets equal up to ties)
-        ts = s.float().topk(k, dim=-1).values
-        assert torch.equal(gs, ts)
+        # and against torch.topk: the scores are distinct, so values and indices
+        # are unique and must agree exactly
+        tv, tp = s.topk(k, dim=-1)
+        assert torch.equal(gs, tv)
+        assert torch.equal(gi, torch.gather(i, 1, tp))
