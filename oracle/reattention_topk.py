@@ -1,7 +1,8 @@
 """CPU oracle of the ReAttention recall scorer — TEST INFRASTRUCTURE ONLY.
 
 Only the tests, ``__graft_entry__.smoke()`` (as a checker) and ``bench.py``'s
-CPU-baseline leg may import this module. The product path never does.
+CPU-baseline leg, reference arm and post-timing result check may import this
+module. The product path never does.
 
 A plain-PyTorch fp32 restatement, on the CPU, of the reference's dense recall
 path (RUSH-Intelligence/Prism-Test, eval_harness/attention_methods/):

@@ -1,6 +1,6 @@
 """Generates the golden vectors in this directory by running the REFERENCE's own
-code (RUSH-Intelligence/Prism-Test, imported read-only from a checkout given by
---reference, default /root/reference):
+code (RUSH-Intelligence/Prism-Test, imported read-only from a checkout whose root
+is given by --reference or the PRISM_REFERENCE environment variable):
 
     eval_harness/attention_methods/_method_base.py  build_cos_sin,
         apply_rotary_pos_emb, undo_rotary_pos_emb
@@ -16,11 +16,12 @@ un-rotates the bf16 keys in fp32 with ``undo_rotary_pos_emb`` and selects with
 bits), inv_freq, and the reference's top-k indices and scores.
 
 The checkout is not needed to *use* the vectors; only to regenerate them:
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH
 """
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 import zlib
 from pathlib import Path
@@ -49,8 +50,11 @@ def bf16_bits(t: torch.Tensor) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("PRISM_REFERENCE"),
+                    help="root of a RUSH-Intelligence/Prism-Test checkout (or set PRISM_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference checkout with --reference PATH or PRISM_REFERENCE")
     sys.path.insert(0, args.reference)
     from eval_harness.attention_methods._method_base import (  # noqa: E402
         apply_rotary_pos_emb, build_cos_sin, undo_rotary_pos_emb)

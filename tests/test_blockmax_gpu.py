@@ -52,3 +52,44 @@ def test_blockmax_rope_keys(cuda_device, topk):
     s_want = torch.gather(scores, -1, want.long())
     assert bool(((s_got - s_want).abs() <= tol).all())
     assert float((got == want).float().mean()) > 0.99
+
+
+# ---- pinned to the reference kernels ------------------------------------------------
+# tests/golden/blockmax_*.npz hold the outputs of the reference's own Triton kernels
+# (_einsum_topk_1_kernel / _einsum_topk_4_kernel, run by Triton's interpreter on
+# integer inputs, tests/golden/make_blockmax_golden.py): exact arithmetic, so the
+# oracle and the CUDA path must reproduce them exactly, ties included.
+from pathlib import Path  # noqa: E402
+
+import numpy as np  # noqa: E402
+
+BLOCKMAX_GOLDEN = sorted((Path(__file__).parent / "golden").glob("blockmax_*.npz"))
+
+
+def _golden(path, dtype):
+    z = np.load(path)
+    q = torch.from_numpy(z["q"]).to(dtype)
+    k = torch.from_numpy(z["k"]).to(dtype)
+    return q, k, int(z["topk"]), torch.from_numpy(z["out"])
+
+
+def test_blockmax_golden_present():
+    assert len(BLOCKMAX_GOLDEN) >= 6
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
+@pytest.mark.parametrize("path", BLOCKMAX_GOLDEN, ids=[p.stem for p in BLOCKMAX_GOLDEN])
+def test_oracle_matches_reference_kernel(path, dtype):
+    q, k, topk, want = _golden(path, dtype)
+    got = orc.blockmax_topk(q.float(), k.float(), topk)
+    assert torch.equal(got, want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
+@pytest.mark.parametrize("path", BLOCKMAX_GOLDEN, ids=[p.stem for p in BLOCKMAX_GOLDEN])
+def test_blockmax_matches_reference_kernel(cuda_device, path, dtype):
+    q, k, topk, want = _golden(path, dtype)
+    got = einsum_topk_func(q.to(cuda_device), k.to(cuda_device), topk, mode="blockmax").cpu()
+    assert got.dtype == torch.int32 and got.shape == want.shape
+    assert torch.equal(got, want)

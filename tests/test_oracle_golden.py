@@ -8,7 +8,8 @@ import torch
 
 from oracle import reattention_topk as orc
 
-GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith(("post_", "recall_", "attn_")))
+GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz")
+                if not p.stem.startswith(("post_", "recall_", "attn_", "blockmax_", "dropin_")))
 
 
 def load_case(path):

@@ -13,7 +13,8 @@ from tests.parity import check_parity
 
 pytestmark = pytest.mark.gpu
 
-GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith(("post_", "recall_", "attn_")))
+GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz")
+                if not p.stem.startswith(("post_", "recall_", "attn_", "blockmax_", "dropin_")))
 
 
 def _golden(path, dev):
