@@ -7,20 +7,29 @@
 Metric: KV tokens scored and top-k'd per second (keys of the cached sequence
 processed per second, all heads), whole job.
 
-* N = 1 runs ``decode-128k``: one decode step, 32 query / 8 KV heads,
-  head_dim 128, 131072 RoPE'd bf16 keys, k = 4096 per query head.
-* N > 1 (one process per GPU, launched by torchrun) runs ``decode-1m-sharded``:
-  1,048,576 keys split evenly over the N ranks (strong scaling), k = 8192; every
-  rank's merge kernel reads the other ranks' sorted runs from their GPUs over
-  NVLink (peer-mapped buffers; ``--exchange nccl``: NCCL all-gather, then merge).
+The headline workload is ``decode-1m-sharded`` at every N (strong scaling on one
+configuration): one decode step, 32 query / 8 KV heads, head_dim 128, 1,048,576
+RoPE'd bf16 keys, k = 8192 per query head. At N = 1 one GPU holds the whole 2 GB
+cache; at N > 1 (one process per GPU, launched by torchrun) the keys are split
+evenly over the ranks and every rank's merge kernel reads the other ranks' sorted
+runs from their GPUs over NVLink (peer-mapped buffers; ``--exchange nccl``: NCCL
+all-gather, then merge).
+
+The same line carries sub-records measured in the same run: ``decode_128k``
+(N = 1 only: 131072 keys, k = 4096) and ``shared_context_256k`` (every N: 8
+queries over 262144 Student-t keys, 28 / 4 heads, k = 4096, sequence-sharded at
+N > 1). ``--workload NAME`` measures one workload alone.
 
 A step is one full call of the op on resident inputs; W untimed steps, then K
-steps timed with CUDA events between barriers, max over ranks. The key cache
-(268 MB at 128K, 2 GB at 1M) is larger than the 126 MB L2, so no flush is
+steps timed with CUDA events between barriers, max over ranks. The key caches
+(268 MB per rank at the least) are larger than the 126 MB L2, so no flush is
 needed between steps. ``e2e`` repeats the K steps through the same public call
 with pinned host inputs copied in and the result (indices + scores) copied out
-inside the timed region. ``--impl reference`` times the reference's dense
-PyTorch path restated in the CPU oracle on the host cores (rank 0 only).
+inside the timed region. After the timed region every workload's result is
+checked (``parity``): the ranks agree, a sharded result equals a one-GPU call
+over the whole cache bit for bit, and whole rows match the CPU oracle under the
+parity rules. ``--impl reference`` times the reference's dense PyTorch path
+restated in the CPU oracle on the host cores (rank 0 only).
 """
 from __future__ import annotations
 
@@ -52,6 +61,8 @@ def parse():
     ap.add_argument("--workload", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="measure the headline workload only (no decode_128k / shared_context_256k records)")
     ap.add_argument("--recall-type", default="qk", choices=["qk", "qkv", "qkv2"],
                     help="value-norm weighting of the keys (qkv: L1, qkv2: L2)")
     ap.add_argument("--chunks", type=int, default=0,
@@ -212,11 +223,11 @@ def dist_env():
 
 def pick_workload(args, world):
     from prism_test_b200 import workloads as W
-    name = args.workload or ("decode-128k" if world == 1 else "decode-1m-sharded")
+    name = args.workload or "decode-1m-sharded"
     return W.WORKLOADS[name]
 
 
-def config_of(wl, world, recall_type="qk", exchange="nccl"):
+def config_of(wl, world, recall_type="qk", exchange="peer"):
     return {
         "workload": wl.name, "B": wl.B, "Hq": wl.Hq, "Hkv": wl.Hkv, "Sq": wl.Sq, "Sk": wl.Sk,
         "topk": wl.topk, "head_dim": wl.D, "rope_theta": wl.theta, "key_dtype": "bf16",
@@ -416,8 +427,9 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": dt * 1e3, "higher_is_better": True,
-        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32 (tf32 MMA)",
-        "data": "synthetic", "config": config_of(wl, world, rt),
+        "scaling": "strong" if wl.name == "decode-1m-sharded" or world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f32 (tf32 MMA)",
+        "data": "synthetic", "config": config_of(wl, world, rt, args.exchange),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -426,28 +438,131 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------- GPU arm
-def main():
-    args = parse()
-    if args.impl == "reference":
-        return run_reference(args)
-    if args.stage == "attention":
-        return run_attention(args)
-    if args.stage == "merge":
-        return run_merge(args)
-    world, rank, local = dist_env()
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
+# (name in kernels_ms_per_step, kernel id of the library's profiling aid)
+KERNEL_IDS = (("score", "KERNEL_SCORE"), ("select", "KERNEL_SELECT"), ("merge", "KERNEL_MERGE"),
+              ("value_norms", "KERNEL_WEIGHT"), ("score_weighting", "KERNEL_SCALE"),
+              ("threshold", "KERNEL_THRESHOLD"))
+
+
+class Ranks:
+    """This process's place in the job (one process per GPU) and the helpers that
+    every rank calls in the same order."""
+
+    def __init__(self, world, rank, local, dev):
+        self.world, self.rank, self.local, self.dev = world, rank, local, dev
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, v: float) -> float:
+        if self.world == 1:
+            return v
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        t = torch.tensor([v], device=self.dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def all_equal(self, t: torch.Tensor) -> bool:
+        """Whether every rank holds the same small int64 tensor."""
+        if self.world == 1:
+            return True
+        import torch.distributed as dist
+        hi, lo = t.clone(), t.clone()
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        return bool(torch.equal(hi, lo))
+
+
+def kernel_times(lib):
+    """{name: (launches, total ms)} of the library's event pairs since profiling started."""
+    import ctypes
+    from prism_test_b200 import _lib
+    out = {}
+    for name, attr in KERNEL_IDS:
+        n, t = ctypes.c_int64(0), ctypes.c_double(0.0)
+        lib.prism_profile_read(getattr(_lib, attr), ctypes.byref(n), ctypes.byref(t))
+        out[name] = (n.value, t.value)
+    return out
+
+
+def result_check(wl, ranks: Ranks, x: dict, v, idx, sc, recall_type: str, budget_s: float = 60.0) -> dict:
+    """The result of one step, checked after the timed region:
+
+    * every rank holds the same result (checksums compared over the process group);
+    * at N > 1, rank 0 regenerates the whole key cache from the same seeds and the
+      sharded result must equal a one-GPU call over it bit for bit (same scores for
+      the same keys, ties toward lower indices);
+    * rank 0 checks whole query-head groups of rows, one KV head at a time, spread
+      over the heads, against the CPU oracle with the parity rules (scores within
+      1e-3, index sets equal up to near-ties at the k-th score), until the budget
+      is spent (at least one KV head)."""
+    from prism_test_b200 import einsum_topk_func
+    from prism_test_b200 import workloads as W
+    rows = idx.numel() // wl.topk
+    ck = torch.stack([idx.long().sum(), sc.view(torch.int32).long().sum(),
+                      (idx.reshape(rows, -1)[:, ::97].long() * 131).sum()])
+    out = {"rows": rows, "ranks_agree": ranks.all_equal(ck)}
+    if ranks.rank != 0:
+        return out
+    t0 = time.perf_counter()
+    q, k, vv, inv = x["q"], x["k"], v, x["inv_freq"]
+    if ranks.world > 1:
+        full = W.make_inputs(wl, ranks.dev)
+        q, k, inv = full["q"], full["k"], full["inv_freq"]
+        vv = W.make_values(wl, ranks.dev) if recall_type != "qk" else None
+        ri, rs = einsum_topk_func(q, k, wl.topk, inv_freq=inv, return_scores=True,
+                                  causal_offset=wl.causal_offset, values=vv, recall_type=recall_type)
+        torch.cuda.synchronize()
+        out["bitwise_equal_single_gpu"] = bool(torch.equal(ri, idx) and torch.equal(rs, sc))
+        del ri, rs
+    from oracle import reattention_topk as orc
+    from oracle.parity import REL, REL_WEIGHTED, check_parity
+    G = wl.Hq // wl.Hkv
+    order = []
+    for h in [0, wl.Hkv - 1] + list(range(wl.Hkv // 2, wl.Hkv - 1)) + list(range(1, wl.Hkv // 2)):
+        if 0 <= h < wl.Hkv and h not in order:
+            order.append(h)
+    checked, swaps, worst, err = 0, 0, 0.0, None
+    inv_c = inv.cpu() if inv is not None else None
+    for h in order:
+        if checked and time.perf_counter() - t0 > budget_s:
+            break
+        sl = slice(h * G, (h + 1) * G)
+        w = orc.recall_weights(vv[:, h:h + 1].cpu(), recall_type) if recall_type != "qk" else None
+        try:
+            st = check_parity(idx[:, sl], sc[:, sl], q[:, sl].cpu(), k[:, h:h + 1].cpu(), wl.topk,
+                              inv_c, 0, wl.causal_offset, 0,
+                              rel=REL if recall_type == "qk" else REL_WEIGHTED, weights=w)
+        except AssertionError as e:  # noqa: PERF203
+            err = f"KV head {h}: {str(e)[:300]}"
+            checked += wl.B * G * wl.Sq
+            break
+        checked += st["rows"]
+        swaps += st["swapped"]
+        worst = max(worst, st["max_rel_err"])
+    ok = err is None and out["ranks_agree"] and out.get("bitwise_equal_single_gpu", True)
+    out.update({"rows_checked": checked, "near_tie_swaps": swaps, "max_rel_err": worst, "ok": bool(ok),
+                "rule": "scores within 1e-3 of the fp32 oracle (x max(|s|, ||q|| ||k||)); index sets "
+                        "equal up to near-ties at the k-th score",
+                "seconds": round(time.perf_counter() - t0, 1)})
+    if err:
+        out["error"] = err
+    return out
+
+
+def measure(wl, args, ranks: Ranks, *, e2e: bool, cpu_base: bool, clocks_on: bool) -> dict:
+    """One workload on every rank: W warm-up steps, a profiling pass (every library
+    launch between its own pair of events), then K steps as replays of a CUDA graph of
+    one call (host Python/ctypes overhead would otherwise starve the device), timed
+    between CUDA events with all ranks entering together, max over ranks; then, if
+    asked, the end-to-end pass and the CPU baseline; then the result check."""
     from prism_test_b200 import _lib, einsum_topk_func
     from prism_test_b200 import workloads as W
     from prism_test_b200.sharded import shard_bounds, sharded_einsum_topk
-
     lib = _lib.load()
-    wl = pick_workload(args, world)
+    world, rank, dev = ranks.world, ranks.rank, ranks.dev
     start, stop = shard_bounds(wl.Sk, rank, world)
     x = W.make_inputs(wl, dev, shard=(rank, world) if world > 1 else None)
     q, k, inv = x["q"], x["k"], x["inv_freq"]
@@ -466,120 +581,69 @@ def main():
         return sharded_einsum_topk(qq, kk, wl.topk, shard_start=start, inv_freq=inv, return_scores=True,
                                    v_shard=vv, recall_type=rt, chunks=chunks, exchange=exchange)
 
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        import torch.distributed as dist
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    for _ in range(max(3, args.warmup)):
+    warm = max(3, args.warmup)
+    for _ in range(warm):
         step(q, k)
     torch.cuda.synchronize()
-    barrier()
+    ranks.barrier()
     torch.cuda.synchronize()
 
     # per-kernel device times: every launch bracketed by events (profiling mode)
-    lib.prism_profile_start(4 * args.steps + 16)
+    lib.prism_profile_start(8 * args.steps + 16)
     n0 = lib.prism_launch_count()
     for _ in range(args.steps):
         step(q, k)
     torch.cuda.synchronize()
     lib.prism_profile_stop()
     launches_per_step = (lib.prism_launch_count() - n0) / args.steps
-    barrier()
+    ktimes = kernel_times(lib)
+    ranks.barrier()
     torch.cuda.synchronize()
 
-    # whole steps: the call (with its NCCL all-gather on several GPUs) is captured
-    # once in a CUDA graph and replayed, so host-side Python/ctypes overhead does
-    # not starve the device
-    graph = None
-    if True:
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(2):
-                step(q, k)
-        torch.cuda.current_stream().wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
             step(q, k)
-        for _ in range(3):
-            graph.replay()
-        torch.cuda.synchronize()
-    clocks = ClockSampler(local)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(q, k)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(ranks.local) if clocks_on else None
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    clocks.start()
-    # every rank enters the timed region together (the sampler start is host work)
+    if clocks:
+        clocks.start()
     torch.cuda.synchronize()
-    barrier()
+    ranks.barrier()  # every rank enters the timed region together
     torch.cuda.synchronize()
     ev0.record()
     for _ in range(args.steps):
-        if graph is not None:
-            graph.replay()
-        else:
-            step(q, k)
+        graph.replay()
     ev1.record()
     torch.cuda.synchronize()
-    clocks.stop()
-    launches = int(round(launches_per_step * args.steps))
-    barrier()
+    if clocks:
+        clocks.stop()
+    ranks.barrier()
     torch.cuda.synchronize()
-    ms = max_over_ranks(ev0.elapsed_time(ev1))
-    ms_per_step = ms / args.steps
+    ms = ranks.max(ev0.elapsed_time(ev1))
     del graph  # a graph holding NCCL work must go before the process group
     torch.cuda.synchronize()
 
-    # dominant kernel: the scorer (un-rotate + q·K^T), timed per launch
-    n_sc = _lib.ctypes.c_int64(0)
-    t_sc = _lib.ctypes.c_double(0.0)
-    lib.prism_profile_read(_lib.KERNEL_SCORE, _lib.ctypes.byref(n_sc), _lib.ctypes.byref(t_sc))
-    n_se = _lib.ctypes.c_int64(0)
-    t_se = _lib.ctypes.c_double(0.0)
-    lib.prism_profile_read(_lib.KERNEL_SELECT, _lib.ctypes.byref(n_se), _lib.ctypes.byref(t_se))
-    n_me = _lib.ctypes.c_int64(0)
-    t_me = _lib.ctypes.c_double(0.0)
-    lib.prism_profile_read(_lib.KERNEL_MERGE, _lib.ctypes.byref(n_me), _lib.ctypes.byref(t_me))
-    n_we = _lib.ctypes.c_int64(0)
-    t_we = _lib.ctypes.c_double(0.0)
-    lib.prism_profile_read(_lib.KERNEL_WEIGHT, _lib.ctypes.byref(n_we), _lib.ctypes.byref(t_we))
-    n_sa = _lib.ctypes.c_int64(0)
-    t_sa = _lib.ctypes.c_double(0.0)
-    lib.prism_profile_read(_lib.KERNEL_SCALE, _lib.ctypes.byref(n_sa), _lib.ctypes.byref(t_sa))
-    n_th = _lib.ctypes.c_int64(0)
-    t_th = _lib.ctypes.c_double(0.0)
-    lib.prism_profile_read(_lib.KERNEL_THRESHOLD, _lib.ctypes.byref(n_th), _lib.ctypes.byref(t_th))
-    score_ms = t_sc.value / max(1, n_sc.value)
-    prefill = wl.Sq >= 128 and inv is None  # the tcgen05 path: tensor-bound
-    if prefill:
-        work_per_launch = prefill_flops(wl)
-        peak, peak_kind = measured_peaks("bf16_tflops_sustained")
-        achieved = work_per_launch / (score_ms * 1e-3) / 1e12
-        roof = {"bound": "tensor", "unit": "TFLOP/s", "flops_per_launch": work_per_launch,
-                "kernel": "prefill candidate pass (tcgen05 kind::f16 M128 N128, TMEM accumulators, "
-                          "threshold epilogue)",
-                "peak_note": "sustained bf16 GEMM peak: the kernel runs inside a long step loop"}
-    else:
-        work_per_launch = (stop - start) * wl.B * wl.Hkv * wl.D * 2  # keys of this rank, read once
-        peak, peak_kind = measured_peaks()
-        achieved = work_per_launch / (score_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "unit": "GB/s", "bytes_per_launch": work_per_launch,
-                "kernel": "decode scorer (TMA ring, fused inverse RoPE, fp32 q·K^T)"}
-    achieved = max_over_ranks(-achieved) * -1.0 if world > 1 else achieved  # slowest rank
-
-    value = wl.Sk * args.steps / (ms * 1e-3)
+    n_sc, t_sc = ktimes["score"]
+    score_ms = ranks.max(t_sc / max(1, n_sc))  # the slowest rank's scorer launch
+    res = {"wl": wl, "start": start, "stop": stop, "ms": ms, "ms_per_step": ms / args.steps,
+           "score_ms": score_ms,
+           "value": wl.Sk * args.steps / (ms * 1e-3), "launches": int(round(launches_per_step * args.steps)),
+           "launches_per_step": launches_per_step, "ktimes": ktimes,
+           "clocks": clocks.summary() if clocks else None, "chunks": chunks,
+           "exchange": "peer" if exchange is not None else ("nccl" if world > 1 else None)}
 
     # ---- end to end through the public call, host buffers ----
-    e2e = None
-    if not args.no_e2e:
+    if e2e:
         q_h = q.cpu().pin_memory()
         k_h = k.cpu().pin_memory()
         rows = wl.B * wl.Hq * wl.Sq
@@ -589,7 +653,8 @@ def main():
         k_d = torch.empty_like(k)
         v_h = v.cpu().pin_memory() if v is not None else None
         v_d = torch.empty_like(v) if v is not None else None
-        for _ in range(2):
+
+        def e2e_step():
             q_d.copy_(q_h, non_blocking=True)
             k_d.copy_(k_h, non_blocking=True)
             if v_d is not None:
@@ -597,73 +662,156 @@ def main():
             oi, os_ = step(q_d, k_d, v_d)
             idx_h.copy_(oi.reshape(-1), non_blocking=True)
             sc_h.copy_(os_.reshape(-1), non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
         torch.cuda.synchronize()
-        barrier()
+        ranks.barrier()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
-            q_d.copy_(q_h, non_blocking=True)
-            k_d.copy_(k_h, non_blocking=True)
-            if v_d is not None:
-                v_d.copy_(v_h, non_blocking=True)
-            oi, os_ = step(q_d, k_d, v_d)
-            idx_h.copy_(oi.reshape(-1), non_blocking=True)
-            sc_h.copy_(os_.reshape(-1), non_blocking=True)
+            e2e_step()
         e1.record()
         torch.cuda.synchronize()
-        barrier()
+        ranks.barrier()
         torch.cuda.synchronize()
-        ems = max_over_ranks(e0.elapsed_time(e1))
-        e2e = {"value": wl.Sk * args.steps / (ems * 1e-3), "unit": UNIT,
-               "h2d_bytes_per_step": int(q_h.numel() * q_h.element_size() + k_h.numel() * k_h.element_size()
-                                         + (v_h.numel() * v_h.element_size() if v_h is not None else 0)) * world,
-               "d2h_bytes_per_step": int(idx_h.numel() * 4 + sc_h.numel() * 4) * world,
-               "ms_per_step": ems / args.steps}
+        ems = ranks.max(e0.elapsed_time(e1))
+        res["e2e"] = {"value": wl.Sk * args.steps / (ems * 1e-3), "unit": UNIT,
+                      "h2d_bytes_per_step": int(q_h.numel() * q_h.element_size() + k_h.numel() * k_h.element_size()
+                                                + (v_h.numel() * v_h.element_size() if v_h is not None else 0)) * world,
+                      "d2h_bytes_per_step": int(idx_h.numel() * 4 + sc_h.numel() * 4) * world,
+                      "ms_per_step": ems / args.steps}
+        del q_h, k_h, v_h, q_d, k_d, v_d
 
-    base = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        base = cpu_baseline(wl, recall_type=rt)
+    if cpu_base and rank == 0 and world == 1:
+        res["cpu_baseline"] = cpu_baseline(wl, recall_type=rt)
 
-    exchange_status = None
+    # ---- the result of one more step, checked (not timed) ----
+    idx, sc = step(q, k)
+    torch.cuda.synchronize()
+    res["parity"] = result_check(wl, ranks, x, v, idx, sc, rt)
     if exchange is not None:
-        exchange_status = max_over_ranks(float(exchange.status()))
+        res["exchange_status"] = int(ranks.max(float(exchange.status())))
         exchange.close()
+    del x, q, k, v, idx, sc
+    torch.cuda.empty_cache()
+    return res
+
+
+def roofline_of(res, rt="qk") -> tuple:
+    """(roofline of the dominant kernel, roofline of the whole step) of one measurement."""
+    wl = res["wl"]
+    score_ms = res["score_ms"]
+    prefill = wl.Sq >= 128 and not wl.rope  # the tcgen05 path: tensor-bound
+    if prefill:
+        work = prefill_flops(wl)
+        peak, src = measured_peaks("bf16_tflops_sustained")
+        achieved = work / (score_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "unit": "TFLOP/s", "flops_per_launch": work,
+                "kernel": "prefill candidate pass (tcgen05 kind::f16 M128 N128, TMEM accumulators, "
+                          "threshold epilogue)",
+                "peak_note": "sustained bf16 GEMM peak: the kernel runs inside a long step loop"}
+        step_work = work
+        step_achieved = work / (res["ms_per_step"] * 1e-3) / 1e12
+    else:
+        work = (res["stop"] - res["start"]) * wl.B * wl.Hkv * wl.D * 2  # keys of this rank, read once
+        peak, src = measured_peaks()
+        achieved = work / (score_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "unit": "GB/s", "bytes_per_launch": work,
+                "kernel": "decode scorer (TMA ring, fused inverse RoPE, fp32 q·K^T)"}
+        step_work = work
+        step_achieved = work / (res["ms_per_step"] * 1e-3) / 1e9
+    roof.update(achieved=achieved, peak=peak, frac=achieved / peak, peak_source=src,
+                traffic=ncu_traffic("score", wl.name) if res["stop"] - res["start"] == wl.Sk else None,
+                launch_ms=score_ms)
+    step_roof = {"what": "the whole step (score + select (+ exchange and merge)) against the same "
+                         "algorithmic work and peak", "achieved": step_achieved, "peak": peak,
+                 "unit": roof["unit"], "frac": step_achieved / peak, "work_per_step": step_work}
+    return roof, step_roof
+
+
+def kernels_ms(res, steps):
+    return {name: t / max(1, steps) for name, (n, t) in res["ktimes"].items()}
+
+
+def sub_record(res, args) -> dict:
+    """A compact record of a secondary workload measured in the same run."""
+    wl = res["wl"]
+    roof, step_roof = roofline_of(res, args.recall_type)
+    return {"workload": wl.name, "value": res["value"], "unit": UNIT, "ms_per_step": res["ms_per_step"],
+            "config": config_of(wl, res_world(res), args.recall_type, res["exchange"] or "peer"),
+            "roofline": roof, "step_roofline": step_roof, "kernels_ms_per_step": kernels_ms(res, args.steps),
+            "gpu_launches_per_step": res["launches_per_step"], "parity": res["parity"],
+            **({"exchange_status": res["exchange_status"]} if "exchange_status" in res else {})}
+
+
+def res_world(res):
+    wl = res["wl"]
+    return max(1, wl.Sk // max(1, res["stop"] - res["start"]))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.stage == "attention":
+        return run_attention(args)
+    if args.stage == "merge":
+        return run_merge(args)
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        # generous: rank 0 checks the result against the CPU oracle while the others wait
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
+    from prism_test_b200 import workloads as W
+    ranks = Ranks(world, rank, local, dev)
+    rt = args.recall_type
+    wl = pick_workload(args, world)
+    main_res = measure(wl, args, ranks, e2e=not args.no_e2e, cpu_base=not args.no_cpu_baseline, clocks_on=True)
+    subs = {}
+    if args.workload is None and not args.no_sub:
+        # the 128K decode step at N = 1, and the shared-context workload at every N
+        names = (["decode-128k"] if world == 1 else []) + ["shared-context-256k"]
+        for name in names:
+            subs[name.replace("-", "_")] = sub_record(
+                measure(W.WORKLOADS[name], args, ranks, e2e=False, cpu_base=False, clocks_on=False), args)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    roof, step_roof = roofline_of(main_res, rt)
+    prefill = wl.Sq >= 128 and not wl.rope
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak" if world == 1 else "strong", "vs_baseline": None,
+        "metric": METRIC, "value": main_res["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": main_res["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong" if wl.name == "decode-1m-sharded" or world > 1 else "weak", "vs_baseline": None,
         "dtype": "bf16 in, fp32 accumulate (tcgen05)" if prefill else "f32 (tf32 MMA)",
         "data": "synthetic (seeded; see prism_test_b200/workloads.py)",
-        "config": config_of(wl, world, rt, "peer" if exchange is not None else "nccl"),
-        "roofline": dict(roof, achieved=achieved, peak=peak, frac=achieved / peak,
-                         peak_source=peak_kind, traffic=ncu_traffic("score", wl.name),
-                         launch_ms=score_ms),
-        "kernels_ms_per_step": {
-            "score": t_sc.value / max(1, args.steps),
-            "select": t_se.value / max(1, args.steps),
-            "merge": t_me.value / max(1, args.steps),
-            "value_norms": t_we.value / max(1, args.steps),
-            "score_weighting": t_sa.value / max(1, args.steps),
-            "threshold": t_th.value / max(1, args.steps),
-        },
-        "gpu_launches": int(launches),
+        "config": config_of(wl, world, rt, main_res["exchange"] or "peer"),
+        "roofline": roof,
+        "step_roofline": step_roof,
+        "kernels_ms_per_step": kernels_ms(main_res, args.steps),
+        "gpu_launches": main_res["launches"],
         "timing": "CUDA graph of one call, replayed",
-        "clocks": clocks.summary(),
-        "e2e": e2e,
-        "cpu_baseline": base,
+        "clocks": main_res["clocks"],
+        "e2e": main_res.get("e2e"),
+        "cpu_baseline": main_res.get("cpu_baseline"),
+        "parity": main_res["parity"],
     }
-    if exchange_status is not None:
-        line["exchange_status"] = int(exchange_status)  # 0: every bounded peer wait succeeded
+    if "exchange_status" in main_res:
+        line["exchange_status"] = main_res["exchange_status"]  # 0: every bounded peer wait succeeded
+    line.update(subs)
     print(json.dumps(line), flush=True)
-    return 0
+    ok = main_res["parity"]["ok"] and all(s["parity"].get("ok", False) for s in subs.values())
+    return 0 if ok else 1
 
 
 if __name__ == "__main__":
