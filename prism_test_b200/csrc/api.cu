@@ -33,6 +33,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 constexpr size_t kStatusBytes = 256;  // status word + padding, keeps scores 256-B aligned
+constexpr size_t kWorkOffset = 64;    // decode scorer work counters inside the status block
+constexpr int64_t kMaxWorkCounters = (kStatusBytes - kWorkOffset) / 4;
 constexpr int64_t kMaxPosition = int64_t(1) << 22;
 
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
@@ -210,7 +212,10 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
   int* status = reinterpret_cast<int*>(ws);
   float* scores = reinterpret_cast<float*>(ws + kStatusBytes);
   const int64_t ld = round_up(Sk, 4);
-  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream);
+  // the status block holds the status word and, from byte kWorkOffset, the decode
+  // scorer's work counters (one per batch row); one memset clears what is used
+  const bool dyn_work = !streaming && B <= kMaxWorkCounters;
+  cudaError_t e = cudaMemsetAsync(status, 0, dyn_work ? kWorkOffset + size_t(B) * 4 : sizeof(int), stream);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
 
   const int nsm = num_sms_current_device();
@@ -278,6 +283,7 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
     return PRISM_OK;
   }
   if (prism::decode_hp_supported(a, dtype)) {
+    a.work = dyn_work ? reinterpret_cast<unsigned int*>(ws + kWorkOffset) : nullptr;
     e = launch_counted(PRISM_KERNEL_SCORE, stream,
                        [&] { return prism::launch_decode_scores_hp(a, nsm, stream); });
     if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");

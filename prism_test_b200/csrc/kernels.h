@@ -27,6 +27,7 @@ struct DecodeArgs {
   int64_t ld;
   int ntiles;
   int* status;
+  unsigned int* work;       // nullptr, or B work counters, zero at launch (dynamic slice claims)
 };
 
 // rows (Hq * sq_n) resident per CTA must not exceed this

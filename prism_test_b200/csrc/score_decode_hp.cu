@@ -54,6 +54,8 @@ struct __align__(16) HpTail {
   // MMA of head pair hp, as fp32 (bf16 queries are exact in TF32)
   float2 bfrag[kMaxPairs][16][32];
   uint64_t full[kWarps][kStages];
+  int slice_of[kWarps][4];  // the warp's q-th slice (q mod 4), written by its lane 0 at the claim
+  unsigned int next;         // next unclaimed slice of this CTA's range
 };
 
 __device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -65,7 +67,7 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <bool kRope>
+template <bool kRope, bool kDyn>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_hp_kernel(const __grid_constant__ CUtensorMap kmap, const DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -85,11 +87,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* ring = smem + warp * kStages * copy_bytes;
   uint64_t* full = tail->full[warp];
 
-  // blocks of this warp: a contiguous range of the row's kPc-position slices
+  // Work: slices of kPc positions (all KV heads). Static (kDyn false): each warp
+  // streams a fixed contiguous range. Dynamic (long rows, many slices per warp):
+  // two levels, so that warps and SMs that stream faster take more slices and all
+  // finish together — the first 7/8 of the slices are split into one contiguous
+  // range per CTA, whose warps take them one at a time from a shared-memory
+  // counter (a warp's first slice is fixed: the range start plus its warp
+  // number); the last 1/8 is a pool that CTAs done with their range claim from a
+  // global counter per batch row (a.work, zero at launch). A slice is claimed
+  // when lane 0 issues its first copy.
   const int nsub = (a.Sk + kPc - 1) / kPc;
   const int64_t gw = int64_t(blockIdx.x) * kWarps + warp, nw = int64_t(gridDim.x) * kWarps;
   const int i_begin = int(gw * nsub / nw), i_end = int((gw + 1) * nsub / nw);
   const int ncopies = (i_end - i_begin) * copies;
+  unsigned int* const work = kDyn ? a.work + blockIdx.y : nullptr;
+  const int nstat = nsub - nsub / 8;
+  const int cta_begin = int(int64_t(blockIdx.x) * nstat / gridDim.x);
+  const int cta_end = int(int64_t(blockIdx.x + 1) * nstat / gridDim.x);
+  int* const slice_of = tail->slice_of[warp];
+  bool first = true;       // lane 0: the warp's first claim
+  bool exhausted = false;  // lane 0: no slice left to issue
+  auto claim = [&]() -> int {
+    if (first) {
+      first = false;
+      if (cta_begin + warp < cta_end) return cta_begin + warp;
+    }
+    const int v = int(atomicAdd(&tail->next, 1u));
+    if (v < cta_end) return v;
+    const int w = nstat + int(atomicAdd(work, 1u));
+    return w < nsub ? w : nsub;
+  };
+  if (kDyn) {
+    if (tid == 0) tail->next = unsigned(cta_begin + kWarps);
+    __syncthreads();
+  }
 
   asm volatile("griddepcontrol.launch_dependents;");
   if (lane == 0) {
@@ -100,17 +131,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
 
   const int kb_coord = (a.B > 1 && a.k_sb != 0) ? b : 0;
-  // copy t of this warp: sub-tile i_begin + t / copies, heads [part * 2ppc, +2ppc)
+  // copy t of this warp (lane 0): part t % copies (heads [part * 2ppc, +2ppc)) of
+  // the warp's (t / copies)-th slice, claimed with its first part
   auto issue = [&](int t, int s) {
-    const uint64_t pol = l2_policy_evict_first();
-    const int i = i_begin + (t >> cshift);
+    const int q = t >> cshift;
     const int part = t & (copies - 1);
+    int i;
+    if (!kDyn) {
+      if (t >= ncopies) return;
+      i = i_begin + q;
+    } else {
+      if (exhausted) return;
+      if (part == 0) {
+        i = claim();
+        slice_of[q & 3] = i;
+        if (i >= nsub) {
+          exhausted = true;
+          return;
+        }
+      } else {
+        i = slice_of[q & 3];
+      }
+    }
+    const uint64_t pol = l2_policy_evict_first();
     mbar_arrive_expect_tx(&full[s], copy_bytes);
     tma_load_4d(ring + s * copy_bytes, &kmap, 0, i * kPc, part * 2 * ppc, kb_coord, &full[s], pol);
   };
   if (lane == 0) {
-    for (int t = 0; t < kStages && t < ncopies; ++t) issue(t, t);
+    for (int t = 0; t < kStages; ++t) issue(t, t);
   }
+  __syncwarp();
 
   // ---- per-lane constants ------------------------------------------------------------
   // this lane's 16 frequencies (pairs 16c + 2i, 16c + 2i + 1)
@@ -160,7 +210,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t lane_off = uint32_t(g) * kRowBytes + 32 * c;
 
   int t = 0;  // copies consumed
-  for (int i = i_begin; i < i_end; ++i) {
+  for (int qs = 0;; ++qs) {
+    // dynamic: the slice lane 0 claimed (written before an earlier __syncwarp)
+    const int i = kDyn ? slice_of[qs & 3] : i_begin + qs;
+    if (kDyn ? i >= nsub : i >= i_end) break;
     // cos/sin of this lane's 16 pairs at its position in each sub-tile (overlaps
     // the copy), pre-scaled for the truncating TF32 operand
     // (each value twice: the packed FMAs below pair the two heads of a head
@@ -192,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (slot == 0) {
         if (hp > 0) {  // release the previous copy of this block
           __syncwarp();
-          if (lane == 0 && t - 1 + kStages < ncopies) issue(t - 1 + kStages, (t - 1) % kStages);
+          if (lane == 0) issue(t - 1 + kStages, (t - 1) % kStages);
         }
         const int s = t % kStages;
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (t / kStages) & 1))) {
@@ -257,13 +310,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float v1 = hsel ? acc0[3] + acc1[3] : acc0[1] + acc1[1];
         if (pos < a.Sk) {
           const int64_t ro = row_base + int64_t(hp) * pair_stride;
-          if (wr0) a.scores[ro + pos] = int64_t(pos) > vis0 ? -INFINITY : v0;
-          if (wr1) a.scores[ro + row1_delta + pos] = int64_t(pos) > vis1 ? -INFINITY : v1;
+          const float s0 = int64_t(pos) > vis0 ? -INFINITY : v0;
+          const float s1 = int64_t(pos) > vis1 ? -INFINITY : v1;
+          if (wr0) a.scores[ro + pos] = s0;
+          if (wr1) a.scores[ro + row1_delta + pos] = s1;
         }
       }
     }
     __syncwarp();  // every lane is done with the last copy of this block
-    if (lane == 0 && t - 1 + kStages < ncopies) issue(t - 1 + kStages, (t - 1) % kStages);
+    if (lane == 0) issue(t - 1 + kStages, (t - 1) % kStages);
+    if (kDyn) __syncwarp();  // the claims lane 0 just made are visible to the warp
   }
 }
 
@@ -275,7 +331,12 @@ size_t hp_smem_bytes(int Hkv) {
 template <bool kRope>
 cudaError_t launch_hp(const DecodeArgs& a, int num_sms, cudaStream_t stream) {
   const size_t smem = hp_smem_bytes(a.Hkv);
-  auto kern = decode_hp_kernel<kRope>;
+  const int nsub_ = (a.Sk + kPc - 1) / kPc;
+  const int ctas_ = a.B > 1 ? (num_sms + a.B - 1) / a.B : num_sms;
+  // dynamic distribution once each warp has many slices (long rows): its claims
+  // cost less than the imbalance they remove
+  const bool dyn = a.work != nullptr && nsub_ >= 16 * ctas_ * kWarps;
+  auto kern = dyn ? decode_hp_kernel<kRope, true> : decode_hp_kernel<kRope, false>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;

@@ -55,6 +55,8 @@ struct SelectSmem {
   unsigned long long rthr;      // run merge: threshold candidate
   uint32_t big;           // largest fine bin
   int ncand;
+  uint32_t fcount[4], fkmax[4];  // fast path: every cluster CTA's candidates and largest key
+  uint32_t nsamp;         // fast path: sampled columns of the row
 };
 
 __device__ __forceinline__ uint64_t pack_cand(uint32_t key, uint32_t idx) {
@@ -309,6 +311,44 @@ __device__ __forceinline__ void load_keys(const float* sc, int64_t base, int64_t
   }
 }
 
+// load_keys in two halves: the loads are issued first (raw fp32, absent columns
+// as NaN placeholders) and converted later, so that other work can overlap them.
+__device__ __forceinline__ void load_raw(const float* sc, int64_t base, int64_t n, float4 (&v)[kKeys / 4]) {
+#pragma unroll
+  for (int u = 0; u < kKeys / 4; ++u) {
+    const int64_t e = base + (int64_t(u * kThreads + int(threadIdx.x)) << 2);
+    if (e + 4 <= n) {
+      v[u] = __ldcg(reinterpret_cast<const float4*>(sc + e));
+    } else {
+      v[u].x = e + 0 < n ? sc[e + 0] : 0.f;
+      v[u].y = e + 1 < n ? sc[e + 1] : 0.f;
+      v[u].z = e + 2 < n ? sc[e + 2] : 0.f;
+      v[u].w = e + 3 < n ? sc[e + 3] : 0.f;
+    }
+  }
+}
+__device__ __forceinline__ void convert_raw(const float4 (&v)[kKeys / 4], int64_t base, int64_t n,
+                                            uint32_t (&kv)[kKeys]) {
+  if (base + int64_t(kThreads) * kKeys <= n) {  // every column of this CTA's pass exists
+#pragma unroll
+    for (int u = 0; u < kKeys / 4; ++u) {
+      kv[4 * u + 0] = float_to_okey(v[u].x);
+      kv[4 * u + 1] = float_to_okey(v[u].y);
+      kv[4 * u + 2] = float_to_okey(v[u].z);
+      kv[4 * u + 3] = float_to_okey(v[u].w);
+    }
+    return;
+  }
+#pragma unroll
+  for (int u = 0; u < kKeys / 4; ++u) {
+    const int64_t e = base + (int64_t(u * kThreads + int(threadIdx.x)) << 2);
+    kv[4 * u + 0] = e + 0 < n ? float_to_okey(v[u].x) : 0u;
+    kv[4 * u + 1] = e + 1 < n ? float_to_okey(v[u].y) : 0u;
+    kv[4 * u + 2] = e + 2 < n ? float_to_okey(v[u].z) : 0u;
+    kv[4 * u + 3] = e + 3 < n ? float_to_okey(v[u].w) : 0u;
+  }
+}
+
 __device__ __forceinline__ int64_t key_column(int64_t base, int j) {
   return base + (int64_t((j >> 2) * kThreads + int(threadIdx.x)) << 2) + (j & 3);
 }
@@ -380,36 +420,161 @@ __device__ __forceinline__ uint32_t bin_of_position(const SelectSmem& sm, uint32
 constexpr int kSampleBins = 4096;                // 12-bit digits (key >> 20)
 constexpr int kSampleCopies = 4;                 // private copies, one per lane & 3
 constexpr int kSampleStride = kSampleBins + 4;
-// Keys j = 0, 9, 18, 27 of a thread are sampled: column offsets (u*1024 + t)*4 + e
-// for (u, e) = (0, 0), (2, 1), (4, 2), (6, 3) — one column in eight.
-__device__ __forceinline__ bool sampled_key(int j) { return j == 0 || j == 9 || j == 18 || j == 27; }
-
-// Number of sampled columns below n (the same for every CTA of the row).
-__device__ __forceinline__ uint32_t sampled_columns(int64_t n) {
-  uint32_t ns = 0;
-  for (int r = 0; r < kCluster; ++r)
-    for (int u = 0; u < 4; ++u) {
-      const int64_t first = int64_t(r) * kThreads * kKeys + int64_t(2 * u) * kThreads * 4 + u;
-      const int64_t cnt = first < n ? (n - first + 3) / 4 : 0;
-      ns += uint32_t(cnt < kThreads ? cnt : kThreads);
+// Row sample of the fast paths: 8 consecutive columns of every 2^cshift (128 for a
+// row held in registers, 256 for longer rows), at an offset hashed from the chunk
+// number. Every CTA of a cluster reads the same columns and so computes the same
+// threshold on its own, with no exchange: the lower edge of the 12-bit key digit
+// holding sample rank 1.1 e + 4 sqrt(e) + 8, e = k * ns / n the expected sample
+// rank of the k-th key (1 = every key when that rank exceeds the sample). Private
+// histogram copies in sm.buf (zero on entry), the sum in sm.hist.
+// `after_issue` runs once, after the first sample loads are issued (the caller's
+// own loads then queue behind them).
+// Visits every sampled key: f(order key). `after_issue` runs once, after the first
+// loads are issued.
+template <typename F, typename G>
+__device__ __forceinline__ void for_each_sample(const SelectArgs& a, const float* sc, int cshift,
+                                                F&& f, G&& after_issue) {
+  const int tid = threadIdx.x;
+  const int64_t chunk = int64_t(1) << cshift;
+  const int oshift = 32 - (cshift - 3);  // hash -> one of chunk / 8 offsets
+  const int64_t ngroups = (a.n + chunk - 1) >> cshift;
+  for (int64_t g0 = 0; g0 < ngroups; g0 += int64_t(kThreads) * 2) {
+    float4 v[2][2];
+    int64_t e[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t g = g0 + int64_t(u) * kThreads + tid;
+      e[u] = (g << cshift) + 8 * int64_t((uint32_t(g) * 0x9E3779B1u) >> oshift);
+      const bool full = g < ngroups && e[u] + 8 <= a.n;
+      v[u][0] = full ? __ldcg(reinterpret_cast<const float4*>(sc + e[u])) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[u][1] = full ? __ldcg(reinterpret_cast<const float4*>(sc + e[u] + 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!full) e[u] = g < ngroups ? -e[u] - 1 : INT64_MIN;  // partial or absent chunk
     }
-  return ns;
+    if (g0 == 0) after_issue();
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (e[u] == INT64_MIN) continue;
+      const bool full = e[u] >= 0;
+      const int64_t eb = full ? e[u] : -e[u] - 1;
+      const float fv[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w,
+                           v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+#pragma unroll
+      for (int x = 0; x < 8; ++x) {
+        if (eb + x >= a.n) continue;
+        f(float_to_okey(full ? fv[x] : sc[eb + x]));
+      }
+    }
+  }
+}
+
+// `after_issue` runs once, after the first sample loads are issued (the caller's
+// own loads then queue behind them). With `refine`, the sample is read a second
+// time to place the threshold inside its 12-bit digit: the digit's sampled keys
+// are counted by their next 8 key bits and the threshold becomes the lower edge
+// of the sub-digit holding the remaining rank, so the candidates exceed the
+// target by at most 1/256 of a digit instead of a whole digit.
+template <typename F>
+__device__ uint32_t row_sample_threshold_cta(const SelectArgs& a, const float* sc, SelectSmem& sm,
+                                             int cshift, bool refine, F&& after_issue) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  uint32_t* priv = reinterpret_cast<uint32_t*>(sm.buf);
+  uint32_t* my_samp = priv + (lane & (kSampleCopies - 1)) * kSampleStride;
+  uint32_t ns = 0;
+  for_each_sample(a, sc, cshift, [&](uint32_t key) {
+    atomicAdd(&my_samp[key >> 20], 1u);
+    ++ns;
+  }, after_issue);
+  ns = __reduce_add_sync(0xffffffffu, ns);
+  if (lane == 0 && ns) atomicAdd(&sm.nsamp, ns);
+  __syncthreads();
+  for (int i = tid; i < kSampleBins; i += kThreads) {
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int q = 0; q < kSampleCopies; ++q) cnt += priv[q * kSampleStride + i];
+    sm.hist[i] = cnt;
+  }
+  __syncthreads();
+  const double nsd = double(sm.nsamp);
+  const double expect = double(a.k) * nsd / double(a.n);
+  const double m = expect * 1.1 + 4.0 * sqrt(expect) + 8.0;
+  if (!(m < nsd)) return 1u;  // every key
+  find_bin(sm, kSampleBins, uint32_t(m));
+  const uint32_t b = sm.bin;
+  if (!refine) return b << 20;
+  const uint32_t need = uint32_t(m) - sm.above;  // >= 1: rank m lies inside digit b
+  for (int i = tid; i < 256; i += kThreads) sm.hist[i] = 0u;
+  __syncthreads();
+  for_each_sample(a, sc, cshift, [&](uint32_t key) {
+    if ((key >> 20) == b) atomicAdd(&sm.hist[(key >> 12) & 0xffu], 1u);
+  }, [] {});
+  __syncthreads();
+  find_bin(sm, 256, need);
+  return (b << 20) | (sm.bin << 12);
+}
+
+// dst[0, n) = src[0, n) (global, L2) with eight loads of each thread in flight,
+// every candidate also counted into its fine bin of [thr, kmax] (sm.hist zero on
+// entry).
+__device__ __forceinline__ void copy_in_counted(SelectSmem& sm, uint64_t* dst, const uint64_t* src,
+                                                uint32_t n, uint32_t kmax, int shift) {
+  for (uint32_t b = 0; b < n; b += 8 * kThreads) {
+    uint64_t v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t i = b + u * kThreads + threadIdx.x;
+      v[u] = i < n ? __ldcg(src + i) : 0ull;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t i = b + u * kThreads + threadIdx.x;
+      if (i < n) {
+        dst[i] = v[u];
+        atomicAdd(&sm.hist[(kmax - uint32_t(v[u] >> 32)) >> shift], 1u);
+      }
+    }
+  }
+}
+
+// Warp-aggregated slot of this thread's first hit among the CTA's candidates
+// (sm.woff counts the CTA's candidates so far).
+__device__ __forceinline__ uint32_t hit_slot(uint32_t hit, SelectSmem& sm) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t mine = __popc(hit);
+  uint32_t incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
+  uint32_t wbase = 0;
+  if (lane == 31 && wtot) wbase = atomicAdd(&sm.woff, wtot);
+  return __shfl_sync(0xffffffffu, wbase, 31) + incl - mine;
 }
 
 // Every CTA of the cluster holds all nc candidates in sm.buf (identical slots).
 // Fine-bin counting sort as on the general leader path; CTA r then ranks and
 // stores the whole bins that cover output positions [r*P, (r+1)*P), P = ceil(k/4).
 // A straddling bin is ranked by both neighbours, which store identical values.
-__device__ void replicated_sort_store(const SelectArgs& a, int64_t row, SelectSmem& sm,
-                                      uint32_t nc, uint32_t thr, uint32_t kmax, unsigned rank,
-                                      unsigned nparts = kCluster) {
-  const int tid = threadIdx.x, lane = tid & 31;
+// Fine-bin width (as a shift of the key difference) for candidates in [thr, kmax].
+__device__ __forceinline__ int fine_shift(uint32_t thr, uint32_t kmax) {
   const uint32_t range = kmax - thr;
   int shift = 0;
   while ((range >> shift) >= uint32_t(kFineBins)) ++shift;
-  for (uint32_t i = tid; i < nc; i += kThreads)
-    atomicAdd(&sm.hist[(kmax - uint32_t(sm.buf[i] >> 32)) >> shift], 1u);
-  __syncthreads();
+  return shift;
+}
+
+// With `built`, sm.hist already holds the fine-bin counts of the nc candidates.
+__device__ void replicated_sort_store(const SelectArgs& a, int64_t row, SelectSmem& sm,
+                                      uint32_t nc, uint32_t thr, uint32_t kmax, unsigned rank,
+                                      unsigned nparts = kCluster, bool built = false) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int shift = fine_shift(thr, kmax);
+  if (!built) {
+    for (uint32_t i = tid; i < nc; i += kThreads)
+      atomicAdd(&sm.hist[(kmax - uint32_t(sm.buf[i] >> 32)) >> shift], 1u);
+    __syncthreads();
+  }
   {
     constexpr int kPer = kFineBins / kThreads;
     uint32_t h[kPer], tot = 0, hmax = 0;
@@ -510,12 +675,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   SelectSmem* lead = cluster.map_shared_rank(&sm, 0);
   uint32_t* lead_slice = cluster.map_shared_rank(sm.hist, 0) + rank * kLevelBins;
 
+  static_assert(kPriv * kPrivStride >= kSampleCopies * kSampleStride, "sample copies fit the private histograms");
   for (int i = tid; i < kPriv * kPrivStride; i += kThreads) priv[i] = 0u;
-  for (int i = tid; i < kSampleBins; i += kThreads) sm.hist[i] = 0u;
   if (tid == 0) {
     sm.kmax = 0;
     sm.woff = 0;
     sm.big = 0;
+    sm.nsamp = 0;
   }
   if (tid < kCluster) sm.acc[tid] = 0;
   __syncthreads();
@@ -523,118 +689,131 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
   grid_dependency_wait();
   asm volatile("griddepcontrol.launch_dependents;");  // e.g. the publish of the peer exchange
   uint32_t kv[kKeys];
-  if (kResident) load_keys(sc, my_base, a.n, kv);
+  float4 raw[kKeys / 4];
 
-  if (kResident) {
-    // ---- fast path: threshold from a 1/8 sample, candidates in every CTA -------------
-    uint32_t* my_samp = priv + (lane & (kSampleCopies - 1)) * kSampleStride;
+  {
+    // ---- fast path -------------------------------------------------------------------
+    // Every CTA computes the threshold T from the same row sample; its keys >= T
+    // are its candidates. The CTAs tell each other their counts; when the row's
+    // total is within [k, kCap], each CTA appends its candidates to its slot range
+    // of the row's candidate buffer (L2), and after a cluster barrier every CTA
+    // loads all of them, counting-sorts them and stores its quarter of the output.
+    // Rows longer than one pass stream their keys once, appending the hits to the
+    // CTA's quarter of the buffer.
+    uint64_t* cand = cand_all + row * cand_cap;
+    // the row's own keys are loaded (rows held in registers) while the sample is
+    // counted, their loads queued behind the sample's
+    const uint32_t thr = row_sample_threshold_cta(a, sc, sm, kResident ? 7 : 8, !kResident, [&] {
+      if (kResident) load_raw(sc, my_base, a.n, raw);
+    });
+    const uint32_t quarter = uint32_t(cand_cap / kCluster);
     uint32_t kmx = 0;
+    uint32_t hit = 0, slot0 = 0;
+    if (kResident) {
+      convert_raw(raw, my_base, a.n, kv);
 #pragma unroll
-    for (int j = 0; j < kKeys; ++j) {
-      kmx = max(kmx, kv[j]);
-      if (sampled_key(j) && kv[j] != 0u) atomicAdd(&my_samp[kv[j] >> 20], 1u);
+      for (int j = 0; j < kKeys; ++j) {
+        kmx = max(kmx, kv[j]);
+        if (kv[j] >= thr) hit |= 1u << j;
+      }
+      slot0 = hit_slot(hit, sm);
+    } else {
+      uint64_t* mine_buf = cand + int64_t(rank) * quarter;
+      for (int64_t p = 0; p < npass; ++p) {
+        uint32_t kp[kKeys];
+        const int64_t base = p * kPass + my_base;
+        load_keys(sc, base, a.n, kp);
+        uint32_t h = 0;
+#pragma unroll
+        for (int j = 0; j < kKeys; ++j) {
+          kmx = max(kmx, kp[j]);
+          if (kp[j] >= thr) h |= 1u << j;
+        }
+        const uint32_t slot = hit_slot(h, sm);
+        if (h != 0u && slot + uint32_t(__popc(h)) <= quarter) {
+          uint64_t* dst = mine_buf + slot;
+#pragma unroll
+          for (int j = 0; j < kKeys; ++j) {
+            if (h & (1u << j)) {
+              const int64_t col = key_column(base, j);
+              dst[__popc(h & ((1u << j) - 1u))] = pack_cand(kp[j], ix ? uint32_t(ix[col]) : uint32_t(col));
+            }
+          }
+        }
+      }
     }
     kmx = __reduce_max_sync(0xffffffffu, kmx);
     if (lane == 0) atomicMax(&sm.kmax, kmx);
     __syncthreads();
-    cluster_wait();  // the leader's histogram is zeroed
-    uint32_t* lead_hist = cluster.map_shared_rank(sm.hist, 0);
-    for (int i = tid; i < kSampleBins; i += kThreads) {
-      uint32_t c = 0;
-#pragma unroll
-      for (int q = 0; q < kSampleCopies; ++q) c += priv[q * kSampleStride + i];
-      if (c) atomicAdd(&lead_hist[i], c);
+    // every CTA's count and largest key to every CTA (the first wait completes the
+    // kernel-start barrier phase: every CTA has started)
+    cluster_wait();
+    if (tid < kCluster) {
+      SelectSmem* peer = cluster.map_shared_rank(&sm, tid);
+      peer->fcount[rank] = sm.woff;
+      peer->fkmax[rank] = sm.kmax;
     }
-    if (tid == 0) atomicMax(&lead->kmax, sm.kmax);
-    cluster.sync();  // the sample histogram is complete
-    if (rank == 0) {
-      // threshold: lower edge of the digit holding sample rank m, a margin of 10%
-      // plus four binomial deviations below the expected rank of the k-th key
-      const double ns = double(sampled_columns(a.n));
-      const double expect = double(a.k) * ns / double(a.n);
-      const double m = expect * 1.1 + 4.0 * sqrt(expect) + 8.0;
-      if (m < ns) {
-        find_bin(sm, kSampleBins, uint32_t(m));
-        if (tid == 0) sm.thr = sm.bin << 20;
-      } else if (tid == 0) {
-        sm.thr = 1u;  // every key
-      }
-      if (tid == 0) sm.count = 0;
+    cluster_arrive();
+    cluster_wait();
+    uint32_t total = 0, cbase = 0, kmax = 0, most = 0;
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) {
+      if (r < int(rank)) cbase += sm.fcount[r];
+      total += sm.fcount[r];
+      most = max(most, sm.fcount[r]);
+      kmax = max(kmax, sm.fkmax[r]);
     }
-    cluster.sync();  // threshold ready
-    if (tid == 0) {
-      sm.thr = lead->thr;
-      sm.kmax = lead->kmax;
-    }
-    __syncthreads();
-    const uint32_t fthr = sm.thr;
-    uint32_t hit = 0;
+    // the same decision in every CTA of the cluster
+    if (total >= uint32_t(a.k) && total <= uint32_t(kCap) && (kResident || most <= quarter)) {
+      const int shift = fine_shift(thr, kmax);
+      for (int i = tid; i < kFineBins; i += kThreads) sm.hist[i] = 0u;  // the sort's fine bins
+      if (tid == 0) sm.big = 0;
+      if (kResident) {
+        // this CTA's candidates, compacted in its candidate space first (free: the
+        // sample's private histograms are summed), then stored to its slot range
+        // with coalesced stores
+        uint64_t* stage = sm.buf;
+        const uint32_t ncta = sm.fcount[rank];
+        // a hit's slot follows from the hit mask (no running count), its column
+        // from the key layout
+        uint64_t* dst = stage + slot0;
+        const uint32_t colbase = uint32_t(my_base) + uint32_t(tid) * 4u;
+        if (ix == nullptr) {
 #pragma unroll
-    for (int j = 0; j < kKeys; ++j)
-      if (kv[j] >= fthr) hit |= 1u << j;
-    const uint32_t mine = __popc(hit);
-    uint32_t incl = mine;
+          for (int j = 0; j < kKeys; ++j)
+            if (hit & (1u << j))
+              dst[__popc(hit & ((1u << j) - 1u))] =
+                  pack_cand(kv[j], colbase + uint32_t((j >> 2) * kThreads * 4 + (j & 3)));
+        } else {
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
-    uint32_t wbase = 0;
-    if (lane == 31 && wtot) wbase = atomicAdd(&sm.woff, wtot);
-    wbase = __shfl_sync(0xffffffffu, wbase, 31);
-    __syncthreads();
-    if (tid == 0) sm.cbase = sm.woff ? atomicAdd(&lead->count, sm.woff) : 0u;
-    __syncthreads();
-    uint64_t* rbuf[kCluster];
-#pragma unroll
-    for (int r = 0; r < kCluster; ++r) rbuf[r] = cluster.map_shared_rank(sm.buf, r);
-    // this CTA's candidates are compacted in its fine-bin histogram space first
-    // (free until the sort), then copied to every CTA with coalesced stores
-    uint64_t* stage = reinterpret_cast<uint64_t*>(sm.hist);
-    const uint32_t ncta = sm.woff, cbase = sm.cbase;
-    const bool staged = ncta <= uint32_t(kFineBins / 2);
-    uint32_t slot = (staged ? 0u : cbase) + wbase + incl - mine;
-#pragma unroll
-    for (int j = 0; j < kKeys; ++j) {
-      if (hit & (1u << j)) {
-        const int64_t col = key_column(my_base, j);
-        const uint64_t v = pack_cand(kv[j], ix ? uint32_t(ix[col]) : uint32_t(col));
-        if (staged) {
-          stage[slot] = v;
-        } else if (slot < uint32_t(kCap)) {
-#pragma unroll
-          for (int r = 0; r < kCluster; ++r) rbuf[r][slot] = v;
+          for (int j = 0; j < kKeys; ++j)
+            if (hit & (1u << j))
+              dst[__popc(hit & ((1u << j) - 1u))] =
+                  pack_cand(kv[j], uint32_t(ix[colbase + uint32_t((j >> 2) * kThreads * 4 + (j & 3))]));
         }
-        ++slot;
-      }
-    }
-    if (staged) {
-      __syncthreads();
-      for (uint32_t i = tid; i < ncta; i += kThreads) {
-        const uint64_t v = stage[i];
-        if (cbase + i < uint32_t(kCap)) {
-#pragma unroll
-          for (int r = 0; r < kCluster; ++r) rbuf[r][cbase + i] = v;
+        __syncthreads();
+        for (uint32_t i = tid; i < ncta; i += kThreads) cand[cbase + i] = stage[i];
+        cluster_arrive();  // the candidate stores are visible to the cluster after the wait
+        cluster_wait();
+        copy_in_counted(sm, sm.buf, cand, total, kmax, shift);
+      } else {
+        __syncthreads();  // the fine bins are zero
+        uint32_t off = 0;
+#pragma unroll 1
+        for (int r = 0; r < kCluster; ++r) {
+          copy_in_counted(sm, sm.buf + off, cand + int64_t(r) * quarter, sm.fcount[r], kmax, shift);
+          off += sm.fcount[r];
         }
       }
-    }
-    cluster.sync();  // every CTA holds all candidates
-    if (tid == 0) sm.count = lead->count;
-    __syncthreads();
-    const uint32_t total = sm.count;
-    if (total >= uint32_t(a.k) && total <= uint32_t(kCap)) {
-      for (int i = tid; i < kFineBins; i += kThreads) sm.hist[i] = 0u;  // was the staging area
       __syncthreads();
-      replicated_sort_store(a, row, sm, total, fthr, sm.kmax, rank);
+      replicated_sort_store(a, row, sm, total, thr, kmax, rank, kCluster, true);
       return;
     }
-    // the sample missed (fewer than k keys above the threshold, or more than kCap):
-    // take the exact path below from a clean state
+    // the sample missed (fewer than k keys above the threshold, or more than the
+    // buffer holds): the exact path below, from a clean state
+    __syncthreads();
     for (int i = tid; i < kPriv * kPrivStride; i += kThreads) priv[i] = 0u;
     if (tid == 0) sm.woff = 0;
-    cluster.sync();  // nobody reads the leader's counter any more
-    if (tid == 0) sm.count = 0;
     __syncthreads();
     cluster_arrive();
   }

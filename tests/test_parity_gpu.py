@@ -65,6 +65,11 @@ CASES = [
     (1, 32, 8, 5, 2500, 200, True, torch.float16),     # 20 rows per KV head, fp16
     (1, 32, 8, 8, 2500, 200, False, torch.bfloat16),   # 32 rows per KV head, Hkv 8, raw keys
     (2, 28, 4, 6, 1777, 50, True, torch.float16),      # 42 rows, ragged n-tiles, B = 2
+    # the head-pair decode scorer counts the select's threshold sample
+    (3, 32, 8, 1, 9000, 700, True, torch.bfloat16),    # 96 rows: one CTA per row
+    (1, 8, 4, 1, 200000, 2000, True, torch.bfloat16),  # rows longer than one select pass
+    (2, 16, 4, 1, 40001, 4096, True, torch.bfloat16),  # batch 2, ragged length
+    (1, 4, 2, 1, 17, 17, True, torch.bfloat16),        # k = Sk: every key a candidate
 ]
 
 
@@ -178,37 +183,63 @@ def test_full_size_1m_shard(cuda_device):
     check_parity(idx, sc, x["q"], x["k"], wl.topk, x["inv_freq"], x["pos_offset"], index_base=x["index_base"])
 
 
-def _sampled_mask(n):
-    """Columns the select kernel's 1/16 threshold sample reads (white-box)."""
+def _sampled_mask(n, chunk=128):
+    """Columns the select kernels' threshold sample reads (white-box): 8 consecutive
+    columns of every ``chunk`` at an offset hashed from the chunk number — chunk 128
+    for the one-CTA-per-row kernel and for cluster rows held in registers, 256 for
+    longer cluster rows."""
     import numpy as np
-    g = np.arange((n + 127) // 128, dtype=np.uint64)
-    off = ((g * np.uint64(0x9E3779B1)) & np.uint64(0xFFFFFFFF)) >> np.uint64(28)
+    shift = 32 - (chunk // 8).bit_length() + 1
+    g = np.arange((n + chunk - 1) // chunk, dtype=np.uint64)
+    off = ((g * np.uint64(0x9E3779B1)) & np.uint64(0xFFFFFFFF)) >> np.uint64(shift)
     m = np.zeros(n, dtype=bool)
     for gi, o in zip(g.tolist(), off.tolist()):
-        s = 128 * gi + 8 * o
+        s = chunk * gi + 8 * o
         if s + 8 <= n:
             m[s:s + 8] = True
     return torch.from_numpy(m)
 
 
+def _misleading_keys(n, Hkv, mask, sampled_high, seed):
+    """Keys along q's first axis whose magnitudes make the sampled columns all high
+    (too few candidates above the sampled threshold) or all low (too many)."""
+    g = torch.Generator().manual_seed(seed)
+    mag = torch.rand(Hkv, n, generator=g)
+    mag = torch.where(mask[None, :], mag + (2.0 if sampled_high else -2.0), mag)
+    k = torch.zeros(1, Hkv, n, 128)
+    k[0, :, :, 0] = mag
+    k[0, :, :, 1:] = 0.01 * torch.randn(Hkv, n, 127, generator=g)
+    return k
+
+
 @pytest.mark.parametrize("sampled_high", [True, False])
-def test_select_threshold_miss_falls_back_exactly(sampled_high, cuda_device):
-    # keys along q with magnitudes chosen so the sample misleads the threshold:
-    # sampled columns high -> too few candidates; sampled columns low -> too many
-    n, topk = 40000, 3000
-    q = torch.zeros(1, 1, 1, 128)
+@pytest.mark.parametrize("case", ["row-kernel", "cluster", "cluster-long"])
+def test_select_threshold_miss_falls_back_exactly(case, sampled_high, cuda_device):
+    # every threshold sample the select uses, defeated on purpose: the result must
+    # still be the exact top-k (the kernels fall back to the exact radix path)
+    if case == "row-kernel":      # 64 rows: one CTA per row
+        n, topk, Hq, Hkv, mask = 40000, 3000, 64, 1, _sampled_mask(40000)
+    elif case == "cluster":       # 4 rows: one 4-CTA cluster per row, keys in registers
+        n, topk, Hq, Hkv, mask = 100000, 3000, 4, 2, _sampled_mask(100000)
+    else:                         # the same, rows longer than one pass of the cluster
+        n, topk, Hq, Hkv, mask = 300000, 3000, 4, 2, _sampled_mask(300000, 256)
+    q = torch.zeros(1, Hq, 1, 128)
     q[..., 0] = 1.0
-    m = _sampled_mask(n)
-    g = torch.Generator().manual_seed(5)
-    mag = torch.rand(n, generator=g)
-    mag = torch.where(m, mag + (2.0 if sampled_high else -2.0), mag)
-    k = torch.zeros(1, 1, n, 128)
-    k[0, 0, :, 0] = mag
-    k[0, 0, :, 1:] = 0.01 * torch.randn(n, 127, generator=g)
+    k = _misleading_keys(n, Hkv, mask, sampled_high, seed=5)
     q = q.to(torch.bfloat16).to(cuda_device)
     k = k.to(torch.bfloat16).to(cuda_device)
     idx, sc = einsum_topk_func(q, k, topk, return_scores=True)
     check_parity(idx, sc, q, k, topk)
+
+
+def test_full_size_1m_one_gpu(cuda_device):
+    # the whole 1M-key cache on one GPU: rows longer than one select pass, with the
+    # scorer's threshold sample
+    wl = W.WORKLOADS["decode-1m-sharded"]
+    x = W.make_inputs(wl, cuda_device)
+    idx, sc = einsum_topk_func(x["q"], x["k"], wl.topk, inv_freq=x["inv_freq"], return_scores=True)
+    st = check_parity(idx, sc, x["q"], x["k"], wl.topk, x["inv_freq"])
+    assert st["rows"] == 32
 
 
 def test_topk_merge_large_rows(cuda_device):

@@ -15,7 +15,7 @@ import torch
 from prism_test_b200 import _lib, topk_merge
 
 SCRATCH_BYTES = 8 << 20
-KPASS = 131072  # columns the select cluster holds in registers; longer rows take the exact path
+KPASS = 131072  # columns the select cluster holds in registers; longer rows are streamed
 
 
 @pytest.fixture(scope="module")
@@ -48,14 +48,14 @@ def _distinct_rows(rows, n, seed):
 
 
 def _cluster_sampled_mask(n):
-    """Columns the cluster select's 1/8 threshold sample reads (white-box): thread t
-    of CTA r samples columns r*32768 + (u*1024 + t)*4 + e for (u, e) in
-    (0, 0), (2, 1), (4, 2), (6, 3)."""
-    t = torch.arange(1024)
-    cols = [r * 32768 + (u * 1024 + t) * 4 + e for r in range(4) for u, e in ((0, 0), (2, 1), (4, 2), (6, 3))]
-    cols = torch.cat(cols)
+    """Columns the cluster select's threshold sample reads for rows held in
+    registers (white-box): 8 consecutive columns of every 128, at an offset hashed
+    from the chunk number."""
     m = torch.zeros(n, dtype=torch.bool)
-    m[cols[cols < n]] = True
+    for g in range((n + 127) // 128):
+        s = 128 * g + 8 * (((g * 0x9E3779B1) & 0xFFFFFFFF) >> 28)
+        if s + 8 <= n:
+            m[s:s + 8] = True
     return m
 
 
@@ -92,12 +92,13 @@ def test_noalloc_scratch_bound_of_the_test_cases():
 @pytest.mark.gpu
 def test_noalloc_matches_workspace_merge_twice_in_a_row(cuda_device, lib):
     # Cases that write the static scratch (fewer than 64 rows, so one 4-CTA cluster
-    # per row; the exact path appends every row's candidates to its scratch slice):
-    #   rows longer than the 131072 columns a cluster holds in registers, one of them
-    #   63 rows x 16384 candidates (63 * 16384 * 8 B, next to the 8 MiB limit), and
-    #   rows whose threshold sample is defeated, so the fast path falls back.
-    # Then cases that leave it alone: 64 rows (one CTA per row) and a short row
-    # set that the fast path resolves in shared memory.
+    # per row, whose CTAs exchange the row's candidates through its scratch slice):
+    #   rows longer than the 131072 columns a cluster holds in registers (streamed
+    #   once), 63 rows x k = 16384 (the exact path fills 63 * 16384 * 8 B, next to
+    #   the 8 MiB limit), rows whose threshold sample is defeated (the fast path
+    #   falls back to the exact path), and a short row set.
+    # Then a case that leaves it alone: 64 rows (one CTA per row, candidates in
+    # shared memory).
     torch.manual_seed(0)
     cases = []
     s, i = _distinct_rows(8, 2 * KPASS, seed=21)
@@ -106,10 +107,10 @@ def test_noalloc_matches_workspace_merge_twice_in_a_row(cuda_device, lib):
     cases.append((s, i, 16384))
     s, i = _sample_defeating_rows(8, 100000, seed=23)
     cases.append((s, i, 3000))
-    s, i = _distinct_rows(64, 65536, seed=24)
-    cases.append((s, i, 8192))
     s, i = _distinct_rows(5, 1000, seed=25)
     cases.append((s, i, 37))
+    s, i = _distinct_rows(64, 65536, seed=24)
+    cases.append((s, i, 8192))
     cases = [(s.to(cuda_device), i.to(cuda_device), k) for s, i, k in cases]
 
     # every case twice, one after the other on one stream and without
