@@ -612,6 +612,8 @@ def measure(wl, args, ranks: Ranks, *, e2e: bool, cpu_base: bool, clocks_on: boo
     for _ in range(3):
         graph.replay()
     torch.cuda.synchronize()
+    if exchange is not None:
+        exchange.timings(reset=True)
     clocks = ClockSampler(ranks.local) if clocks_on else None
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
@@ -632,6 +634,13 @@ def measure(wl, args, ranks: Ranks, *, e2e: bool, cpu_base: bool, clocks_on: boo
     ms = ranks.max(ev0.elapsed_time(ev1))
     del graph  # a graph holding NCCL work must go before the process group
     torch.cuda.synchronize()
+    xtime = None
+    if exchange is not None:
+        # device time per merge in the timed steps, the slowest rank's
+        tm = exchange.timings(reset=True)
+        xtime = {key: ranks.max(tm[key]) for key in ("wait_us", "merge_us", "ack_us")}
+        xtime["what"] = ("per peer merge, slowest rank: waiting for every rank's run from the merge's "
+                         "start, merging, waiting for the acknowledgements (%globaltimer)")
 
     n_sc, t_sc = ktimes["score"]
     score_ms = ranks.max(t_sc / max(1, n_sc))  # the slowest rank's scorer launch
@@ -640,7 +649,8 @@ def measure(wl, args, ranks: Ranks, *, e2e: bool, cpu_base: bool, clocks_on: boo
            "value": wl.Sk * args.steps / (ms * 1e-3), "launches": int(round(launches_per_step * args.steps)),
            "launches_per_step": launches_per_step, "ktimes": ktimes,
            "clocks": clocks.summary() if clocks else None, "chunks": chunks,
-           "exchange": "peer" if exchange is not None else ("nccl" if world > 1 else None)}
+           "exchange": "peer" if exchange is not None else ("nccl" if world > 1 else None),
+           "exchange_timing": xtime}
 
     # ---- end to end through the public call, host buffers ----
     if e2e:
@@ -744,6 +754,7 @@ def sub_record(res, args) -> dict:
             "config": config_of(wl, res_world(res), args.recall_type, res["exchange"] or "peer"),
             "roofline": roof, "step_roofline": step_roof, "kernels_ms_per_step": kernels_ms(res, args.steps),
             "gpu_launches_per_step": res["launches_per_step"], "parity": res["parity"],
+            **({"exchange_timing": res["exchange_timing"]} if res.get("exchange_timing") else {}),
             **({"exchange_status": res["exchange_status"]} if "exchange_status" in res else {})}
 
 
@@ -808,6 +819,8 @@ def main():
     }
     if "exchange_status" in main_res:
         line["exchange_status"] = main_res["exchange_status"]  # 0: every bounded peer wait succeeded
+    if main_res.get("exchange_timing"):
+        line["exchange_timing"] = main_res["exchange_timing"]
     line.update(subs)
     print(json.dumps(line), flush=True)
     ok = main_res["parity"]["ok"] and all(s["parity"].get("ok", False) for s in subs.values())

@@ -256,6 +256,14 @@ PRISM_API int prism_peer_publish(void* const* bufs, int32_t world, int32_t rank,
 PRISM_API int prism_peer_merge(void* const* bufs, int32_t world, int32_t rank, int64_t rows,
                                int32_t topk, int32_t wait_acks, int64_t timeout_ns,
                                int32_t* out_idx, float* out_scores, void* stream);
+/*
+ * Measurement of this rank's peer merges (device time, %globaltimer): out[0] the
+ * number of merges since the last reset, out[1..3] the nanoseconds they spent in
+ * total waiting for the ranks' runs to be published (from the merge's start),
+ * merging, and waiting for the other ranks' acknowledgements. Synchronises
+ * `stream`; reset != 0 zeroes the sums afterwards. No reference counterpart.
+ */
+PRISM_API int prism_peer_read_timings(void* own_buf, uint64_t* out4, int32_t reset, void* stream);
 
 /*
  * prism_topk_merge without a workspace, for callers that cannot allocate device

@@ -94,6 +94,7 @@ SIGNATURES = {
     "prism_peer_merge": (ctypes.c_int, [
         ctypes.POINTER(_vp), _c_i32, _c_i32, _c_i64, _c_i32, _c_i32, _c_i64, _vp, _vp, _vp,
     ]),
+    "prism_peer_read_timings": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint64), _c_i32, _vp]),
     "prism_read_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), _vp]),
     "prism_profile_start": (ctypes.c_int, [_c_i32]),
     "prism_profile_stop": (ctypes.c_int, []),

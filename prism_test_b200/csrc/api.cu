@@ -1,6 +1,7 @@
 // C-ABI entry points (include/prism_b200.h): argument checking, workspace
 // layout and kernel orchestration on the caller's stream.
 #include <algorithm>
+#include <cstddef>
 #include <atomic>
 #include <vector>
 #include <climits>
@@ -757,6 +758,31 @@ int prism_peer_merge(void* const* bufs, int32_t world, int32_t rank, int64_t row
     return prism::launch_merge_runs(rs, world, rows, topk, topk, out_idx, out_scores, sync, stream);
   });
   if (e != cudaSuccess) return cuda_fail(e, "peer merge kernel launch");
+  return PRISM_OK;
+}
+
+int prism_peer_read_timings(void* own_buf, uint64_t* out4, int32_t reset, void* stream_ptr) {
+  g_last_error.clear();
+  if (!own_buf || !out4) return fail(PRISM_E_INVALID, "null pointer argument");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  auto* h = static_cast<prism::PeerHeader*>(own_buf);
+  uint64_t host[4] = {0, 0, 0, 0};
+  static_assert(offsetof(prism::PeerHeader, merge_ns) == offsetof(prism::PeerHeader, wait_ns) + 8 &&
+                    offsetof(prism::PeerHeader, ack_ns) == offsetof(prism::PeerHeader, wait_ns) + 16 &&
+                    offsetof(prism::PeerHeader, merges) == offsetof(prism::PeerHeader, wait_ns) + 24,
+                "timing sums are contiguous");
+  cudaError_t e = cudaMemcpyAsync(host, &h->wait_ns, sizeof(host), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the exchange timings");
+  out4[0] = host[3];
+  out4[1] = host[0];
+  out4[2] = host[1];
+  out4[3] = host[2];
+  if (reset) {
+    e = cudaMemsetAsync(&h->wait_ns, 0, sizeof(host), stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "resetting the exchange timings");
+  }
   return PRISM_OK;
 }
 

@@ -126,6 +126,11 @@ struct PeerHeader {
   uint64_t step;                // this rank's exchange step (advanced by the publish)
   uint64_t ready[kPeerMaxRanks];  // ready[r] == s: rank r's run of step s is complete
   uint64_t ack[kPeerMaxRanks];    // ack[r] == s: rank r has read this rank's run of step s
+  // measurement (%globaltimer ns): the current merge's start and the end of its
+  // ready waits (merge CTA 0), and sums over the merges since the last reset of
+  // the time spent waiting for the ranks' runs, merging, and waiting for the acks
+  uint64_t t_start, t_ready;
+  uint64_t wait_ns, merge_ns, ack_ns, merges;
 };
 static_assert(sizeof(PeerHeader) <= kPeerHeaderBytes, "peer header too large");
 constexpr int kMergeRunsMax = 16;

@@ -1498,13 +1498,18 @@ __global__ void __cluster_dims__(kMergeParts, 1, 1) __launch_bounds__(kThreads, 
   if (tid < nruns) s_runs[tid] = rs.run[tid];
   grid_dependency_wait();  // a dependent launch after the publish (peer exchange)
   PeerHeader* self = sync.self;
-  uint64_t step = 0;
+  uint64_t step = 0, t_start = 0;
   if (self != nullptr) {
     step = self->step;
+    t_start = globaltimer_ns();
     if (tid < nruns && !wait_flag_eq(&self->ready[tid], step, sync.timeout_ns))
       set_status(&self->status, kStatusTimeout);
   }
   __syncthreads();
+  if (self != nullptr && blockIdx.x == 0 && tid == 0) {
+    self->t_start = t_start;
+    self->t_ready = globaltimer_ns();
+  }
   merge_row(s_runs, nruns, rows, run_len, k, out_idx, out_scores, sm, row, part);
   if (self == nullptr) return;
   __syncthreads();  // this CTA's reads of the runs are complete
@@ -1512,6 +1517,7 @@ __global__ void __cluster_dims__(kMergeParts, 1, 1) __launch_bounds__(kThreads, 
     __threadfence();
     if (atomicAdd(&self->done, 1u) == gridDim.x - 1) {
       self->done = 0;
+      const uint64_t t_merged = globaltimer_ns();
       __threadfence_system();
       for (int r = 0; r < nruns; ++r) st_release_sys(&sync.peer[r]->ack[sync.rank], step);
       if (sync.wait_acks) {
@@ -1521,6 +1527,13 @@ __global__ void __cluster_dims__(kMergeParts, 1, 1) __launch_bounds__(kThreads, 
             break;
           }
       }
+      // this merge's share of the time: waiting for the runs (merge CTA 0),
+      // merging (until the last CTA finished), waiting for the acknowledgements
+      const uint64_t t0 = self->t_start, t1 = self->t_ready, t3 = globaltimer_ns();
+      self->wait_ns += t1 - t0;
+      self->merge_ns += t_merged > t1 ? t_merged - t1 : 0;
+      self->ack_ns += t3 - t_merged;
+      self->merges += 1;
     }
   }
 }

@@ -119,6 +119,19 @@ class PeerExchange:
                    "prism_read_status")
         return st.value
 
+    def timings(self, reset: bool = True) -> dict:
+        """This rank's merges since the last reset, in device time: how many, and the
+        microseconds per merge spent waiting for the ranks' runs (from the merge's
+        start), merging, and waiting for the other ranks' acknowledgements."""
+        lib = _lib.load()
+        out = (ctypes.c_uint64 * 4)()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(lib.prism_peer_read_timings(ctypes.c_void_p(self._own), out, 1 if reset else 0, stream),
+                   "prism_peer_read_timings")
+        n = int(out[0])
+        per = (lambda v: v / n / 1e3) if n else (lambda v: 0.0)
+        return {"merges": n, "wait_us": per(out[1]), "merge_us": per(out[2]), "ack_us": per(out[3])}
+
     def close(self) -> None:
         """Collective: unmaps the peers' buffers and frees this rank's."""
         if self._own is None:
