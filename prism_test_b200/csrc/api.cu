@@ -105,6 +105,14 @@ bool use_stream(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk, int32_t topk, int
 size_t stream_workspace(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk, int32_t topk) {
   return kStatusBytes + prism::prefill_stream_workspace_bytes(B * Hq * Sq, Sk, topk);
 }
+// Exact mode on the queries-as-M scorer streams its top-k (thresholded candidates,
+// no score matrix) for long contexts shared by many query rows.
+bool wide_stream_shape(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk, int32_t topk) {
+  return Sq >= 2 && B * Hq * Sq >= 64 && Sk >= 32768 && topk <= 4096 && int64_t(topk) * 16 <= Sk;
+}
+size_t wide_stream_workspace(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk, int32_t topk) {
+  return kStatusBytes + prism::wide_stream_workspace_bytes(B * Hq * Sq, Sk, topk);
+}
 // the value-norm weights of the weighted call follow, 256-byte aligned
 size_t weights_offset(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk) {
   return size_t(round_up(int64_t(exact_workspace(B, Hq, Sq, Sk)), 256));
@@ -131,7 +139,10 @@ size_t prism_einsum_topk_workspace_size(int64_t B, int64_t Hq, int64_t Sq, int64
     if (topk < 1 || topk > kStreamMinTopk) return 0;
     return stream_workspace(B, Hq, Sq, Sk, topk);
   }
-  return exact_workspace(B, Hq, Sq, Sk);
+  const size_t ex = exact_workspace(B, Hq, Sq, Sk);
+  if (mode == PRISM_MODE_EXACT && topk >= 1 && wide_stream_shape(B, Hq, Sq, Sk, topk))
+    return std::max(ex, wide_stream_workspace(B, Hq, Sq, Sk, topk));
+  return ex;
 }
 
 }  // extern "C"
@@ -281,6 +292,28 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
     });
     if (e != cudaSuccess) return cuda_fail(e, "prefill select launch");
     g_launches.fetch_add(3, std::memory_order_relaxed);  // the select phase launches 4 kernels
+    return PRISM_OK;
+  }
+  // the queries-as-M scorer on a long shared context: streaming top-k
+  if (mode == PRISM_MODE_EXACT && !weight && wide_stream_shape(B, Hq, Sq, Sk, topk) &&
+      !prism::decode_hp_supported(a, dtype) && !prism::decode_mma_supported(a) &&
+      prism::decode_wide_supported(a)) {
+    if (workspace_bytes < wide_stream_workspace(B, Hq, Sq, Sk, topk))
+      return fail(PRISM_E_WORKSPACE, "workspace needs %zu bytes, got %zu",
+                  wide_stream_workspace(B, Hq, Sq, Sk, topk), workspace_bytes);
+    void* pws = ws + kStatusBytes;
+    e = launch_counted(PRISM_KERNEL_THRESHOLD, stream,
+                       [&] { return prism::wide_stream_threshold(a, dtype, topk, pws, nsm, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "wide threshold launch");
+    e = launch_counted(PRISM_KERNEL_SCORE, stream,
+                       [&] { return prism::wide_stream_candidates(a, dtype, topk, pws, nsm, stream); });
+    if (e != cudaSuccess) return cuda_fail(e, "wide candidate launch");
+    e = launch_counted(PRISM_KERNEL_SELECT, stream, [&] {
+      return prism::prefill_stream_select(a, dtype, topk, index_base, out_idx, out_scores, pws, stream,
+                                          B * Hq * Sq);
+    });
+    if (e != cudaSuccess) return cuda_fail(e, "wide stream select launch");
+    g_launches.fetch_add(4, std::memory_order_relaxed);  // sample + thresholds, select phase of 4
     return PRISM_OK;
   }
   if (prism::decode_hp_supported(a, dtype)) {

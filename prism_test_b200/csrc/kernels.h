@@ -51,6 +51,15 @@ cudaError_t launch_decode_scores_mma(const DecodeArgs& a, int dtype, int num_sms
 bool decode_wide_supported(const DecodeArgs& a);
 cudaError_t launch_decode_scores_wide(const DecodeArgs& a, int dtype, int num_sms,
                                       cudaStream_t stream);
+// The same scorer for the streaming top-k (no score matrix): a threshold sample
+// (the scores of every kWideSampleStride-th stage of 128 / Hkv positions, into
+// a.scores as [rows, a.ld] with a.ld >= wide_sample_cols), and the candidate pass
+// (keys at or above thr[row] appended to the rows' lists).
+constexpr int kWideSampleStride = 16;
+int64_t wide_sample_cols(int Hkv, int64_t Sk);
+cudaError_t launch_wide_sample(const DecodeArgs& a, int dtype, int num_sms, cudaStream_t stream);
+cudaError_t launch_wide_candidates(const DecodeArgs& a, int dtype, const float* thr, uint32_t* counts,
+                                   uint64_t* cand, int64_t cap, int num_sms, cudaStream_t stream);
 
 // CUDA-core path for <= 4 query rows per KV head, Hkv in {1, 2, 4, 8, 16}.
 bool decode_g4_supported(const DecodeArgs& a);
@@ -74,7 +83,8 @@ cudaError_t launch_prefill_candidates_tc(const DecodeArgs& a, int dtype, const f
                                          uint32_t* counts, uint64_t* cand, int64_t cap,
                                          cudaStream_t stream);
 int64_t prefill_cand_cap(int64_t Sk, int topk);
-size_t prefill_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk);
+// nfall: rows the exact fallback can take per call (< 0: the prefill default, 64)
+size_t prefill_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk, int64_t nfall = -1);
 // The streaming path in three phases on one workspace `ws` of
 // prefill_stream_workspace_bytes(rows, Sk, topk) bytes (256-aligned):
 // thresholds (one tcgen05 launch), candidates (one tcgen05 launch), selection
@@ -85,7 +95,35 @@ cudaError_t prefill_stream_candidates(const DecodeArgs& a, int dtype, int topk, 
                                       cudaStream_t stream);
 cudaError_t prefill_stream_select(const DecodeArgs& a, int dtype, int topk, int64_t index_base,
                                   int32_t* out_idx, float* out_scores, void* ws,
+                                  cudaStream_t stream, int64_t nfall = -1);
+// The streaming workspace's thresholds, candidate counts [rows, 2], candidate
+// lists [rows, cap] and fallback flags (two ints), for other candidate producers.
+struct StreamBuffers {
+  float* thr;
+  uint32_t* counts;
+  uint64_t* cand;
+  int64_t cap;
+  int* flags;
+};
+StreamBuffers stream_buffers(int64_t rows, int64_t Sk, int topk, void* ws, int64_t nfall);
+
+// Streaming top-k on the queries-as-M scorer (many query rows per KV head, RoPE'd
+// keys allowed): a threshold sample, per-row thresholds, the candidate pass and
+// the streaming selection with its exact fallback. `ws` is
+// wide_stream_workspace_bytes(rows, Sk, topk) bytes, 256-byte aligned.
+size_t wide_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk);
+struct WideStreamPtrs {
+  StreamBuffers sb;
+  float* S;      // the threshold sample [rows, ld_s]
+  int64_t ld_s;
+};
+WideStreamPtrs wide_stream_ptrs(const DecodeArgs& a, int topk, void* ws);
+// phases: the sample and the thresholds (also clears the counts and flags), the
+// candidate pass; then prefill_stream_select on the same workspace
+cudaError_t wide_stream_threshold(const DecodeArgs& a, int dtype, int topk, void* ws, int num_sms,
                                   cudaStream_t stream);
+cudaError_t wide_stream_candidates(const DecodeArgs& a, int dtype, int topk, void* ws, int num_sms,
+                                   cudaStream_t stream);
 
 // --- exact per-row top-k selection over a score matrix ----------------------
 struct SelectArgs {

@@ -17,10 +17,12 @@
 // row), or whose fine bins hold more than kRankMax members (massive ties), are
 // listed for the exact fallback: all their scores recomputed on CUDA cores into
 // a scratch row, the library's general selection on those rows, and a copy of
-// the results into place. At most kFallbackRows rows per call can take the
-// fallback; more set kStatusCapacity.
+// the results into place. At most `nfall` rows per call can take the fallback
+// (kFallbackRows on the prefill path; every row on the queries-as-M streaming
+// path, whose workspace has room for it); more set kStatusCapacity.
 #include "common.cuh"
 #include "kernels.h"
+#include "rope_sincos.cuh"
 
 namespace prism {
 namespace {
@@ -44,6 +46,7 @@ struct PsArgs {
   float* out_scores;
   int* nflag;
   int32_t* flag_rows;
+  int nfall;
   int* status;
 };
 
@@ -56,7 +59,7 @@ __device__ __forceinline__ int64_t visible_keys(int64_t row, int Sq, int causal,
 
 __device__ __forceinline__ void flag_row(const PsArgs& a, int64_t row) {
   const int slot = atomicAdd(a.nflag, 1);
-  if (slot < kFallbackRows)
+  if (slot < a.nfall)
     a.flag_rows[slot] = int32_t(row);
   else
     set_status(a.status, kStatusCapacity);
@@ -233,13 +236,13 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
 
 // Exact scores of the listed rows (CUDA cores): scratch[slot, j] for every key j
 // (masked keys -inf). Block 0 also publishes the number of listed rows it will
-// serve (min(nflag, kFallbackRows)).
+// serve (min(nflag, nfall)).
 template <typename T>
 __global__ void __launch_bounds__(256)
     fallback_scores_kernel(const DecodeArgs a, const int* nflag, const int32_t* flag_rows,
-                           int* nserve, float* scratch) {
+                           int nfall, int* nserve, float* scratch) {
   __shared__ float qs[128];
-  const int nf = *nflag < kFallbackRows ? *nflag : kFallbackRows;
+  const int nf = *nflag < nfall ? *nflag : nfall;
   if (blockIdx.x == 0 && threadIdx.x == 0) *nserve = nf;
   const int slot = blockIdx.x;
   if (slot >= nf) return;
@@ -260,6 +263,31 @@ __global__ void __launch_bounds__(256)
   const T* kb = static_cast<const T*>(a.k) + (a.B > 1 ? int64_t(b) * a.k_sb : 0) +
                 int64_t(kvh) * a.k_sh;
   float* out = scratch + int64_t(slot) * a.ld;
+  if (a.inv_freq != nullptr) {
+    // RoPE'd keys: un-rotated on the fly (the fp32 angle fp32(pos) * inv_freq[i],
+    // sin/cos of it, x_i c + x_{i+64} s and x_{i+64} c - x_i s), dot product in fp32
+    __shared__ float invf[64];
+    if (threadIdx.x < 64) invf[threadIdx.x] = a.inv_freq[threadIdx.x];
+    __syncthreads();
+    for (int64_t j = threadIdx.x; j < a.Sk; j += 256) {
+      if (j >= nvis) {
+        out[j] = -INFINITY;
+        continue;
+      }
+      const T* kr = kb + j * 128;
+      const float pf = static_cast<float>(a.pos_offset + j);
+      float acc = 0.f;
+      for (int i = 0; i < 64; ++i) {
+        float sv, cv;
+        rope_sincos(__fmul_rn(pf, invf[i]), sv, cv);
+        const float x0 = to_f32<T>(kr[i]), x1 = to_f32<T>(kr[i + 64]);
+        acc = fmaf(qs[i], fmaf(x0, cv, x1 * sv), acc);
+        acc = fmaf(qs[i + 64], fmaf(x1, cv, -(x0 * sv)), acc);
+      }
+      out[j] = acc;
+    }
+    return;
+  }
   for (int64_t j = threadIdx.x; j < a.Sk; j += 256) {
     if (j >= nvis) {
       out[j] = -INFINITY;
@@ -307,7 +335,7 @@ struct PsLayout {
   size_t thr, counts, cand, flags, flag_rows, scratch, sel_ws, cidx, csc, total;
 };
 
-PsLayout ps_layout(int64_t rows, int64_t Sk, int topk) {
+PsLayout ps_layout(int64_t rows, int64_t Sk, int topk, int64_t nfall) {
   PsLayout L{};
   const int64_t cap = prefill_cand_cap(Sk, topk);
   const int64_t ld = (Sk + 3) / 4 * 4;
@@ -321,15 +349,15 @@ PsLayout ps_layout(int64_t rows, int64_t Sk, int topk) {
   L.flags = o;  // nflag, nserve
   o += 256;
   L.flag_rows = o;
-  o += up256(kFallbackRows * 4);
+  o += up256(size_t(nfall) * 4);
   L.scratch = o;
-  o += up256(size_t(kFallbackRows) * size_t(ld) * 4);
+  o += up256(size_t(nfall) * size_t(ld) * 4);
   L.sel_ws = o;
-  o += up256(select_workspace_bytes(kFallbackRows, Sk));
+  o += up256(select_workspace_bytes(nfall, Sk));
   L.cidx = o;
-  o += up256(size_t(kFallbackRows) * size_t(topk) * 4);
+  o += up256(size_t(nfall) * size_t(topk) * 4);
   L.csc = o;
-  o += up256(size_t(kFallbackRows) * size_t(topk) * 4);
+  o += up256(size_t(nfall) * size_t(topk) * 4);
   L.total = o;
   return L;
 }
@@ -341,8 +369,8 @@ int64_t prefill_cand_cap(int64_t Sk, int topk) {
   return c < Sk ? c : Sk;
 }
 
-size_t prefill_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk) {
-  return ps_layout(rows, Sk, topk).total;
+size_t prefill_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk, int64_t nfall) {
+  return ps_layout(rows, Sk, topk, nfall < 0 ? kFallbackRows : nfall).total;
 }
 
 namespace {
@@ -359,9 +387,9 @@ struct PsPtrs {
   float* csc;
   int64_t cap;
 };
-PsPtrs ps_ptrs(const DecodeArgs& d, int topk, void* ws) {
+PsPtrs ps_ptrs(const DecodeArgs& d, int topk, void* ws, int64_t nfall) {
   const int64_t rows = int64_t(d.B) * d.Hq * d.Sq;
-  const PsLayout L = ps_layout(rows, d.Sk, topk);
+  const PsLayout L = ps_layout(rows, d.Sk, topk, nfall);
   uint8_t* w = static_cast<uint8_t*>(ws);
   PsPtrs p;
   p.thr = reinterpret_cast<float*>(w + L.thr);
@@ -379,9 +407,21 @@ PsPtrs ps_ptrs(const DecodeArgs& d, int topk, void* ws) {
 }
 }  // namespace
 
+StreamBuffers stream_buffers(int64_t rows, int64_t Sk, int topk, void* ws, int64_t nfall) {
+  const PsLayout L = ps_layout(rows, Sk, topk, nfall);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  StreamBuffers s;
+  s.thr = reinterpret_cast<float*>(w + L.thr);
+  s.counts = reinterpret_cast<uint32_t*>(w + L.counts);
+  s.cand = reinterpret_cast<uint64_t*>(w + L.cand);
+  s.cap = prefill_cand_cap(Sk, topk);
+  s.flags = reinterpret_cast<int*>(w + L.flags);
+  return s;
+}
+
 cudaError_t prefill_stream_threshold(const DecodeArgs& d, int dtype, int topk, void* ws,
                                      cudaStream_t stream) {
-  const PsPtrs p = ps_ptrs(d, topk, ws);
+  const PsPtrs p = ps_ptrs(d, topk, ws, kFallbackRows);
   cudaError_t e = cudaMemsetAsync(p.nflag, 0, 2 * sizeof(int), stream);
   if (e != cudaSuccess) return e;
   return launch_prefill_threshold_tc(d, dtype, topk, p.thr, stream);
@@ -389,14 +429,15 @@ cudaError_t prefill_stream_threshold(const DecodeArgs& d, int dtype, int topk, v
 
 cudaError_t prefill_stream_candidates(const DecodeArgs& d, int dtype, int topk, void* ws,
                                       cudaStream_t stream) {
-  const PsPtrs p = ps_ptrs(d, topk, ws);
+  const PsPtrs p = ps_ptrs(d, topk, ws, kFallbackRows);
   return launch_prefill_candidates_tc(d, dtype, p.thr, p.counts, p.cand, p.cap, stream);
 }
 
 cudaError_t prefill_stream_select(const DecodeArgs& d, int dtype, int topk, int64_t index_base,
                                   int32_t* out_idx, float* out_scores, void* ws,
-                                  cudaStream_t stream) {
-  const PsPtrs w = ps_ptrs(d, topk, ws);
+                                  cudaStream_t stream, int64_t nfall_in) {
+  const int64_t nfall = nfall_in < 0 ? kFallbackRows : nfall_in;
+  const PsPtrs w = ps_ptrs(d, topk, ws, nfall);
   const int64_t rows = int64_t(d.B) * d.Hq * d.Sq;
   PsArgs p{};
   p.cand = w.cand;
@@ -412,6 +453,7 @@ cudaError_t prefill_stream_select(const DecodeArgs& d, int dtype, int topk, int6
   p.out_scores = out_scores;
   p.nflag = w.nflag;
   p.flag_rows = w.flag_rows;
+  p.nfall = int(nfall);
   p.status = d.status;
   const size_t smem = size_t(w.cap) * 6 + kPsBins * 4;
   cudaError_t e = cudaFuncSetAttribute(prefill_select_kernel,
@@ -423,17 +465,17 @@ cudaError_t prefill_stream_select(const DecodeArgs& d, int dtype, int topk, int6
 
   // exact fallback for the listed rows (kernels return at once when none are)
   if (dtype == kBF16)
-    fallback_scores_kernel<__nv_bfloat16><<<kFallbackRows, 256, 0, stream>>>(
-        d, w.nflag, w.flag_rows, w.nserve, w.scratch);
+    fallback_scores_kernel<__nv_bfloat16><<<unsigned(nfall), 256, 0, stream>>>(
+        d, w.nflag, w.flag_rows, int(nfall), w.nserve, w.scratch);
   else
-    fallback_scores_kernel<__half><<<kFallbackRows, 256, 0, stream>>>(d, w.nflag, w.flag_rows,
-                                                                     w.nserve, w.scratch);
+    fallback_scores_kernel<__half><<<unsigned(nfall), 256, 0, stream>>>(d, w.nflag, w.flag_rows,
+                                                                       int(nfall), w.nserve, w.scratch);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   SelectArgs s{};
   s.scores = w.scratch;
   s.idx_in = nullptr;
-  s.rows = kFallbackRows;
+  s.rows = nfall;
   s.n = d.Sk;
   s.ld = d.ld;
   s.k = topk;
@@ -444,7 +486,7 @@ cudaError_t prefill_stream_select(const DecodeArgs& d, int dtype, int topk, int6
   s.rows_dyn = w.nserve;
   e = launch_select_topk(s, w.sel_ws, stream);
   if (e != cudaSuccess) return e;
-  fallback_scatter_kernel<<<kFallbackRows, 256, 0, stream>>>(w.nserve, w.flag_rows, topk, w.cidx,
+  fallback_scatter_kernel<<<unsigned(nfall), 256, 0, stream>>>(w.nserve, w.flag_rows, topk, w.cidx,
                                                              w.csc, out_idx, out_scores);
   return cudaGetLastError();
 }

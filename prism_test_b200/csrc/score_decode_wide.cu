@@ -22,6 +22,17 @@
 // the cos/sin table, and only after it is the stage of the previous iteration
 // refilled.
 //
+// Modes (the epilogue's work):
+//   kWScores  the fp32 score matrix [rows, ld] (masked keys -inf);
+//   kWSample  the scores of every tstride-th stage only (a threshold sample:
+//             Tp consecutive positions of every tstride * Tp), written compactly
+//             to [rows, ld] with sample column = sampled stage * Tp + offset;
+//   kWCand    no scores: every visible key scoring at or above its row's
+//             threshold thr[row] (NaN included) is appended, packed as
+//             (fp32 score bits << 32) | ~key, to the row's candidate list
+//             [rows, cap] through a per-row counter (counts[2 row]; the count
+//             may exceed cap, which the selection then recomputes exactly).
+//
 // Precision: as in the other tensor-core scorers, cos/sin are scaled by
 // (1 + 2^-11) so that the operand truncation of TF32 lands within 2^-11 of the
 // rotated key; queries (bf16/fp16) are exact in TF32, accumulation is fp32.
@@ -37,10 +48,23 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 4;
+constexpr int kStages = 4;             // key ring depth (3 in the candidate mode)
+constexpr int kCandBuf = 16;           // candidate mode: entries per row staged in shared memory
+constexpr int kCandFlush = 4;          // candidate mode: stages between flushes
+constexpr int kMaxLocalRows = 256;     // Hkv * rows per KV head
 constexpr int kCsRow = 576;   // bytes per position in the cos/sin table
 constexpr int kCsLane = 144;  // bytes between consecutive lanes' 128-byte blocks
 constexpr float kTruncScale = 1.0f + 0x1.0p-11f;
+
+enum WideMode : int { kWScores = 0, kWSample = 1, kWCand = 2 };
+
+struct WideExtra {
+  int tstride;            // kWSample: every tstride-th stage
+  const float* thr;       // kWCand: per-row thresholds
+  uint32_t* counts;       // kWCand: [rows, 2] (front list count, 0)
+  uint64_t* cand;         // kWCand: [rows, cap]
+  int64_t cap;
+};
 
 struct __align__(16) WideTail {
   uint64_t full[kStages];
@@ -61,9 +85,13 @@ __device__ __forceinline__ int dim_of(int s, int c) {
   return s < 8 ? 16 * c + 2 * s : 64 + 16 * c + 2 * (s - 8);
 }
 
-template <typename T, bool kRope, int kMT>
+__host__ __device__ constexpr int wide_stages(int mode) { return mode == 2 ? 3 : kStages; }
+
+template <typename T, bool kRope, int kMT, int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
-    decode_wide_kernel(const __grid_constant__ CUtensorMap kmap, const DecodeArgs a, int Tp) {
+    decode_wide_kernel(const __grid_constant__ CUtensorMap kmap, const DecodeArgs a, int Tp,
+                       const WideExtra x) {
+  constexpr int kStages = wide_stages(kMode);
   extern __shared__ __align__(128) uint8_t smem[];
   const int Hkv = a.Hkv;
   const int R = a.G * a.sq_n;
@@ -73,6 +101,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* stages = smem;
   uint8_t* cs_tab = smem + kStages * stage_bytes;  // [2][Tp][kCsRow]
   WideTail* tail = reinterpret_cast<WideTail*>(cs_tab + 2 * Tp * kCsRow);
+  // candidate mode: per (KV head, row) a small staging list in shared memory,
+  // flushed to the row's global list every kCandFlush stages with one atomic
+  uint32_t* ccount = reinterpret_cast<uint32_t*>(tail + 1);          // [kMaxLocalRows]
+  uint64_t* cbuf = reinterpret_cast<uint64_t*>(ccount + kMaxLocalRows);  // [kMaxLocalRows][kCandBuf]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -93,6 +125,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (kRope) {
     for (int i = tid; i < kHeadDim / 2; i += kThreads) tail->inv_freq[i] = a.inv_freq[i];
   }
+  if (kMode == kWCand) {
+    for (int i = tid; i < kMaxLocalRows; i += kThreads) ccount[i] = 0u;
+  }
+  // score row of local row lr = h * R + r (KV head h, row r of its query group)
+  auto score_row = [&](int lr) -> int64_t {
+    const int hh = lr / R, r = lr - hh * R;
+    return (int64_t(b) * a.Hq + hh * a.G + r / a.sq_n) * a.Sq + a.s0 + r % a.sq_n;
+  };
+  // moves every staged candidate to its row's global list (all threads; the
+  // caller brackets it with block barriers)
+  auto flush = [&]() {
+    for (int lr = tid; lr < Hkv * R; lr += kThreads) {
+      const uint32_t n = min(ccount[lr], uint32_t(kCandBuf));
+      if (n == 0) continue;
+      const int64_t srow = score_row(lr);
+      const uint32_t base = atomicAdd(&x.counts[2 * srow], n);
+      for (uint32_t e = 0; e < n; ++e)
+        if (base + e < uint64_t(x.cap)) x.cand[srow * x.cap + base + e] = cbuf[lr * kCandBuf + e];
+      ccount[lr] = 0u;
+    }
+  };
 
   // A fragments of this warp's m-tiles: rows 16 mt + g (+ 8), dims of k-step s
   // at columns c (a0, a1) and c + 4 (a2, a3)
@@ -114,10 +167,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
-  // output rows of this lane: 16 mt + g and + 8 of each m-tile
+  // output rows of this lane: 16 mt + g and + 8 of each m-tile (score row index;
+  // row_off = the row's offset in the score matrix, thr_row its threshold)
   int64_t row_off[kMT][2];
   int64_t vis[kMT][2];
   bool wr[kMT][2];
+  float thr_row[kMT][2];
 #pragma unroll
   for (int j = 0; j < kMT; ++j) {
 #pragma unroll
@@ -126,17 +181,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       wr[j][half] = mt0 + j < M && r < R;
       const int rr = r < R ? r : R - 1;
       const int s_abs = a.s0 + rr % a.sq_n;
-      row_off[j][half] = ((int64_t(b) * a.Hq + h * a.G + rr / a.sq_n) * a.Sq + s_abs) * a.ld;
+      const int64_t srow = (int64_t(b) * a.Hq + h * a.G + rr / a.sq_n) * a.Sq + s_abs;
+      row_off[j][half] = kMode == kWCand ? srow : srow * a.ld;
       vis[j][half] = a.causal ? a.causal_offset + s_abs : INT64_MAX;
+      thr_row[j][half] = kMode == kWCand && wr[j][half] ? x.thr[srow] : 0.f;
     }
   }
   __syncthreads();
 
   const int kb_coord = (a.B > 1 && a.k_sb != 0) ? b : 0;
+  // stage t of the loop holds keys of tile t * tstride (kWSample) or t
+  const int tstep = kMode == kWSample ? x.tstride : 1;
   auto issue = [&](int t, int s) {
     const uint64_t pol = l2_policy_evict_first();
     mbar_arrive_expect_tx(&tail->full[s], stage_bytes);
-    tma_load_4d(stages + s * stage_bytes, &kmap, 0, t * Tp, 0, kb_coord, &tail->full[s], pol);
+    tma_load_4d(stages + s * stage_bytes, &kmap, 0, t * tstep * Tp, 0, kb_coord, &tail->full[s], pol);
   };
   if (tid == 0) {
     for (int k = 0; k < kStages - 1 && t_begin + k < t_end; ++k) issue(t_begin + k, k);
@@ -147,7 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool active = mt0 < M;
   int it = 0;
   for (int t = t_begin; t < t_end; ++t, ++it) {
-    const int p0 = t * Tp;
+    const int p0 = t * tstep * Tp;  // the stage's first key position
+    const int c0 = t * Tp;          // kWSample: its first sample column
     const uint32_t cs_buf = cs_base + (it & 1) * Tp * kCsRow;
     if (kRope) {
       for (int idx = tid; idx < Tp * 32; idx += kThreads) {
@@ -174,6 +234,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();  // stage t and its cos/sin are ready; every warp is past stage t-1
     if (tail->abort) return;
     if (tid == 0 && t + kStages - 1 < t_end) issue(t + kStages - 1, (it + kStages - 1) % kStages);
+    if (kMode == kWCand && it > 0 && it % kCandFlush == 0) {
+      flush();
+      __syncthreads();  // the staging lists are empty again
+    }
     if (!active) continue;
 
     const uint32_t st = smem_base + s * stage_bytes;
@@ -202,14 +266,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           kr[8 + i] = hi;
         }
       }
-      float acc[kMT][4];
+      // two accumulators per m-tile (k-steps 0-7 and 8-15), so that each warp keeps
+      // 2 kMT independent MMA chains in flight, summed at the end
+      float acc[kMT][4], acc2[kMT][4];
 #pragma unroll
-      for (int j = 0; j < kMT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+      for (int j = 0; j < kMT; ++j) {
+        acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        acc2[j][0] = acc2[j][1] = acc2[j][2] = acc2[j][3] = 0.f;
+      }
 #pragma unroll
-      for (int ks = 0; ks < 16; ++ks) {
+      for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
-        for (int j = 0; j < kMT; ++j)
+        for (int j = 0; j < kMT; ++j) {
           mma_tf32(acc[j], aq[j][ks], __float_as_uint(kr[ks].x), __float_as_uint(kr[ks].y));
+          mma_tf32(acc2[j], aq[j][8 + ks], __float_as_uint(kr[8 + ks].x), __float_as_uint(kr[8 + ks].y));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kMT; ++j) {
+        acc[j][0] += acc2[j][0];
+        acc[j][1] += acc2[j][1];
+        acc[j][2] += acc2[j][2];
+        acc[j][3] += acc2[j][3];
       }
       // acc[j]: (row g, keys 2c, 2c+1), (row g+8, keys 2c, 2c+1)
       const int pos = p0 + n0 + 2 * c;
@@ -218,9 +296,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           if (!wr[j][half]) continue;
-          float* o = a.scores + row_off[j][half];
+          if (kMode == kWCand) {
+            // visible keys at or above the row's threshold (!(v < thr): NaN too)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int p = pos + e;
+              const float v = acc[j][2 * half + e];
+              if (p < a.Sk && int64_t(p) <= vis[j][half] && !(v < thr_row[j][half])) {
+                const uint64_t pk = (uint64_t(__float_as_uint(v)) << 32) | uint64_t(~uint32_t(p));
+                const int lr = h * R + 16 * (mt0 + j) + g + 8 * half;
+                const uint32_t slot = atomicAdd(&ccount[lr], 1u);
+                if (slot < uint32_t(kCandBuf)) {
+                  cbuf[lr * kCandBuf + slot] = pk;
+                } else {  // the staging list is full: straight to the row's list
+                  const int64_t srow = row_off[j][half];
+                  const uint32_t gs = atomicAdd(&x.counts[2 * srow], 1u);
+                  if (gs < uint64_t(x.cap)) x.cand[srow * x.cap + gs] = pk;
+                }
+              }
+            }
+            continue;
+          }
           const float v0 = int64_t(pos) > vis[j][half] ? -INFINITY : acc[j][2 * half];
           const float v1 = int64_t(pos + 1) > vis[j][half] ? -INFINITY : acc[j][2 * half + 1];
+          if (kMode == kWSample) {
+            // every sample column of the stage is written, beyond Sk too (as -inf:
+            // the threshold kernel skips columns past the end)
+            float* o = a.scores + row_off[j][half] + c0 + n0 + 2 * c;
+            *reinterpret_cast<float2*>(o) = make_float2(pos < a.Sk ? v0 : -INFINITY,
+                                                        pos + 1 < a.Sk ? v1 : -INFINITY);
+            continue;
+          }
+          float* o = a.scores + row_off[j][half];
           if (pos + 1 < a.Sk) {
             *reinterpret_cast<float2*>(o + pos) = make_float2(v0, v1);
           } else if (pos < a.Sk) {
@@ -230,17 +337,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  if (kMode == kWCand) {
+    __syncthreads();  // every warp is done with its last stage
+    flush();
+  }
 }
 
-size_t wide_smem_bytes(int Hkv, int Tp) {
-  return size_t(kStages) * Hkv * Tp * kRowBytes + size_t(2) * Tp * kCsRow + sizeof(WideTail);
+size_t wide_smem_bytes(int Hkv, int Tp, int mode = kWScores) {
+  return size_t(wide_stages(mode)) * Hkv * Tp * kRowBytes + size_t(2) * Tp * kCsRow + sizeof(WideTail) +
+         (mode == kWCand ? size_t(kMaxLocalRows) * (4 + 8 * kCandBuf) : 0);
 }
 
-template <typename T, bool kRope, int kMT>
-cudaError_t launch_wide(const DecodeArgs& a, int num_sms, cudaStream_t stream) {
+template <typename T, bool kRope, int kMT, int kMode>
+cudaError_t launch_wide(const DecodeArgs& a, int num_sms, const WideExtra& x, cudaStream_t stream) {
   const int Tp = 128 / a.Hkv;
-  const size_t smem = wide_smem_bytes(a.Hkv, Tp);
-  auto kern = decode_wide_kernel<T, kRope, kMT>;
+  const size_t smem = wide_smem_bytes(a.Hkv, Tp, kMode);
+  auto kern = decode_wide_kernel<T, kRope, kMT, kMode>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
@@ -250,19 +362,31 @@ cudaError_t launch_wide(const DecodeArgs& a, int num_sms, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   DecodeArgs b = a;
   b.ntiles = (a.Sk + Tp - 1) / Tp;
+  if (kMode == kWSample) b.ntiles = (b.ntiles + x.tstride - 1) / x.tstride;  // sampled stages
   int ctas = num_sms;
   if (a.B > 1) ctas = (num_sms + a.B - 1) / a.B;
   ctas = max(1, min(ctas, b.ntiles));
-  kern<<<dim3(ctas, a.B), kThreads, smem, stream>>>(kmap, b, Tp);
+  kern<<<dim3(ctas, a.B), kThreads, smem, stream>>>(kmap, b, Tp, x);
   return cudaGetLastError();
 }
 
-template <typename T, bool kRope>
-cudaError_t launch_wide_mt(const DecodeArgs& a, int num_sms, cudaStream_t stream) {
+template <typename T, bool kRope, int kMode>
+cudaError_t launch_wide_mt(const DecodeArgs& a, int num_sms, const WideExtra& x, cudaStream_t stream) {
   const int M = (a.G * a.sq_n + 15) / 16;
   const int wph = kWarps / a.Hkv;
-  return M <= wph ? launch_wide<T, kRope, 1>(a, num_sms, stream)
-                  : launch_wide<T, kRope, 2>(a, num_sms, stream);
+  return M <= wph ? launch_wide<T, kRope, 1, kMode>(a, num_sms, x, stream)
+                  : launch_wide<T, kRope, 2, kMode>(a, num_sms, x, stream);
+}
+
+template <int kMode>
+cudaError_t launch_wide_mode(const DecodeArgs& a, int dtype, int num_sms, const WideExtra& x,
+                             cudaStream_t stream) {
+  const bool rope = a.inv_freq != nullptr;
+  if (dtype == kBF16)
+    return rope ? launch_wide_mt<__nv_bfloat16, true, kMode>(a, num_sms, x, stream)
+                : launch_wide_mt<__nv_bfloat16, false, kMode>(a, num_sms, x, stream);
+  return rope ? launch_wide_mt<__half, true, kMode>(a, num_sms, x, stream)
+              : launch_wide_mt<__half, false, kMode>(a, num_sms, x, stream);
 }
 
 }  // namespace
@@ -278,12 +402,23 @@ bool decode_wide_supported(const DecodeArgs& a) {
 
 cudaError_t launch_decode_scores_wide(const DecodeArgs& a, int dtype, int num_sms,
                                       cudaStream_t stream) {
-  const bool rope = a.inv_freq != nullptr;
-  if (dtype == kBF16)
-    return rope ? launch_wide_mt<__nv_bfloat16, true>(a, num_sms, stream)
-                : launch_wide_mt<__nv_bfloat16, false>(a, num_sms, stream);
-  return rope ? launch_wide_mt<__half, true>(a, num_sms, stream)
-              : launch_wide_mt<__half, false>(a, num_sms, stream);
+  return launch_wide_mode<kWScores>(a, dtype, num_sms, WideExtra{1, nullptr, nullptr, nullptr, 0}, stream);
+}
+
+int64_t wide_sample_cols(int Hkv, int64_t Sk) {
+  const int64_t Tp = 128 / Hkv;
+  const int64_t ntiles = (Sk + Tp - 1) / Tp;
+  return (ntiles + kWideSampleStride - 1) / kWideSampleStride * Tp;
+}
+
+cudaError_t launch_wide_sample(const DecodeArgs& a, int dtype, int num_sms, cudaStream_t stream) {
+  return launch_wide_mode<kWSample>(a, dtype, num_sms,
+                                    WideExtra{kWideSampleStride, nullptr, nullptr, nullptr, 0}, stream);
+}
+
+cudaError_t launch_wide_candidates(const DecodeArgs& a, int dtype, const float* thr, uint32_t* counts,
+                                   uint64_t* cand, int64_t cap, int num_sms, cudaStream_t stream) {
+  return launch_wide_mode<kWCand>(a, dtype, num_sms, WideExtra{1, thr, counts, cand, cap}, stream);
 }
 
 }  // namespace prism

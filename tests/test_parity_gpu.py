@@ -294,3 +294,48 @@ def test_wide_rows_causal(cuda_device):
     inv = W.rope_inv_freq(128, 1e6).to(cuda_device)
     idx, sc = einsum_topk_func(q, k, 400, inv_freq=inv, causal_offset=3990, return_scores=True)
     check_parity(idx, sc, q, k, 400, inv, 0, 3990)
+
+
+# ---- streaming top-k on the queries-as-M scorer (many rows per KV head, long context) --
+# A threshold sample (every 16th stage of 128 / Hkv positions), per-row thresholds,
+# a candidate pass and the streaming selection with its exact fallback: no score
+# matrix. Taken for exact calls with Sq >= 2, >= 64 rows, Sk >= 32768, topk * 16 <= Sk.
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Sk,topk,rope,dtype,causal", [
+    (1, 28, 4, 8, 40000, 1000, True, torch.bfloat16, None),      # ragged Sk, RoPE
+    (1, 28, 4, 8, 40000, 1000, True, torch.bfloat16, 39990),     # causal chunk tail
+    (1, 16, 2, 8, 65536, 4096, False, torch.float16, None),      # raw fp16 keys, Hkv 2
+    (2, 32, 8, 4, 36000, 500, True, torch.bfloat16, None),       # batch 2, Hkv 8
+])
+def test_wide_stream_shapes(B, Hq, Hkv, Sq, Sk, topk, rope, dtype, causal, cuda_device):
+    g = torch.Generator(device=cuda_device).manual_seed(Sk + Hq)
+    q = torch.randn(B, Hq, Sq, 128, generator=g, device=cuda_device).to(dtype)
+    k = torch.randn(B, Hkv, Sk, 128, generator=g, device=cuda_device).to(dtype)
+    inv = W.rope_inv_freq(128, 1e6).to(cuda_device) if rope else None
+    idx, sc = einsum_topk_func(q, k, topk, inv_freq=inv, pos_offset=5 if rope else 0,
+                               causal_offset=causal, return_scores=True)
+    check_parity(idx, sc, q, k, topk, inv, 5 if rope else 0, causal)
+
+
+@pytest.mark.parametrize("sampled_high", [True, False])
+def test_wide_stream_threshold_miss_falls_back_exactly(sampled_high, cuda_device):
+    # keys along q whose magnitudes make the sampled stages (positions p with
+    # (p // 32) % 16 == 0 for Hkv = 4) all high (too few candidates) or all low
+    # (too many): the rows are recomputed exactly, RoPE included
+    B, Hq, Hkv, Sq, Sk, topk = 1, 28, 4, 8, 36000, 800
+    q = torch.zeros(B, Hq, Sq, 128)
+    q[..., 0] = 1.0
+    q[..., 64] = 0.5
+    pos = torch.arange(Sk)
+    mask = (pos // 32) % 16 == 0
+    gen = torch.Generator().manual_seed(9)
+    mag = torch.rand(Hkv, Sk, generator=gen)
+    mag = torch.where(mask[None, :], mag + (2.0 if sampled_high else -2.0), mag)
+    raw = torch.zeros(B, Hkv, Sk, 128)
+    raw[0, :, :, 0] = mag
+    raw[0, :, :, 1:] = 0.01 * torch.randn(Hkv, Sk, 127, generator=gen)
+    inv = W.rope_inv_freq(128, 1e6)
+    cos, sin = W.rope_cos_sin(pos, inv)
+    k = W.apply_rope(raw, cos, sin).to(torch.bfloat16).to(cuda_device)
+    q = q.to(torch.bfloat16).to(cuda_device)
+    idx, sc = einsum_topk_func(q, k, topk, inv_freq=inv.to(cuda_device), return_scores=True)
+    check_parity(idx, sc, q, k, topk, inv.to(cuda_device))
