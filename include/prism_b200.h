@@ -257,6 +257,36 @@ PRISM_API int prism_peer_merge(void* const* bufs, int32_t world, int32_t rank, i
                                int32_t topk, int32_t wait_acks, int64_t timeout_ns,
                                int32_t* out_idx, float* out_scores, void* stream);
 /*
+ * One step of the sequence-sharded recall as a single call — the composition the
+ * reference's single-GPU _dense_topk (eval_harness/attention_methods/
+ * reattention.py:486-498) becomes when the key cache is split over the GPUs of
+ * one node: this rank's exact local top-k of its key slice (prism_einsum_topk
+ * with pos_offset = index_base = shard_start, written into its exchange run),
+ * then prism_peer_publish, then prism_peer_merge into out_idx / out_scores
+ * ([B, Hq, Sq, topk] int32 global indices / fp32 scores, the same on every rank).
+ *   k_shard     this rank's keys [B, Hkv, Sk_shard, 128], first key at absolute
+ *               position / global index shard_start; Sk_shard >= topk
+ *   exchange_bufs  every rank's exchange buffer of
+ *               prism_peer_buffer_bytes(B * Hq * Sq, topk) bytes, as mapped here
+ *               (prism_peer_alloc on each rank, the IPC handles exchanged by the
+ *               caller, prism_peer_open of the other ranks' handles)
+ *   wait_acks / timeout_ns  as for prism_peer_merge (wait_acks = 1 unless the
+ *               caller keeps every rank from rewriting its run before all ranks
+ *               have read it)
+ *   workspace   prism_einsum_topk_workspace_size(B, Hq, Sq, Sk_shard, topk,
+ *               PRISM_MODE_EXACT) bytes, 256-byte aligned
+ * Every rank makes the call for the same step, with the same shapes, in the same
+ * order relative to its other exchange calls.
+ */
+PRISM_API int prism_sharded_topk(const void* q, const void* k_shard, const float* inv_freq, int dtype,
+                                 int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk_shard,
+                                 int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                                 int64_t shard_start, int32_t topk, void* const* exchange_bufs,
+                                 int32_t world, int32_t rank, int32_t wait_acks, int64_t timeout_ns,
+                                 int32_t* out_idx, float* out_scores, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/*
  * Measurement of this rank's peer merges (device time, %globaltimer): out[0] the
  * number of merges since the last reset, out[1..3] the nanoseconds they spent in
  * total waiting for the ranks' runs to be published (from the merge's start),

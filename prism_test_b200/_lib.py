@@ -95,6 +95,11 @@ SIGNATURES = {
         ctypes.POINTER(_vp), _c_i32, _c_i32, _c_i64, _c_i32, _c_i32, _c_i64, _vp, _vp, _vp,
     ]),
     "prism_peer_read_timings": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_uint64), _c_i32, _vp]),
+    "prism_sharded_topk": (ctypes.c_int, [
+        _vp, _vp, _vp, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+        ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64), _c_i64, _c_i32,
+        ctypes.POINTER(_vp), _c_i32, _c_i32, _c_i32, _c_i64, _vp, _vp, _vp, ctypes.c_size_t, _vp,
+    ]),
     "prism_read_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int), _vp]),
     "prism_profile_start": (ctypes.c_int, [_c_i32]),
     "prism_profile_stop": (ctypes.c_int, []),

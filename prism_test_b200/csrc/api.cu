@@ -794,6 +794,38 @@ int prism_peer_merge(void* const* bufs, int32_t world, int32_t rank, int64_t row
   return PRISM_OK;
 }
 
+int prism_sharded_topk(const void* q, const void* k_shard, const float* inv_freq, int dtype, int64_t B,
+                       int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk_shard, int64_t D,
+                       const int64_t* q_strides, const int64_t* k_strides, int64_t shard_start,
+                       int32_t topk, void* const* exchange_bufs, int32_t world, int32_t rank,
+                       int32_t wait_acks, int64_t timeout_ns, int32_t* out_idx, float* out_scores,
+                       void* workspace, size_t workspace_bytes, void* stream_ptr) {
+  g_last_error.clear();
+  prism::PeerSync sync;
+  int rc = peer_sync(exchange_bufs, world, rank, sync);
+  if (rc != PRISM_OK) return rc;
+  if (!out_idx) return fail(PRISM_E_INVALID, "null pointer argument");
+  if (B <= 0 || Hq <= 0 || Sq <= 0 || topk < 1)
+    return fail(PRISM_E_INVALID, "all of B, Hq, Sq and topk must be positive");
+  if (Sk_shard < topk)
+    return fail(PRISM_E_UNSUPPORTED, "every shard must hold at least topk keys (Sk_shard=%lld, topk=%d)",
+                (long long)Sk_shard, topk);
+  if (shard_start < 0) return fail(PRISM_E_INVALID, "shard_start must be >= 0");
+  const int64_t rows = B * Hq * Sq;
+  // this rank's run in its exchange buffer: [2, rows, topk] (score bits, indices)
+  uint8_t* run = static_cast<uint8_t*>(exchange_bufs[rank]) + prism::kPeerHeaderBytes;
+  float* run_scores = reinterpret_cast<float*>(run);
+  int32_t* run_idx = reinterpret_cast<int32_t*>(run) + rows * topk;
+  rc = einsum_topk_impl(q, k_shard, inv_freq, dtype, B, Hq, Hkv, Sq, Sk_shard, D, q_strides, k_strides,
+                        shard_start, -1, topk, PRISM_MODE_EXACT, shard_start, run_idx, run_scores,
+                        workspace, workspace_bytes, stream_ptr, nullptr);
+  if (rc != PRISM_OK) return rc;
+  rc = prism_peer_publish(exchange_bufs, world, rank, stream_ptr);
+  if (rc != PRISM_OK) return rc;
+  return prism_peer_merge(exchange_bufs, world, rank, rows, topk, wait_acks, timeout_ns, out_idx,
+                          out_scores, stream_ptr);
+}
+
 int prism_peer_read_timings(void* own_buf, uint64_t* out4, int32_t reset, void* stream_ptr) {
   g_last_error.clear();
   if (!own_buf || !out4) return fail(PRISM_E_INVALID, "null pointer argument");

@@ -184,6 +184,58 @@ def test_peer_exchange_argument_errors(cuda_device):
         bufs.free()
 
 
+# ---- the single C-ABI sharded call ------------------------------------------------------
+def _sharded_c(lib, q, k_shard, inv, start, topk, bufs, world, rank, wait_acks=1):
+    """prism_sharded_topk through the C ABI: this rank's local top-k into its exchange
+    run, the publish and the merge; int32 / fp32 [B, Hq, Sq, topk]."""
+    B, Hq, Sq, D = q.shape
+    Hkv, Sk = k_shard.shape[1], k_shard.shape[2]
+    out_i = torch.empty((B, Hq, Sq, topk), dtype=torch.int32, device=q.device)
+    out_s = torch.empty((B, Hq, Sq, topk), dtype=torch.float32, device=q.device)
+    ws_bytes = lib.prism_einsum_topk_workspace_size(B, Hq, Sq, Sk, topk, _lib.MODE_EXACT)
+    ws = torch.empty(int(ws_bytes), dtype=torch.uint8, device=q.device)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    rc = lib.prism_sharded_topk(q.data_ptr(), k_shard.data_ptr(), inv.data_ptr() if inv is not None else None,
+                                0, B, Hq, Hkv, Sq, Sk, D, _lib.i64_array(q.stride()), _lib.i64_array(k_shard.stride()),
+                                int(start), int(topk), bufs, world, rank, wait_acks, 0,
+                                out_i.data_ptr(), out_s.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    _lib.check(rc, "prism_sharded_topk")
+    return out_i, out_s
+
+
+def test_sharded_c_abi_one_rank(cuda_device):
+    # world = 1: the call's merge of one run returns the local top-k of the shard
+    # at its global offset, exactly as prism_einsum_topk does
+    lib = _lib.load()
+    g = torch.Generator().manual_seed(3)
+    B, Hq, Hkv, Sk, topk, start = 1, 8, 2, 20000, 700, 123456
+    q = torch.randn(B, Hq, 1, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    k = torch.randn(B, Hkv, Sk, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    inv = W.rope_inv_freq(128, 5e5).to(cuda_device)
+    rows = B * Hq
+    nbytes = lib.prism_peer_buffer_bytes(rows, topk)
+    own = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+    _lib.check(lib.prism_peer_alloc(nbytes, ctypes.byref(own), handle), "prism_peer_alloc")
+    try:
+        bufs = (ctypes.c_void_p * 1)(own.value)
+        want_i, want_s = einsum_topk_func(q, k, topk, inv_freq=inv, pos_offset=start, index_base=start,
+                                          return_scores=True)
+        for _ in range(3):  # several steps on one buffer
+            gi, gs = _sharded_c(lib, q, k, inv, start, topk, bufs, 1, 0)
+            torch.cuda.synchronize()
+            assert torch.equal(gi, want_i) and torch.equal(gs, want_s)
+        # argument checks: a shard shorter than k, a rank outside the world
+        short = k[:, :, :topk - 1]
+        with pytest.raises(AssertionError, match="at least topk"):
+            _sharded_c(lib, q, short.contiguous(), inv, start, topk, bufs, 1, 0)
+        with pytest.raises(AssertionError, match="outside"):
+            _sharded_c(lib, q, k, inv, start, topk, bufs, 1, 1)
+    finally:
+        torch.cuda.synchronize()
+        lib.prism_peer_free(own)
+
+
 # ---- two ranks on two GPUs ------------------------------------------------------------
 def _free_port():
     with socket.socket() as s:
@@ -241,6 +293,12 @@ def _two_gpu_worker(rank, world, port, errq):
                 torch.cuda.synchronize()
                 assert torch.equal(gi, want_i) and torch.equal(gs, want_s)
             del graph
+            # the same step through the single C-ABI call, on the same exchange
+            lib = _lib.load()
+            for _ in range(2):
+                ci, cs = _sharded_c(lib, qd, kd, invd, start, topk, ex._bufs, world, rank)
+                torch.cuda.synchronize()
+                assert torch.equal(ci, want_i) and torch.equal(cs, want_s)
             assert ex.status() == 0
         finally:
             ex.close()
