@@ -238,6 +238,9 @@ PRISM_API int prism_topk_merge_runs(const int32_t* runs, int32_t nruns, int64_t 
  *      [rows, topk] (same result as prism_topk_merge_runs), then tells every rank
  *      its run was read; with wait_acks != 0 its last CTA also waits until every
  *      rank has read this rank's run, so step 1 of the next step may overwrite it.
+ *   prism_peer_wait_acks: on the device, waits until every rank has read this
+ *      rank's run of the current step — step 1's guard when the previous merge ran
+ *      with wait_acks = 0 (as prism_sharded_topk's does).
  * bufs is a HOST array of the world buffers as mapped in this process (the own
  * one at bufs[rank]), each 256-byte aligned; world <= PRISM_PEER_MAX_RANKS.
  * Steps are counted on the device, so the calls can be captured in a CUDA graph.
@@ -256,6 +259,8 @@ PRISM_API int prism_peer_publish(void* const* bufs, int32_t world, int32_t rank,
 PRISM_API int prism_peer_merge(void* const* bufs, int32_t world, int32_t rank, int64_t rows,
                                int32_t topk, int32_t wait_acks, int64_t timeout_ns,
                                int32_t* out_idx, float* out_scores, void* stream);
+PRISM_API int prism_peer_wait_acks(void* const* bufs, int32_t world, int32_t rank, int64_t timeout_ns,
+                                   void* stream);
 /*
  * One step of the sequence-sharded recall as a single call — the composition the
  * reference's single-GPU _dense_topk (eval_harness/attention_methods/
@@ -270,9 +275,12 @@ PRISM_API int prism_peer_merge(void* const* bufs, int32_t world, int32_t rank, i
  *               prism_peer_buffer_bytes(B * Hq * Sq, topk) bytes, as mapped here
  *               (prism_peer_alloc on each rank, the IPC handles exchanged by the
  *               caller, prism_peer_open of the other ranks' handles)
- *   wait_acks / timeout_ns  as for prism_peer_merge (wait_acks = 1 unless the
- *               caller keeps every rank from rewriting its run before all ranks
- *               have read it)
+ *   wait_acks   1: before the call rewrites this rank's run, it waits (on the
+ *               device, while its scorer runs) until every rank has acknowledged
+ *               reading the run of the previous step; the merge then only sends
+ *               this rank's acknowledgements. 0: the caller guarantees that no rank
+ *               rewrites its run before all ranks have read it.
+ *   timeout_ns  bound of every device-side wait (<= 0: 2 s)
  *   workspace   prism_einsum_topk_workspace_size(B, Hq, Sq, Sk_shard, topk,
  *               PRISM_MODE_EXACT) bytes, 256-byte aligned
  * Every rank makes the call for the same step, with the same shapes, in the same

@@ -91,6 +91,7 @@ SIGNATURES = {
     "prism_peer_close": (ctypes.c_int, [_vp]),
     "prism_peer_free": (ctypes.c_int, [_vp]),
     "prism_peer_publish": (ctypes.c_int, [ctypes.POINTER(_vp), _c_i32, _c_i32, _vp]),
+    "prism_peer_wait_acks": (ctypes.c_int, [ctypes.POINTER(_vp), _c_i32, _c_i32, _c_i64, _vp]),
     "prism_peer_merge": (ctypes.c_int, [
         ctypes.POINTER(_vp), _c_i32, _c_i32, _c_i64, _c_i32, _c_i32, _c_i64, _vp, _vp, _vp,
     ]),

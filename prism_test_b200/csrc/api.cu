@@ -151,12 +151,17 @@ namespace {
 
 // Shared body of prism_einsum_topk and prism_einsum_topk_weighted: `weight`
 // (already validated) scales the score matrix between scoring and selection.
+// `acks` (the sharded call): the outputs are this rank's exchange run, so the
+// kernels that write them first wait until every rank has read the previous
+// step's run — on the score-matrix paths right before the selection (the wait
+// overlaps the scorer), on the streaming paths before the first kernel.
 int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dtype, int64_t B,
                      int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D,
                      const int64_t* q_strides, const int64_t* k_strides, int64_t pos_offset,
                      int64_t causal_offset, int32_t topk, int32_t mode, int64_t index_base,
                      int32_t* out_idx, float* out_scores, void* workspace,
-                     size_t workspace_bytes, void* stream_ptr, const prism::WeightArgs* weight) {
+                     size_t workspace_bytes, void* stream_ptr, const prism::WeightArgs* weight,
+                     const prism::PeerSync* acks = nullptr, int acks_world = 0) {
   if (!q || !k || !out_idx || !q_strides || !k_strides)
     return fail(PRISM_E_INVALID, "null pointer argument");
   if (dtype != PRISM_DTYPE_BF16 && dtype != PRISM_DTYPE_FP16)
@@ -278,7 +283,14 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
   // specialised kernels take every query row of a KV head in one launch:
   // tensor-core tiles (keys as M for <= 16 rows per KV head, queries as M up
   // to 256 / Hkv rows), CUDA cores for <= 4
+  auto wait_acks = [&]() -> cudaError_t {
+    if (acks == nullptr) return cudaSuccess;
+    return launch_counted(PRISM_KERNEL_MERGE, stream,
+                          [&] { return prism::launch_peer_wait_acks(*acks, acks_world, stream); });
+  };
   if (streaming) {  // thresholds, candidates, per-row selection + exact fallback
+    e = wait_acks();
+    if (e != cudaSuccess) return cuda_fail(e, "peer ack wait launch");
     void* pws = ws + kStatusBytes;
     e = launch_counted(PRISM_KERNEL_THRESHOLD, stream,
                        [&] { return prism::prefill_stream_threshold(a, dtype, topk, pws, stream); });
@@ -301,6 +313,8 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
     if (workspace_bytes < wide_stream_workspace(B, Hq, Sq, Sk, topk))
       return fail(PRISM_E_WORKSPACE, "workspace needs %zu bytes, got %zu",
                   wide_stream_workspace(B, Hq, Sq, Sk, topk), workspace_bytes);
+    e = wait_acks();
+    if (e != cudaSuccess) return cuda_fail(e, "peer ack wait launch");
     void* pws = ws + kStatusBytes;
     e = launch_counted(PRISM_KERNEL_THRESHOLD, stream,
                        [&] { return prism::wide_stream_threshold(a, dtype, topk, pws, nsm, stream); });
@@ -373,6 +387,8 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
   s.out_scores = out_scores;
   s.status = status;
   void* cand_ws = ws + kStatusBytes + round_up(int64_t(scores_bytes(B * Hq * Sq, Sk)), 256);
+  e = wait_acks();
+  if (e != cudaSuccess) return cuda_fail(e, "peer ack wait launch");
   if (mode == PRISM_MODE_BLOCKMAX) {
     e = launch_counted(PRISM_KERNEL_SELECT, stream,
                        [&] { return prism::launch_select_blockmax(s, stream); });
@@ -770,6 +786,21 @@ int prism_peer_publish(void* const* bufs, int32_t world, int32_t rank, void* str
   return PRISM_OK;
 }
 
+int prism_peer_wait_acks(void* const* bufs, int32_t world, int32_t rank, int64_t timeout_ns,
+                         void* stream_ptr) {
+  g_last_error.clear();
+  prism::PeerSync sync;
+  const int rc = peer_sync(bufs, world, rank, sync);
+  if (rc != PRISM_OK) return rc;
+  sync.timeout_ns = timeout_ns > 0 ? timeout_ns : int64_t(prism::kWaitTimeoutNs);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  cudaError_t e = launch_counted(PRISM_KERNEL_MERGE, stream, [&] {
+    return prism::launch_peer_wait_acks(sync, world, stream);
+  });
+  if (e != cudaSuccess) return cuda_fail(e, "ack wait kernel launch");
+  return PRISM_OK;
+}
+
 int prism_peer_merge(void* const* bufs, int32_t world, int32_t rank, int64_t rows, int32_t topk,
                      int32_t wait_acks, int64_t timeout_ns, int32_t* out_idx, float* out_scores,
                      void* stream_ptr) {
@@ -816,13 +847,17 @@ int prism_sharded_topk(const void* q, const void* k_shard, const float* inv_freq
   uint8_t* run = static_cast<uint8_t*>(exchange_bufs[rank]) + prism::kPeerHeaderBytes;
   float* run_scores = reinterpret_cast<float*>(run);
   int32_t* run_idx = reinterpret_cast<int32_t*>(run) + rows * topk;
+  sync.timeout_ns = timeout_ns > 0 ? timeout_ns : int64_t(prism::kWaitTimeoutNs);
   rc = einsum_topk_impl(q, k_shard, inv_freq, dtype, B, Hq, Hkv, Sq, Sk_shard, D, q_strides, k_strides,
                         shard_start, -1, topk, PRISM_MODE_EXACT, shard_start, run_idx, run_scores,
-                        workspace, workspace_bytes, stream_ptr, nullptr);
+                        workspace, workspace_bytes, stream_ptr, nullptr, wait_acks ? &sync : nullptr,
+                        world);
   if (rc != PRISM_OK) return rc;
   rc = prism_peer_publish(exchange_bufs, world, rank, stream_ptr);
   if (rc != PRISM_OK) return rc;
-  return prism_peer_merge(exchange_bufs, world, rank, rows, topk, wait_acks, timeout_ns, out_idx,
+  // the merge sends its acknowledgements; the next call waits for the others' before
+  // it rewrites the run, while its scorer runs
+  return prism_peer_merge(exchange_bufs, world, rank, rows, topk, 0, timeout_ns, out_idx,
                           out_scores, stream_ptr);
 }
 

@@ -186,6 +186,9 @@ cudaError_t launch_merge_runs(const RunSet& rs, int nruns, int64_t rows, int64_t
                               int32_t* out_idx, float* out_scores, const PeerSync& sync,
                               cudaStream_t stream);
 cudaError_t launch_peer_publish(const PeerSync& sync, int world, cudaStream_t stream);
+// Waits until every rank acknowledged this rank's run of the current step (see
+// select_topk.cu); launched before a local top-k that rewrites the run.
+cudaError_t launch_peer_wait_acks(const PeerSync& sync, int world, cudaStream_t stream);
 
 // Post-selection: sorted union of the selected middle positions (optionally the
 // recall_clip most frequent), each widened to [p + lo, p + hi) and clamped to

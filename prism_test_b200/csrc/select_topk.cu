@@ -1538,6 +1538,19 @@ __global__ void __cluster_dims__(kMergeParts, 1, 1) __launch_bounds__(kThreads, 
   }
 }
 
+// Before this rank's next local top-k overwrites its run: waits until every rank
+// has acknowledged reading the run of the current step (the acks the ranks' merges
+// of that step sent). A dependent launch after the scorer, which does not touch the
+// run: the wait overlaps it, then griddepcontrol.wait orders the scorer's writes
+// before the selection that follows. One warp; bounded like every exchange wait.
+__global__ void peer_wait_acks_kernel(const PeerSync sync, int world) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  const uint64_t s = sync.self->step;
+  if (int(threadIdx.x) < world && !wait_flag_eq(&sync.self->ack[threadIdx.x], s, sync.timeout_ns))
+    set_status(&sync.self->status, kStatusTimeout);
+  grid_dependency_wait();
+}
+
 // Publish side of the peer exchange: advances this rank's step and marks its run
 // of that step ready in every rank's header (including its own). One warp.
 __global__ void peer_publish_kernel(const PeerSync sync, int world) {
@@ -1592,6 +1605,11 @@ cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int6
   RunSet rs{};
   for (int r = 0; r < nruns; ++r) rs.run[r] = runs + int64_t(r) * 2 * rows * run_len;
   return launch_merge_runs(rs, nruns, rows, run_len, k, out_idx, out_scores, PeerSync{}, stream);
+}
+
+cudaError_t launch_peer_wait_acks(const PeerSync& sync, int world, cudaStream_t stream) {
+  if (world < 1 || world > kPeerMaxRanks || sync.self == nullptr) return cudaErrorInvalidValue;
+  return launch_maybe_dependent(peer_wait_acks_kernel, dim3(1), dim3(32), 0, true, stream, sync, world);
 }
 
 cudaError_t launch_peer_publish(const PeerSync& sync, int world, cudaStream_t stream) {

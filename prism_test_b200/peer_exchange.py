@@ -11,10 +11,15 @@ NVLink, instead of N * k per row.
 Per step, on the current stream of every rank (``prism_peer_*`` in
 include/prism_b200.h):
 
-1. the local top-k is written into :attr:`PeerExchange.run`;
+1. the local top-k is written into :attr:`PeerExchange.run` (after
+   :meth:`PeerExchange.wait_acks` when the previous step was a
+   :meth:`PeerExchange.sharded_topk`);
 2. ``prism_peer_publish`` marks this rank's run of the step ready on every rank;
 3. ``prism_peer_merge`` waits for every rank's run, merges, acknowledges the reads
    and waits until this rank's run has been read everywhere.
+
+:meth:`PeerExchange.sharded_topk` runs the three steps as one C call and moves
+the last wait to the start of the next step, where it overlaps the scorer.
 
 Steps are counted on the device, so the whole step can be captured in a CUDA
 graph and replayed. Every wait is bounded (``timeout_s``); an expired wait sets
@@ -23,6 +28,7 @@ the status word :meth:`status` reads, and the exchange must then be rebuilt.
 from __future__ import annotations
 
 import ctypes
+from typing import Optional
 
 import torch
 import torch.distributed as dist
@@ -91,6 +97,7 @@ class PeerExchange:
                 self._own = None
                 raise
         self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
+        self._ws = None  # scratch of sharded_topk, grown on demand
         # this rank's run, int32 [2, rows, topk]: fp32 score bits, global indices
         self.run = torch.as_tensor(
             _DeviceArray(self._own + _lib.PEER_HEADER_BYTES, (2, self.rows, self.topk), "<i4"),
@@ -109,6 +116,46 @@ class PeerExchange:
         _lib.check(lib.prism_peer_merge(self._bufs, self.world, self.rank, self.rows, self.topk, 1,
                                         self.timeout_ns, out_idx.data_ptr(), out_scores.data_ptr(), stream),
                    "prism_peer_merge")
+
+    def wait_acks(self) -> None:
+        """On the current stream: wait until every rank has read this rank's run of
+        the current step. Needed before writing :attr:`run` when the previous step
+        ran :meth:`sharded_topk` (whose merge does not wait for the reads)."""
+        lib = _lib.load()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(lib.prism_peer_wait_acks(self._bufs, self.world, self.rank, self.timeout_ns, stream),
+                   "prism_peer_wait_acks")
+
+    def sharded_topk(self, q: torch.Tensor, k_shard: torch.Tensor, shard_start: int,
+                     inv_freq: Optional[torch.Tensor], out_idx: torch.Tensor,
+                     out_scores: torch.Tensor) -> None:
+        """One sequence-sharded step in one C call (``prism_sharded_topk``): the exact
+        local top-k of ``k_shard`` (keys at global positions / indices from
+        ``shard_start``) written into this rank's run, the publish and the merge into
+        out_idx / out_scores ([rows, topk]). The wait for the other ranks to have read
+        the previous step's run runs on the device while this step's scorer runs."""
+        assert out_idx.shape == (self.rows, self.topk) and out_idx.dtype == torch.int32
+        assert out_scores.shape == (self.rows, self.topk) and out_scores.dtype == torch.float32
+        assert out_idx.is_contiguous() and out_scores.is_contiguous()
+        lib = _lib.load()
+        B, Hq, Sq, D = q.shape
+        Hkv, Sk = k_shard.shape[1], k_shard.shape[2]
+        if B * Hq * Sq != self.rows:
+            raise ValueError(f"exchange built for {self.rows} rows, call has {B * Hq * Sq}")
+        dtype = _lib.DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.DTYPE_FP16
+        ws_bytes = int(lib.prism_einsum_topk_workspace_size(B, Hq, Sq, Sk, self.topk, _lib.MODE_EXACT))
+        if self._ws is None or self._ws.numel() < ws_bytes:
+            self._ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.device)
+        inv = None
+        if inv_freq is not None:
+            inv = inv_freq.to(device=self.device, dtype=torch.float32).contiguous()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = lib.prism_sharded_topk(
+            q.data_ptr(), k_shard.data_ptr(), inv.data_ptr() if inv is not None else None, dtype,
+            B, Hq, Hkv, Sq, Sk, D, _lib.i64_array(q.stride()), _lib.i64_array(k_shard.stride()),
+            int(shard_start), self.topk, self._bufs, self.world, self.rank, 1, self.timeout_ns,
+            out_idx.data_ptr(), out_scores.data_ptr(), self._ws.data_ptr(), self._ws.numel(), stream)
+        _lib.check(rc, "prism_sharded_topk")
 
     def status(self) -> int:
         """The exchange's device status word (0, or 1 after an expired wait); resets it."""

@@ -107,11 +107,16 @@ def sharded_einsum_topk(
         rows = B * Hq * Sq
         if (exchange.rows, exchange.topk) != (rows, topk):
             raise ValueError(f"exchange built for {exchange.rows} x {exchange.topk}, call needs {rows} x {topk}")
-        extra = {} if recall_type == "qk" else dict(values=v_shard, recall_type=recall_type)
-        _local_packed(local_topk, q, k_shard, topk, inv_freq, shard_start, extra, dest=exchange.run)
         out_i = torch.empty((rows, topk), dtype=torch.int32, device=q.device)
         out_s = torch.empty((rows, topk), dtype=torch.float32, device=q.device)
-        exchange.merge(out_i, out_s)
+        if recall_type == "qk" and local_topk is einsum_topk_func and k_shard.shape[2] >= topk:
+            # one C call: local top-k into the run, publish, merge
+            exchange.sharded_topk(q, k_shard, shard_start, inv_freq, out_i, out_s)
+        else:
+            extra = {} if recall_type == "qk" else dict(values=v_shard, recall_type=recall_type)
+            exchange.wait_acks()  # the run may still be read by a sharded_topk step's merges
+            _local_packed(local_topk, q, k_shard, topk, inv_freq, shard_start, extra, dest=exchange.run)
+            exchange.merge(out_i, out_s)
         out_i, out_s = out_i.reshape(B, Hq, Sq, topk), out_s.reshape(B, Hq, Sq, topk)
         return (out_i, out_s) if return_scores else out_i
     pending = []

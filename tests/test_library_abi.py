@@ -170,6 +170,9 @@ def test_peer_exchange_validation(lib):
     assert lib.prism_peer_publish(mis, 2, 0, None) == _lib.PRISM_E_INVALID
     nul = (ctypes.c_void_p * 2)(1 << 20, None)
     assert lib.prism_peer_publish(nul, 2, 0, None) == _lib.PRISM_E_INVALID
+    assert lib.prism_peer_wait_acks(fake, 0, 0, 0, None) == _lib.PRISM_E_UNSUPPORTED
+    assert lib.prism_peer_wait_acks(fake, 3, 5, 0, None) == _lib.PRISM_E_INVALID
+    assert lib.prism_peer_wait_acks(mis, 2, 0, 0, None) == _lib.PRISM_E_INVALID
     out = 4 << 20
     assert lib.prism_peer_merge(fake, 3, 0, 4, 16, 1, 0, None, None, None) == _lib.PRISM_E_INVALID
     assert lib.prism_peer_merge(fake, 3, 0, 0, 16, 1, 0, out, None, None) == _lib.PRISM_E_INVALID

@@ -299,6 +299,16 @@ def _two_gpu_worker(rank, world, port, errq):
                 ci, cs = _sharded_c(lib, qd, kd, invd, start, topk, ex._bufs, world, rank)
                 torch.cuda.synchronize()
                 assert torch.equal(ci, want_i) and torch.equal(cs, want_s)
+            # steps whose local top-k the caller writes into the run (publish + merge
+            # path) between single-call steps, whose merges leave the read
+            # acknowledgements to the next step
+            def wrapped(*a, **kw):
+                return einsum_topk_func(*a, **kw)
+            for fn in (wrapped, None, wrapped, None):
+                gi, gs = sharded_einsum_topk(qd, kd, topk, shard_start=start, inv_freq=invd,
+                                             return_scores=True, exchange=ex, local_topk=fn)
+                torch.cuda.synchronize()
+                assert torch.equal(gi, want_i) and torch.equal(gs, want_s)
             assert ex.status() == 0
         finally:
             ex.close()
