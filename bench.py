@@ -441,7 +441,7 @@ def run_reference(args):
 # (name in kernels_ms_per_step, kernel id of the library's profiling aid)
 KERNEL_IDS = (("score", "KERNEL_SCORE"), ("select", "KERNEL_SELECT"), ("merge", "KERNEL_MERGE"),
               ("value_norms", "KERNEL_WEIGHT"), ("score_weighting", "KERNEL_SCALE"),
-              ("threshold", "KERNEL_THRESHOLD"))
+              ("threshold", "KERNEL_THRESHOLD"), ("unrotate", "KERNEL_UNROTATE"))
 
 
 class Ranks:
@@ -714,14 +714,15 @@ def roofline_of(res, rt="qk") -> tuple:
     """(roofline of the dominant kernel, roofline of the whole step) of one measurement."""
     wl = res["wl"]
     score_ms = res["score_ms"]
-    prefill = wl.Sq >= 128 and not wl.rope  # the tcgen05 path: tensor-bound
+    prefill = wl.Sq >= 128  # the tcgen05 path: tensor-bound
     if prefill:
         work = prefill_flops(wl)
         peak, src = measured_peaks("bf16_tflops_sustained")
         achieved = work / (score_ms * 1e-3) / 1e12
         roof = {"bound": "tensor", "unit": "TFLOP/s", "flops_per_launch": work,
                 "kernel": "prefill candidate pass (tcgen05 kind::f16 M128 N128, TMEM accumulators, "
-                          "threshold epilogue)",
+                          "threshold epilogue" + (", hi + lo un-rotated key planes: twice the MMAs of the "
+                                                  "FLOPs counted)" if wl.rope else ")"),
                 "peak_note": "sustained bf16 GEMM peak: the kernel runs inside a long step loop"}
         step_work = work
         step_achieved = work / (res["ms_per_step"] * 1e-3) / 1e12
@@ -799,7 +800,7 @@ def main():
     if rank != 0:
         return 0
     roof, step_roof = roofline_of(main_res, rt)
-    prefill = wl.Sq >= 128 and not wl.rope
+    prefill = wl.Sq >= 128
     line = {
         "metric": METRIC, "value": main_res["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": main_res["ms_per_step"], "higher_is_better": True,

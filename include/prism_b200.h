@@ -79,14 +79,21 @@ extern "C" {
  *              key sample, the keys at or above them, a selection per row, and
  *              an exact recompute of any row the threshold missed. Exact mode
  *              takes it by itself when Sq >= 128, Sk >= 8192, topk <= 4096 and
- *              the score matrix would be 2 GiB or more; it needs raw keys
- *              (inv_freq NULL), at least 128 query rows per KV head, 16-byte
- *              aligned query rows and topk <= 4096 (PRISM_E_UNSUPPORTED otherwise).
+ *              the score matrix would be 2 GiB or more; it needs at least 128
+ *              query rows per KV head, 16-byte aligned query rows and
+ *              topk <= 4096 (PRISM_E_UNSUPPORTED otherwise), and, for RoPE'd
+ *              keys, prism_einsum_topk_rope_workspace_size() bytes of workspace.
  *   index_base added to every output index (global index of key 0 of this shard).
  *   out_idx    [B, Hq, Sq, topk] int32, contiguous. Sorted by descending score,
  *              ties by ascending index.
  *   out_scores [B, Hq, Sq, topk] fp32, contiguous, or NULL.
  *   workspace  device memory of at least prism_einsum_topk_workspace_size() bytes.
+ *              RoPE'd keys with at least 128 query rows per KV head (prefill
+ *              chunks) are scored on the tensor cores from un-rotated copies of
+ *              the keys kept in the workspace: give
+ *              prism_einsum_topk_rope_workspace_size() bytes (the score-matrix
+ *              path falls back to the CUDA-core scorers with less; the streaming
+ *              path returns PRISM_E_WORKSPACE).
  *   stream     cudaStream_t.
  */
 PRISM_API int prism_einsum_topk(const void* q, const void* k, const float* inv_freq, int dtype,
@@ -131,6 +138,16 @@ PRISM_API size_t prism_einsum_topk_workspace_size(int64_t B, int64_t Hq, int64_t
 PRISM_API size_t prism_einsum_topk_weighted_workspace_size(int64_t B, int64_t Hq, int64_t Hkv,
                                                            int64_t Sq, int64_t Sk, int32_t topk,
                                                            int32_t mode, int32_t recall_weight);
+/*
+ * Workspace bytes for a call with RoPE'd keys (inv_freq != NULL), to
+ * prism_einsum_topk (recall_weight PRISM_RECALL_QK) or prism_einsum_topk_weighted:
+ * the size above plus, when the call has at least 128 query rows per KV head,
+ * B * Hkv * Sk * 512 bytes for the keys un-rotated once into two 16-bit planes
+ * (hi + lo within 2^-17 of the fp32 un-rotated key) that the tcgen05 scorer reads.
+ */
+PRISM_API size_t prism_einsum_topk_rope_workspace_size(int64_t B, int64_t Hq, int64_t Hkv,
+                                                       int64_t Sq, int64_t Sk, int32_t topk,
+                                                       int32_t mode, int32_t recall_weight);
 PRISM_API int prism_einsum_topk_weighted(const void* q, const void* k, const void* v,
                                          const float* inv_freq, int dtype, int64_t B, int64_t Hq,
                                          int64_t Hkv, int64_t Sq, int64_t Sk, int64_t D,
@@ -282,7 +299,9 @@ PRISM_API int prism_peer_wait_acks(void* const* bufs, int32_t world, int32_t ran
  *               rewrites its run before all ranks have read it.
  *   timeout_ns  bound of every device-side wait (<= 0: 2 s)
  *   workspace   prism_einsum_topk_workspace_size(B, Hq, Sq, Sk_shard, topk,
- *               PRISM_MODE_EXACT) bytes, 256-byte aligned
+ *               PRISM_MODE_EXACT) bytes, 256-byte aligned (with inv_freq:
+ *               prism_einsum_topk_rope_workspace_size(B, Hq, Hkv, Sq, Sk_shard, topk,
+ *               PRISM_MODE_EXACT, PRISM_RECALL_QK))
  * Every rank makes the call for the same step, with the same shapes, in the same
  * order relative to its other exchange calls.
  */
@@ -384,6 +403,7 @@ PRISM_API int prism_read_status(void* workspace, int* status_out, void* stream);
 #define PRISM_KERNEL_SCALE 4  /* weighting of the score matrix by those norms */
 #define PRISM_KERNEL_THRESHOLD 5 /* sampled per-row thresholds of the streaming prefill path */
 #define PRISM_KERNEL_ATTN 6   /* attention over the selected view */
+#define PRISM_KERNEL_UNROTATE 7 /* RoPE'd keys un-rotated into planes for the tensor-core scorer */
 PRISM_API int prism_profile_start(int32_t capacity);
 PRISM_API int prism_profile_stop(void);
 PRISM_API int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms);

@@ -87,20 +87,27 @@ def check_parity(idx: torch.Tensor, scores: Optional[torch.Tensor], q: torch.Ten
 
 
 def check_rows_parity(idx: torch.Tensor, scores: torch.Tensor, q: torch.Tensor, k: torch.Tensor,
-                      topk: int, rows, causal_offset: Optional[int] = None, rel: float = REL) -> int:
+                      topk: int, rows, causal_offset: Optional[int] = None, rel: float = REL,
+                      inv_freq: Optional[torch.Tensor] = None, pos_offset: int = 0) -> int:
     """The parity rules on selected flattened rows (b, hq, s) only, for shapes whose
-    full oracle does not fit in memory; keys raw (no RoPE). Returns near-tie swaps."""
+    full oracle does not fit in memory; RoPE'd keys (inv_freq given) are un-rotated
+    once per (batch, KV head) by the oracle. Returns near-tie swaps."""
     B, Hq, Sq, _ = q.shape
     Hkv, Sk = k.shape[1], k.shape[2]
     G = Hq // Hkv
     idx = idx.reshape(B * Hq * Sq, topk)
     scores = scores.reshape(B * Hq * Sq, topk)
+    inv = inv_freq.cpu() if inv_freq is not None else None
+    raw = {}  # (b, kv head) -> fp32 raw keys [Sk, D]
     swaps = 0
     for row in rows:
         s = row % Sq
         b, hq = divmod(row // Sq, Hq)
         qv = q[b, hq, s].float().cpu()
-        kk = k[b, hq // G].float().cpu()
+        if (b, hq // G) not in raw:
+            kh = k[b:b + 1, hq // G:hq // G + 1].cpu()
+            raw[(b, hq // G)] = orc.unrotate_keys(kh, inv, pos_offset)[0, 0].float()
+        kk = raw[(b, hq // G)]
         full = kk @ qv                                            # [Sk]
         tol = rel * qv.norm() * kk.norm(dim=-1)                   # [Sk]
         if causal_offset is not None:

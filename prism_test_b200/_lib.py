@@ -32,6 +32,7 @@ KERNEL_WEIGHT = 3
 KERNEL_SCALE = 4
 KERNEL_THRESHOLD = 5
 KERNEL_ATTN = 6
+KERNEL_UNROTATE = 7
 RECALL_QK = 0
 RECALL_QKV = 1
 RECALL_QKV2 = 2
@@ -59,6 +60,9 @@ SIGNATURES = {
         _vp, _vp, _vp, ctypes.c_size_t, _vp,
     ]),
     "prism_einsum_topk_weighted_workspace_size": (ctypes.c_size_t, [
+        _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32,
+    ]),
+    "prism_einsum_topk_rope_workspace_size": (ctypes.c_size_t, [
         _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32,
     ]),
     "prism_einsum_topk_workspace_size": (ctypes.c_size_t, [

@@ -57,7 +57,7 @@ std::vector<cudaEvent_t> g_prof_pool;  // 2 * capacity events
 std::vector<ProfRec> g_prof_recs;
 bool g_prof_on = false;
 size_t g_prof_next = 0;
-int64_t g_prof_untimed[7] = {0, 0, 0, 0, 0, 0, 0};
+int64_t g_prof_untimed[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 
 // Runs `launch` (which enqueues one kernel on `stream`), counting it and, while
 // profiling is on, bracketing it with a pair of events from the pool.
@@ -116,6 +116,11 @@ size_t wide_stream_workspace(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk, int3
 // the value-norm weights of the weighted call follow, 256-byte aligned
 size_t weights_offset(int64_t B, int64_t Hq, int64_t Sq, int64_t Sk) {
   return size_t(round_up(int64_t(exact_workspace(B, Hq, Sq, Sk)), 256));
+}
+// RoPE'd keys reach the tcgen05 scorer (>= kPrefillMinRows query rows per KV head)
+// through un-rotated hi / lo key planes placed after the rest of the workspace
+bool rope_planes_shape(int64_t Hq, int64_t Hkv, int64_t Sq) {
+  return Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) * Sq >= prism::kPrefillMinRows;
 }
 
 }  // namespace
@@ -202,10 +207,6 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
     if (topk > kStreamMinTopk)
       return fail(PRISM_E_UNSUPPORTED, "the streaming prefill path takes topk <= %lld, got %d",
                   (long long)kStreamMinTopk, topk);
-    if (inv_freq)
-      return fail(PRISM_E_UNSUPPORTED,
-                  "the streaming prefill path (score matrix of 2 GiB or more, or "
-                  "PRISM_MODE_EXACT_STREAM) takes raw keys: pass inv_freq = NULL");
     if (weight)
       return fail(PRISM_E_UNSUPPORTED, "value-weighted recall is not available on the streaming "
                                        "prefill path");
@@ -223,6 +224,18 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
     return fail(PRISM_E_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return fail(PRISM_E_INVALID, "workspace must be 256-byte aligned");
+  // RoPE'd keys on the tcgen05 scorer: the un-rotated planes after `need`. The
+  // streaming path requires them; the score-matrix path uses the CUDA-core scorers
+  // when the workspace has no room for them.
+  const size_t planes_off = size_t(round_up(int64_t(need), 256));
+  const size_t planes_end = planes_off + prism::rope_planes_bytes(B, Hkv, Sk);
+  const bool want_planes = inv_freq != nullptr && rope_planes_shape(Hq, Hkv, Sq);
+  if (streaming && inv_freq != nullptr && workspace_bytes < planes_end)
+    return fail(PRISM_E_WORKSPACE,
+                "RoPE'd keys on the streaming path need %zu bytes of workspace "
+                "(prism_einsum_topk_rope_workspace_size), got %zu",
+                planes_end, workspace_bytes);
+  const bool use_planes = want_planes && workspace_bytes >= planes_end;
 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -280,6 +293,11 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
   a.ld = ld;
   a.ntiles = int((Sk + 127) / 128);
   a.status = status;
+  a.planes = use_planes ? static_cast<void*>(ws + planes_off) : nullptr;
+  auto unrotate = [&]() -> cudaError_t {
+    return launch_counted(PRISM_KERNEL_UNROTATE, stream,
+                          [&] { return prism::launch_unrotate_planes(a, dtype, nsm, stream); });
+  };
   // specialised kernels take every query row of a KV head in one launch:
   // tensor-core tiles (keys as M for <= 16 rows per KV head, queries as M up
   // to 256 / Hkv rows), CUDA cores for <= 4
@@ -291,6 +309,10 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
   if (streaming) {  // thresholds, candidates, per-row selection + exact fallback
     e = wait_acks();
     if (e != cudaSuccess) return cuda_fail(e, "peer ack wait launch");
+    if (a.planes != nullptr) {
+      e = unrotate();
+      if (e != cudaSuccess) return cuda_fail(e, "key un-rotation launch");
+    }
     void* pws = ws + kStatusBytes;
     e = launch_counted(PRISM_KERNEL_THRESHOLD, stream,
                        [&] { return prism::prefill_stream_threshold(a, dtype, topk, pws, stream); });
@@ -344,6 +366,10 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
                        [&] { return prism::launch_decode_scores_wide(a, dtype, nsm, stream); });
     if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
   } else if (prism::prefill_tc_supported(a)) {
+    if (a.planes != nullptr) {
+      e = unrotate();
+      if (e != cudaSuccess) return cuda_fail(e, "key un-rotation launch");
+    }
     e = launch_counted(PRISM_KERNEL_SCORE, stream,
                        [&] { return prism::launch_prefill_scores_tc(a, dtype, stream); });
     if (e != cudaSuccess) return cuda_fail(e, "prefill score kernel launch");
@@ -425,6 +451,15 @@ size_t prism_einsum_topk_weighted_workspace_size(int64_t B, int64_t Hq, int64_t 
   if (recall_weight == PRISM_RECALL_QK) return base;
   if (recall_weight != PRISM_RECALL_QKV && recall_weight != PRISM_RECALL_QKV2) return 0;
   return weights_offset(B, Hq, Sq, Sk) + prism::weight_workspace_bytes(B, Hkv, Sk);
+}
+
+size_t prism_einsum_topk_rope_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq,
+                                             int64_t Sk, int32_t topk, int32_t mode,
+                                             int32_t recall_weight) {
+  const size_t base =
+      prism_einsum_topk_weighted_workspace_size(B, Hq, Hkv, Sq, Sk, topk, mode, recall_weight);
+  if (base == 0 || !rope_planes_shape(Hq, Hkv, Sq)) return base;
+  return size_t(round_up(int64_t(base), 256)) + prism::rope_planes_bytes(B, Hkv, Sk);
 }
 
 int prism_einsum_topk_weighted(const void* q, const void* k, const void* v, const float* inv_freq,
@@ -672,7 +707,7 @@ int prism_profile_stop(void) {
 
 int prism_profile_read(int32_t kernel, int64_t* launches, double* total_ms) {
   g_last_error.clear();
-  if (!launches || !total_ms || kernel < 0 || kernel > PRISM_KERNEL_ATTN)
+  if (!launches || !total_ms || kernel < 0 || kernel > PRISM_KERNEL_UNROTATE)
     return fail(PRISM_E_INVALID, "bad kernel id or null output");
   int64_t n = 0;
   double ms = 0.0;

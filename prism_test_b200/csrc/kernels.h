@@ -28,6 +28,8 @@ struct DecodeArgs {
   int ntiles;
   int* status;
   unsigned int* work;       // nullptr, or B work counters, zero at launch (dynamic slice claims)
+  void* planes;             // RoPE'd keys on the tcgen05 scorer: the un-rotated keys as 16-bit
+                            // hi / lo planes (rope_planes_bytes), or nullptr
 };
 
 // rows (Hq * sq_n) resident per CTA must not exceed this
@@ -69,8 +71,14 @@ cudaError_t launch_decode_scores_g4(const DecodeArgs& a, int dtype, int num_sms,
 // Tensor-core (tcgen05) scorer for raw keys (inv_freq == nullptr) and at least
 // kPrefillMinRows query rows per KV head; q rows 16-byte aligned.
 constexpr int kPrefillMinRows = 128;
+// RoPE'd keys take it through un-rotated planes (a.planes, written by
+// launch_unrotate_planes): [nb, Hkv, 2, Sk, 128] of the keys' dtype, hi then lo,
+// hi + lo = the fp32 un-rotated key within 2^-17 relative; nb = B, or 1 when the
+// keys are shared across the batch (k_sb == 0).
 bool prefill_tc_supported(const DecodeArgs& a);
 cudaError_t launch_prefill_scores_tc(const DecodeArgs& a, int dtype, cudaStream_t stream);
+size_t rope_planes_bytes(int64_t B, int64_t Hkv, int64_t Sk);
+cudaError_t launch_unrotate_planes(const DecodeArgs& a, int dtype, int num_sms, cudaStream_t stream);
 
 // Streaming prefill top-k (no score matrix): per-row thresholds from a strided
 // key sample (every kSampleStride-th key), then the candidates >= threshold,

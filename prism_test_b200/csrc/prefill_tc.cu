@@ -20,6 +20,14 @@
 // zero). 16-bit products are exact in the fp32 accumulator, so the scores equal
 // the fp32 einsum of the oracle up to summation order.
 //
+// RoPE'd keys (the cache _unrotate_keys un-rotates, reattention.py:743-793, with
+// undo_rotary_pos_emb, _method_base.py:336-350): unrotate_planes_kernel first
+// writes each key un-rotated in fp32 and split into two 16-bit planes, hi =
+// round(k) and lo = round(k - hi) (|k - hi - lo| <= 2^-17 |k|). The ring then
+// carries two 32 KB items per key tile, hi and lo, and the MMA issuer adds q·lo
+// into the accumulator after q·hi: 16 MMA steps per key tile and query tile.
+// The rotation runs once per key, not once per CTA that reads the key.
+//
 // Modes (the epilogue's work):
 //   kScores  writes the fp32 score matrix [rows, ld] (masked keys -inf) for the
 //            selection kernels;
@@ -45,6 +53,7 @@
 // kStatusTimeout, the roles leave their loops, and the TMEM is still freed.
 #include "common.cuh"
 #include "kernels.h"
+#include "rope_sincos.cuh"
 #include "tc_sm100.cuh"
 #include "tensor_map.h"
 
@@ -102,6 +111,8 @@ struct PfArgs {
   int64_t cap;
   int topk;
   int pairs;           // CTAs per (batch, KV head)
+  int parts;           // ring items per key tile: 1 (the keys), 2 (hi and lo planes)
+  int kbatched;        // the key map has a batch dimension (else every batch row reads batch 0)
   int* status;
 };
 
@@ -201,19 +212,22 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
     // ---- TMA producer ------------------------------------------------------------
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      const int kb = (a.B > 1) ? b : 0;
-      for (int t = 0; t < nkt; ++t) {
-        const int s = t % kStages;
-        if (t >= kStages &&
-            !mbar_wait_bounded(&bars->empty[s], uint32_t((t / kStages - 1) & 1))) {
+      const int kb = a.kbatched ? b : 0;
+      const int nit = nkt * a.parts;  // ring items: key tile t, part p at u = t * parts + p
+      for (int u = 0; u < nit; ++u) {
+        const int s = u % kStages;
+        if (u >= kStages &&
+            !mbar_wait_bounded(&bars->empty[s], uint32_t((u / kStages - 1) & 1))) {
           set_status(a.status, kStatusTimeout);
           break;
         }
+        const int t = a.parts == 1 ? u : u >> 1;
+        const int hh = h * a.parts + (u - t * a.parts);  // the head's key plane
         const int tt = tile_of(t);  // tile within the pass
         mbar_arrive_expect_tx(&bars->full[s], kTileBytes);
         uint8_t* dst = smem + kBOff + uint32_t(s) * kTileBytes;
-        tma_load_4d(dst, &kmap, 0, tt * 128, h, kb, &bars->full[s], pol);
-        tma_load_4d(dst + kAtomBytes, &kmap, 64, tt * 128, h, kb, &bars->full[s], pol);
+        tma_load_4d(dst, &kmap, 0, tt * 128, hh, kb, &bars->full[s], pol);
+        tma_load_4d(dst + kAtomBytes, &kmap, 64, tt * 128, hh, kb, &bars->full[s], pol);
       }
     }
   } else if (warp == 1) {
@@ -222,27 +236,31 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
       constexpr uint32_t idesc = idesc_kind_f16(kBF16, 128, 128);
       bool ok = true;
       for (int t = 0; t < nkt && ok; ++t) {
-        const int s = t % kStages, buf = t & 1;
-        ok = mbar_wait_bounded(&bars->full[s], uint32_t((t / kStages) & 1));
-        if (ok && t >= 2) ok = mbar_wait_bounded(&bars->tempty[buf], uint32_t((t / 2 - 1) & 1));
+        const int buf = t & 1;
+        if (t >= 2) ok = mbar_wait_bounded(&bars->tempty[buf], uint32_t((t / 2 - 1) & 1));
+        for (int part = 0; part < a.parts && ok; ++part) {
+          const int u = t * a.parts + part, s = u % kStages;
+          ok = mbar_wait_bounded(&bars->full[s], uint32_t((u / kStages) & 1));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t bsm = sbase + kBOff + uint32_t(s) * kTileBytes;
+#pragma unroll
+          for (int qt = 0; qt < 2; ++qt) {
+            const uint32_t asm_ = sbase + kAOff + uint32_t(qt) * kTileBytes;
+            const uint32_t d = tmem + uint32_t(buf) * 256 + uint32_t(qt) * 128;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const uint32_t koff = uint32_t(ks >> 2) * kAtomBytes + uint32_t(ks & 3) * 32;
+              tc_mma_f16(d, sw128_kmajor_desc(asm_ + koff), sw128_kmajor_desc(bsm + koff), idesc,
+                         (part > 0 || ks > 0) ? 1u : 0u);
+            }
+          }
+          tc_commit(&bars->empty[s]);
+        }
         if (!ok) {
           set_status(a.status, kStatusTimeout);
           break;
         }
-        tc_fence_after();
-        const uint32_t bsm = sbase + kBOff + uint32_t(s) * kTileBytes;
-#pragma unroll
-        for (int qt = 0; qt < 2; ++qt) {
-          const uint32_t asm_ = sbase + kAOff + uint32_t(qt) * kTileBytes;
-          const uint32_t d = tmem + uint32_t(buf) * 256 + uint32_t(qt) * 128;
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const uint32_t koff = uint32_t(ks >> 2) * kAtomBytes + uint32_t(ks & 3) * 32;
-            tc_mma_f16(d, sw128_kmajor_desc(asm_ + koff), sw128_kmajor_desc(bsm + koff), idesc,
-                       ks > 0 ? 1u : 0u);
-          }
-        }
-        tc_commit(&bars->empty[s]);
         tc_commit(&bars->tfull[buf]);
       }
       tc_commit(&bars->done);
@@ -435,6 +453,92 @@ __global__ void __launch_bounds__(PfCfg<kMode>::kThreads, 1)
   }
 }
 
+// 16-bit hi / lo split of two fp32 values, packed (element 0 in the low half)
+template <typename T>
+struct Split16;
+template <>
+struct Split16<__nv_bfloat16> {
+  __device__ __forceinline__ static void run(float x, float y, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+  }
+};
+template <>
+struct Split16<__half> {
+  __device__ __forceinline__ static void run(float x, float y, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x, y);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+  }
+};
+
+// One warp per key position at a time: lane l takes the frequency pairs 2l and
+// 2l + 1, i.e. dimensions {2l, 2l + 1} and {64 + 2l, 65 + 2l}; the angles
+// fp32(pos) * inv_freq[i] and their sin / cos are computed once per position and
+// applied to the key of every (batch, KV head). Un-rotation as in the decode
+// scorers: r_i = x_i c + x_{i+64} s, r_{i+64} = x_{i+64} c - x_i s, in fp32.
+template <typename T>
+__global__ void __launch_bounds__(256) unrotate_planes_kernel(const DecodeArgs a, int nb) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w0 = (int64_t(blockIdx.x) * 256 + threadIdx.x) >> 5;
+  const int64_t nw = int64_t(gridDim.x) * 8;
+  const float f0 = a.inv_freq[2 * lane], f1 = a.inv_freq[2 * lane + 1];
+  const int64_t plane_words = int64_t(a.Sk) * 64;  // 32-bit words per plane
+  const T* kbase = static_cast<const T*>(a.k);
+  uint32_t* out = static_cast<uint32_t*>(a.planes);
+  const int nh = nb * a.Hkv;
+  for (int64_t j = w0; j < a.Sk; j += nw) {
+    const float pf = static_cast<float>(a.pos_offset + j);
+    float s0, c0, s1, c1;
+    rope_sincos(__fmul_rn(pf, f0), s0, c0);
+    rope_sincos(__fmul_rn(pf, f1), s1, c1);
+#pragma unroll 4
+    for (int bh = 0; bh < nh; ++bh) {
+      const int b = bh / a.Hkv, h = bh - b * a.Hkv;
+      const uint32_t* kr =
+          reinterpret_cast<const uint32_t*>(kbase + int64_t(b) * a.k_sb + int64_t(h) * a.k_sh + j * 128);
+      const uint32_t wa = __ldcs(kr + lane), wb = __ldcs(kr + 32 + lane);
+      float x0, x0b, x1, x1b;
+      Unpack<T>::run(wa, x0, x0b);  // dimensions 2l, 2l + 1
+      Unpack<T>::run(wb, x1, x1b);  // dimensions 64 + 2l, 65 + 2l
+      const float r0 = fmaf(x0, c0, x1 * s0), r0b = fmaf(x0b, c1, x1b * s1);
+      const float r1 = fmaf(x1, c0, -(x0 * s0)), r1b = fmaf(x1b, c1, -(x0b * s1));
+      uint32_t h0, l0, h1, l1;
+      Split16<T>::run(r0, r0b, h0, l0);
+      Split16<T>::run(r1, r1b, h1, l1);
+      uint32_t* hi = out + int64_t(bh) * 2 * plane_words + j * 64;
+      uint32_t* lo = hi + plane_words;
+      hi[lane] = h0;
+      hi[32 + lane] = h1;
+      lo[lane] = l0;
+      lo[32 + lane] = l1;
+    }
+  }
+}
+
+// batch rows of the planes: one set when the keys are shared across the batch
+int plane_batches(const DecodeArgs& d) { return d.B > 1 && d.k_sb != 0 ? d.B : 1; }
+
+// the key map of a launch: the keys, or (RoPE'd keys) the hi / lo planes
+cudaError_t key_map(const DecodeArgs& d, int dtype, int key_stride, CUtensorMap* m, PfArgs& a) {
+  if (d.inv_freq != nullptr) {
+    if (d.planes == nullptr) return cudaErrorInvalidValue;
+    const int nb = plane_batches(d);
+    a.parts = 2;
+    a.kbatched = nb > 1;
+    return make_key_tensor_map_sw128(m, d.planes, dtype, nb, 2 * int64_t(d.Hkv), d.Sk,
+                                     2 * int64_t(d.Hkv) * d.Sk * 128, int64_t(d.Sk) * 128, key_stride);
+  }
+  a.parts = 1;
+  a.kbatched = d.B > 1 && d.k_sb != 0;
+  return make_key_tensor_map_sw128(m, d.k, dtype, d.B, d.Hkv, d.Sk, d.k_sb, d.k_sh, key_stride);
+}
+
 PfArgs make_args(const DecodeArgs& d) {
   PfArgs a{};
   a.q = d.q;
@@ -469,27 +573,41 @@ cudaError_t launch_mode(const CUtensorMap& kmap, const PfArgs& a, int dtype, int
 
 }  // namespace
 
+size_t rope_planes_bytes(int64_t B, int64_t Hkv, int64_t Sk) {
+  return size_t(B) * size_t(Hkv) * 2 * size_t(Sk) * 128 * 2;
+}
+
+cudaError_t launch_unrotate_planes(const DecodeArgs& d, int dtype, int num_sms, cudaStream_t stream) {
+  if (d.inv_freq == nullptr || d.planes == nullptr) return cudaErrorInvalidValue;
+  const int64_t want = (int64_t(d.Sk) + 7) / 8;  // one warp per position
+  const unsigned grid = unsigned(want < int64_t(num_sms) * 8 ? want : int64_t(num_sms) * 8);
+  if (dtype == kBF16)
+    unrotate_planes_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(d, plane_batches(d));
+  else
+    unrotate_planes_kernel<__half><<<grid, 256, 0, stream>>>(d, plane_batches(d));
+  return cudaGetLastError();
+}
+
 bool prefill_tc_supported(const DecodeArgs& a) {
-  return a.inv_freq == nullptr && int64_t(a.G) * a.Sq >= kPrefillMinRows &&
+  return (a.inv_freq == nullptr || a.planes != nullptr) && int64_t(a.G) * a.Sq >= kPrefillMinRows &&
          (a.q_ss % 8) == 0 && (a.q_sh % 8) == 0 && (a.q_sb % 8) == 0 &&
          (reinterpret_cast<uintptr_t>(a.q) & 15u) == 0;
 }
 
 cudaError_t launch_prefill_scores_tc(const DecodeArgs& d, int dtype, cudaStream_t stream) {
   CUtensorMap kmap;
-  cudaError_t e = make_key_tensor_map_sw128(&kmap, d.k, dtype, d.B, d.Hkv, d.Sk, d.k_sb, d.k_sh);
+  PfArgs a = make_args(d);
+  cudaError_t e = key_map(d, dtype, 1, &kmap, a);
   if (e != cudaSuccess) return e;
-  const PfArgs a = make_args(d);
   return launch_mode<kScores>(kmap, a, dtype, int64_t(a.pairs) * d.B * d.Hkv, stream);
 }
 
 cudaError_t launch_prefill_threshold_tc(const DecodeArgs& d, int dtype, int topk, float* thr,
                                         cudaStream_t stream) {
   CUtensorMap smap;
-  cudaError_t e = make_key_tensor_map_sw128(&smap, d.k, dtype, d.B, d.Hkv, d.Sk, d.k_sb, d.k_sh,
-                                            kSampleStride);
-  if (e != cudaSuccess) return e;
   PfArgs a = make_args(d);
+  cudaError_t e = key_map(d, dtype, kSampleStride, &smap, a);
+  if (e != cudaSuccess) return e;
   a.thr = thr;
   a.topk = topk;
   return launch_mode<kSample>(smap, a, dtype, int64_t(a.pairs) * d.B * d.Hkv, stream);
@@ -499,9 +617,9 @@ cudaError_t launch_prefill_candidates_tc(const DecodeArgs& d, int dtype, const f
                                          uint32_t* counts, uint64_t* cand, int64_t cap,
                                          cudaStream_t stream) {
   CUtensorMap kmap;
-  cudaError_t e = make_key_tensor_map_sw128(&kmap, d.k, dtype, d.B, d.Hkv, d.Sk, d.k_sb, d.k_sh);
-  if (e != cudaSuccess) return e;
   PfArgs a = make_args(d);
+  cudaError_t e = key_map(d, dtype, 1, &kmap, a);
+  if (e != cudaSuccess) return e;
   a.thr = const_cast<float*>(thr);
   a.counts = counts;
   a.cand = cand;

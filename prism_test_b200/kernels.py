@@ -182,8 +182,9 @@ def einsum_topk_func(
                 torch.empty((batch, num_heads, seqlen_q, topk), dtype=torch.float32, device=q.device)
                 if return_scores else None
             )
-        ws_bytes = lib.prism_einsum_topk_weighted_workspace_size(
-            batch, num_heads, num_heads_k, seqlen_q, seqlen_k, topk, mode_code, weight_code)
+        size_fn = (lib.prism_einsum_topk_rope_workspace_size if invf_ptr is not None
+                   else lib.prism_einsum_topk_weighted_workspace_size)
+        ws_bytes = size_fn(batch, num_heads, num_heads_k, seqlen_q, seqlen_k, topk, mode_code, weight_code)
         ws = torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=q.device)
         stream = torch.cuda.current_stream(q.device).cuda_stream
         if weight_code == _lib.RECALL_QK:

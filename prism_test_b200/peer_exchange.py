@@ -143,7 +143,11 @@ class PeerExchange:
         if B * Hq * Sq != self.rows:
             raise ValueError(f"exchange built for {self.rows} rows, call has {B * Hq * Sq}")
         dtype = _lib.DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.DTYPE_FP16
-        ws_bytes = int(lib.prism_einsum_topk_workspace_size(B, Hq, Sq, Sk, self.topk, _lib.MODE_EXACT))
+        if inv_freq is not None:
+            ws_bytes = int(lib.prism_einsum_topk_rope_workspace_size(B, Hq, Hkv, Sq, Sk, self.topk,
+                                                                     _lib.MODE_EXACT, _lib.RECALL_QK))
+        else:
+            ws_bytes = int(lib.prism_einsum_topk_workspace_size(B, Hq, Sq, Sk, self.topk, _lib.MODE_EXACT))
         if self._ws is None or self._ws.numel() < ws_bytes:
             self._ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.device)
         inv = None

@@ -70,6 +70,9 @@ WORKLOADS: Dict[str, Workload] = {
     # the same chunk cut to its last 512 query rows (profiling-sized)
     "prefill-chunk-128k-512rows": Workload("prefill-chunk-128k-512rows", 1, 32, 8, 512, 131072,
                                            5e5, 2048, causal_offset=130560, rope=False),
+    # the same chunk over a RoPE'd cache (keys un-rotated on the device first)
+    "prefill-chunk-128k-rope": Workload("prefill-chunk-128k-rope", 1, 32, 8, 4096, 131072, 5e5, 2048,
+                                        causal_offset=126976, rope=True),
     # 1M-key decode, sequence-sharded over N GPUs
     "decode-1m-sharded": Workload("decode-1m-sharded", 1, 32, 8, 1, 1 << 20, 5e5, 8192,
                                   planted_per_qhead=64, planted_sigma=5.0),

@@ -86,6 +86,18 @@ def test_argument_validation(lib, over, code):
     assert _lib.last_error()
 
 
+def test_rope_streaming_needs_the_planes(lib):
+    # RoPE'd keys on the streaming path: the plain streaming workspace is refused
+    # (before any CUDA call), naming the size function that covers the planes
+    shape = dict(Hq=4, Hkv=2, Sq=64, Sk=256, qs=(64 * 4 * 128, 64 * 128, 128, 1), mode=_lib.MODE_EXACT_STREAM,
+                 inv=16)
+    plain = lib.prism_einsum_topk_workspace_size(1, 4, 64, 256, 8, _lib.MODE_EXACT_STREAM)
+    rope = lib.prism_einsum_topk_rope_workspace_size(1, 4, 2, 64, 256, 8, _lib.MODE_EXACT_STREAM, _lib.RECALL_QK)
+    assert rope == (plain + 255) // 256 * 256 + 2 * 256 * 512
+    assert _call(lib, wsb=plain, **shape) == _lib.PRISM_E_WORKSPACE
+    assert "prism_einsum_topk_rope_workspace_size" in _lib.last_error()
+
+
 def test_merge_argument_validation(lib):
     rc = lib.prism_topk_merge(16, 16, 4, 10, 10, 3, 16, None, 16, 1 << 20, None)  # ld % 4 != 0
     assert rc == _lib.PRISM_E_INVALID
@@ -143,6 +155,25 @@ def test_recall_type_errors_match_reference():
         _recall_weight_code("qkv2_pe")
     with pytest.raises(ValueError, match="Use one of: qk, qkv, qkv2"):
         _recall_weight_code("k")
+
+
+def test_rope_workspace_size(lib):
+    # decode shapes (fewer than 128 query rows per KV head): the plain size
+    plain = lib.prism_einsum_topk_weighted_workspace_size(1, 32, 8, 1, 131072, 4096, 0, _lib.RECALL_QK)
+    assert lib.prism_einsum_topk_rope_workspace_size(1, 32, 8, 1, 131072, 4096, 0, _lib.RECALL_QK) == plain
+    # prefill shapes: + the un-rotated hi / lo planes, B * Hkv * Sk * 512 bytes
+    for args in ((2, 32, 8, 32, 9000, 512, 0, _lib.RECALL_QK),           # score matrix
+                 (1, 32, 8, 4096, 131072, 2048, 0, _lib.RECALL_QK),      # streaming by itself
+                 (1, 8, 2, 64, 20000, 300, _lib.MODE_EXACT_STREAM, _lib.RECALL_QK),
+                 (1, 8, 2, 128, 8192, 1, _lib.MODE_BLOCKMAX, _lib.RECALL_QK),
+                 (1, 8, 2, 64, 5000, 100, 0, _lib.RECALL_QKV2)):
+        base = lib.prism_einsum_topk_weighted_workspace_size(*args)
+        B, Hkv, Sk = args[0], args[2], args[4]
+        want = (base + 255) // 256 * 256 + B * Hkv * Sk * 512
+        assert lib.prism_einsum_topk_rope_workspace_size(*args) == want, args
+    assert lib.prism_einsum_topk_rope_workspace_size(1, 8, 3, 64, 5000, 100, 0, 0) == \
+        lib.prism_einsum_topk_weighted_workspace_size(1, 8, 3, 64, 5000, 100, 0, 0)
+    assert lib.prism_einsum_topk_rope_workspace_size(0, 8, 2, 64, 5000, 100, 0, 0) == 0
 
 
 def test_weighted_workspace_size(lib):
