@@ -435,9 +435,8 @@ template <typename F, typename G>
 __device__ __forceinline__ void for_each_sample(const SelectArgs& a, const float* sc, int cshift,
                                                 F&& f, G&& after_issue) {
   const int tid = threadIdx.x;
-  const int64_t chunk = int64_t(1) << cshift;
   const int oshift = 32 - (cshift - 3);  // hash -> one of chunk / 8 offsets
-  const int64_t ngroups = (a.n + chunk - 1) >> cshift;
+  const int64_t ngroups = (a.n + (int64_t(1) << cshift) - 1) >> cshift;
   for (int64_t g0 = 0; g0 < ngroups; g0 += int64_t(kThreads) * 2) {
     float4 v[2][2];
     int64_t e[2];
@@ -718,25 +717,56 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
       }
       slot0 = hit_slot(hit, sm);
     } else {
+      // the stream, in half passes (16 keys per thread), software-pipelined: the
+      // loads of the next half are in flight while this half is compared and its
+      // hits appended
       uint64_t* mine_buf = cand + int64_t(rank) * quarter;
-      for (int64_t p = 0; p < npass; ++p) {
-        uint32_t kp[kKeys];
-        const int64_t base = p * kPass + my_base;
-        load_keys(sc, base, a.n, kp);
-        uint32_t h = 0;
+      const int64_t nhalf = npass * 2;
+      auto load_half = [&](int64_t hh, float4 (&v)[4]) {
+        const int64_t base = (hh >> 1) * kPass + my_base;
 #pragma unroll
-        for (int j = 0; j < kKeys; ++j) {
-          kmx = max(kmx, kp[j]);
-          if (kp[j] >= thr) h |= 1u << j;
+        for (int u = 0; u < 4; ++u) {
+          const int64_t e = base + (int64_t((4 * int(hh & 1) + u) * kThreads + tid) << 2);
+          if (e + 4 <= a.n) {
+            v[u] = __ldcs(reinterpret_cast<const float4*>(sc + e));
+          } else {
+            v[u].x = e + 0 < a.n ? sc[e + 0] : 0.f;
+            v[u].y = e + 1 < a.n ? sc[e + 1] : 0.f;
+            v[u].z = e + 2 < a.n ? sc[e + 2] : 0.f;
+            v[u].w = e + 3 < a.n ? sc[e + 3] : 0.f;
+          }
         }
-        const uint32_t slot = hit_slot(h, sm);
-        if (h != 0u && slot + uint32_t(__popc(h)) <= quarter) {
-          uint64_t* dst = mine_buf + slot;
+      };
+      float4 nx[4];
+      load_half(0, nx);
+      for (int64_t hh = 0; hh < nhalf; ++hh) {
+        const float4 cu[4] = {nx[0], nx[1], nx[2], nx[3]};
+        if (hh + 1 < nhalf) load_half(hh + 1, nx);
+        const int64_t base = (hh >> 1) * kPass + my_base;
+        const int64_t cb = base + (int64_t(4 * int(hh & 1) * kThreads + tid) << 2);  // column of key 0
+        uint32_t kp[16], h = 0;
 #pragma unroll
-          for (int j = 0; j < kKeys; ++j) {
-            if (h & (1u << j)) {
-              const int64_t col = key_column(base, j);
-              dst[__popc(h & ((1u << j) - 1u))] = pack_cand(kp[j], ix ? uint32_t(ix[col]) : uint32_t(col));
+        for (int u = 0; u < 4; ++u) {
+          const float fv[4] = {cu[u].x, cu[u].y, cu[u].z, cu[u].w};
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const int j = 4 * u + x;
+            const int64_t col = cb + int64_t(u) * kThreads * 4 + x;
+            kp[j] = col < a.n ? float_to_okey(fv[x]) : 0u;
+            kmx = max(kmx, kp[j]);
+            if (kp[j] >= thr && kp[j] != 0u) h |= 1u << j;
+          }
+        }
+        if (__any_sync(0xffffffffu, h != 0u)) {
+          const uint32_t slot = hit_slot(h, sm);
+          if (h != 0u && slot + uint32_t(__popc(h)) <= quarter) {
+            uint64_t* dst = mine_buf + slot;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if (h & (1u << j)) {
+                const int64_t col = cb + int64_t(j >> 2) * kThreads * 4 + (j & 3);
+                dst[__popc(h & ((1u << j) - 1u))] = pack_cand(kp[j], ix ? uint32_t(ix[col]) : uint32_t(col));
+              }
             }
           }
         }
