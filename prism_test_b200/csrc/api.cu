@@ -362,8 +362,10 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
                        [&] { return prism::launch_decode_scores_mma(a, dtype, nsm, stream); });
     if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
   } else if (prism::decode_wide_supported(a)) {
-    e = launch_counted(PRISM_KERNEL_SCORE, stream,
-                       [&] { return prism::launch_decode_scores_wide(a, dtype, nsm, stream); });
+    e = launch_counted(PRISM_KERNEL_SCORE, stream, [&] {
+      return prism::wide_tc_supported(a) ? prism::launch_wide_tc_scores(a, dtype, nsm, stream)
+                                         : prism::launch_decode_scores_wide(a, dtype, nsm, stream);
+    });
     if (e != cudaSuccess) return cuda_fail(e, "decode score kernel launch");
   } else if (prism::prefill_tc_supported(a)) {
     if (a.planes != nullptr) {

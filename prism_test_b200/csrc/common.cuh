@@ -95,6 +95,27 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// The same wait for roles with many waiting threads: try_wait with a suspend-time
+// hint, so that a waiting thread sleeps until the phase completes (or the hint
+// runs out) instead of polling the barrier in shared memory.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_sleep_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait_sleep(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait_sleep(bar, parity))
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+  return true;
+}
+
 // L2 policy: stream-once data (the key cache) is marked evict-first so that
 // the score buffer written alongside it stays resident in L2.
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {

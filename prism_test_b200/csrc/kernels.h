@@ -62,6 +62,14 @@ int64_t wide_sample_cols(int Hkv, int64_t Sk);
 cudaError_t launch_wide_sample(const DecodeArgs& a, int dtype, int num_sms, cudaStream_t stream);
 cudaError_t launch_wide_candidates(const DecodeArgs& a, int dtype, const float* thr, uint32_t* counts,
                                    uint64_t* cand, int64_t cap, int num_sms, cudaStream_t stream);
+// The same three modes on the tensor cores (score_wide_tc.cu): Hkv in {2, 4}, at
+// most 64 query rows per KV head, 16-byte aligned score rows; same outputs.
+bool wide_tc_supported(const DecodeArgs& a);
+cudaError_t launch_wide_tc_scores(const DecodeArgs& a, int dtype, int num_sms, cudaStream_t stream);
+cudaError_t launch_wide_tc_sample(const DecodeArgs& a, int dtype, int num_sms, cudaStream_t stream);
+cudaError_t launch_wide_tc_candidates(const DecodeArgs& a, int dtype, const float* thr, uint32_t* counts,
+                                      uint64_t* cand, int64_t cap, uint64_t* seg, uint32_t* segn,
+                                      int num_sms, cudaStream_t stream);
 
 // CUDA-core path for <= 4 query rows per KV head, Hkv in {1, 2, 4, 8, 16}.
 bool decode_g4_supported(const DecodeArgs& a);
@@ -120,10 +128,18 @@ StreamBuffers stream_buffers(int64_t rows, int64_t Sk, int topk, void* ws, int64
 // the streaming selection with its exact fallback. `ws` is
 // wide_stream_workspace_bytes(rows, Sk, topk) bytes, 256-byte aligned.
 size_t wide_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk);
+// Candidate segments of the tensor-core candidate pass: CTA c's epilogue group g
+// appends row r's candidates to segment (r, 2 c + g) of kWideSegCap entries without
+// atomics (beyond that, to the row's list through its counter);
+// wide_stream_candidates then gathers the segments into the rows' lists.
+constexpr int kWideMaxSegs = 512;   // 2 per CTA of a batch row
+constexpr int kWideSegCap = 64;
 struct WideStreamPtrs {
   StreamBuffers sb;
   float* S;      // the threshold sample [rows, ld_s]
   int64_t ld_s;
+  uint64_t* seg;   // [rows, kWideMaxSegs, kWideSegCap]
+  uint32_t* segn;  // [rows, kWideMaxSegs] entries in each segment (zero before the pass)
 };
 WideStreamPtrs wide_stream_ptrs(const DecodeArgs& a, int topk, void* ws);
 // phases: the sample and the thresholds (also clears the counts and flags), the

@@ -12,7 +12,8 @@
 //      of the k-th key): the digit holding rank m, then, inside it, the 8-bit
 //      sub-digit holding the remaining rank (a second look at the row's samples);
 //   3. the scorer's candidate pass: every visible key at or above its row's
-//      threshold appended to the row's list;
+//      threshold appended to the row's list (the tensor-core pass appends to a
+//      segment per CTA, gathered into the list by wide_gather_kernel);
 //   4. the streaming selection (prefill_select.cu): each row's candidates sorted;
 //      rows whose count lies outside [min(k, visible), cap] recomputed exactly
 //      (any number of them: the fallback's scratch holds every row).
@@ -141,21 +142,68 @@ int64_t sample_ld(int64_t Sk) {
   return ((Sk + 15) / 16 + 64 + 3) / 4 * 4;
 }
 
+size_t seg_bytes(int64_t rows) { return size_t(rows) * kWideMaxSegs * kWideSegCap * 8; }
+size_t segn_bytes(int64_t rows) { return size_t(rows) * kWideMaxSegs * 4; }
+
+// One CTA per row: the row's segments appended to its list after the entries the
+// candidate pass placed there through the counter; the count becomes the total
+// (which may exceed the capacity: the selection then recomputes the row exactly).
+__global__ void __launch_bounds__(256) wide_gather_kernel(const uint64_t* __restrict__ seg,
+                                                          const uint32_t* __restrict__ segn,
+                                                          uint32_t* counts, uint64_t* cand, int64_t cap) {
+  __shared__ uint32_t off[kWideMaxSegs + 1];
+  __shared__ uint32_t wtot[8];
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  static_assert(kWideMaxSegs == 512, "two segments per thread");
+  const uint32_t n0 = segn[row * kWideMaxSegs + 2 * tid], n1 = segn[row * kWideMaxSegs + 2 * tid + 1];
+  const uint32_t n = n0 + n1;
+  uint32_t x = n;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wtot[warp] = x;
+  __syncthreads();
+  uint32_t wb = 0;
+  for (int w = 0; w < warp; ++w) wb += wtot[w];
+  const uint32_t base = counts[2 * row];
+  off[2 * tid] = base + wb + x - n;
+  off[2 * tid + 1] = base + wb + x - n1;
+  if (tid == 255) off[kWideMaxSegs] = base + wb + x;
+  __syncthreads();
+  // every entry: segment s = i / kWideSegCap, entry i % kWideSegCap
+  const uint64_t* src = seg + row * kWideMaxSegs * kWideSegCap;
+  uint64_t* dst = cand + row * cap;
+  for (int i = tid; i < kWideMaxSegs * kWideSegCap; i += 256) {
+    const int s = i / kWideSegCap, e = i % kWideSegCap;
+    const uint32_t o = off[s] + uint32_t(e);
+    if (o < off[s + 1] && o < uint64_t(cap)) dst[o] = src[i];
+  }
+  if (tid == 0) counts[2 * row] = off[kWideMaxSegs];
+}
+
 }  // namespace
 
 // the exact fallback can take every row (its scratch is rows x Sk fp32, the size
 // of the score matrix the path does not write)
 size_t wide_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk) {
-  return up256(prefill_stream_workspace_bytes(rows, Sk, topk, rows)) + size_t(rows) * size_t(sample_ld(Sk)) * 4;
+  return up256(prefill_stream_workspace_bytes(rows, Sk, topk, rows)) + up256(size_t(rows) * size_t(sample_ld(Sk)) * 4) +
+         up256(seg_bytes(rows)) + segn_bytes(rows);
 }
 
 WideStreamPtrs wide_stream_ptrs(const DecodeArgs& a, int topk, void* ws) {
   const int64_t rows = int64_t(a.B) * a.Hq * a.Sq;
   WideStreamPtrs p;
   p.sb = stream_buffers(rows, a.Sk, topk, ws, rows);
-  p.S = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) +
-                                 up256(prefill_stream_workspace_bytes(rows, a.Sk, topk, rows)));
+  uint8_t* w = static_cast<uint8_t*>(ws) + up256(prefill_stream_workspace_bytes(rows, a.Sk, topk, rows));
+  p.S = reinterpret_cast<float*>(w);
   p.ld_s = sample_ld(a.Sk);
+  w += up256(size_t(rows) * size_t(p.ld_s) * 4);
+  p.seg = reinterpret_cast<uint64_t*>(w);
+  w += up256(seg_bytes(rows));
+  p.segn = reinterpret_cast<uint32_t*>(w);
   return p;
 }
 
@@ -166,11 +214,13 @@ cudaError_t wide_stream_threshold(const DecodeArgs& a, int dtype, int topk, void
   if (wide_sample_cols(a.Hkv, a.Sk) > p.ld_s) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(p.sb.counts, 0, size_t(rows) * 2 * sizeof(uint32_t), stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(p.sb.flags, 0, 2 * sizeof(int), stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.segn, 0, segn_bytes(rows), stream);
   if (e != cudaSuccess) return e;
   DecodeArgs s = a;  // the sample's scores, compactly
   s.scores = p.S;
   s.ld = p.ld_s;
-  e = launch_wide_sample(s, dtype, num_sms, stream);
+  e = wide_tc_supported(s) ? launch_wide_tc_sample(s, dtype, num_sms, stream)
+                           : launch_wide_sample(s, dtype, num_sms, stream);
   if (e != cudaSuccess) return e;
   // sample column c holds position (c / Tp) * 16 * Tp + c % Tp: the columns below
   // Sk are the first nvalid
@@ -185,7 +235,14 @@ cudaError_t wide_stream_threshold(const DecodeArgs& a, int dtype, int topk, void
 cudaError_t wide_stream_candidates(const DecodeArgs& a, int dtype, int topk, void* ws, int num_sms,
                                    cudaStream_t stream) {
   const WideStreamPtrs p = wide_stream_ptrs(a, topk, ws);
-  return launch_wide_candidates(a, dtype, p.sb.thr, p.sb.counts, p.sb.cand, p.sb.cap, num_sms, stream);
+  if (!wide_tc_supported(a) || 2 * num_sms > kWideMaxSegs)
+    return launch_wide_candidates(a, dtype, p.sb.thr, p.sb.counts, p.sb.cand, p.sb.cap, num_sms, stream);
+  cudaError_t e = launch_wide_tc_candidates(a, dtype, p.sb.thr, p.sb.counts, p.sb.cand, p.sb.cap, p.seg, p.segn,
+                                            num_sms, stream);
+  if (e != cudaSuccess) return e;
+  const int64_t rows = int64_t(a.B) * a.Hq * a.Sq;
+  wide_gather_kernel<<<dim3(unsigned(rows)), 256, 0, stream>>>(p.seg, p.segn, p.sb.counts, p.sb.cand, p.sb.cap);
+  return cudaGetLastError();
 }
 
 }  // namespace prism
