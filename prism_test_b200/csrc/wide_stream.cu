@@ -219,8 +219,10 @@ cudaError_t wide_stream_threshold(const DecodeArgs& a, int dtype, int topk, void
   DecodeArgs s = a;  // the sample's scores, compactly
   s.scores = p.S;
   s.ld = p.ld_s;
-  e = wide_tc_supported(s) ? launch_wide_tc_sample(s, dtype, num_sms, stream)
-                           : launch_wide_sample(s, dtype, num_sms, stream);
+  // the sample (1/16 of the tiles, a few per CTA) on the mma.sync kernel: the
+  // tensor-core kernel's set-up (TMEM, the queries, the pipeline fill) outweighs
+  // so little work
+  e = launch_wide_sample(s, dtype, num_sms, stream);
   if (e != cudaSuccess) return e;
   // sample column c holds position (c / Tp) * 16 * Tp + c % Tp: the columns below
   // Sk are the first nvalid
