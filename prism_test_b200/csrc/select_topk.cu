@@ -119,13 +119,15 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, SelectSmem& sm, 
 }
 
 // Largest bin b with sum(hist[b..nbins)) >= need; sm.bin / sm.above (count above b).
-__device__ void find_bin(SelectSmem& sm, int nbins, uint32_t need) {
+// `hist` (default sm.hist): the histogram to search.
+__device__ void find_bin(SelectSmem& sm, int nbins, uint32_t need, const uint32_t* hist = nullptr) {
+  const uint32_t* hh = hist ? hist : sm.hist;
   const int t = threadIdx.x;
   const int hi_bin = nbins - 1 - 4 * t;
   uint32_t local = 0;
   if (hi_bin >= 0) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) local += (hi_bin - u >= 0) ? sm.hist[hi_bin - u] : 0u;
+    for (int u = 0; u < 4; ++u) local += (hi_bin - u >= 0) ? hh[hi_bin - u] : 0u;
   }
   if (t == 0) {
     sm.bin = 0;
@@ -136,7 +138,7 @@ __device__ void find_bin(SelectSmem& sm, int nbins, uint32_t need) {
     uint32_t c = excl;
     for (int u = 0; u < 4; ++u) {
       const int bb = hi_bin - u;
-      const uint32_t h = sm.hist[bb];
+      const uint32_t h = hh[bb];
       if (c + h >= need) {
         sm.bin = uint32_t(bb);
         sm.above = c;
@@ -431,18 +433,21 @@ constexpr int kSampleStride = kSampleBins + 4;
 // own loads then queue behind them).
 // Visits every sampled key: f(order key). `after_issue` runs once, after the first
 // loads are issued.
+// With nparts > 1, only the chunks g with g % nparts == part.
 template <typename F, typename G>
 __device__ __forceinline__ void for_each_sample(const SelectArgs& a, const float* sc, int cshift,
-                                                F&& f, G&& after_issue) {
+                                                F&& f, G&& after_issue, int part = 0, int nparts = 1) {
   const int tid = threadIdx.x;
   const int oshift = 32 - (cshift - 3);  // hash -> one of chunk / 8 offsets
   const int64_t ngroups = (a.n + (int64_t(1) << cshift) - 1) >> cshift;
-  for (int64_t g0 = 0; g0 < ngroups; g0 += int64_t(kThreads) * 2) {
+  const int64_t nmine = (ngroups - part + nparts - 1) / nparts;  // this part's chunks
+  for (int64_t g0 = 0; g0 < nmine; g0 += int64_t(kThreads) * 2) {
     float4 v[2][2];
     int64_t e[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const int64_t g = g0 + int64_t(u) * kThreads + tid;
+      const int64_t gi = g0 + int64_t(u) * kThreads + tid;
+      const int64_t g = gi < nmine ? gi * nparts + part : ngroups;
       e[u] = (g << cshift) + 8 * int64_t((uint32_t(g) * 0x9E3779B1u) >> oshift);
       const bool full = g < ngroups && e[u] + 8 <= a.n;
       v[u][0] = full ? __ldcg(reinterpret_cast<const float4*>(sc + e[u])) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -508,6 +513,77 @@ __device__ uint32_t row_sample_threshold_cta(const SelectArgs& a, const float* s
   }, [] {});
   __syncthreads();
   find_bin(sm, 256, need);
+  return (b << 20) | (sm.bin << 12);
+}
+
+// row_sample_threshold_cta for a row streamed by a cluster (2^8-column chunks, with
+// the refinement), the sample split over the cluster: CTA `rank` counts the chunks
+// g with g % kCluster == rank, the histograms are summed through distributed shared
+// memory, so every CTA reaches the same threshold from a quarter of the loads.
+// Cluster barriers: on entry the kernel-start arrive is outstanding; on return one
+// arrive is outstanding again (the caller's next cluster_wait completes it).
+__device__ uint32_t row_sample_threshold_split(const SelectArgs& a, const float* sc, SelectSmem& sm,
+                                               cg::cluster_group& cluster, unsigned rank) {
+  constexpr int cshift = 8;
+  const int tid = threadIdx.x, lane = tid & 31;
+  uint32_t* priv = reinterpret_cast<uint32_t*>(sm.buf);
+  uint32_t* my_samp = priv + (lane & (kSampleCopies - 1)) * kSampleStride;
+  uint32_t* tot = priv;                  // the summed histogram (the copies are summed first)
+  uint32_t* tot2 = priv + kSampleBins;   // the summed refinement histogram
+  uint32_t ns = 0;
+  for_each_sample(a, sc, cshift, [&](uint32_t key) {
+    atomicAdd(&my_samp[key >> 20], 1u);
+    ++ns;
+  }, [] {}, int(rank), kCluster);
+  ns = __reduce_add_sync(0xffffffffu, ns);
+  if (lane == 0 && ns) atomicAdd(&sm.nsamp, ns);
+  __syncthreads();
+  for (int i = tid; i < kSampleBins; i += kThreads) {
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int q = 0; q < kSampleCopies; ++q) cnt += priv[q * kSampleStride + i];
+    sm.hist[i] = cnt;
+  }
+  __syncthreads();
+  cluster_wait();    // the kernel-start phase: every CTA has started
+  cluster_arrive();  // this CTA's partial histogram and count
+  cluster_wait();
+  uint32_t nsamp = 0;
+#pragma unroll
+  for (int r = 0; r < kCluster; ++r) nsamp += *cluster.map_shared_rank(&sm.nsamp, r);
+  for (int i = tid; i < kSampleBins; i += kThreads) {
+    uint32_t s = 0;
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) s += cluster.map_shared_rank(sm.hist, r)[i];
+    tot[i] = s;
+  }
+  __syncthreads();
+  cluster_arrive();  // done reading the peers' histograms
+  const double nsd = double(nsamp);
+  const double expect = double(a.k) * nsd / double(a.n);
+  const double m = expect * 1.1 + 4.0 * sqrt(expect) + 8.0;
+  if (!(m < nsd)) return 1u;  // every key (the same answer in every CTA)
+  find_bin(sm, kSampleBins, uint32_t(m), tot);
+  const uint32_t b = sm.bin;
+  const uint32_t need = uint32_t(m) - sm.above;  // >= 1: rank m lies inside digit b
+  cluster_wait();    // every CTA is done with the partial histograms
+  for (int i = tid; i < 256; i += kThreads) sm.hist[i] = 0u;
+  __syncthreads();
+  for_each_sample(a, sc, cshift, [&](uint32_t key) {
+    if ((key >> 20) == b) atomicAdd(&sm.hist[(key >> 12) & 0xffu], 1u);
+  }, [] {}, int(rank), kCluster);
+  __syncthreads();
+  cluster_arrive();  // this CTA's refinement histogram
+  cluster_wait();
+  for (int i = tid; i < 256; i += kThreads) {
+    uint32_t s = 0;
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) s += cluster.map_shared_rank(sm.hist, r)[i];
+    tot2[i] = s;
+  }
+  __syncthreads();
+  cluster_arrive();  // done reading (outstanding for the caller)
+  find_bin(sm, 256, need, tot2);
   return (b << 20) | (sm.bin << 12);
 }
 
@@ -702,9 +778,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     uint64_t* cand = cand_all + row * cand_cap;
     // the row's own keys are loaded (rows held in registers) while the sample is
     // counted, their loads queued behind the sample's
-    const uint32_t thr = row_sample_threshold_cta(a, sc, sm, kResident ? 7 : 8, !kResident, [&] {
-      if (kResident) load_raw(sc, my_base, a.n, raw);
-    });
+    uint32_t thr;
+    if (kResident) {
+      thr = row_sample_threshold_cta(a, sc, sm, 7, false, [&] { load_raw(sc, my_base, a.n, raw); });
+    } else {
+      thr = row_sample_threshold_split(a, sc, sm, cluster, rank);
+    }
     const uint32_t quarter = uint32_t(cand_cap / kCluster);
     uint32_t kmx = 0;
     uint32_t hit = 0, slot0 = 0;
@@ -776,7 +855,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0) atomicMax(&sm.kmax, kmx);
     __syncthreads();
     // every CTA's count and largest key to every CTA (the first wait completes the
-    // kernel-start barrier phase: every CTA has started)
+    // outstanding arrive: the kernel-start one, or the split sample's last)
     cluster_wait();
     if (tid < kCluster) {
       SelectSmem* peer = cluster.map_shared_rank(&sm, tid);
