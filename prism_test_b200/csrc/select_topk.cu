@@ -1497,9 +1497,25 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t q0 = uint32_t(uint64_t(total) * part / kMergeParts);
     const uint32_t q1 = uint32_t(uint64_t(total) * (part + 1) / kMergeParts);
-    for (int r = 0; r < nruns; ++r) {
-      const uint32_t o = sm.roff[r], e1 = min(o + sm.rlen[r], q1);
-      for (uint32_t e = max(o, q0) + tid; e < e1; e += kThreads) sm.buf[e] = cand_at(r, e - o);
+    // eight independent loads per thread in flight (one interconnect round trip for a
+    // quarter of up to 8192 entries), whichever runs they fall in
+    for (uint32_t e0 = q0; e0 < q1; e0 += 8 * kThreads) {
+      uint64_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint32_t e = e0 + uint32_t(u * kThreads + tid);
+        v[u] = 0;
+        if (e < q1) {
+          int r = 0;
+          while (e >= sm.roff[r + 1]) ++r;
+          v[u] = cand_at(r, e - sm.roff[r]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint32_t e = e0 + uint32_t(u * kThreads + tid);
+        if (e < q1) sm.buf[e] = v[u];
+      }
     }
     cluster.sync();  // every quarter is staged
     for (unsigned c = 0; c < unsigned(kMergeParts); ++c) {
