@@ -345,8 +345,7 @@ int einsum_topk_impl(const void* q, const void* k, const float* inv_freq, int dt
                        [&] { return prism::wide_stream_candidates(a, dtype, topk, pws, nsm, stream); });
     if (e != cudaSuccess) return cuda_fail(e, "wide candidate launch");
     e = launch_counted(PRISM_KERNEL_SELECT, stream, [&] {
-      return prism::prefill_stream_select(a, dtype, topk, index_base, out_idx, out_scores, pws, stream,
-                                          B * Hq * Sq);
+      return prism::wide_stream_select(a, dtype, topk, index_base, out_idx, out_scores, pws, stream);
     });
     if (e != cudaSuccess) return cuda_fail(e, "wide stream select launch");
     g_launches.fetch_add(4, std::memory_order_relaxed);  // sample + thresholds, select phase of 4

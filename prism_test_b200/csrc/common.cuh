@@ -209,6 +209,12 @@ __device__ __forceinline__ float to_f32<__half>(__half v) {
   return __half2float(v);
 }
 
+// Programmatic dependent launch: wait until the kernel before this one in the
+// stream has completed and its writes are visible; a no-op for a normal launch.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Launches kern<<<grid, block, smem, stream>>>(args...), as a programmatic
 // dependent launch when pdl: the kernel may be scheduled while the previous
 // kernel in the stream drains, and must read that kernel's output only after

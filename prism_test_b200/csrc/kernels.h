@@ -109,9 +109,12 @@ cudaError_t prefill_stream_threshold(const DecodeArgs& a, int dtype, int topk, v
                                      cudaStream_t stream);
 cudaError_t prefill_stream_candidates(const DecodeArgs& a, int dtype, int topk, void* ws,
                                       cudaStream_t stream);
+// seg / segn: candidate segments (the queries-as-M tensor-core pass) appended to the
+// rows' lists first.
 cudaError_t prefill_stream_select(const DecodeArgs& a, int dtype, int topk, int64_t index_base,
                                   int32_t* out_idx, float* out_scores, void* ws,
-                                  cudaStream_t stream, int64_t nfall = -1);
+                                  cudaStream_t stream, int64_t nfall = -1, const uint64_t* seg = nullptr,
+                                  const uint32_t* segn = nullptr);
 // The streaming workspace's thresholds, candidate counts [rows, 2], candidate
 // lists [rows, cap] and fallback flags (two ints), for other candidate producers.
 struct StreamBuffers {
@@ -130,8 +133,8 @@ StreamBuffers stream_buffers(int64_t rows, int64_t Sk, int topk, void* ws, int64
 size_t wide_stream_workspace_bytes(int64_t rows, int64_t Sk, int topk);
 // Candidate segments of the tensor-core candidate pass: CTA c's epilogue group g
 // appends row r's candidates to segment (r, 2 c + g) of kWideSegCap entries without
-// atomics (beyond that, to the row's list through its counter);
-// wide_stream_candidates then gathers the segments into the rows' lists.
+// atomics (beyond that, to the row's list through its counter); the streaming
+// selection appends the segments to the rows' lists before it reads them.
 constexpr int kWideMaxSegs = 512;   // 2 per CTA of a batch row
 constexpr int kWideSegCap = 64;
 struct WideStreamPtrs {
@@ -148,6 +151,10 @@ cudaError_t wide_stream_threshold(const DecodeArgs& a, int dtype, int topk, void
                                   cudaStream_t stream);
 cudaError_t wide_stream_candidates(const DecodeArgs& a, int dtype, int topk, void* ws, int num_sms,
                                    cudaStream_t stream);
+// the streaming selection on the wide path's workspace (segments included; every row
+// can take the exact fallback)
+cudaError_t wide_stream_select(const DecodeArgs& a, int dtype, int topk, int64_t index_base, int32_t* out_idx,
+                               float* out_scores, void* ws, cudaStream_t stream);
 
 // --- exact per-row top-k selection over a score matrix ----------------------
 struct SelectArgs {

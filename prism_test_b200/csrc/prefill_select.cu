@@ -8,7 +8,7 @@
 //
 // prefill_select_kernel, one 256-thread CTA per row: the row's n candidates
 // (packed (fp32 score bits << 32) | ~index) are loaded into shared memory as
-// order-preserving score keys and counting-sorted into 2048 fine bins between the
+// order-preserving score keys and index words and counting-sorted into 2048 fine bins between the
 // row's largest and smallest candidate, logarithmic in the distance above the
 // smallest (NaN, which ranks first, in bin 0; computed from the value, not from
 // the packed key, whose spacing explodes around zero); a candidate's output position is its bin's start plus
@@ -33,7 +33,7 @@ constexpr int kPsRankMax = 64;
 constexpr int kFallbackRows = 64;
 
 struct PsArgs {
-  const uint64_t* cand;
+  uint64_t* cand;
   const uint32_t* counts;
   int64_t cap;
   int k;
@@ -48,6 +48,8 @@ struct PsArgs {
   int32_t* flag_rows;
   int nfall;
   int* status;
+  const uint64_t* seg;   // nullptr, or the candidate segments of the queries-as-M tensor-core
+  const uint32_t* segn;  //   pass ([rows, kWideMaxSegs, kWideSegCap] and their counts)
 };
 
 __device__ __forceinline__ int64_t visible_keys(int64_t row, int Sq, int causal,
@@ -94,19 +96,35 @@ __device__ __forceinline__ uint32_t ps_scan(uint32_t v, uint32_t* wtot, uint32_t
 
 __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  // candidates' score keys only (their indices are re-read from the row's list,
-  // which is still in L2, for ties and for the output): 6 bytes per candidate
+  // candidates: score keys and index words (10 bytes per candidate with perm)
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem);                      // [cap]
-  uint32_t* hist = keys + a.cap;                                           // [kPsBins]
+  uint32_t* idxw = keys + a.cap;                                           // [cap] ~index
+  uint32_t* hist = idxw + a.cap;                                           // [kPsBins]
   uint16_t* perm = reinterpret_cast<uint16_t*>(hist + kPsBins);            // [cap]
   __shared__ uint32_t wtot[kPsThreads / 32];
   __shared__ uint32_t s_kmax, s_kmin, s_big;  // max / min key of the finite scores
 
+  __shared__ uint32_t soff[kWideMaxSegs + 1];  // segments: start of each in the appended entries
+  // a dependent launch: the candidate pass's lists and counts are complete after the wait
+  grid_dependency_wait();
+  asm volatile("griddepcontrol.launch_dependents;");
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31;
-  // the row's candidates: n0 from the front of its list, n1 from the back
-  const uint32_t n0 = a.counts[2 * row], n1 = a.counts[2 * row + 1];
-  const uint32_t n = n0 + n1;
+  // the row's candidates at positions [0, n0) from the front of its list, then the
+  // entries of the candidate pass's segments (nseg of them), then n1 from the back
+  const uint32_t n0 = a.counts[2 * row];
+  const uint32_t n1 = a.counts[2 * row + 1];
+  uint32_t nseg = 0;
+  if (a.seg != nullptr) {
+    static_assert(kWideMaxSegs == 2 * kPsThreads, "two segments per thread");
+    const uint32_t* sn = a.segn + row * kWideMaxSegs;
+    const uint32_t c0 = sn[2 * tid], c1 = sn[2 * tid + 1];
+    const uint32_t ex = ps_scan(c0 + c1, wtot, &nseg);
+    soff[2 * tid] = ex;
+    soff[2 * tid + 1] = ex + c0;
+    if (tid == 0) soff[kWideMaxSegs] = nseg;
+  }
+  const uint32_t n = n0 + nseg + n1;
   const int64_t nvis = visible_keys(row, a.Sq, a.causal, a.causal_offset, a.Sk);
   const uint32_t keff = uint32_t(nvis < a.k ? nvis : a.k);
   int32_t* oi = a.out_idx + row * a.k;
@@ -128,15 +146,42 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
   }
   for (int i = tid; i < kPsBins; i += kPsThreads) hist[i] = 0u;
   __syncthreads();
-  const uint64_t* src = a.cand + row * a.cap;
-  auto cand_at = [&](uint32_t i) { return i < n0 ? src[i] : src[a.cap - 1 - (i - n0)]; };
   uint32_t kmx = 0u, kmn = 0xffffffffu;
-  for (uint32_t i = tid; i < n; i += kPsThreads) {
-    const uint32_t key = float_to_okey(__uint_as_float(uint32_t(cand_at(i) >> 32)));
+  auto put = [&](uint32_t i, uint64_t x) {  // candidate i into shared memory
+    const uint32_t key = float_to_okey(__uint_as_float(uint32_t(x >> 32)));
     keys[i] = key;
+    idxw[i] = uint32_t(x);
     if (key != 0xffffffffu) {  // NaN is binned apart
       kmx = max(kmx, key);
       kmn = min(kmn, key);
+    }
+  };
+  const uint64_t* src = a.cand + row * a.cap;
+  for (uint32_t i = tid; i < n0; i += kPsThreads) put(i, src[i]);
+  for (uint32_t i = tid; i < n1; i += kPsThreads) put(n0 + nseg + i, src[a.cap - 1 - i]);
+  if (nseg > 0) {
+    // the segments' entries, eight loads in flight per thread
+    const uint64_t* sg = a.seg + row * kWideMaxSegs * kWideSegCap;
+    for (uint32_t i0 = tid; i0 < nseg; i0 += 8 * kPsThreads) {
+      uint64_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint32_t i = i0 + uint32_t(u * kPsThreads);
+        if (i < nseg) {
+          int lo = 0, hi = kWideMaxSegs;  // soff[lo] <= i < soff[hi]: lo is the entry's segment
+          while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (soff[mid] <= i) lo = mid;
+            else hi = mid;
+          }
+          v[u] = sg[lo * kWideSegCap + (i - soff[lo])];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint32_t i = i0 + uint32_t(u * kPsThreads);
+        if (i < nseg) put(n0 + i, v[u]);
+      }
     }
   }
   kmx = __reduce_max_sync(0xffffffffu, kmx);
@@ -220,15 +265,15 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
       p += ky > kx;
       ties += ky == kx;  // this candidate included
     }
-    const uint64_t x = cand_at(i);
+    const uint32_t xi = idxw[i];  // ~index
     if (ties > 1) {  // equal scores: the lower index goes first
       for (uint32_t j = s; j < e; ++j) {
         const uint32_t pj = perm[j];
-        if (pj != i && keys[pj] == kx) p += uint32_t(cand_at(pj)) > uint32_t(x);  // lower index
+        if (pj != i && keys[pj] == kx) p += idxw[pj] > xi;  // lower index
       }
     }
     if (p < keff) {
-      oi[p] = int32_t(int64_t(~uint32_t(x)) + a.index_base);
+      oi[p] = int32_t(int64_t(~xi) + a.index_base);
       if (os) os[p] = okey_to_float(kx);
     }
   }
@@ -242,6 +287,8 @@ __global__ void __launch_bounds__(256)
     fallback_scores_kernel(const DecodeArgs a, const int* nflag, const int32_t* flag_rows,
                            int nfall, int* nserve, float* scratch) {
   __shared__ float qs[128];
+  grid_dependency_wait();  // a dependent launch: the listed rows are complete after the wait
+  asm volatile("griddepcontrol.launch_dependents;");
   const int nf = *nflag < nfall ? *nflag : nfall;
   if (blockIdx.x == 0 && threadIdx.x == 0) *nserve = nf;
   const int slot = blockIdx.x;
@@ -320,6 +367,7 @@ __global__ void __launch_bounds__(256)
 __global__ void fallback_scatter_kernel(const int* nserve, const int32_t* flag_rows, int k,
                                         const int32_t* cidx, const float* csc, int32_t* out_idx,
                                         float* out_scores) {
+  grid_dependency_wait();  // a dependent launch: the fallback's selection is complete after the wait
   const int slot = blockIdx.x;
   if (slot >= *nserve) return;
   const int64_t row = flag_rows[slot];
@@ -435,7 +483,8 @@ cudaError_t prefill_stream_candidates(const DecodeArgs& d, int dtype, int topk, 
 
 cudaError_t prefill_stream_select(const DecodeArgs& d, int dtype, int topk, int64_t index_base,
                                   int32_t* out_idx, float* out_scores, void* ws,
-                                  cudaStream_t stream, int64_t nfall_in) {
+                                  cudaStream_t stream, int64_t nfall_in, const uint64_t* seg,
+                                  const uint32_t* segn) {
   const int64_t nfall = nfall_in < 0 ? kFallbackRows : nfall_in;
   const PsPtrs w = ps_ptrs(d, topk, ws, nfall);
   const int64_t rows = int64_t(d.B) * d.Hq * d.Sq;
@@ -455,22 +504,24 @@ cudaError_t prefill_stream_select(const DecodeArgs& d, int dtype, int topk, int6
   p.flag_rows = w.flag_rows;
   p.nfall = int(nfall);
   p.status = d.status;
-  const size_t smem = size_t(w.cap) * 6 + kPsBins * 4;
+  p.seg = seg;
+  p.segn = segn;
+  const size_t smem = size_t(w.cap) * 10 + kPsBins * 4;
   cudaError_t e = cudaFuncSetAttribute(prefill_select_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  prefill_select_kernel<<<dim3(unsigned(rows)), kPsThreads, smem, stream>>>(p);
-  e = cudaGetLastError();
+  e = launch_maybe_dependent(prefill_select_kernel, dim3(unsigned(rows)), dim3(kPsThreads), smem, true, stream, p);
   if (e != cudaSuccess) return e;
 
   // exact fallback for the listed rows (kernels return at once when none are)
   if (dtype == kBF16)
-    fallback_scores_kernel<__nv_bfloat16><<<unsigned(nfall), 256, 0, stream>>>(
-        d, w.nflag, w.flag_rows, int(nfall), w.nserve, w.scratch);
+    e = launch_maybe_dependent(fallback_scores_kernel<__nv_bfloat16>, dim3(unsigned(nfall)), dim3(256), 0, true,
+                               stream, d, static_cast<const int*>(w.nflag), static_cast<const int32_t*>(w.flag_rows),
+                               int(nfall), w.nserve, w.scratch);
   else
-    fallback_scores_kernel<__half><<<unsigned(nfall), 256, 0, stream>>>(d, w.nflag, w.flag_rows,
-                                                                       int(nfall), w.nserve, w.scratch);
-  e = cudaGetLastError();
+    e = launch_maybe_dependent(fallback_scores_kernel<__half>, dim3(unsigned(nfall)), dim3(256), 0, true, stream, d,
+                               static_cast<const int*>(w.nflag), static_cast<const int32_t*>(w.flag_rows),
+                               int(nfall), w.nserve, w.scratch);
   if (e != cudaSuccess) return e;
   SelectArgs s{};
   s.scores = w.scratch;
@@ -486,9 +537,10 @@ cudaError_t prefill_stream_select(const DecodeArgs& d, int dtype, int topk, int6
   s.rows_dyn = w.nserve;
   e = launch_select_topk(s, w.sel_ws, stream);
   if (e != cudaSuccess) return e;
-  fallback_scatter_kernel<<<unsigned(nfall), 256, 0, stream>>>(w.nserve, w.flag_rows, topk, w.cidx,
-                                                             w.csc, out_idx, out_scores);
-  return cudaGetLastError();
+  return launch_maybe_dependent(fallback_scatter_kernel, dim3(unsigned(nfall)), dim3(256), 0, true, stream,
+                                static_cast<const int*>(w.nserve), static_cast<const int32_t*>(w.flag_rows), topk,
+                                static_cast<const int32_t*>(w.cidx), static_cast<const float*>(w.csc), out_idx,
+                                out_scores);
 }
 
 }  // namespace prism

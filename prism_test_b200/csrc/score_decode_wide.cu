@@ -159,11 +159,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool live = mt0 + j < M && r < R;
       const T* qr = qg + int64_t(b) * a.q_sb + int64_t(h * a.G + (live ? r : 0) / a.sq_n) * a.q_sh +
                     int64_t(a.s0 + (live ? r : 0) % a.sq_n) * a.q_ss;
+      // dims 16c + 2s, +1 (k-step s < 8) and 64 + 16c + 2(s - 8), +1 (s >= 8): two
+      // runs of 16 elements, read as 16-byte words when the row is aligned
+      if (live && (reinterpret_cast<uintptr_t>(qr) & 15u) == 0) {
+        uint4 w[4];
+        w[0] = __ldg(reinterpret_cast<const uint4*>(qr + 16 * c));
+        w[1] = __ldg(reinterpret_cast<const uint4*>(qr + 16 * c + 8));
+        w[2] = __ldg(reinterpret_cast<const uint4*>(qr + 64 + 16 * c));
+        w[3] = __ldg(reinterpret_cast<const uint4*>(qr + 64 + 16 * c + 8));
+        const uint32_t ws[16] = {w[0].x, w[0].y, w[0].z, w[0].w, w[1].x, w[1].y, w[1].z, w[1].w,
+                                 w[2].x, w[2].y, w[2].z, w[2].w, w[3].x, w[3].y, w[3].z, w[3].w};
 #pragma unroll
-      for (int s = 0; s < 16; ++s) {
-        const int d = dim_of(s, c);
-        aq[j][s][half] = live ? __float_as_uint(to_f32(qr[d])) : 0u;
-        aq[j][s][2 + half] = live ? __float_as_uint(to_f32(qr[d + 1])) : 0u;
+        for (int s = 0; s < 16; ++s) {
+          float lo, hi;
+          Unpack<T>::run(ws[s], lo, hi);
+          aq[j][s][half] = __float_as_uint(lo);
+          aq[j][s][2 + half] = __float_as_uint(hi);
+        }
+      } else {
+#pragma unroll
+        for (int s = 0; s < 16; ++s) {
+          const int d = dim_of(s, c);
+          aq[j][s][half] = live ? __float_as_uint(to_f32(qr[d])) : 0u;
+          aq[j][s][2 + half] = live ? __float_as_uint(to_f32(qr[d + 1])) : 0u;
+        }
       }
     }
   }

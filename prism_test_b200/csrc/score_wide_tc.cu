@@ -10,10 +10,11 @@
 // The MMA: D[query row, key] over M = 128 query rows (a pair of KV heads' rows, 64
 // each, held in tensor memory as the A operand, loaded once), N = 2 Tn keys (the
 // tile's Tn = 128 / Hkv positions of both heads of the pair), K = 128 dimensions
-// taken twice: the key un-rotated in fp32 and split into bf16 (fp16) hi = round(k)
-// and lo = round(k - hi), |k - hi - lo| <= 2^-17 |k|, both accumulated into the
-// same fp32 accumulator. Of each 128 x 2 Tn accumulator the two diagonal blocks
-// (a head's rows against the same head's keys) are kept.
+// taken twice: the key un-rotated in fp32 and split into 16-bit halves hi and
+// lo = round(k - hi) (bf16: hi = k truncated, |k - hi - lo| < 2^-16 |k|; fp16: hi =
+// round(k)), both accumulated into the same fp32 accumulator. Of each 128 x 2 Tn
+// accumulator the two diagonal blocks (a head's rows against the same head's keys)
+// are kept.
 //
 // Roles (576 threads):
 //   warp 0: idle after the set-up (the converters' first thread prefetches the
@@ -114,25 +115,29 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
-// hi / lo 16-bit halves of two fp32 values, packed (first value in the low half)
+// hi / lo 16-bit halves of two fp32 values (v.x in the low half of each word).
+// bf16: hi truncates (the top 16 bits: one byte permute), lo = v - hi is exact in
+// fp32 and rounds to bf16 — |v - hi - lo| <= 2^-9 |v - hi| < 2^-16 |v|; fp16: hi
+// and lo rounded to nearest.
 template <typename T>
 struct SplitPair;
 template <>
 struct SplitPair<__nv_bfloat16> {
-  __device__ __forceinline__ static void run(float x, float y, uint32_t& hi, uint32_t& lo) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
-    const float2 hf = __bfloat1622float2(h);
-    const __nv_bfloat162 l = __floats2bfloat162_rn(x - hf.x, y - hf.y);
-    hi = *reinterpret_cast<const uint32_t*>(&h);
+  __device__ __forceinline__ static void run(float2 v, uint32_t& hi, uint32_t& lo) {
+    const uint32_t bx = __float_as_uint(v.x), by = __float_as_uint(v.y);
+    hi = __byte_perm(bx, by, 0x7632);
+    const float2 rest = __ffma2_rn(make_float2(__uint_as_float(bx & 0xffff0000u), __uint_as_float(by & 0xffff0000u)),
+                                   make_float2(-1.f, -1.f), v);  // exact
+    const __nv_bfloat162 l = __float22bfloat162_rn(rest);
     lo = *reinterpret_cast<const uint32_t*>(&l);
   }
 };
 template <>
 struct SplitPair<__half> {
-  __device__ __forceinline__ static void run(float x, float y, uint32_t& hi, uint32_t& lo) {
-    const __half2 h = __floats2half2_rn(x, y);
+  __device__ __forceinline__ static void run(float2 v, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __float22half2_rn(v);
     const float2 hf = __half22float2(h);
-    const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+    const __half2 l = __float22half2_rn(make_float2(v.x - hf.x, v.y - hf.y));
     hi = *reinterpret_cast<const uint32_t*>(&h);
     lo = *reinterpret_cast<const uint32_t*>(&l);
   }
@@ -193,18 +198,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const T* qr = qg + int64_t(b) * a.q_sb +
                     int64_t(h * a.G + (live ? rloc : 0) / a.sq_n) * a.q_sh +
                     int64_t(a.s0 + (live ? rloc : 0) % a.sq_n) * a.q_ss;
+      // the row's bf16 (fp16) pairs are already the 32-bit columns: 16-byte loads
+      // when the row is 16-byte aligned, else 4-byte ones (rows start at even
+      // elements: the q strides are even)
+      const bool v16 = (reinterpret_cast<uintptr_t>(qr) & 15u) == 0;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t r[32];
+        if (live && v16) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          uint32_t w = 0u;
-          if (live) {
-            const uint16_t lo16 = *reinterpret_cast<const uint16_t*>(qr + 64 * half + 2 * c);
-            const uint16_t hi16 = *reinterpret_cast<const uint16_t*>(qr + 64 * half + 2 * c + 1);
-            w = uint32_t(lo16) | (uint32_t(hi16) << 16);
+          for (int c = 0; c < 8; ++c) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(qr + 64 * half) + c);
+            r[4 * c] = w.x;
+            r[4 * c + 1] = w.y;
+            r[4 * c + 2] = w.z;
+            r[4 * c + 3] = w.w;
           }
-          r[c] = w;
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) r[c] = live ? __ldg(reinterpret_cast<const uint32_t*>(qr + 64 * half) + c) : 0u;
         }
         tmem_st32(tmem + (uint32_t(quad * 32) << 16) + uint32_t(hp * 64 + half * 32), r);
       }
@@ -294,11 +306,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             wh[h] = __ldg(reinterpret_cast<const uint4*>(row + 64 + 8 * fg));
           }
         }
-        float cs[8], sn[8];
+        float2 cs2[4], sn2[4], nsn2[4];  // (cos, sin, -sin) of frequency pairs 8 fg + 2u, +1
         if (kRope) {
           const float pf = static_cast<float>(a.pos_offset + pos);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) rope_sincos_fast(__fmul_rn(pf, inv[j]), sn[j], cs[j]);
+          for (int u = 0; u < 4; ++u) {
+            rope_sincos_fast(__fmul_rn(pf, inv[2 * u]), sn2[u].x, cs2[u].x);
+            rope_sincos_fast(__fmul_rn(pf, inv[2 * u + 1]), sn2[u].y, cs2[u].y);
+            nsn2[u] = make_float2(-sn2[u].x, -sn2[u].y);
+          }
         }
         if (!waited) {  // the slot's previous tile has been read by the tensor cores
           waited = true;
@@ -317,19 +333,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t hl[4], ll[4], hh[4], lh[4];  // hi / lo of dimensions 8 fg.. and 64 + 8 fg..
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            float x0, x1, y0, y1;  // x: dims 8 fg + 2u, +1; y: the same + 64
-            Unpack<T>::run(wlo[u], x0, x1);
-            Unpack<T>::run(whi[u], y0, y1);
-            float r0 = x0, r1 = x1, q0 = y0, q1 = y1;
-            if (kRope) {
-              const float c0 = cs[2 * u], s0 = sn[2 * u], c1 = cs[2 * u + 1], s1 = sn[2 * u + 1];
-              r0 = fmaf(x0, c0, y0 * s0);
-              r1 = fmaf(x1, c1, y1 * s1);
-              q0 = fmaf(y0, c0, -(x0 * s0));
-              q1 = fmaf(y1, c1, -(x1 * s1));
+            float2 xv, yv;  // x: dims 8 fg + 2u, +1; y: the same + 64
+            Unpack<T>::run(wlo[u], xv.x, xv.y);
+            Unpack<T>::run(whi[u], yv.x, yv.y);
+            float2 r = xv, q = yv;
+            if (kRope) {  // packed fp32x2: r = x c + y s, q = y c - x s
+              r = __ffma2_rn(xv, cs2[u], __fmul2_rn(yv, sn2[u]));
+              q = __ffma2_rn(yv, cs2[u], __fmul2_rn(xv, nsn2[u]));
             }
-            SplitPair<T>::run(r0, r1, hl[u], ll[u]);
-            SplitPair<T>::run(q0, q1, hh[u], lh[u]);
+            SplitPair<T>::run(r, hl[u], ll[u]);
+            SplitPair<T>::run(q, hh[u], lh[u]);
           }
           // row (h & 1) Tn + p of the pair's blocks: hi atom 0, hi atom 1, lo atom 0, lo atom 1
           uint8_t* hip = bt + uint32_t((h >> 1) * 4) * blk + uint32_t((h & 1) * Tn + p) * 128 + sw;
@@ -472,7 +485,9 @@ cudaError_t launch_tc_mode(const DecodeArgs& a, int dtype, int num_sms, const Tc
 
 bool wide_tc_supported(const DecodeArgs& a) {
   const int H = a.Hkv;
-  return (H == 2 || H == 4) && a.G * a.sq_n <= kRowsPerHead && a.G * a.sq_n >= 1 &&
+  const bool q_ok = (reinterpret_cast<uintptr_t>(a.q) & 3u) == 0 && a.q_sb % 2 == 0 && a.q_sh % 2 == 0 &&
+                    a.q_ss % 2 == 0;  // 4-byte query words
+  return q_ok && (H == 2 || H == 4) && a.G * a.sq_n <= kRowsPerHead && a.G * a.sq_n >= 1 &&
          (reinterpret_cast<uintptr_t>(a.scores) & 15u) == 0 && a.ld % 4 == 0;
 }
 

@@ -278,11 +278,6 @@ __device__ void select_row_general(const SelectArgs& a, int64_t row, SelectSmem&
   write_out(a, row, sm);
 }
 
-__device__ __forceinline__ void grid_dependency_wait() {
-  // programmatic dependent launch: wait until the producing kernel (the scorer)
-  // has completed and its writes are visible; a no-op for a normal launch
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
 
 // ---- cluster select ------------------------------------------------------------------
 // Thread t of CTA r holds, for pass p, the kKeys keys of columns

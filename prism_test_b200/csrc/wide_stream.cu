@@ -13,7 +13,7 @@
 //      sub-digit holding the remaining rank (a second look at the row's samples);
 //   3. the scorer's candidate pass: every visible key at or above its row's
 //      threshold appended to the row's list (the tensor-core pass appends to a
-//      segment per CTA, gathered into the list by wide_gather_kernel);
+//      segment per CTA, which the selection appends to the list);
 //   4. the streaming selection (prefill_select.cu): each row's candidates sorted;
 //      rows whose count lies outside [min(k, visible), cap] recomputed exactly
 //      (any number of them: the fallback's scratch holds every row).
@@ -29,6 +29,7 @@ namespace {
 
 constexpr int kWtThreads = 512;
 constexpr int kWtCopies = 2;  // private histogram copies (lane & 1)
+constexpr int kWtBatch = 8;   // sample loads in flight per thread
 
 // Largest bin b of hist[0, nb) with sum(hist[b..nb)) >= need (need >= 1 and the
 // total reaches it): *bin_out = b, *above_out = sum(hist[b+1..nb)).
@@ -86,13 +87,26 @@ __global__ void __launch_bounds__(kWtThreads)
   __syncthreads();
   uint32_t* my = hist[tid & (kWtCopies - 1)];
   const int64_t n4 = nvalid >> 2;
-  for (int64_t c4 = tid; c4 < n4; c4 += kWtThreads) {
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(srow) + c4);
+  // every thread's 16-byte words of the sample, eight loads in flight at a time
+  auto for_each_word = [&](auto&& f) {
+    for (int64_t base = 0; base < n4; base += kWtBatch * kWtThreads) {
+      float4 v[kWtBatch];
+#pragma unroll
+      for (int u = 0; u < kWtBatch; ++u) {
+        const int64_t c4 = base + u * kWtThreads + tid;
+        if (c4 < n4) v[u] = __ldcg(reinterpret_cast<const float4*>(srow) + c4);
+      }
+#pragma unroll
+      for (int u = 0; u < kWtBatch; ++u)
+        if (base + u * kWtThreads + tid < n4) f(v[u]);
+    }
+  };
+  for_each_word([&](const float4& v) {
     atomicAdd(&my[float_to_okey(v.x) >> 20], 1u);
     atomicAdd(&my[float_to_okey(v.y) >> 20], 1u);
     atomicAdd(&my[float_to_okey(v.z) >> 20], 1u);
     atomicAdd(&my[float_to_okey(v.w) >> 20], 1u);
-  }
+  });
   for (int64_t c = (n4 << 2) + tid; c < nvalid; c += kWtThreads) atomicAdd(&my[float_to_okey(srow[c]) >> 20], 1u);
   __syncthreads();
   for (int i = tid; i < 4096; i += kWtThreads) {
@@ -114,15 +128,14 @@ __global__ void __launch_bounds__(kWtThreads)
   uint32_t* sub = hist[1];
   for (int i = tid; i < 256; i += kWtThreads) sub[i] = 0u;
   __syncthreads();
-  for (int64_t c4 = tid; c4 < n4; c4 += kWtThreads) {
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(srow) + c4);
+  for_each_word([&](const float4& v) {
     const float f[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const uint32_t key = float_to_okey(f[u]);
       if ((key >> 20) == b) atomicAdd(&sub[(key >> 12) & 0xffu], 1u);
     }
-  }
+  });
   for (int64_t c = (n4 << 2) + tid; c < nvalid; c += kWtThreads) {
     const uint32_t key = float_to_okey(srow[c]);
     if ((key >> 20) == b) atomicAdd(&sub[(key >> 12) & 0xffu], 1u);
@@ -144,45 +157,6 @@ int64_t sample_ld(int64_t Sk) {
 
 size_t seg_bytes(int64_t rows) { return size_t(rows) * kWideMaxSegs * kWideSegCap * 8; }
 size_t segn_bytes(int64_t rows) { return size_t(rows) * kWideMaxSegs * 4; }
-
-// One CTA per row: the row's segments appended to its list after the entries the
-// candidate pass placed there through the counter; the count becomes the total
-// (which may exceed the capacity: the selection then recomputes the row exactly).
-__global__ void __launch_bounds__(256) wide_gather_kernel(const uint64_t* __restrict__ seg,
-                                                          const uint32_t* __restrict__ segn,
-                                                          uint32_t* counts, uint64_t* cand, int64_t cap) {
-  __shared__ uint32_t off[kWideMaxSegs + 1];
-  __shared__ uint32_t wtot[8];
-  const int64_t row = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  static_assert(kWideMaxSegs == 512, "two segments per thread");
-  const uint32_t n0 = segn[row * kWideMaxSegs + 2 * tid], n1 = segn[row * kWideMaxSegs + 2 * tid + 1];
-  const uint32_t n = n0 + n1;
-  uint32_t x = n;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) wtot[warp] = x;
-  __syncthreads();
-  uint32_t wb = 0;
-  for (int w = 0; w < warp; ++w) wb += wtot[w];
-  const uint32_t base = counts[2 * row];
-  off[2 * tid] = base + wb + x - n;
-  off[2 * tid + 1] = base + wb + x - n1;
-  if (tid == 255) off[kWideMaxSegs] = base + wb + x;
-  __syncthreads();
-  // every entry: segment s = i / kWideSegCap, entry i % kWideSegCap
-  const uint64_t* src = seg + row * kWideMaxSegs * kWideSegCap;
-  uint64_t* dst = cand + row * cap;
-  for (int i = tid; i < kWideMaxSegs * kWideSegCap; i += 256) {
-    const int s = i / kWideSegCap, e = i % kWideSegCap;
-    const uint32_t o = off[s] + uint32_t(e);
-    if (o < off[s + 1] && o < uint64_t(cap)) dst[o] = src[i];
-  }
-  if (tid == 0) counts[2 * row] = off[kWideMaxSegs];
-}
 
 }  // namespace
 
@@ -219,10 +193,8 @@ cudaError_t wide_stream_threshold(const DecodeArgs& a, int dtype, int topk, void
   DecodeArgs s = a;  // the sample's scores, compactly
   s.scores = p.S;
   s.ld = p.ld_s;
-  // the sample (1/16 of the tiles, a few per CTA) on the mma.sync kernel: the
-  // tensor-core kernel's set-up (TMEM, the queries, the pipeline fill) outweighs
-  // so little work
-  e = launch_wide_sample(s, dtype, num_sms, stream);
+  e = wide_tc_supported(s) ? launch_wide_tc_sample(s, dtype, num_sms, stream)
+                           : launch_wide_sample(s, dtype, num_sms, stream);
   if (e != cudaSuccess) return e;
   // sample column c holds position (c / Tp) * 16 * Tp + c % Tp: the columns below
   // Sk are the first nvalid
@@ -239,12 +211,15 @@ cudaError_t wide_stream_candidates(const DecodeArgs& a, int dtype, int topk, voi
   const WideStreamPtrs p = wide_stream_ptrs(a, topk, ws);
   if (!wide_tc_supported(a) || 2 * num_sms > kWideMaxSegs)
     return launch_wide_candidates(a, dtype, p.sb.thr, p.sb.counts, p.sb.cand, p.sb.cap, num_sms, stream);
-  cudaError_t e = launch_wide_tc_candidates(a, dtype, p.sb.thr, p.sb.counts, p.sb.cand, p.sb.cap, p.seg, p.segn,
-                                            num_sms, stream);
-  if (e != cudaSuccess) return e;
-  const int64_t rows = int64_t(a.B) * a.Hq * a.Sq;
-  wide_gather_kernel<<<dim3(unsigned(rows)), 256, 0, stream>>>(p.seg, p.segn, p.sb.counts, p.sb.cand, p.sb.cap);
-  return cudaGetLastError();
+  return launch_wide_tc_candidates(a, dtype, p.sb.thr, p.sb.counts, p.sb.cand, p.sb.cap, p.seg, p.segn, num_sms,
+                                   stream);
+}
+
+cudaError_t wide_stream_select(const DecodeArgs& a, int dtype, int topk, int64_t index_base, int32_t* out_idx,
+                               float* out_scores, void* ws, cudaStream_t stream) {
+  const WideStreamPtrs p = wide_stream_ptrs(a, topk, ws);
+  return prefill_stream_select(a, dtype, topk, index_base, out_idx, out_scores, ws, stream,
+                               int64_t(a.B) * a.Hq * a.Sq, p.seg, p.segn);
 }
 
 }  // namespace prism
