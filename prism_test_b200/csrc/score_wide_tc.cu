@@ -363,6 +363,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---- epilogue: thread = query row rloc of head 2 hp + e_head, chunk g ------------
+    // a dependent launch: the thresholds (and the buffers the kernel before may still
+    // read) are settled after the wait; the other roles read only the keys
+    grid_dependency_wait();
     const int g = (warp - kEpiWarp0) >> 2;         // epilogue group
     const int hp = Hkv == 4 ? g : 0;               // the head pair of this thread's row
     const int h = 2 * hp + e_head;
@@ -467,8 +470,7 @@ cudaError_t launch_tc(const DecodeArgs& a, int num_sms, const TcExtra& x, cudaSt
   int ctas = num_sms;
   if (a.B > 1) ctas = (num_sms + a.B - 1) / a.B;
   ctas = max(1, min(ctas, d.ntiles));
-  kern<<<dim3(ctas, a.B), kThreads, kSmem, stream>>>(d, x);
-  return cudaGetLastError();
+  return launch_maybe_dependent(kern, dim3(ctas, a.B), dim3(kThreads), kSmem, true, stream, d, x);
 }
 
 template <int kMode>

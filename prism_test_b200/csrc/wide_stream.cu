@@ -76,6 +76,8 @@ __global__ void __launch_bounds__(kWtThreads)
   __shared__ uint32_t hist[kWtCopies][4096];
   __shared__ uint32_t wtot[kWtThreads / 32];
   __shared__ uint32_t s_bin, s_above;
+  grid_dependency_wait();  // a dependent launch: the sample is complete after the wait
+  asm volatile("griddepcontrol.launch_dependents;");
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x;
   const float* srow = S + row * ld_s;
@@ -201,9 +203,8 @@ cudaError_t wide_stream_threshold(const DecodeArgs& a, int dtype, int topk, void
   const int64_t Tp = 128 / a.Hkv, span = int64_t(kWideSampleStride) * Tp;
   const int64_t last = (a.Sk - 1) / span;  // last sampled stage
   const int64_t nvalid = last * Tp + std::min<int64_t>(Tp, a.Sk - last * span);
-  wide_threshold_kernel<<<dim3(unsigned(rows)), kWtThreads, 0, stream>>>(p.S, p.ld_s, nvalid, a.Sk, topk,
-                                                                         p.sb.thr);
-  return cudaGetLastError();
+  return launch_maybe_dependent(wide_threshold_kernel, dim3(unsigned(rows)), dim3(kWtThreads), 0, true, stream,
+                                static_cast<const float*>(p.S), p.ld_s, nvalid, int64_t(a.Sk), topk, p.sb.thr);
 }
 
 cudaError_t wide_stream_candidates(const DecodeArgs& a, int dtype, int topk, void* ws, int num_sms,
