@@ -316,6 +316,32 @@ def test_wide_stream_shapes(B, Hq, Hkv, Sq, Sk, topk, rope, dtype, causal, cuda_
     check_parity(idx, sc, q, k, topk, inv, 5 if rope else 0, causal)
 
 
+@pytest.mark.parametrize("Hkv,dtype", [(4, torch.bfloat16), (2, torch.float16)])
+def test_wide_stream_concentrated_hits_overflow_segments(Hkv, dtype, cuda_device):
+    # 600 keys in one stretch of the cache aligned with every query row of their head:
+    # the CTAs covering that stretch find far more than a candidate segment holds
+    # (64 per row and CTA half), and the rest goes to the rows' lists through their
+    # counters
+    g = torch.Generator(device=cuda_device).manual_seed(41)
+    B, Sq, Sk, topk = 1, 8, 40000, 2000
+    Hq = Hkv * 7
+    G = Hq // Hkv
+    dirs = torch.randn(Hkv, 128, generator=g, device=cuda_device)
+    dirs = dirs / dirs.norm(dim=-1, keepdim=True)
+    # every query row of head h: a common direction dirs[h] plus noise
+    q = torch.randn(B, Hq, Sq, 128, generator=g, device=cuda_device) + \
+        3.0 * dirs.repeat_interleave(G, dim=0)[None, :, None, :]
+    k = torch.randn(B, Hkv, Sk, 128, generator=g, device=cuda_device)
+    for h in range(Hkv):
+        k[0, h, 10000:10600] = 4.0 * 11.3 * dirs[h] + 0.5 * k[0, h, 10000:10600]
+    q, k = q.to(dtype), k.to(dtype)
+    idx, sc = einsum_topk_func(q, k, topk, return_scores=True)
+    check_parity(idx, sc, q, k, topk)
+    # most of the planted keys are in every row's top-k
+    planted = ((idx >= 10000) & (idx < 10600)).sum(-1).float()
+    assert float(planted.min()) > 300
+
+
 @pytest.mark.parametrize("sampled_high", [True, False])
 def test_wide_stream_threshold_miss_falls_back_exactly(sampled_high, cuda_device):
     # keys along q whose magnitudes make the sampled stages (positions p with
