@@ -710,6 +710,27 @@ def measure(wl, args, ranks: Ranks, *, e2e: bool, cpu_base: bool, clocks_on: boo
     return res
 
 
+def path_of(wl, rt="qk", sk=None) -> str:
+    """The library path a workload takes (the dispatch of prism_einsum_topk in exact
+    mode): "prefill" (Sq >= 128: tcgen05 candidate pass, tensor-bound), "wide" (many
+    query rows share one long context: tcgen05 queries-as-M candidate pass, HBM-bound)
+    or "decode" (the streaming decode scorer). ``sk``: the keys of this rank's shard."""
+    sk = wl.Sk if sk is None else sk
+    if wl.Sq >= 128:
+        return "prefill"
+    rows = wl.B * wl.Hq * wl.Sq
+    if (rt == "qk" and wl.Sq >= 2 and rows >= 64 and sk >= 32768 and wl.topk <= 4096
+            and wl.topk * 16 <= sk and wl.Hkv in (2, 4) and wl.Hq // wl.Hkv * wl.Sq <= 64):
+        return "wide"
+    return "decode"
+
+
+def dtype_of(wl, rt="qk", sk=None) -> str:
+    return {"prefill": "bf16 in, fp32 accumulate (tcgen05)",
+            "wide": "fp32 keys as bf16 hi + lo, fp32 accumulate (tcgen05)",
+            "decode": "f32 (tf32 MMA)"}[path_of(wl, rt, sk)]
+
+
 def roofline_of(res, rt="qk") -> tuple:
     """(roofline of the dominant kernel, roofline of the whole step) of one measurement."""
     wl = res["wl"]
@@ -731,7 +752,10 @@ def roofline_of(res, rt="qk") -> tuple:
         peak, src = measured_peaks()
         achieved = work / (score_ms * 1e-3) / 1e9
         roof = {"bound": "hbm", "unit": "GB/s", "bytes_per_launch": work,
-                "kernel": "decode scorer (TMA ring, fused inverse RoPE, fp32 q·K^T)"}
+                "kernel": ("queries-as-M candidate pass (tcgen05 kind::f16 M128 N64, query rows in "
+                           "TMEM, keys un-rotated once into bf16 hi + lo tiles, threshold epilogue)"
+                           if path_of(wl, rt, res["stop"] - res["start"]) == "wide" else
+                           "decode scorer (TMA ring, fused inverse RoPE, fp32 q·K^T)")}
         step_work = work
         step_achieved = work / (res["ms_per_step"] * 1e-3) / 1e9
     roof.update(achieved=achieved, peak=peak, frac=achieved / peak, peak_source=src,
@@ -752,6 +776,7 @@ def sub_record(res, args) -> dict:
     wl = res["wl"]
     roof, step_roof = roofline_of(res, args.recall_type)
     return {"workload": wl.name, "value": res["value"], "unit": UNIT, "ms_per_step": res["ms_per_step"],
+            "dtype": dtype_of(wl, args.recall_type, res["stop"] - res["start"]),
             "config": config_of(wl, res_world(res), args.recall_type, res["exchange"] or "peer"),
             "roofline": roof, "step_roofline": step_roof, "kernels_ms_per_step": kernels_ms(res, args.steps),
             "gpu_launches_per_step": res["launches_per_step"], "parity": res["parity"],
@@ -800,12 +825,11 @@ def main():
     if rank != 0:
         return 0
     roof, step_roof = roofline_of(main_res, rt)
-    prefill = wl.Sq >= 128
     line = {
         "metric": METRIC, "value": main_res["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": main_res["ms_per_step"], "higher_is_better": True,
         "scaling": "strong" if wl.name == "decode-1m-sharded" or world > 1 else "weak", "vs_baseline": None,
-        "dtype": "bf16 in, fp32 accumulate (tcgen05)" if prefill else "f32 (tf32 MMA)",
+        "dtype": dtype_of(wl, rt, main_res["stop"] - main_res["start"]),
         "data": "synthetic (seeded; see prism_test_b200/workloads.py)",
         "config": config_of(wl, world, rt, main_res["exchange"] or "peer"),
         "roofline": roof,
