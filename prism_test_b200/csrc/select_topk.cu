@@ -1256,23 +1256,25 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_row_kernel(const Sele
 // the largest summary entry whose bound, summed over the runs, reaches k: the
 // global k-th candidate is at or above T, and fewer than k + (N + 1) s candidates
 // are, however the top keys are split over the runs. Those prefixes are staged in
-// shared memory and every staged candidate is ranked by binary searches in the
-// other runs' prefixes (ties between equal candidates: lower run first); the
-// candidates ranked below k are the output, each written to its rank. If ties at
-// T make the prefixes exceed 16384 entries, the binary searches run in global
+// shared memory (sized on the host for that bound) and merged pairwise by a
+// merge-path tree (ties between equal candidates: lower run first), or, where two
+// tree buffers do not fit, every staged candidate is ranked by binary searches in
+// the other runs' prefixes; the candidates ranked below k are the output. If ties
+// at T make the prefixes exceed the staging, the binary searches run in global
 // memory instead (slow, same result).
+//
+// Few rows: a cluster of 4 CTAs of 1024 threads per row (each stages a quarter and
+// makes a quarter of the result). More rows than a wave of such clusters: one CTA
+// of 256 threads per row, several per SM, so that every row runs at once.
 constexpr int kMergeMaxRuns = kMergeRunsMax;
 constexpr int kMergeSumm = 128;
-constexpr int kMergeParts = 4;  // CTAs per row of the run merge
-constexpr uint32_t kTreeCap = 12288;  // entries per merge-tree ping-pong buffer (2 x 96 KB)
-// the merge tree's two buffers of kTreeCap entries span buf, hist and perm (back to back)
-static_assert(offsetof(SelectSmem, buf) == 0 && offsetof(SelectSmem, hist) == sizeof(uint64_t) * kCap &&
-                  offsetof(SelectSmem, perm) + sizeof(uint16_t) * kCap >= 2 * sizeof(uint64_t) * kTreeCap,
-              "merge tree buffers do not fit buf + hist + perm");
-// the merge keeps kCap 4-byte score keys in hist and perm, which lie back to back
-static_assert(offsetof(SelectSmem, perm) == offsetof(SelectSmem, hist) + sizeof(uint32_t) * kFineBins &&
-                  sizeof(uint32_t) * kFineBins + sizeof(uint16_t) * kCap >= sizeof(uint32_t) * kCap,
-              "score-key staging does not fit hist + perm");
+constexpr int kMergeMaxSmem = 227 * 1024;  // dynamic shared memory of one merge CTA, at most
+
+struct MergeShared {
+  uint32_t rlen[kMergeMaxRuns + 1], roff[kMergeMaxRuns + 1];  // prefix length, staging offset
+  unsigned long long rthr;                                      // threshold candidate
+  const int32_t* runs[kMergeMaxRuns];                           // the run pointers
+};
 
 __device__ __forceinline__ uint64_t run_cand(const int32_t* const* runs, int r, int64_t rows,
                                              int64_t row, int64_t run_len, int64_t j) {
@@ -1334,27 +1336,29 @@ __device__ __forceinline__ void merge_path_range(const uint64_t* X, uint32_t a, 
   }
 }
 
-// Runs the levels on the staged prefixes (in buffer A = smem entries [0, kTreeCap))
-// and writes result positions [p0, p1) of the row.
-__device__ void merge_tree(uint64_t* bufs, const uint32_t* roff, int nruns, uint32_t total, uint32_t p0,
-                           uint32_t p1, int32_t* oi, float* os) {
+// Runs the levels on the staged prefixes (in buffer A = bufs[0, cap); buffer B =
+// bufs[cap, 2 cap), used when there are more than two runs) and writes result
+// positions [p0, p1) of the row.
+template <int kT>
+__device__ void merge_tree(uint64_t* bufs, uint32_t cap, const uint32_t* roff, int nruns, uint32_t total,
+                           uint32_t p0, uint32_t p1, int32_t* oi, float* os) {
   const int tid = threadIdx.x;
   int levels = 0;
   while ((1 << levels) < nruns) ++levels;
   uint64_t* src = bufs;
-  uint64_t* dst = bufs + kTreeCap;
+  uint64_t* dst = bufs + cap;
   auto to_result = [&](uint32_t d, uint64_t x) {
     oi[d] = int32_t(~uint32_t(x));
     if (os) os[d] = okey_to_float(uint32_t(x >> 32));
   };
   if (levels == 0) {
-    for (uint32_t d = p0 + tid; d < p1; d += kThreads) to_result(d, src[d]);
+    for (uint32_t d = p0 + tid; d < p1; d += kT) to_result(d, src[d]);
     return;
   }
   for (int l = 0; l < levels; ++l) {
     const bool last = l == levels - 1;
     const uint32_t s0 = last ? p0 : 0u, s1 = last ? p1 : total;  // positions of this level to make
-    const uint32_t per = (s1 - s0 + kThreads - 1) / kThreads;
+    const uint32_t per = (s1 - s0 + kT - 1) / kT;
     uint32_t pos = s0 + min(s1 - s0, per * uint32_t(tid));
     const uint32_t end = min(s1, pos + per);
     while (pos < end) {
@@ -1381,39 +1385,48 @@ __device__ void merge_tree(uint64_t* bufs, const uint32_t* roff, int nruns, uint
   }
 }
 
+// summ: [nruns][kMergeSumm] summary entries; buf: the staging of cap entries (tree:
+// two buffers of cap entries; else cap entries and their cap 4-byte score keys).
+template <int kT, int kParts>
 __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, int64_t run_len, int k,
-                          int32_t* __restrict__ out_idx, float* __restrict__ out_scores,
-                          SelectSmem& sm, int64_t row, unsigned part) {
+                          int32_t* __restrict__ out_idx, float* __restrict__ out_scores, MergeShared& sm,
+                          uint64_t* summ, uint64_t* buf, uint32_t cap, bool tree, int64_t row,
+                          unsigned part) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   auto cand_at = [&](int r, int64_t j) { return run_cand(runs, r, rows, row, run_len, j); };
-  uint64_t* summ = reinterpret_cast<uint64_t*>(sm.hist);  // [nruns][kMergeSumm]
+  auto parts_sync = [&] {  // every CTA of the row
+    if constexpr (kParts > 1) cg::this_cluster().sync();
+    else __syncthreads();
+  };
 
   // ---- threshold from the run summaries ----------------------------------------------------
   const int64_t sstep = k / kMergeSumm > 1 ? k / kMergeSumm : 1;
   const int nsum = int(run_len / sstep < kMergeSumm ? run_len / sstep : kMergeSumm);
   if (tid == 0) sm.rthr = 0;
   {
-    // each CTA of the row's cluster loads a quarter of the summary entries (scattered
-    // words, which may cross the interconnect) and copies the rest from its cluster
-    // peers' shared memory
-    cg::cluster_group cluster = cg::this_cluster();
+    // each CTA of the row loads its share of the summary entries (scattered words,
+    // which may cross the interconnect) and copies the rest from its cluster peers'
+    // shared memory
     const int ns = nruns * nsum;
-    for (int e = ns * int(part) / kMergeParts + tid; e < ns * int(part + 1) / kMergeParts; e += kThreads) {
+    for (int e = ns * int(part) / kParts + tid; e < ns * int(part + 1) / kParts; e += kT) {
       const int r = e / nsum, i = e - r * nsum;
       summ[r * kMergeSumm + i] = cand_at(r, (int64_t(i) + 1) * sstep - 1);
     }
-    cluster.sync();
-    for (unsigned c = 0; c < unsigned(kMergeParts); ++c) {
-      if (c == part) continue;
-      const uint64_t* src = cluster.map_shared_rank(summ, c);
-      for (int e = ns * int(c) / kMergeParts + tid; e < ns * int(c + 1) / kMergeParts; e += kThreads) {
-        const int at = (e / nsum) * kMergeSumm + e % nsum;
-        summ[at] = src[at];
+    parts_sync();
+    if constexpr (kParts > 1) {
+      cg::cluster_group cluster = cg::this_cluster();
+      for (unsigned c = 0; c < unsigned(kParts); ++c) {
+        if (c == part) continue;
+        const uint64_t* src = cluster.map_shared_rank(summ, c);
+        for (int e = ns * int(c) / kParts + tid; e < ns * int(c + 1) / kParts; e += kT) {
+          const int at = (e / nsum) * kMergeSumm + e % nsum;
+          summ[at] = src[at];
+        }
       }
+      cluster.sync();  // every CTA holds every summary; nobody reads a peer's copy any more
     }
-    cluster.sync();  // every CTA holds every summary; nobody reads a peer's copy any more
   }
-  for (int e = tid; e < nruns * nsum; e += kThreads) {
+  for (int e = tid; e < nruns * nsum; e += kT) {
     const uint64_t v = summ[(e / nsum) * kMergeSumm + e % nsum];
     int64_t c = 0;
     for (int q = 0; q < nruns; ++q) {
@@ -1444,8 +1457,8 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
   // prefix of each run at or above T: warp r narrows the boundary 32-fold per step,
   // starting from the window its summary leaves (c summary entries >= T: the
   // boundary lies in [c * sstep, (c + 1) * sstep - 1], or beyond the summarised part)
-  if (warp < nruns) {
-    const uint64_t* sw = summ + warp * kMergeSumm;
+  for (int r = warp; r < nruns; r += kT / 32) {
+    const uint64_t* sw = summ + r * kMergeSumm;
     int ns_ge = 0;
     for (int i = lane; i < nsum; i += 32) ns_ge += sw[i] >= thr ? 1 : 0;
 #pragma unroll
@@ -1456,22 +1469,22 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
     if (hi - lo <= 64) {
       // the whole window in one round: entries lo + lane and lo + 32 + lane
       const int64_t p0 = lo + lane, p1 = lo + 32 + lane;
-      const bool g0 = p0 < hi && cand_at(warp, p0) >= thr;
-      const bool g1 = p1 < hi && cand_at(warp, p1) >= thr;
+      const bool g0 = p0 < hi && cand_at(r, p0) >= thr;
+      const bool g1 = p1 < hi && cand_at(r, p1) >= thr;
       lo += __popc(__ballot_sync(0xffffffffu, g0)) + __popc(__ballot_sync(0xffffffffu, g1));
       hi = lo;
     }
     while (lo < hi) {
       const int64_t step = (hi - lo + 31) / 32;
       const int64_t p = lo + int64_t(lane) * step;
-      const bool ge = p < hi && cand_at(warp, p) >= thr;
+      const bool ge = p < hi && cand_at(r, p) >= thr;
       const int c = __popc(__ballot_sync(0xffffffffu, ge));  // passing probes: lanes 0 .. c-1
       if (c == 0) break;
       const int64_t nhi = lo + int64_t(c) * step;
       lo = lo + int64_t(c - 1) * step + 1;
       hi = nhi < hi ? nhi : hi;
     }
-    if (lane == 0) sm.rlen[warp] = uint32_t(lo);
+    if (lane == 0) sm.rlen[r] = uint32_t(lo);
   }
   __syncthreads();
   if (tid == 0) {
@@ -1484,21 +1497,19 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
   }
   __syncthreads();
   const uint32_t total = sm.roff[nruns];
-  const bool staged = total <= uint32_t(kCap);  // the same on every CTA of the cluster
+  const bool staged = total <= cap;  // the same on every CTA of the row
   if (staged) {
-    // each CTA of the row's cluster loads a quarter of the staged entries (so each
-    // entry is read once, from wherever the run lives), then copies the other
-    // quarters from its cluster peers' shared memory
-    cg::cluster_group cluster = cg::this_cluster();
-    const uint32_t q0 = uint32_t(uint64_t(total) * part / kMergeParts);
-    const uint32_t q1 = uint32_t(uint64_t(total) * (part + 1) / kMergeParts);
-    // eight independent loads per thread in flight (one interconnect round trip for a
-    // quarter of up to 8192 entries), whichever runs they fall in
-    for (uint32_t e0 = q0; e0 < q1; e0 += 8 * kThreads) {
+    // each CTA of the row loads its share of the staged entries (so each entry is
+    // read once, from wherever the run lives), then copies the other shares from
+    // its cluster peers' shared memory
+    const uint32_t q0 = uint32_t(uint64_t(total) * part / kParts);
+    const uint32_t q1 = uint32_t(uint64_t(total) * (part + 1) / kParts);
+    // eight independent loads per thread in flight, whichever runs they fall in
+    for (uint32_t e0 = q0; e0 < q1; e0 += 8 * kT) {
       uint64_t v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const uint32_t e = e0 + uint32_t(u * kThreads + tid);
+        const uint32_t e = e0 + uint32_t(u * kT + tid);
         v[u] = 0;
         if (e < q1) {
           int r = 0;
@@ -1508,31 +1519,33 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const uint32_t e = e0 + uint32_t(u * kThreads + tid);
-        if (e < q1) sm.buf[e] = v[u];
+        const uint32_t e = e0 + uint32_t(u * kT + tid);
+        if (e < q1) buf[e] = v[u];
       }
     }
-    cluster.sync();  // every quarter is staged
-    for (unsigned c = 0; c < unsigned(kMergeParts); ++c) {
-      if (c == part) continue;
-      const uint64_t* src = cluster.map_shared_rank(sm.buf, c);
-      const uint32_t c1 = uint32_t(uint64_t(total) * (c + 1) / kMergeParts);
-      for (uint32_t e = uint32_t(uint64_t(total) * c / kMergeParts) + tid; e < c1; e += kThreads)
-        sm.buf[e] = src[e];
+    parts_sync();  // every share is staged
+    if constexpr (kParts > 1) {
+      cg::cluster_group cluster = cg::this_cluster();
+      for (unsigned c = 0; c < unsigned(kParts); ++c) {
+        if (c == part) continue;
+        const uint64_t* src = cluster.map_shared_rank(buf, c);
+        const uint32_t c1 = uint32_t(uint64_t(total) * (c + 1) / kParts);
+        for (uint32_t e = uint32_t(uint64_t(total) * c / kParts) + tid; e < c1; e += kT) buf[e] = src[e];
+      }
+      cluster.sync();  // every CTA holds all entries; nobody reads a peer's copy any more
     }
-    cluster.sync();  // every CTA holds all entries; nobody reads a peer's copy any more
-    if (total <= kTreeCap) {
-      // this CTA makes a quarter of the k result positions (the last level)
+    if (tree) {
+      // this CTA makes its share of the k result positions (the last level)
       const uint32_t kk = min(uint32_t(k), total);
-      merge_tree(reinterpret_cast<uint64_t*>(&sm), sm.roff, nruns, total,
-                 uint32_t(uint64_t(kk) * part / kMergeParts), uint32_t(uint64_t(kk) * (part + 1) / kMergeParts),
-                 out_idx + row * k, out_scores ? out_scores + row * k : nullptr);
+      merge_tree<kT>(buf, cap, sm.roff, nruns, total, uint32_t(uint64_t(kk) * part / kParts),
+                     uint32_t(uint64_t(kk) * (part + 1) / kParts), out_idx + row * k,
+                     out_scores ? out_scores + row * k : nullptr);
       return;
     }
     // the score keys alone, for the binary searches (4-byte probes; the index
     // word is read only when two score keys are equal)
-    uint32_t* sk = reinterpret_cast<uint32_t*>(sm.hist);  // hist and perm: kCap words
-    for (uint32_t e = tid; e < total; e += kThreads) sk[e] = uint32_t(sm.buf[e] >> 32);
+    uint32_t* sk = reinterpret_cast<uint32_t*>(buf + cap);
+    for (uint32_t e = tid; e < total; e += kT) sk[e] = uint32_t(buf[e] >> 32);
     __syncthreads();
   }
   // rank every prefix candidate: its position in its run plus, in every other run,
@@ -1540,12 +1553,12 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
   int32_t* oi = out_idx + row * k;
   float* os = out_scores ? out_scores + row * k : nullptr;
   if (staged) {
-    const uint32_t* sk = reinterpret_cast<const uint32_t*>(sm.hist);
-    for (uint32_t e = part * kThreads + tid; e < total; e += kMergeParts * kThreads) {
+    const uint32_t* sk = reinterpret_cast<const uint32_t*>(buf + cap);
+    for (uint32_t e = part * kT + tid; e < total; e += kParts * kT) {
       int r = 0;
       while (e >= sm.roff[r + 1]) ++r;
       const uint32_t j = e - sm.roff[r];
-      const uint32_t xs = sk[e], xi = uint32_t(sm.buf[e]);
+      const uint32_t xs = sk[e], xi = uint32_t(buf[e]);
       uint32_t p = j;
       for (int q = 0; q < nruns; ++q) {
         if (q == r) continue;
@@ -1556,7 +1569,7 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
           const uint32_t vs = sk[o + mid];
           bool ahead = vs > xs;
           if (vs == xs) {
-            const uint32_t vi = uint32_t(sm.buf[o + mid]);
+            const uint32_t vi = uint32_t(buf[o + mid]);
             ahead = vi > xi || (q < r && vi == xi);
           }
           if (ahead) lo = mid + 1;
@@ -1571,7 +1584,7 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
     }
     return;
   }
-  for (uint32_t e = part * kThreads + tid; e < total; e += kMergeParts * kThreads) {
+  for (uint32_t e = part * kT + tid; e < total; e += kParts * kT) {
     int r = 0;
     while (e >= sm.roff[r + 1]) ++r;
     const uint32_t j = e - sm.roff[r];
@@ -1603,19 +1616,21 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
 // bounded by sync.timeout_ns and report kStatusTimeout in this rank's header; a
 // CTA whose wait expired merges whatever the buffers hold (every access stays in
 // bounds, and every CTA of a cluster takes the same cluster barriers).
-__global__ void __cluster_dims__(kMergeParts, 1, 1) __launch_bounds__(kThreads, 1)
+template <int kT, int kParts>
+__global__ void __cluster_dims__(kParts, 1, 1) __launch_bounds__(kT, kT >= 1024 ? 1 : 4)
     merge_runs_kernel(const RunSet rs, int nruns, int64_t rows, int64_t run_len, int k,
                       int32_t* __restrict__ out_idx, float* __restrict__ out_scores,
-                      const PeerSync sync) {
+                      const PeerSync sync, uint32_t cap, int tree) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  SelectSmem& sm = *reinterpret_cast<SelectSmem*>(smem_raw);
-  // kMergeParts CTAs per row: each finds the same candidates, and ranks and writes
-  // its own share of them
-  const int64_t row = blockIdx.x / kMergeParts;
-  const unsigned part = blockIdx.x % kMergeParts;
+  __shared__ MergeShared sm;
+  uint64_t* summ = reinterpret_cast<uint64_t*>(smem_raw);  // [nruns][kMergeSumm]
+  uint64_t* buf = summ + nruns * kMergeSumm;
+  // kParts CTAs per row: each finds the same candidates, and ranks and writes its
+  // own share of them
+  const int64_t row = blockIdx.x / kParts;
+  const unsigned part = blockIdx.x % kParts;
   const int tid = threadIdx.x;
-  __shared__ const int32_t* s_runs[kMergeMaxRuns];  // the run pointers, indexed by run
-  if (tid < nruns) s_runs[tid] = rs.run[tid];
+  if (tid < nruns) sm.runs[tid] = rs.run[tid];
   grid_dependency_wait();  // a dependent launch after the publish (peer exchange)
   PeerHeader* self = sync.self;
   uint64_t step = 0, t_start = 0;
@@ -1630,7 +1645,8 @@ __global__ void __cluster_dims__(kMergeParts, 1, 1) __launch_bounds__(kThreads, 
     self->t_start = t_start;
     self->t_ready = globaltimer_ns();
   }
-  merge_row(s_runs, nruns, rows, run_len, k, out_idx, out_scores, sm, row, part);
+  merge_row<kT, kParts>(sm.runs, nruns, rows, run_len, k, out_idx, out_scores, sm, summ, buf, cap, tree != 0,
+                        row, part);
   if (self == nullptr) return;
   __syncthreads();  // this CTA's reads of the runs are complete
   if (tid == 0) {
@@ -1708,15 +1724,37 @@ cudaError_t launch_merge_runs(const RunSet& rs, int nruns, int64_t rows, int64_t
                               cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   if (nruns < 1 || nruns > kMergeMaxRuns) return cudaErrorInvalidValue;
-  const size_t smem = sizeof(SelectSmem);
-  cudaError_t e = cudaFuncSetAttribute(merge_runs_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  // staging for the prefixes at or above the threshold: fewer than k + (N + 1) s
+  // entries (s per summary entry), and never more than the runs hold
+  const int64_t sstep = k / kMergeSumm > 1 ? k / kMergeSumm : 1;
+  const int64_t bound = std::min<int64_t>(int64_t(k) + (nruns + 1) * sstep, int64_t(nruns) * run_len);
+  const size_t summ = size_t(nruns) * kMergeSumm * sizeof(uint64_t);
+  const size_t room = (kMergeMaxSmem - summ) / 8;  // 8-byte words left for the staging
+  // the tree wants a second buffer when it has more than one level
+  const size_t tree_words = size_t(bound) * (nruns > 2 ? 2 : 1);
+  const bool tree = tree_words <= room;
+  // else the ranking by binary searches: the entries and their 4-byte keys
+  const uint32_t cap = tree ? uint32_t(bound) : uint32_t(std::min<size_t>(size_t(bound), room * 8 / 12));
+  const size_t smem = summ + (tree ? tree_words * 8 : size_t(cap) * 12);
+  int dev = 0, nsm = 148;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   // the peer merge follows the publish as a dependent launch (it reads the step
   // the publish wrote only after its griddepcontrol.wait)
-  return launch_maybe_dependent(merge_runs_kernel, dim3(unsigned(rows * kMergeParts)), dim3(kThreads), smem,
-                                sync.self != nullptr, stream, rs, nruns, rows, run_len, k, out_idx,
-                                out_scores, sync);
+  const bool pdl = sync.self != nullptr;
+  if (rows * 4 <= nsm) {  // a 4-CTA cluster per row, one wave
+    auto kern = merge_runs_kernel<1024, 4>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    return launch_maybe_dependent(kern, dim3(unsigned(rows * 4)), dim3(1024), smem, pdl, stream, rs, nruns,
+                                  rows, run_len, k, out_idx, out_scores, sync, cap, int(tree));
+  }
+  auto kern = merge_runs_kernel<256, 1>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  return launch_maybe_dependent(kern, dim3(unsigned(rows)), dim3(256), smem, pdl, stream, rs, nruns, rows,
+                                run_len, k, out_idx, out_scores, sync, cap, int(tree));
 }
 
 cudaError_t launch_merge_runs(const int32_t* runs, int nruns, int64_t rows, int64_t run_len, int k,

@@ -78,8 +78,15 @@ def _runs(nruns, rows, run_len, seed, kind="normal", pad=0):
     (3, 5, 4000, 2500, "normal", 0),      # runs longer than k
     (4, 3, 1000, 1000, "normal", 600),    # duplicate (-inf, INT32_MAX) padding in every run
     (2, 2, 16384, 16384, "flat", 0),      # ties beyond the staging capacity
-    (2, 3, 12800, 12800, "normal", 0),    # more staged entries than the merge tree holds
+    (2, 3, 12800, 12800, "normal", 0),    # a long staging (one tree level)
+    (4, 3, 14000, 14000, "normal", 0),    # two tree buffers do not fit: ranking by binary searches
     (7, 4, 3000, 2900, "ties", 40),       # an odd number of runs: a list without a partner
+    # more rows than a wave of 4-CTA clusters: one CTA per row, several per SM
+    (2, 224, 4096, 4096, "normal", 0),    # the 2-rank shared-context merge
+    (8, 224, 4096, 4096, "ties", 0),
+    (5, 50, 3000, 2900, "normal", 30),
+    (4, 40, 14000, 14000, "normal", 0),   # ranking by binary searches
+    (2, 40, 16384, 16384, "flat", 0),     # ties beyond the staging capacity
 ])
 def test_merge_runs_edge_cases(cuda_device, nruns, rows, run_len, topk, kind, pad):
     v, idx = _runs(nruns, rows, run_len, seed=nruns * 1000 + topk, kind=kind, pad=pad)
