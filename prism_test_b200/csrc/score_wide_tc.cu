@@ -72,6 +72,7 @@ enum TcMode : int { kTScores = 0, kTSample = 1, kTCand = 2 };
 struct TcBars {
   uint64_t b_full[kBSlots], b_empty[kBSlots];
   uint64_t d_full[2], d_empty[2];
+  uint64_t q_full;  // the queries are in TMEM (the four loading warps arrive)
   uint32_t tmem_base;
   int abort;
 };
@@ -172,6 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->d_full[s], 1);
       mbar_init(&bars->d_empty[s], kEpiWarps);
     }
+    mbar_init(&bars->q_full, 4);
     bars->abort = 0;
     fence_mbar_init();
   }
@@ -186,7 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("griddepcontrol.launch_dependents;");
 
   // ---- the queries into TMEM (A operand): lane L of head pair hp holds query row
-  // L % 64 of head 2 hp + L / 64, column c dimensions (2c, 2c + 1) ----------------------
+  // L % 64 of head 2 hp + L / 64, column c dimensions (2c, 2c + 1); the MMA issuer
+  // waits for them on q_full ------------------------------------------------------
   const int quad = warp & 3;
   const int e_head = quad >> 1;                    // epilogue: head 2 hp + e_head of each pair
   const int rloc = (quad & 1) * 32 + lane;         // epilogue: row within the head (< 64)
@@ -222,10 +225,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars->q_full);
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  // The sample pass (a few tiles per CTA) lets the converters start on the first
+  // key tiles while the queries load; the long passes start every role together,
+  // which measured faster for them.
+  if constexpr (kMode != kTSample) __syncthreads();
 
   const T* kb = static_cast<const T*>(a.k) + ((a.B > 1 && a.k_sb != 0) ? int64_t(b) * a.k_sb : 0);
   auto tile_pos = [&](int it) { return (t_begin + it) * tstep * Tn; };  // first position of loop tile it
@@ -237,9 +244,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = idesc_kind_f16(std::is_same<T, __nv_bfloat16>::value, 128, 2 * Tn);
       const uint32_t blk16 = uint32_t(2 * Tn * 128) >> 4;  // one block, in 16-byte units
+      const bool q_ok = mbar_wait_bounded(&bars->q_full, 0u);
       for (int it = 0; it < nit; ++it) {
         const int bs = it % kBSlots, db = it & 1;
-        bool ok = mbar_wait_sleep_bounded(&bars->b_full[bs], uint32_t((it / kBSlots) & 1));
+        bool ok = q_ok && mbar_wait_sleep_bounded(&bars->b_full[bs], uint32_t((it / kBSlots) & 1));
         if (ok && it >= 2) ok = mbar_wait_sleep_bounded(&bars->d_empty[db], uint32_t((it / 2 - 1) & 1));
         if (!ok || *reinterpret_cast<volatile int*>(&bars->abort)) {
           if (!ok) set_status(a.status, kStatusTimeout);
