@@ -27,7 +27,11 @@
 namespace prism {
 namespace {
 
+// threads of a selection CTA: 256 for the many rows of a prefill chunk; 512 (one per
+// candidate segment) for the few rows of the queries-as-M tensor-core pass
 constexpr int kPsThreads = 256;
+constexpr int kPsThreadsSeg = 512;
+static_assert(kWideMaxSegs == kPsThreadsSeg, "one candidate segment per thread");
 constexpr int kPsBins = 2048;
 constexpr int kPsRankMax = 64;
 constexpr int kFallbackRows = 64;
@@ -67,7 +71,8 @@ __device__ __forceinline__ void flag_row(const PsArgs& a, int64_t row) {
     set_status(a.status, kStatusCapacity);
 }
 
-// exclusive block scan of one value per thread (256 threads)
+// exclusive block scan of one value per thread (kT threads)
+template <int kT>
 __device__ __forceinline__ uint32_t ps_scan(uint32_t v, uint32_t* wtot, uint32_t* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t x = v;
@@ -79,32 +84,33 @@ __device__ __forceinline__ uint32_t ps_scan(uint32_t v, uint32_t* wtot, uint32_t
   if (lane == 31) wtot[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    uint32_t w = lane < kPsThreads / 32 ? wtot[lane] : 0u;
+    uint32_t w = lane < kT / 32 ? wtot[lane] : 0u;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += y;
     }
-    if (lane < kPsThreads / 32) wtot[lane] = w;
+    if (lane < kT / 32) wtot[lane] = w;
   }
   __syncthreads();
   const uint32_t r = (warp ? wtot[warp - 1] : 0u) + x - v;
-  *total = wtot[kPsThreads / 32 - 1];
+  *total = wtot[kT / 32 - 1];
   __syncthreads();
   return r;
 }
 
-__global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs a) {
+template <int kT>
+__global__ void __launch_bounds__(kT) prefill_select_kernel(const PsArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   // candidates: score keys and index words (10 bytes per candidate with perm)
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem);                      // [cap]
   uint32_t* idxw = keys + a.cap;                                           // [cap] ~index
   uint32_t* hist = idxw + a.cap;                                           // [kPsBins]
   uint16_t* perm = reinterpret_cast<uint16_t*>(hist + kPsBins);            // [cap]
-  __shared__ uint32_t wtot[kPsThreads / 32];
+  __shared__ uint32_t wtot[kT / 32];
   __shared__ uint32_t s_kmax, s_kmin, s_big;  // max / min key of the finite scores
 
-  __shared__ uint32_t soff[kWideMaxSegs + 1];  // segments: start of each in the appended entries
+  __shared__ uint32_t soff[kT == kPsThreadsSeg ? kWideMaxSegs : 1];  // segments: start of each
   // a dependent launch: the candidate pass's lists and counts are complete after the wait
   grid_dependency_wait();
   asm volatile("griddepcontrol.launch_dependents;");
@@ -114,15 +120,13 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
   // entries of the candidate pass's segments (nseg of them), then n1 from the back
   const uint32_t n0 = a.counts[2 * row];
   const uint32_t n1 = a.counts[2 * row + 1];
-  uint32_t nseg = 0;
-  if (a.seg != nullptr) {
-    static_assert(kWideMaxSegs == 2 * kPsThreads, "two segments per thread");
-    const uint32_t* sn = a.segn + row * kWideMaxSegs;
-    const uint32_t c0 = sn[2 * tid], c1 = sn[2 * tid + 1];
-    const uint32_t ex = ps_scan(c0 + c1, wtot, &nseg);
-    soff[2 * tid] = ex;
-    soff[2 * tid + 1] = ex + c0;
-    if (tid == 0) soff[kWideMaxSegs] = nseg;
+  uint32_t nseg = 0, my_seg_n = 0, my_seg_off = 0;  // this thread's segment: entries, start
+  if constexpr (kT == kPsThreadsSeg) {
+    if (a.seg != nullptr) {
+      my_seg_n = a.segn[row * kWideMaxSegs + tid];
+      my_seg_off = ps_scan<kT>(my_seg_n, wtot, &nseg);
+      soff[tid] = my_seg_off;
+    }
   }
   const uint32_t n = n0 + nseg + n1;
   const int64_t nvis = visible_keys(row, a.Sq, a.causal, a.causal_offset, a.Sk);
@@ -134,7 +138,7 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
     return;
   }
   // masked keys after the visible ones (rows that see fewer than k keys)
-  for (uint32_t p = keff + tid; p < uint32_t(a.k); p += kPsThreads) {
+  for (uint32_t p = keff + tid; p < uint32_t(a.k); p += kT) {
     oi[p] = int32_t(nvis + (p - keff) + a.index_base);
     if (os) os[p] = -INFINITY;
   }
@@ -144,7 +148,7 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
     s_kmin = 0xffffffffu;
     s_big = 0u;
   }
-  for (int i = tid; i < kPsBins; i += kPsThreads) hist[i] = 0u;
+  for (int i = tid; i < kPsBins; i += kT) hist[i] = 0u;
   __syncthreads();
   uint32_t kmx = 0u, kmn = 0xffffffffu;
   auto put = [&](uint32_t i, uint64_t x) {  // candidate i into shared memory
@@ -157,32 +161,34 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
     }
   };
   const uint64_t* src = a.cand + row * a.cap;
-  for (uint32_t i = tid; i < n0; i += kPsThreads) put(i, src[i]);
-  for (uint32_t i = tid; i < n1; i += kPsThreads) put(n0 + nseg + i, src[a.cap - 1 - i]);
-  if (nseg > 0) {
-    // the segments' entries, eight loads in flight per thread
-    const uint64_t* sg = a.seg + row * kWideMaxSegs * kWideSegCap;
-    for (uint32_t i0 = tid; i0 < nseg; i0 += 8 * kPsThreads) {
+  // cnt list entries at(i) into candidates dst0 + i, eight loads in flight per thread
+  auto load_list = [&](uint32_t cnt, uint32_t dst0, auto&& at) {
+    for (uint32_t i0 = tid; i0 < cnt; i0 += 8 * kT) {
       uint64_t v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const uint32_t i = i0 + uint32_t(u * kPsThreads);
-        if (i < nseg) {
-          int lo = 0, hi = kWideMaxSegs;  // soff[lo] <= i < soff[hi]: lo is the entry's segment
-          while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (soff[mid] <= i) lo = mid;
-            else hi = mid;
-          }
-          v[u] = sg[lo * kWideSegCap + (i - soff[lo])];
-        }
+        const uint32_t i = i0 + uint32_t(u * kT);
+        if (i < cnt) v[u] = at(i);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const uint32_t i = i0 + uint32_t(u * kPsThreads);
-        if (i < nseg) put(n0 + i, v[u]);
+        const uint32_t i = i0 + uint32_t(u * kT);
+        if (i < cnt) put(dst0 + i, v[u]);
       }
     }
+  };
+  load_list(n0, 0u, [&](uint32_t i) { return src[i]; });
+  load_list(n1, n0 + nseg, [&](uint32_t i) { return src[a.cap - 1 - i]; });
+  if constexpr (kT == kPsThreadsSeg) if (nseg > 0) {
+    // the segment of every appended entry (perm serves as the map until the sort
+    // below), then the entries, eight loads in flight per thread
+    for (uint32_t j = 0; j < my_seg_n; ++j) perm[my_seg_off + j] = uint16_t(tid);
+    __syncthreads();
+    const uint64_t* sg = a.seg + row * kWideMaxSegs * kWideSegCap;
+    load_list(nseg, n0, [&](uint32_t i) {
+      const uint32_t s = perm[i];
+      return sg[s * kWideSegCap + (i - soff[s])];
+    });
   }
   kmx = __reduce_max_sync(0xffffffffu, kmx);
   kmn = __reduce_min_sync(0xffffffffu, kmn);
@@ -214,10 +220,10 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
     const float y = (okey_to_float(key) - fmin) + c0;
     return uint32_t(kPsBins - 1) - __umulhi(__float_as_uint(y) - b0, mult);
   };
-  for (uint32_t i = tid; i < n; i += kPsThreads) atomicAdd(&hist[bin_of(keys[i])], 1u);
+  for (uint32_t i = tid; i < n; i += kT) atomicAdd(&hist[bin_of(keys[i])], 1u);
   __syncthreads();
   {
-    constexpr int kPer = kPsBins / kPsThreads;
+    constexpr int kPer = kPsBins / kT;
     uint32_t h[kPer], tot = 0, hmax = 0;
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
@@ -228,7 +234,7 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
     hmax = __reduce_max_sync(0xffffffffu, hmax);
     if (lane == 0) atomicMax(&s_big, hmax);
     uint32_t total;
-    uint32_t ex = ps_scan(tot, wtot, &total);
+    uint32_t ex = ps_scan<kT>(tot, wtot, &total);
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
       hist[kPer * tid + u] = ex;  // start of bin
@@ -240,7 +246,7 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
     if (tid == 0) flag_row(a, row);
     return;
   }
-  for (uint32_t i = tid; i < n; i += kPsThreads) perm[atomicAdd(&hist[bin_of(keys[i])], 1u)] = uint16_t(i);
+  for (uint32_t i = tid; i < n; i += kT) perm[atomicAdd(&hist[bin_of(keys[i])], 1u)] = uint16_t(i);
   __syncthreads();  // hist[f] is now the end of bin f
   // candidates in the bins that hold output positions [0, keff)
   uint32_t fend = 0;  // first bin whose start is >= keff
@@ -253,7 +259,7 @@ __global__ void __launch_bounds__(kPsThreads) prefill_select_kernel(const PsArgs
     fend = lo;
   }
   const uint32_t qend = hist[fend < kPsBins ? fend : kPsBins - 1];
-  for (uint32_t q = tid; q < qend; q += kPsThreads) {
+  for (uint32_t q = tid; q < qend; q += kT) {
     const uint32_t i = perm[q];
     const uint32_t kx = keys[i];
     const uint32_t f = bin_of(kx);
@@ -507,10 +513,12 @@ cudaError_t prefill_stream_select(const DecodeArgs& d, int dtype, int topk, int6
   p.seg = seg;
   p.segn = segn;
   const size_t smem = size_t(w.cap) * 10 + kPsBins * 4;
-  cudaError_t e = cudaFuncSetAttribute(prefill_select_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  const bool segs = seg != nullptr;
+  auto kern = segs ? prefill_select_kernel<kPsThreadsSeg> : prefill_select_kernel<kPsThreads>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  e = launch_maybe_dependent(prefill_select_kernel, dim3(unsigned(rows)), dim3(kPsThreads), smem, true, stream, p);
+  e = launch_maybe_dependent(kern, dim3(unsigned(rows)), dim3(segs ? kPsThreadsSeg : kPsThreads), smem, true, stream,
+                             p);
   if (e != cudaSuccess) return e;
 
   // exact fallback for the listed rows (kernels return at once when none are)
