@@ -1255,8 +1255,10 @@ __global__ void __launch_bounds__(kThreads, 1) select_topk_row_kernel(const Sele
 // are at or above a value (s per summary entry at or above it). The threshold T is
 // the largest summary entry whose bound, summed over the runs, reaches k: the
 // global k-th candidate is at or above T, and fewer than k + (N + 1) s candidates
-// are, however the top keys are split over the runs. Those prefixes are staged in
-// shared memory (sized on the host for that bound) and merged pairwise by a
+// are, however the top keys are split over the runs. Each run's entries before its
+// first summary entry below T (its prefix at or above T and at most s - 1 more, which
+// rank after position k; the same bound holds) are staged in shared memory (sized
+// on the host for that bound) and merged pairwise by a
 // merge-path tree (ties between equal candidates: lower run first), or, where two
 // tree buffers do not fit, every staged candidate is ranked by binary searches in
 // the other runs' prefixes; the candidates ranked below k are the output. If ties
@@ -1454,9 +1456,10 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
   }
   __syncthreads();
   const uint64_t thr = sm.rthr;
-  // prefix of each run at or above T: warp r narrows the boundary 32-fold per step,
-  // starting from the window its summary leaves (c summary entries >= T: the
-  // boundary lies in [c * sstep, (c + 1) * sstep - 1], or beyond the summarised part)
+  // the staged length of each run: c summary entries >= T put the boundary of its
+  // prefix at or above T in [c * sstep, (c + 1) * sstep - 1]; the whole window is
+  // staged. Only a long unsummarised tail (runs longer than 128 s) is searched: warp r
+  // narrows the boundary 32-fold per step
   for (int r = warp; r < nruns; r += kT / 32) {
     const uint64_t* sw = summ + r * kMergeSumm;
     int ns_ge = 0;
@@ -1466,6 +1469,13 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
     int64_t lo = int64_t(ns_ge) * sstep;  // entries [0, lo) are >= T, entries [hi, run_len) are < T
     int64_t hi = ns_ge < nsum ? (int64_t(ns_ge) + 1) * sstep - 1 : run_len;
     if (hi > run_len) hi = run_len;
+    if (hi - lo <= sstep) {
+      // stage the whole window (no search across the interconnect): its entries below
+      // T rank after position k (at least k staged entries are at or above T), and the
+      // staging bound k + (N + 1) s still holds
+      if (lane == 0) sm.rlen[r] = uint32_t(hi);
+      continue;
+    }
     if (hi - lo <= 64) {
       // the whole window in one round: entries lo + lane and lo + 32 + lane
       const int64_t p0 = lo + lane, p1 = lo + 32 + lane;
