@@ -1514,11 +1514,13 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
     // its cluster peers' shared memory
     const uint32_t q0 = uint32_t(uint64_t(total) * part / kParts);
     const uint32_t q1 = uint32_t(uint64_t(total) * (part + 1) / kParts);
-    // eight independent loads per thread in flight, whichever runs they fall in
-    for (uint32_t e0 = q0; e0 < q1; e0 += 8 * kT) {
-      uint64_t v[8];
+    // independent loads per thread in flight (a row's whole staging in one round
+    // trip for the one-CTA rows), whichever runs they fall in
+    constexpr int kStage = kT >= 1024 ? 8 : 16;
+    for (uint32_t e0 = q0; e0 < q1; e0 += kStage * kT) {
+      uint64_t v[kStage];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < kStage; ++u) {
         const uint32_t e = e0 + uint32_t(u * kT + tid);
         v[u] = 0;
         if (e < q1) {
@@ -1528,7 +1530,7 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
         }
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < kStage; ++u) {
         const uint32_t e = e0 + uint32_t(u * kT + tid);
         if (e < q1) buf[e] = v[u];
       }
