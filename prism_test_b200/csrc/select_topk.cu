@@ -811,6 +811,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
       };
+      // Keys are compared as floats first (a superset: NaN passes, and -0 against a
+      // +0 threshold) and only those confirmed on their order key; the largest key
+      // is taken over the hits (the fine bins span [thr, largest hit]).
+      const float thr_f = okey_to_float(thr);
       float4 nx[4];
       load_half(0, nx);
       for (int64_t hh = 0; hh < nhalf; ++hh) {
@@ -818,17 +822,19 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
         if (hh + 1 < nhalf) load_half(hh + 1, nx);
         const int64_t base = (hh >> 1) * kPass + my_base;
         const int64_t cb = base + (int64_t(4 * int(hh & 1) * kThreads + tid) << 2);  // column of key 0
-        uint32_t kp[16], h = 0;
+        const bool inside = cb + int64_t(3 * kThreads * 4 + 3) < a.n;  // every key of the half is a column
+        const float fv[16] = {cu[0].x, cu[0].y, cu[0].z, cu[0].w, cu[1].x, cu[1].y, cu[1].z, cu[1].w,
+                              cu[2].x, cu[2].y, cu[2].z, cu[2].w, cu[3].x, cu[3].y, cu[3].z, cu[3].w};
+        uint32_t h = 0;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float fv[4] = {cu[u].x, cu[u].y, cu[u].z, cu[u].w};
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            const int j = 4 * u + x;
-            const int64_t col = cb + int64_t(u) * kThreads * 4 + x;
-            kp[j] = col < a.n ? float_to_okey(fv[x]) : 0u;
-            kmx = max(kmx, kp[j]);
-            if (kp[j] >= thr && kp[j] != 0u) h |= 1u << j;
+        for (int j = 0; j < 16; ++j) {
+          if (!(fv[j] < thr_f)) {
+            const uint32_t key = float_to_okey(fv[j]);
+            const int64_t col = cb + int64_t(j >> 2) * kThreads * 4 + (j & 3);
+            if (key >= thr && (inside || col < a.n)) {
+              h |= 1u << j;
+              kmx = max(kmx, key);
+            }
           }
         }
         if (__any_sync(0xffffffffu, h != 0u)) {
@@ -839,7 +845,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 16; ++j) {
               if (h & (1u << j)) {
                 const int64_t col = cb + int64_t(j >> 2) * kThreads * 4 + (j & 3);
-                dst[__popc(h & ((1u << j) - 1u))] = pack_cand(kp[j], ix ? uint32_t(ix[col]) : uint32_t(col));
+                dst[__popc(h & ((1u << j) - 1u))] =
+                    pack_cand(float_to_okey(fv[j]), ix ? uint32_t(ix[col]) : uint32_t(col));
               }
             }
           }

@@ -155,6 +155,47 @@ def test_topk_merge_matches_torch(cuda_device):
     assert torch.equal(oi, torch.gather(i, 1, rp))
 
 
+def _order_keys(s: torch.Tensor) -> torch.Tensor:
+    """The selection's total order as int64 keys: NaN first, +0 above -0, then the
+    float order (the order key of the library's selection)."""
+    u = s.contiguous().view(torch.int32).long() & 0xFFFFFFFF
+    neg = (u & 0x80000000) != 0
+    key = torch.where(neg, (~u) & 0xFFFFFFFF, u | 0x80000000)
+    return torch.where(torch.isnan(s), torch.full_like(key, 0xFFFFFFFF), key)
+
+
+def test_streamed_select_signed_zero_nan_inf(cuda_device):
+    # rows longer than one pass (streamed): thresholds that land on +0 or -0, NaN
+    # and infinities; expected order: order key descending, then the lower index
+    g = torch.Generator().manual_seed(41)
+    n, k = 300000, 5000
+    s = torch.zeros(4, n)
+    sign = torch.randint(0, 2, (n,), generator=g).bool()
+    s[0] = torch.where(sign, torch.tensor(-0.0), torch.tensor(0.0))
+    s[0, torch.randperm(n, generator=g)[:2000]] = torch.randn(2000, generator=g).abs() + 0.1
+    s[0, torch.randperm(n, generator=g)[:10]] = float("nan")
+    s[1] = -0.0
+    s[1, torch.randperm(n, generator=g)[:100]] = torch.rand(100, generator=g) + 1.0
+    s[2] = torch.randn(n, generator=g)
+    s[2, torch.randperm(n, generator=g)[:7]] = float("inf")
+    s[2, torch.randperm(n, generator=g)[:7]] = float("-inf")
+    s[3] = -1.0 - torch.rand(n, generator=g)  # few zeros: the threshold can land on +0 itself
+    pos = torch.randperm(n, generator=g)
+    s[3, pos[:4000]] = torch.rand(4000, generator=g) + 0.5
+    s[3, pos[4000:7000]] = 0.0
+    s[3, pos[7000:10000]] = -0.0
+    i = torch.arange(n, dtype=torch.int32).expand(4, n).contiguous()
+    oi, os_ = topk_merge(s.to(cuda_device), i.to(cuda_device), k)
+    key = _order_keys(s)
+    # descending key, ascending index: sort by index first (stable), then by key
+    o = torch.sort(key, dim=-1, descending=True, stable=True).indices[:, :k]
+    assert torch.equal(oi.cpu(), o.to(torch.int32))
+    got, want = os_.cpu(), torch.gather(s, 1, o)
+    assert torch.equal(torch.isnan(got), torch.isnan(want))
+    fin = ~torch.isnan(want)
+    assert torch.equal(got[fin].view(torch.int32), want[fin].view(torch.int32))
+
+
 def test_status_word_clean(cuda_device, monkeypatch):
     # with the synchronous check on, every call reads its own device status word
     from prism_test_b200 import kernels
