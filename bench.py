@@ -428,7 +428,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "strong" if wl.name == "decode-1m-sharded" or world > 1 else "weak", "vs_baseline": None,
-        "dtype": "f32 (tf32 MMA)",
+        "dtype": "f32 (host cores)",
         "data": "synthetic", "config": config_of(wl, world, rt, args.exchange),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -87,6 +87,8 @@ def _runs(nruns, rows, run_len, seed, kind="normal", pad=0):
     (5, 50, 3000, 2900, "normal", 30),
     (4, 40, 14000, 14000, "normal", 0),   # ranking by binary searches
     (2, 40, 16384, 16384, "flat", 0),     # ties beyond the staging capacity
+    (16, 40, 2000, 1500, "normal", 0),    # more runs than the CTA's warps
+    (1, 100, 3000, 2000, "ties", 0),      # one run: the tree has no level
 ])
 def test_merge_runs_edge_cases(cuda_device, nruns, rows, run_len, topk, kind, pad):
     v, idx = _runs(nruns, rows, run_len, seed=nruns * 1000 + topk, kind=kind, pad=pad)
