@@ -1346,11 +1346,13 @@ __device__ __forceinline__ void merge_path_range(const uint64_t* X, uint32_t a, 
 }
 
 // Runs the levels on the staged prefixes (in buffer A = bufs[0, cap); buffer B =
-// bufs[cap, 2 cap), used when there are more than two runs) and writes result
-// positions [p0, p1) of the row.
+// bufs[cap, 2 cap), used when there are more than two runs or stage_out is set) and
+// writes result positions [p0, p1) of the row: with stage_out the last level is
+// merged into shared memory too and stored with coalesced stores, else each thread
+// stores its run of consecutive positions as it merges them.
 template <int kT>
 __device__ void merge_tree(uint64_t* bufs, uint32_t cap, const uint32_t* roff, int nruns, uint32_t total,
-                           uint32_t p0, uint32_t p1, int32_t* oi, float* os) {
+                           uint32_t p0, uint32_t p1, int32_t* oi, float* os, bool stage_out) {
   const int tid = threadIdx.x;
   int levels = 0;
   while ((1 << levels) < nruns) ++levels;
@@ -1377,7 +1379,7 @@ __device__ void merge_tree(uint64_t* bufs, uint32_t cap, const uint32_t* roff, i
       const int x1 = min(x0 + (1 << l), nruns), y1 = min(x0 + (2 << l), nruns);
       const uint32_t po = roff[x0], a = roff[x1] - po, b = roff[y1] - roff[x1];
       const uint32_t seg = min(end, po + a + b);
-      if (last) {
+      if (last && !stage_out) {
         merge_path_range(src + po, a, src + po + a, b, pos - po, seg - po,
                          [&](uint32_t d, uint64_t x) { to_result(po + d, x); });
       } else {
@@ -1392,14 +1394,18 @@ __device__ void merge_tree(uint64_t* bufs, uint32_t cap, const uint32_t* roff, i
     src = dst;
     dst = t;
   }
+  // the last level merged into shared memory: its positions go out coalesced
+  if (stage_out)
+    for (uint32_t d = p0 + tid; d < p1; d += kT) to_result(d, src[d]);
 }
 
-// summ: [nruns][kMergeSumm] summary entries; buf: the staging of cap entries (tree:
-// two buffers of cap entries; else cap entries and their cap 4-byte score keys).
+// summ: [nruns][kMergeSumm] summary entries; buf: the staging of cap entries (tree 2:
+// two buffers of cap entries; tree 1: one; tree 0: cap entries and their cap 4-byte
+// score keys, ranked by binary searches).
 template <int kT, int kParts>
 __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, int64_t run_len, int k,
                           int32_t* __restrict__ out_idx, float* __restrict__ out_scores, MergeShared& sm,
-                          uint64_t* summ, uint64_t* buf, uint32_t cap, bool tree, int64_t row,
+                          uint64_t* summ, uint64_t* buf, uint32_t cap, int tree, int64_t row,
                           unsigned part) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   auto cand_at = [&](int r, int64_t j) { return run_cand(runs, r, rows, row, run_len, j); };
@@ -1417,9 +1423,19 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
     // which may cross the interconnect) and copies the rest from its cluster peers'
     // shared memory
     const int ns = nruns * nsum;
-    for (int e = ns * int(part) / kParts + tid; e < ns * int(part + 1) / kParts; e += kT) {
-      const int r = e / nsum, i = e - r * nsum;
-      summ[r * kMergeSumm + i] = cand_at(r, (int64_t(i) + 1) * sstep - 1);
+    const int s0 = ns * int(part) / kParts, s1 = ns * int(part + 1) / kParts;
+    for (int eb = s0 + tid; eb < s1; eb += 8 * kT) {  // eight loads of each thread in flight
+      uint64_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = eb + u * kT;
+        if (e < s1) v[u] = cand_at(e / nsum, (int64_t(e % nsum) + 1) * sstep - 1);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = eb + u * kT;
+        if (e < s1) summ[(e / nsum) * kMergeSumm + e % nsum] = v[u];
+      }
     }
     parts_sync();
     if constexpr (kParts > 1) {
@@ -1435,20 +1451,34 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
       cluster.sync();  // every CTA holds every summary; nobody reads a peer's copy any more
     }
   }
-  for (int e = tid; e < nruns * nsum; e += kT) {
-    const uint64_t v = summ[(e / nsum) * kMergeSumm + e % nsum];
-    int64_t c = 0;
-    for (int q = 0; q < nruns; ++q) {
-      const uint64_t* sq = summ + q * kMergeSumm;
-      int lo = 0, hi = nsum;  // summary entries of run q at or above v
-      while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if (sq[mid] >= v) lo = mid + 1;
-        else hi = mid;
+  {
+    // the largest summary entry whose count reaches k: each thread's best, then the
+    // warp's, then one shared atomic per warp
+    uint64_t best = 0;
+    for (int e = tid; e < nruns * nsum; e += kT) {
+      const int re = e / nsum, ie = e - re * nsum;
+      const uint64_t v = summ[re * kMergeSumm + ie];
+      if (v <= best) continue;
+      int64_t c = ie + 1;  // its own run's summary entries at or above it
+      for (int q = 0; q < nruns; ++q) {
+        if (q == re) continue;
+        const uint64_t* sq = summ + q * kMergeSumm;
+        int lo = 0, hi = nsum;  // summary entries of run q at or above v
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (sq[mid] >= v) lo = mid + 1;
+          else hi = mid;
+        }
+        c += lo;
       }
-      c += lo;
+      if (c * sstep >= int64_t(k)) best = v;
     }
-    if (c * sstep >= int64_t(k)) atomicMax(&sm.rthr, (unsigned long long)v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t u = __shfl_xor_sync(0xffffffffu, best, o);
+      best = u > best ? u : best;
+    }
+    if (lane == 0 && best != 0) atomicMax(&sm.rthr, (unsigned long long)best);
   }
   __syncthreads();
   if (sm.rthr == 0 && warp == 0) {  // no summary reaches k: the largest last candidate
@@ -1558,7 +1588,7 @@ __device__ void merge_row(const int32_t* const* runs, int nruns, int64_t rows, i
       const uint32_t kk = min(uint32_t(k), total);
       merge_tree<kT>(buf, cap, sm.roff, nruns, total, uint32_t(uint64_t(kk) * part / kParts),
                      uint32_t(uint64_t(kk) * (part + 1) / kParts), out_idx + row * k,
-                     out_scores ? out_scores + row * k : nullptr);
+                     out_scores ? out_scores + row * k : nullptr, tree == 2);
       return;
     }
     // the score keys alone, for the binary searches (4-byte probes; the index
@@ -1664,8 +1694,8 @@ __global__ void __cluster_dims__(kParts, 1, 1) __launch_bounds__(kT, kT >= 1024 
     self->t_start = t_start;
     self->t_ready = globaltimer_ns();
   }
-  merge_row<kT, kParts>(sm.runs, nruns, rows, run_len, k, out_idx, out_scores, sm, summ, buf, cap, tree != 0,
-                        row, part);
+  merge_row<kT, kParts>(sm.runs, nruns, rows, run_len, k, out_idx, out_scores, sm, summ, buf, cap, tree, row,
+                        part);
   if (self == nullptr) return;
   __syncthreads();  // this CTA's reads of the runs are complete
   if (tid == 0) {
@@ -1749,20 +1779,25 @@ cudaError_t launch_merge_runs(const RunSet& rs, int nruns, int64_t rows, int64_t
   const int64_t bound = std::min<int64_t>(int64_t(k) + (nruns + 1) * sstep, int64_t(nruns) * run_len);
   const size_t summ = size_t(nruns) * kMergeSumm * sizeof(uint64_t);
   const size_t room = (kMergeMaxSmem - summ) / 8;  // 8-byte words left for the staging
-  // the tree wants a second buffer when it has more than one level
-  const size_t tree_words = size_t(bound) * (nruns > 2 ? 2 : 1);
-  const bool tree = tree_words <= room;
-  // else the ranking by binary searches: the entries and their 4-byte keys
-  const uint32_t cap = tree ? uint32_t(bound) : uint32_t(std::min<size_t>(size_t(bound), room * 8 / 12));
-  const size_t smem = summ + (tree ? tree_words * 8 : size_t(cap) * 12);
   int dev = 0, nsm = 148;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
+  const bool clusters = rows * 4 <= nsm;  // a 4-CTA cluster per row fits one wave
+  // The merge tree (1: each thread stores the result positions it merges; 2, one CTA
+  // per row: the last level merged into shared memory too and stored coalesced, which
+  // measured faster there and slower for the clusters); it wants a second buffer for
+  // more than one level or for the staged last level. Else (0) the ranking by binary
+  // searches: the entries and their 4-byte keys.
+  const size_t words1 = size_t(bound) * (nruns > 2 ? 2 : 1);
+  const int tree = (!clusters && size_t(bound) * 2 <= room) ? 2 : (words1 <= room ? 1 : 0);
+  const size_t tree_words = tree == 2 ? size_t(bound) * 2 : words1;
+  const uint32_t cap = tree ? uint32_t(bound) : uint32_t(std::min<size_t>(size_t(bound), room * 8 / 12));
+  const size_t smem = summ + (tree ? tree_words * 8 : size_t(cap) * 12);
   // the peer merge follows the publish as a dependent launch (it reads the step
   // the publish wrote only after its griddepcontrol.wait)
   const bool pdl = sync.self != nullptr;
-  if (rows * 4 <= nsm) {  // a 4-CTA cluster per row, one wave
+  if (clusters) {
     auto kern = merge_runs_kernel<1024, 4>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
