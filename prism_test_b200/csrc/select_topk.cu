@@ -231,7 +231,7 @@ __device__ void select_row_general(const SelectArgs& a, int64_t row, SelectSmem&
       if (A + sm.hist[b3] <= uint32_t(kCap)) {
         thr = T;
       } else {
-        thr = T + 1;  // keys > T (A < kk of them), then ties in column order
+        thr = T;  // keys > T (A < kk of them; none when T is NaN's key), then ties in column order
         tie_pass = true;
         tie_key = T;
         need_ties = kk - A;
@@ -240,14 +240,14 @@ __device__ void select_row_general(const SelectArgs& a, int64_t row, SelectSmem&
   }
   __syncthreads();
   for_each_key(a, row, 0, a.n, [&](uint32_t key, uint32_t idx) {
-    if (key >= thr) {
+    if (tie_pass ? key > tie_key : key >= thr) {
       const int slot = atomicAdd(&sm.ncand, 1);
       if (slot < kCap) sm.buf[slot] = pack_cand(key, idx);
     }
   });
   __syncthreads();
   if (tie_pass) {
-    const int base0 = sm.ncand;
+    const int base0 = min(sm.ncand, kCap);
     uint32_t taken = 0;
     const float* sc = a.scores + row * a.ld;
     const int32_t* ix = a.idx_in ? a.idx_in + row * a.ld : nullptr;
@@ -262,7 +262,8 @@ __device__ void select_row_general(const SelectArgs& a, int64_t row, SelectSmem&
       }
       uint32_t chunk_total;
       const uint32_t rank = block_excl_scan(tie ? 1u : 0u, sm, &chunk_total);
-      if (tie && taken + rank < need_ties) sm.buf[base0 + taken + rank] = pack_cand(key, idx);
+      if (tie && taken + rank < need_ties && base0 + int(taken + rank) < kCap)
+        sm.buf[base0 + taken + rank] = pack_cand(key, idx);
       taken += chunk_total;
     }
     __syncthreads();
@@ -811,9 +812,14 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
       };
-      // Keys are compared as floats first (a superset: NaN passes, and -0 against a
-      // +0 threshold) and only those confirmed on their order key; the largest key
-      // is taken over the hits (the fine bins span [thr, largest hit]).
+      // Keys are compared as floats: for every threshold up to +inf's order key the
+      // float test equals the order-key test, except -0 against a +0 threshold, which
+      // is lowered to -0 (a superset; every CTA of the row does the same). Thresholds
+      // in the NaN range (rows dominated by NaN) confirm each passing key on its
+      // order key. The largest key is taken over the stored hits (the fine bins span
+      // [thr, largest hit]; a CTA that cannot store all its hits fails the fast path).
+      if (thr == 0x80000000u) thr = 0x7fffffffu;
+      const bool float_exact = thr <= 0xff800000u;
       const float thr_f = okey_to_float(thr);
       float4 nx[4];
       load_half(0, nx);
@@ -826,16 +832,18 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
         const float fv[16] = {cu[0].x, cu[0].y, cu[0].z, cu[0].w, cu[1].x, cu[1].y, cu[1].z, cu[1].w,
                               cu[2].x, cu[2].y, cu[2].z, cu[2].w, cu[3].x, cu[3].y, cu[3].z, cu[3].w};
         uint32_t h = 0;
+        if (float_exact) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (!(fv[j] < thr_f)) {
-            const uint32_t key = float_to_okey(fv[j]);
-            const int64_t col = cb + int64_t(j >> 2) * kThreads * 4 + (j & 3);
-            if (key >= thr && (inside || col < a.n)) {
-              h |= 1u << j;
-              kmx = max(kmx, key);
-            }
-          }
+          for (int j = 0; j < 16; ++j) h |= (fv[j] < thr_f ? 0u : 1u) << j;  // NaN: a hit
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (!(fv[j] < thr_f) && float_to_okey(fv[j]) >= thr) h |= 1u << j;
+        }
+        if (!inside) {  // the padding past the row's end
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (cb + int64_t(j >> 2) * kThreads * 4 + (j & 3) >= a.n) h &= ~(1u << j);
         }
         if (__any_sync(0xffffffffu, h != 0u)) {
           const uint32_t slot = hit_slot(h, sm);
@@ -845,8 +853,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 16; ++j) {
               if (h & (1u << j)) {
                 const int64_t col = cb + int64_t(j >> 2) * kThreads * 4 + (j & 3);
-                dst[__popc(h & ((1u << j) - 1u))] =
-                    pack_cand(float_to_okey(fv[j]), ix ? uint32_t(ix[col]) : uint32_t(col));
+                const uint32_t key = float_to_okey(fv[j]);
+                kmx = max(kmx, key);
+                dst[__popc(h & ((1u << j) - 1u))] = pack_cand(key, ix ? uint32_t(ix[col]) : uint32_t(col));
               }
             }
           }

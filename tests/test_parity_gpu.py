@@ -169,7 +169,7 @@ def test_streamed_select_signed_zero_nan_inf(cuda_device):
     # and infinities; expected order: order key descending, then the lower index
     g = torch.Generator().manual_seed(41)
     n, k = 300000, 5000
-    s = torch.zeros(4, n)
+    s = torch.zeros(5, n)
     sign = torch.randint(0, 2, (n,), generator=g).bool()
     s[0] = torch.where(sign, torch.tensor(-0.0), torch.tensor(0.0))
     s[0, torch.randperm(n, generator=g)[:2000]] = torch.randn(2000, generator=g).abs() + 0.1
@@ -184,7 +184,9 @@ def test_streamed_select_signed_zero_nan_inf(cuda_device):
     s[3, pos[:4000]] = torch.rand(4000, generator=g) + 0.5
     s[3, pos[4000:7000]] = 0.0
     s[3, pos[7000:10000]] = -0.0
-    i = torch.arange(n, dtype=torch.int32).expand(4, n).contiguous()
+    s[4] = torch.randn(n, generator=g)  # mostly NaN: NaN keys tie beyond the candidate buffer
+    s[4, torch.randperm(n, generator=g)[: n * 2 // 5]] = float("nan")
+    i = torch.arange(n, dtype=torch.int32).expand(5, n).contiguous()
     oi, os_ = topk_merge(s.to(cuda_device), i.to(cuda_device), k)
     key = _order_keys(s)
     # descending key, ascending index: sort by index first (stable), then by key
